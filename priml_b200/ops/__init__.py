@@ -1,0 +1,163 @@
+"""Hot ops: hand-written sm_100a kernels on CUDA, pure-torch oracles elsewhere.
+
+Every public op here dispatches on the device of its inputs:
+
+* CUDA tensors run the in-tree extension ``priml_b200.ops._C`` (tcgen05/TMA
+  GEMMs, attention, fused norm/rope/CE/optimizer kernels). When the extension
+  is missing on a CUDA device the op raises -- there is no silent fallback.
+* CPU tensors (and ``PRIML_B200_REFERENCE=1``) run :mod:`priml_b200.ops.reference`.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+from torch import Tensor
+
+from priml_b200.ops import reference
+from priml_b200.ops._loader import native, native_available
+
+__all__ = [
+    "adamw_",
+    "attention",
+    "cross_entropy",
+    "grouped_swiglu_mlp",
+    "linear",
+    "linear_cross_entropy",
+    "linear_swiglu",
+    "native",
+    "native_available",
+    "reference",
+    "reference_forced",
+    "rms_norm",
+    "rotary",
+    "swiglu",
+    "use_native",
+]
+
+
+def use_native(*tensors: Tensor | None) -> bool:
+    """True when these tensors should take the CUDA kernel path."""
+    if os.environ.get("PRIML_B200_REFERENCE", "0") == "1":
+        return False
+    return any(t is not None and t.is_cuda for t in tensors)
+
+
+def reference_forced() -> bool:
+    """True when ``PRIML_B200_REFERENCE=1`` pins every op to the torch oracle."""
+    return os.environ.get("PRIML_B200_REFERENCE", "0") == "1"
+
+
+def _compute_dtype(x: Tensor) -> torch.dtype:
+    if x.is_cuda and torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype
+
+
+def linear(x: Tensor, weight: Tensor, bias: Tensor | None = None) -> Tensor:
+    """``x @ weight.T (+ bias)``; weight ``[N, K]`` in its master dtype."""
+    if use_native(x) and _compute_dtype(x) == torch.bfloat16:
+        from priml_b200.ops import functional
+
+        return functional.linear(x, weight, bias)
+    if x.is_cuda and torch.is_autocast_enabled("cuda"):
+        return torch.nn.functional.linear(x, weight, bias)
+    return reference.linear(x, weight, bias)
+
+
+def rms_norm(x: Tensor, weight: Tensor | None, eps: float | None) -> Tensor:
+    if use_native(x) and _compute_dtype(x) in (torch.bfloat16, torch.float32):
+        from priml_b200.ops import functional
+
+        return functional.rms_norm(x, weight, eps)
+    return reference.rms_norm(x, weight, eps)
+
+
+def rotary(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor) -> tuple[Tensor, Tensor]:
+    """Half-split RoPE of ``[B, S, H, D]`` q/k with ``[S, 1, D/2]`` fp32 factors."""
+    if use_native(q) and q.dtype == torch.bfloat16 and cos.shape[-1] * 2 == q.shape[-1]:
+        from priml_b200.ops import functional
+
+        return functional.rotary(q, k, cos, sin)
+    return reference.rotate_half(q, cos, sin), reference.rotate_half(k, cos, sin)
+
+
+def attention(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    *,
+    causal: bool = True,
+    scale: float | None = None,
+    window: int | None = None,
+) -> Tensor:
+    """Flash attention over ``[B, S, H, D]`` with native GQA (no K/V expansion)."""
+    if use_native(q):
+        from priml_b200.ops import functional
+
+        if functional.attention_supported(q, k, v):
+            return functional.attention(q, k, v, causal=causal, scale=scale, window=window)
+    return reference.attention(q, k, v, causal=causal, scale=scale, window=window)
+
+
+def linear_swiglu(x: Tensor, up_weight: Tensor) -> Tensor:
+    """``silu(x @ Wg^T) * (x @ Wu^T)`` for ``up_weight = [Wg; Wu]`` (``[2H, C]``)."""
+    if use_native(x) and _compute_dtype(x) == torch.bfloat16 and up_weight.shape[0] % 16 == 0 and x.shape[-1] % 8 == 0:
+        from priml_b200.ops import functional
+
+        return functional.linear_swiglu(x, up_weight)
+    return swiglu(linear(x, up_weight))
+
+
+def swiglu(gate_up: Tensor) -> Tensor:
+    if use_native(gate_up) and gate_up.dtype == torch.bfloat16:
+        from priml_b200.ops import functional
+
+        return functional.swiglu(gate_up)
+    return reference.swiglu(gate_up)
+
+
+def cross_entropy(logits: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None) -> Tensor:
+    return reference.cross_entropy(logits, targets, ignore_index=ignore_index, softcap=softcap)
+
+
+def linear_cross_entropy(
+    hidden: Tensor,
+    weight: Tensor,
+    targets: Tensor,
+    *,
+    ignore_index: int = -100,
+    softcap: float | None = None,
+) -> Tensor:
+    """Unreduced CE of ``hidden @ weight.T`` without materializing the logits
+    (chunked over tokens on CUDA; fp32 log-sum-exp)."""
+    if use_native(hidden) and _compute_dtype(hidden) == torch.bfloat16:
+        from priml_b200.ops import functional
+
+        return functional.linear_cross_entropy(hidden, weight, targets, ignore_index=ignore_index, softcap=softcap)
+    return reference.linear_cross_entropy(hidden, weight, targets, ignore_index=ignore_index, softcap=softcap)
+
+
+def grouped_swiglu_mlp(x_sorted: Tensor, up_w: Tensor, down_w: Tensor, offsets: Tensor) -> Tensor:
+    """Grouped SwiGLU experts over expert-sorted rows (device-side offsets)."""
+    if use_native(x_sorted) and _compute_dtype(x_sorted) == torch.bfloat16:
+        from priml_b200.ops import functional
+
+        return functional.grouped_swiglu_mlp(x_sorted, up_w, down_w, offsets)
+    return reference.grouped_swiglu_mlp(x_sorted, up_w, down_w, offsets)
+
+
+def adamw_(
+    params: list[Tensor],
+    grads: list[Tensor],
+    exp_avgs: list[Tensor],
+    exp_avg_sqs: list[Tensor],
+    **hyper: float,
+) -> None:
+    if params and use_native(params[0]):
+        from priml_b200.ops import functional
+
+        functional.adamw_(params, grads, exp_avgs, exp_avg_sqs, **hyper)
+        return
+    reference.adamw_(params, grads, exp_avgs, exp_avg_sqs, **hyper)  # type: ignore[arg-type]

@@ -1,0 +1,108 @@
+"""Kernel micro-benchmarks: ``python -m priml_b200.ops.bench_kernels [--json out.json]``.
+
+Times each kernel with CUDA events on its launching stream after warm-up,
+flushing L2 (a 512 MiB write) outside the timed window before every timed
+launch, and reports achieved TFLOP/s or GB/s against the measured peaks in
+``MEASURED_PEAKS.json`` when present. Shapes are the Llama-1B training step
+(16384 tokens = micro-batch 4 x seq 4096, d_model 2048, GQA 32/8 x 64, SwiGLU 8192,
+vocab 32768).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from collections.abc import Callable
+from pathlib import Path
+
+import torch
+
+PEAKS_FILE = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+
+
+def _peaks() -> tuple[float, float]:
+    try:
+        d = json.loads(PEAKS_FILE.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 6650.0
+
+
+def time_fn(fn: Callable[[], object], iters: int = 10, warmup: int = 3) -> float:
+    """Median milliseconds per call, L2 flushed before each timed call."""
+    flush = torch.empty(512 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def gemm_cases(tokens: int = 16384) -> list[tuple[str, int, int, int, bool, bool]]:
+    """(name, M, N, K, a_mn, b_mn) for the forward, dgrad and wgrad GEMMs."""
+    d, hid, vocab, qkv = 2048, 8192, 32768, 3072
+    cases = []
+    for name, n, k in (("qkv", qkv, d), ("o", d, d), ("up", 2 * hid, d), ("down", d, hid), ("lm_head", vocab, d)):
+        cases.append((f"{name}.fwd", tokens, n, k, False, False))
+        cases.append((f"{name}.dgrad", tokens, k, n, False, True))
+        cases.append((f"{name}.wgrad", n, k, tokens, True, True))
+    return cases
+
+
+def bench_gemms(tokens: int = 16384) -> list[dict]:
+    from priml_b200.ops import native
+
+    peak_tf, _ = _peaks()
+    n = native()
+    rows = []
+    for name, m, nn, k, a_mn, b_mn in gemm_cases(tokens):
+        a = torch.randn((k, m) if a_mn else (m, k), device="cuda", dtype=torch.bfloat16)
+        b = torch.randn((k, nn) if b_mn else (nn, k), device="cuda", dtype=torch.bfloat16)
+        wgrad = name.endswith("wgrad")
+        c = torch.empty(m, nn, device="cuda", dtype=torch.float32 if wgrad else torch.bfloat16)
+        epi = 1 if wgrad else 0
+        ours = time_fn(lambda a=a, b=b, c=c, a_mn=a_mn, b_mn=b_mn, epi=epi: n.gemm(a, b, c, a_mn, b_mn, epi))
+        at = a.T if a_mn else a
+        bt = b if b_mn else b.T
+        cub = time_fn(lambda at=at, bt=bt: torch.matmul(at, bt))
+        flops = 2.0 * m * nn * k
+        rows.append(
+            {
+                "case": name,
+                "M": m,
+                "N": nn,
+                "K": k,
+                "ours_ms": round(ours, 4),
+                "ours_tflops": round(flops / ours / 1e9, 1),
+                "frac_of_measured_peak": round(flops / ours / 1e9 / peak_tf, 3),
+                "cublas_ms": round(cub, 4),
+                "speedup_vs_cublas": round(cub / ours, 3),
+            }
+        )
+        del a, b, c
+    return rows
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--json", type=str, default="")
+    ap.add_argument("--tokens", type=int, default=16384)
+    args = ap.parse_args()
+    rows = bench_gemms(args.tokens)
+    for r in rows:
+        print(json.dumps(r))
+    if args.json:
+        Path(args.json).write_text(json.dumps(rows, indent=1))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,308 @@
+// Python bindings for the sm_100a kernels. The only translation unit that
+// includes torch: it validates shapes / dtypes / strides and passes raw
+// pointers plus the current CUDA stream to the kernels.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define PB_CHECK(cond, msg) TORCH_CHECK(cond, "priml_b200: ", msg)
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  PB_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
+}
+
+// Per-device error status word (int32) that kernels write on a timed-out wait.
+Tensor& status_tensor() {
+  static std::mutex mu;
+  static std::unordered_map<int, Tensor> per_dev;
+  int dev = at::cuda::current_device();
+  std::lock_guard<std::mutex> g(mu);
+  auto it = per_dev.find(dev);
+  if (it == per_dev.end()) {
+    it = per_dev.emplace(dev, torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, dev))).first;
+  }
+  return it->second;
+}
+
+int* status_ptr() { return status_tensor().data_ptr<int>(); }
+
+// Leading stride of a 2-D view whose last dim is contiguous.
+long long row_stride(const Tensor& t) {
+  PB_CHECK(t.dim() == 2, "expected a 2-D tensor");
+  PB_CHECK(t.stride(1) == 1 || t.size(1) == 1, "last dim must be contiguous");
+  return t.size(0) == 1 ? t.size(1) : t.stride(0);
+}
+
+// C (op)= A @ B^T in the layouts documented in gemm.cu.
+// A: [M, K] (a_mn = false) or [K, M] (a_mn = true); B: [N, K] or [K, N]; C: [M, N].
+void gemm(const Tensor& A, const Tensor& B, Tensor& C, bool a_mn, bool b_mn, int64_t epi) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  PB_CHECK(A.scalar_type() == torch::kBFloat16 && B.scalar_type() == torch::kBFloat16, "A and B must be bf16");
+  const int M = a_mn ? A.size(1) : A.size(0);
+  const int K = a_mn ? A.size(0) : A.size(1);
+  const int N = b_mn ? B.size(1) : B.size(0);
+  const int KB = b_mn ? B.size(0) : B.size(1);
+  PB_CHECK(K == KB, "contraction sizes differ");
+  PB_CHECK(C.size(0) == M && C.size(1) == N, "C has the wrong shape");
+  if (epi == 0) PB_CHECK(C.scalar_type() == torch::kBFloat16, "epi 0 writes bf16");
+  if (epi == 1 || epi == 2) PB_CHECK(C.scalar_type() == torch::kFloat32, "epi 1/2 write fp32");
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (epi != 2) C.zero_();
+    return;
+  }
+  const c10::cuda::CUDAGuard guard(A.device());
+  pb::gemm_bf16(A.data_ptr(), row_stride(A), a_mn, B.data_ptr(), row_stride(B), b_mn, C.data_ptr(), row_stride(C), M, N,
+                K, static_cast<int>(epi), nullptr, 0, status_ptr(), stream());
+}
+
+// h = silu(x @ Wg^T) * (x @ Wu^T) with W = [Wg; Wu] ([2H, K]); also writes the bf16 pre-activation gu [M, 2H].
+void gemm_swiglu(const Tensor& X, const Tensor& W, Tensor& H, Tensor& GU) {
+  check_cuda(X, "X");
+  PB_CHECK(X.scalar_type() == torch::kBFloat16 && W.scalar_type() == torch::kBFloat16, "bf16 inputs");
+  const int M = X.size(0), K = X.size(1);
+  const int two_h = W.size(0);
+  PB_CHECK(W.size(1) == K && two_h % 2 == 0, "W must be [2H, K]");
+  PB_CHECK(H.size(0) == M && H.size(1) == two_h / 2 && GU.size(0) == M && GU.size(1) == two_h, "bad outputs");
+  PB_CHECK(H.is_contiguous() && GU.is_contiguous(), "outputs must be contiguous");
+  PB_CHECK((two_h / 2) % 8 == 0, "H must be a multiple of 8");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(X.device());
+  pb::gemm_bf16(X.data_ptr(), row_stride(X), false, W.data_ptr(), row_stride(W), false, H.data_ptr(), H.stride(0), M,
+                two_h, K, 3, GU.data_ptr(), two_h / 2, status_ptr(), stream());
+}
+
+std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const c10::optional<Tensor>& w, double eps, bool out_f32) {
+  check_cuda(x, "x");
+  PB_CHECK(x.is_contiguous(), "x must be contiguous");
+  const int C = x.size(-1);
+  PB_CHECK(C % 8 == 0, "channels must be a multiple of 8");
+  const int R = x.numel() / C;
+  auto y = torch::empty(x.sizes(), x.options().dtype(out_f32 ? torch::kFloat32 : torch::kBFloat16));
+  auto rstd = torch::empty({R}, x.options().dtype(torch::kFloat32));
+  const float* wp = nullptr;
+  Tensor wc;
+  if (w.has_value() && w->defined()) {
+    wc = w->to(torch::kFloat32).contiguous();
+    wp = wc.data_ptr<float>();
+  }
+  if (R > 0)
+    pb::rmsnorm_fwd(x.data_ptr(), x.scalar_type() == torch::kFloat32, wp, y.data_ptr(), out_f32, rstd.data_ptr<float>(),
+                    R, C, static_cast<float>(eps), stream());
+  return {y, rstd};
+}
+
+std::vector<Tensor> rmsnorm_bwd(const Tensor& dy, const Tensor& x, const c10::optional<Tensor>& w, const Tensor& rstd,
+                                bool dx_f32) {
+  const int C = x.size(-1);
+  const int R = x.numel() / C;
+  auto dyc = dy.contiguous();
+  auto dx = torch::empty(x.sizes(), x.options().dtype(dx_f32 ? torch::kFloat32 : torch::kBFloat16));
+  Tensor dw, wc;
+  const float* wp = nullptr;
+  float* dwp = nullptr;
+  if (w.has_value() && w->defined()) {
+    wc = w->to(torch::kFloat32).contiguous();
+    wp = wc.data_ptr<float>();
+    dw = torch::zeros({C}, x.options().dtype(torch::kFloat32));
+    dwp = dw.data_ptr<float>();
+  }
+  if (R > 0)
+    pb::rmsnorm_bwd(dyc.data_ptr(), dyc.scalar_type() == torch::kFloat32, x.data_ptr(),
+                    x.scalar_type() == torch::kFloat32, wp, rstd.data_ptr<float>(), dx.data_ptr(), dx_f32, dwp, R, C,
+                    stream());
+  return {dx, dw};
+}
+
+// x: [B, S, H, D] bf16 (last dim contiguous, any other strides). cos/sin: fp32 [S, D/2] contiguous.
+Tensor rope(const Tensor& x, const Tensor& cos, const Tensor& sin, double sign) {
+  check_cuda(x, "x");
+  PB_CHECK(x.dim() == 4 && x.stride(3) == 1 && x.scalar_type() == torch::kBFloat16, "x must be [B,S,H,D] bf16");
+  const int B = x.size(0), S = x.size(1), H = x.size(2), D = x.size(3);
+  PB_CHECK(D % 4 == 0, "head dim must be a multiple of 4");
+  PB_CHECK(cos.numel() == static_cast<long long>(S) * D / 2, "cos must hold S * D/2 values");
+  auto y = torch::empty({B, S, H, D}, x.options());
+  auto c = cos.to(torch::kFloat32).contiguous();
+  auto s = sin.to(torch::kFloat32).contiguous();
+  if (x.numel() > 0)
+    pb::rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), y.data_ptr(), B, S, H, D, c.data_ptr<float>(),
+                   s.data_ptr<float>(), static_cast<float>(sign), stream());
+  return y;
+}
+
+Tensor swiglu_fwd(const Tensor& gu) {
+  PB_CHECK(gu.is_contiguous() && gu.scalar_type() == torch::kBFloat16, "gu must be contiguous bf16");
+  const int H = gu.size(-1) / 2;
+  PB_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
+  auto sizes = gu.sizes().vec();
+  sizes.back() = H;
+  auto h = torch::empty(sizes, gu.options());
+  const long long R = gu.numel() / (2 * H);
+  if (R > 0) pb::swiglu_fwd(gu.data_ptr(), h.data_ptr(), R, H, stream());
+  return h;
+}
+
+Tensor swiglu_bwd(const Tensor& gu, const Tensor& dh) {
+  const int H = gu.size(-1) / 2;
+  auto dhc = dh.contiguous();
+  auto dgu = torch::empty(gu.sizes(), gu.options());
+  const long long R = gu.numel() / (2 * H);
+  if (R > 0) pb::swiglu_bwd(gu.data_ptr(), dhc.data_ptr(), dgu.data_ptr(), R, H, stream());
+  return dgu;
+}
+
+std::vector<Tensor> ce_fwd(const Tensor& logits, const Tensor& targets, int64_t ignore_index) {
+  PB_CHECK(logits.dim() == 2 && logits.scalar_type() == torch::kBFloat16 && logits.stride(1) == 1, "logits [R, V] bf16");
+  const long long R = logits.size(0);
+  const int V = logits.size(1);
+  auto t = targets.to(torch::kInt64).contiguous();
+  auto loss = torch::empty({R}, logits.options().dtype(torch::kFloat32));
+  auto lse = torch::empty({R}, logits.options().dtype(torch::kFloat32));
+  PB_CHECK(logits.stride(0) % 8 == 0, "logits row stride must be a multiple of 8");
+  if (R > 0)
+    pb::ce_fwd(logits.data_ptr(), logits.stride(0), t.data_ptr<int64_t>(), loss.data_ptr<float>(), lse.data_ptr<float>(),
+               R, V, ignore_index, stream());
+  return {loss, lse};
+}
+
+// Writes d(logits) into `out` (may alias logits).
+void ce_bwd(const Tensor& logits, const Tensor& targets, const Tensor& lse, const Tensor& g, Tensor& out,
+            int64_t ignore_index) {
+  const long long R = logits.size(0);
+  const int V = logits.size(1);
+  auto t = targets.to(torch::kInt64).contiguous();
+  auto gf = g.to(torch::kFloat32).contiguous();
+  const long long g_stride = gf.numel() == 1 ? 0 : 1;
+  PB_CHECK(out.stride(0) == logits.stride(0), "out must share the logits layout");
+  if (R > 0)
+    pb::ce_bwd(logits.data_ptr(), logits.stride(0), t.data_ptr<int64_t>(), lse.data_ptr<float>(), gf.data_ptr<float>(),
+               g_stride, out.data_ptr(), R, V, ignore_index, stream());
+}
+
+// Multi-tensor optimizer plan: device-resident tensor table + chunk map, built once per parameter set.
+class MultiTensorPlan {
+ public:
+  MultiTensorPlan(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> m, std::vector<Tensor> v,
+                  std::vector<c10::optional<Tensor>> shadows, int64_t chunk)
+      : params_(params), grads_(grads), m_(m), v_(v), chunk_(static_cast<int>(chunk)) {
+    PB_CHECK(params.size() == grads.size() && params.size() == m.size() && params.size() == v.size(), "list sizes");
+    std::vector<pb::AdamTensor> table;
+    std::vector<int> ct;
+    std::vector<long long> cs;
+    for (size_t i = 0; i < params.size(); ++i) {
+      PB_CHECK(params[i].scalar_type() == torch::kFloat32 && params[i].is_contiguous(), "params must be fp32 contiguous");
+      PB_CHECK(grads[i].is_contiguous() && grads[i].numel() == params[i].numel(), "grad layout");
+      pb::AdamTensor a{};
+      a.p = params[i].data_ptr<float>();
+      a.g = grads[i].data_ptr();
+      a.g_bf16 = grads[i].scalar_type() == torch::kBFloat16;
+      a.m = m[i].data_ptr<float>();
+      a.v = v[i].data_ptr<float>();
+      a.shadow = nullptr;
+      if (i < shadows.size() && shadows[i].has_value() && shadows[i]->defined()) {
+        PB_CHECK(shadows[i]->scalar_type() == torch::kBFloat16 && shadows[i]->is_contiguous(), "shadow bf16");
+        a.shadow = shadows[i]->data_ptr();
+        shadows_.push_back(*shadows[i]);
+      }
+      a.n = params[i].numel();
+      table.push_back(a);
+      for (long long s = 0; s < a.n; s += chunk_) {
+        ct.push_back(static_cast<int>(i));
+        cs.push_back(s);
+      }
+    }
+    num_chunks_ = static_cast<int>(ct.size());
+    auto dev = params.empty() ? torch::Device(torch::kCUDA) : params[0].device();
+    table_ = torch::empty({static_cast<long long>(table.size() * sizeof(pb::AdamTensor))},
+                          torch::dtype(torch::kUInt8).device(dev));
+    if (!table.empty()) {
+      auto host = torch::from_blob(table.data(), {table_.numel()}, torch::kUInt8).clone();
+      table_.copy_(host);
+      chunk_tensor_ = torch::from_blob(ct.data(), {num_chunks_}, torch::kInt32).to(dev);
+      chunk_start_ = torch::from_blob(cs.data(), {num_chunks_}, torch::kInt64).to(dev);
+    }
+  }
+
+  void adamw(double lr, double beta1, double beta2, double eps, double wd, double bias1, double bias2,
+             const c10::optional<Tensor>& grad_scale) {
+    if (num_chunks_ == 0) return;
+    const float* gs = grad_scale.has_value() && grad_scale->defined() ? grad_scale->data_ptr<float>() : nullptr;
+    pb::adamw_multi(reinterpret_cast<const pb::AdamTensor*>(table_.data_ptr()), chunk_tensor_.data_ptr<int>(),
+                    reinterpret_cast<const long long*>(chunk_start_.data_ptr<int64_t>()), num_chunks_, chunk_, lr, beta1, beta2, eps, wd, bias1, bias2, gs,
+                    stream());
+  }
+
+  // Returns [norm, clip] (fp32 device tensors) without a host sync.
+  std::vector<Tensor> grad_norm_clip(double max_norm) {
+    auto opts = torch::dtype(torch::kFloat32).device(params_.empty() ? torch::Device(torch::kCUDA) : params_[0].device());
+    auto sumsq = torch::zeros({1}, opts);
+    auto norm = torch::empty({1}, opts);
+    auto clip = torch::empty({1}, opts);
+    if (num_chunks_ > 0)
+      pb::multi_sumsq(reinterpret_cast<const pb::AdamTensor*>(table_.data_ptr()), chunk_tensor_.data_ptr<int>(),
+                      reinterpret_cast<const long long*>(chunk_start_.data_ptr<int64_t>()), num_chunks_, chunk_, sumsq.data_ptr<float>(), stream());
+    pb::clip_coef(sumsq.data_ptr<float>(), static_cast<float>(max_norm), clip.data_ptr<float>(), norm.data_ptr<float>(),
+                  stream());
+    return {norm, clip};
+  }
+
+  int64_t num_chunks() const { return num_chunks_; }
+
+ private:
+  std::vector<Tensor> params_, grads_, m_, v_, shadows_;
+  Tensor table_, chunk_tensor_, chunk_start_;
+  int num_chunks_ = 0;
+  int chunk_;
+};
+
+Tensor cast_bf16(const Tensor& x, c10::optional<Tensor> out) {
+  PB_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "x must be contiguous fp32");
+  Tensor y = out.has_value() ? *out : torch::empty(x.sizes(), x.options().dtype(torch::kBFloat16));
+  if (x.numel() > 0) pb::cast_f32_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), stream());
+  return y;
+}
+
+int64_t read_status(bool reset) {
+  auto& s = status_tensor();
+  const int64_t v = s.item<int>();
+  if (reset && v != 0) s.zero_();
+  return v;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "priml_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "tcgen05 GEMM: C (op)= A B^T", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
+        py::arg("b_mn"), py::arg("epi"));
+  m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 GEMM with fused SwiGLU epilogue");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("cast_bf16", &cast_bf16, py::arg("x"), py::arg("out") = py::none());
+  m.def("read_status", &read_status, py::arg("reset") = true);
+  py::class_<MultiTensorPlan>(m, "MultiTensorPlan")
+      .def(py::init<std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>,
+                    std::vector<c10::optional<Tensor>>, int64_t>())
+      .def("adamw", &MultiTensorPlan::adamw)
+      .def("grad_norm_clip", &MultiTensorPlan::grad_norm_clip)
+      .def("num_chunks", &MultiTensorPlan::num_chunks);
+}

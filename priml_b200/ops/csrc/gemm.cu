@@ -1,0 +1,399 @@
+// Persistent warp-specialized bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   C[M, N] (op)= sum_k A(m, k) * B(n, k)        fp32 accumulation in TMEM
+//
+// A is given either K-major ([M, K] row-major) or M-major ([K, M] row-major);
+// likewise B is N x K K-major ([N, K]) or N-major ([K, N]). These three layouts
+// cover every GEMM of a linear layer's training step without any transpose:
+//   forward  y  = x  @ W^T : A = x  (K-major), B = W (K-major)
+//   dgrad    dx = dy @ W   : A = dy (K-major), B = W (N-major)
+//   wgrad    dW = dy^T @ x : A = dy (M-major), B = x (N-major)
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: streams 128x64 A and BNx64 B tiles into a ring of
+//               shared-memory stages (128-byte swizzle), completion via mbarrier tx.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into
+//               one of two TMEM accumulators; tcgen05.commit frees smem stages and
+//               hands finished accumulators to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, convert, store to
+//               global (bf16 / fp32 / fp32 accumulate / fused SwiGLU).
+// The double-buffered accumulator lets the epilogue of tile i overlap the MMAs
+// of tile i+1. Tiles are visited in GROUP_M-grouped order for L2 reuse.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pb {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int GROUP_M = 16;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct GemmParams {
+  int M, N, K;
+  void* C;
+  long long ldc;
+  const void* aux;       // SwiGLU: unused; residual add: [M, ldc] bf16
+  int* status;
+  int num_n_half;        // fused SwiGLU: H (gate/up split point in B rows)
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int group = GROUP_M * num_n;
+  const int g = tile / group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(num_m - first_m, GROUP_M);
+  const int r = tile - g * group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+// EPI: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += acc),
+//      3 = fused SwiGLU: the BN columns hold [gate(BN/2) | up(BN/2)] of the same
+//          hidden units; writes bf16 h = silu(gate) * up into C[M, H] and the raw
+//          pre-activation [gate | up] into aux-out (bf16 [M, 2H]) for backward.
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + S * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * BM, n0 = nb * BN;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutProducer, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+        uint8_t* a_dst = smA + stage * Cfg::kABytes;
+        uint8_t* b_dst = smB + stage * Cfg::kBBytes;
+        const int k0 = kb * BK;
+        if constexpr (A_MN) {
+#pragma unroll
+          for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * (BK * 128), &tmA, &full[stage], m0 + 64 * j, k0);
+        } else {
+          tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+        }
+        if constexpr (EPI == 3) {
+          // gate rows [n0/2, n0/2 + BN/2) and up rows [H + n0/2, ...): one tile holds both halves.
+          const int h0 = n0 / 2;
+          tma_load_2d(b_dst, &tmB, &full[stage], k0, h0);
+          tma_load_2d(b_dst + (BN / 2) * 128, &tmB, &full[stage], k0, p.num_n_half + h0);
+        } else if constexpr (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * (BK * 128), &tmB, &full[stage], n0 + 64 * j, k0);
+        } else {
+          tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+        }
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok) {
+      // Drain: let every load already issued land before the CTA exits.
+      for (int i = 0; i < min(issued, S); ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&full[stage], phase, p.status, kTimeoutDrain, nullptr);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int b = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tempty[b], acc_phase ^ 1u, p.status, kTimeoutMma, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + b * BN;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, p.status, kTimeoutMma, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smA + stage * Cfg::kABytes);
+        const uint32_t b_base = smem_u32(smB + stage * Cfg::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = A_MN ? make_sw128_desc(a_base + kk * 2048, BK * 128, 1024)
+                                   : make_sw128_desc(a_base + kk * 32, 16, 1024);
+          const uint64_t bd = (B_MN && EPI != 3) ? make_sw128_desc(b_base + kk * 2048, BK * 128, 1024)
+                                                 : make_sw128_desc(b_base + kk * 32, 16, 1024);
+          umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) umma_commit(&tfull[b]);
+    }
+    // Wait for every MMA this thread issued before anyone frees TMEM.
+    umma_commit(drain);
+    mbar_wait(drain, 0, p.status, kTimeoutDrain, nullptr);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int wq = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int b = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * BM + wq * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * BN;
+      if constexpr (EPI == 3) {
+        const int H = p.num_n_half;
+        const int h0 = nb * (BN / 2);
+        __nv_bfloat16* hout = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
+        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(p.aux)) +
+                            static_cast<long long>(row) * (2LL * H);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_row + c, g);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+          tmem_wait_ld();
+          const int col = h0 + c;
+          if (row_ok && col < H) {
+            uint32_t hv[16], gv[16], uv[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
+              const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
+              // Round gate/up to bf16 first so forward and backward see the same values.
+              const __nv_bfloat162 gb = __floats2bfloat162_rn(g0, g1);
+              const __nv_bfloat162 ub = __floats2bfloat162_rn(u0, u1);
+              const float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
+              const float s0 = gf.x / (1.f + __expf(-gf.x)), s1 = gf.y / (1.f + __expf(-gf.y));
+              hv[j] = pack_bf16x2(s0 * uf.x, s1 * uf.y);
+              gv[j] = *reinterpret_cast<const uint32_t*>(&gb);
+              uv[j] = *reinterpret_cast<const uint32_t*>(&ub);
+            }
+            if (col + 32 <= H) {
+              uint4* hp = reinterpret_cast<uint4*>(hout + col);
+              uint4* gp = reinterpret_cast<uint4*>(gu + col);
+              uint4* up = reinterpret_cast<uint4*>(gu + H + col);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                hp[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+                gp[q] = make_uint4(gv[4 * q], gv[4 * q + 1], gv[4 * q + 2], gv[4 * q + 3]);
+                up[q] = make_uint4(uv[4 * q], uv[4 * q + 1], uv[4 * q + 2], uv[4 * q + 3]);
+              }
+            } else {
+              const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(hv);
+              const __nv_bfloat16* gb2 = reinterpret_cast<const __nv_bfloat16*>(gv);
+              const __nv_bfloat16* ub2 = reinterpret_cast<const __nv_bfloat16*>(uv);
+              for (int j = 0; j < 32 && col + j < H; ++j) {
+                hout[col + j] = hb[j];
+                gu[col + j] = gb2[j];
+                gu[H + col + j] = ub2[j];
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c, v);
+          tmem_wait_ld();
+          const int col = nb * BN + c;
+          if (!row_ok || col >= p.N) continue;
+          const bool full_chunk = col + 32 <= p.N;
+          if constexpr (EPI == 0) {
+            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+            if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+              uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) o4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            } else {
+              const __nv_bfloat16* pb16 = reinterpret_cast<const __nv_bfloat16*>(pk);
+              for (int j = 0; j < 32 && col + j < p.N; ++j) out[j] = pb16[j];
+            }
+          } else {
+            float* out = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+              float4* o4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 a = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                       __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                if constexpr (EPI == 2) {
+                  const float4 o = o4[q];
+                  a.x += o.x;
+                  a.y += o.y;
+                  a.z += o.z;
+                  a.w += o.w;
+                }
+                o4[q] = a;
+              }
+            } else {
+              for (int j = 0; j < 32 && col + j < p.N; ++j) {
+                const float a = __uint_as_float(v[j]);
+                out[j] = EPI == 2 ? out[j] + a : a;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    configured = true;
+  }
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+}
+
+}  // namespace
+
+// Public entry. Layout flags: a_mn = A stored [K, M]; b_mn = B stored [K, N].
+// lda / ldb are the row strides (elements) of A and B as stored.
+void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
+               long long ldc, int M, int N, int K, int epi, const void* aux, int swiglu_h, int* status,
+               cudaStream_t stream) {
+  const int num_sms = device_sm_count();
+  CUtensorMap ta, tb;
+  // A tile: 128 (M) x 64 (K).
+  if (a_mn) {
+    make_tmap_2d_bf16(&ta, A, /*inner=*/M, /*outer=*/K, lda, /*box_inner=*/64, /*box_outer=*/BK);
+  } else {
+    make_tmap_2d_bf16(&ta, A, K, M, lda, 64, BM);
+  }
+  GemmParams p{M, N, K, C, ldc, aux, status, swiglu_h};
+  if (epi == 3) {
+    // B = up_proj weight [2H, K] (K-major); tile rows are split gate / up.
+    make_tmap_2d_bf16(&tb, B, K, 2 * swiglu_h, ldb, 64, 128);
+    launch<256, false, false, 3>(ta, tb, p, num_sms, stream);
+    return;
+  }
+  constexpr int BN = 256;
+  if (b_mn) {
+    make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, BK);
+  } else {
+    make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, BN);
+  }
+#define PB_DISPATCH(AM, BMJ)                                   \
+  switch (epi) {                                               \
+    case 0: launch<BN, AM, BMJ, 0>(ta, tb, p, num_sms, stream); break; \
+    case 1: launch<BN, AM, BMJ, 1>(ta, tb, p, num_sms, stream); break; \
+    default: launch<BN, AM, BMJ, 2>(ta, tb, p, num_sms, stream); break; \
+  }
+  if (!a_mn && !b_mn) {
+    PB_DISPATCH(false, false)
+  } else if (!a_mn && b_mn) {
+    PB_DISPATCH(false, true)
+  } else if (a_mn && !b_mn) {
+    PB_DISPATCH(true, false)
+  } else {
+    PB_DISPATCH(true, true)
+  }
+#undef PB_DISPATCH
+}
+
+}  // namespace pb

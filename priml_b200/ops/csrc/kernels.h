@@ -1,0 +1,71 @@
+// Host-side entry points of the sm_100a kernels (raw pointers, no torch types),
+// so the .cu files build with nvcc alone and bindings.cpp stays the only
+// translation unit that includes torch.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pb {
+
+int device_sm_count();
+// 2-D bf16 tensor map, 128-byte swizzle. `inner` is the contiguous extent,
+// `row_stride` the stride (elements) between consecutive outer rows.
+void make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
+                       int box_inner, int box_outer);
+// 3-D bf16 tensor map (inner, mid, outer) with element strides for mid/outer.
+void make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long inner, long long mid, long long outer,
+                       long long mid_stride, long long outer_stride, int box_inner, int box_mid, bool swizzle128);
+
+// GEMM: C[M,N] (op)= sum_k A(m,k) B(n,k). epi: 0 bf16, 1 fp32, 2 fp32 +=, 3 fused SwiGLU.
+void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
+               long long ldc, int M, int N, int K, int epi, const void* aux, int swiglu_h, int* status,
+               cudaStream_t stream);
+
+// RMSNorm over the last dim C of R rows. x: bf16 or fp32 (x_f32 selects), y: bf16 or fp32.
+void rmsnorm_fwd(const void* x, bool x_f32, const float* w, void* y, bool y_f32, float* rstd, int R, int C, float eps,
+                 cudaStream_t stream);
+void rmsnorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* w, const float* rstd, void* dx,
+                 bool dx_f32, float* dw, int R, int C, cudaStream_t stream);
+
+// Half-split RoPE on [B, S, H, D] views (last dim contiguous); cos/sin fp32 [S, D/2].
+// sign = +1 forward rotation, -1 inverse (backward).
+void rope_apply(const void* x, long long sb, long long ss, long long sh, void* y, int B, int S, int H, int D,
+                const float* cos, const float* sin, float sign, cudaStream_t stream);
+
+// SwiGLU on [R, 2H] (gate | up) -> [R, H]; backward writes d[gate | up].
+void swiglu_fwd(const void* gu, void* h, long long R, int H, cudaStream_t stream);
+void swiglu_bwd(const void* gu, const void* dh, void* dgu, long long R, int H, cudaStream_t stream);
+
+// Cross-entropy over bf16 logits [R, V] (row stride ld): loss[R] (fp32), lse[R];
+// ignore_index rows get loss 0. Backward writes d(logits) = (softmax - onehot) * g[r] in bf16.
+void ce_fwd(const void* logits, long long ld, const int64_t* targets, float* loss, float* lse, long long R, int V,
+            long long ignore_index, cudaStream_t stream);
+void ce_bwd(const void* logits, long long ld, const int64_t* targets, const float* lse, const float* g,
+            long long g_stride, void* dlogits, long long R, int V, long long ignore_index, cudaStream_t stream);
+
+// Multi-tensor AdamW. Tensor descriptors live in device memory (see AdamTensor).
+struct AdamTensor {
+  float* p;
+  const void* g;  // fp32 or bf16 (g_bf16)
+  float* m;
+  float* v;
+  void* shadow;   // optional bf16 copy of the updated parameter (nullptr = none)
+  long long n;
+  int g_bf16;
+  int pad;
+};
+void adamw_multi(const AdamTensor* tensors, const int* chunk_tensor, const long long* chunk_start, int num_chunks,
+                 int chunk_elems, float lr, float beta1, float beta2, float eps, float weight_decay, float bias1,
+                 float bias2, const float* grad_scale, cudaStream_t stream);
+// Sum of squares of every gradient into out[0] (fp32, zeroed by the caller).
+void multi_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const long long* chunk_start, int num_chunks,
+                 int chunk_elems, float* out, cudaStream_t stream);
+// clip[0] = min(1, max_norm / (sqrt(sumsq[0]) + 1e-6)); norm[0] = sqrt(sumsq[0]).
+void clip_coef(const float* sumsq, float max_norm, float* clip, float* norm, cudaStream_t stream);
+
+// fp32 -> bf16 cast of n elements.
+void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);
+
+}  // namespace pb

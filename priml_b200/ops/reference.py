@@ -1,0 +1,145 @@
+"""Pure-torch oracles for every hand-written kernel.
+
+These are the semantics the CUDA kernels reproduce; tests compare the kernels
+against them computed in fp32. They are also the CPU execution path (the
+reference framework itself runs these ops through ATen:
+``priml/model/norm.py:36-74``, ``priml/model/rope.py:348-387``,
+``priml/model/attention.py:107-193``, ``priml/model/swiglu.py:190-213``,
+``priml/baselines/nanochat/train_step.py:43-79``,
+``priml/optimizers/fused_adamw.py:42-83``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+
+def linear(x: Tensor, weight: Tensor, bias: Tensor | None = None) -> Tensor:
+    w = weight.to(x.dtype)
+    return F.linear(x, w, None if bias is None else bias.to(x.dtype))
+
+
+def rms_norm(x: Tensor, weight: Tensor | None, eps: float | None) -> Tensor:
+    return F.rms_norm(x, (x.shape[-1],), weight, eps)
+
+
+def rotate_half(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
+    """Half-split rotation in fp32, rounded once (HuggingFace convention)."""
+    dtype = x.dtype
+    x = x.float()
+    half = x.shape[-1] // 2
+    x0, x1 = x[..., :half], x[..., half:]
+    return torch.cat([x0 * cos - x1 * sin, x1 * cos + x0 * sin], dim=-1).to(dtype)
+
+
+def attention(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    *,
+    causal: bool = True,
+    scale: float | None = None,
+    window: int | None = None,
+) -> Tensor:
+    """``[B, S, H, D]`` x ``[B, T, Hkv, D]`` -> ``[B, S, H, Dv]``; grouped KV heads
+    are shared by ``H // Hkv`` consecutive query heads. Causal masks are aligned
+    bottom-right (query ``i`` sees keys ``<= T - S + i``); ``window`` limits the
+    look-back to ``window`` keys (``key >= pos - window``)."""
+    B, S, H, D = q.shape
+    T, Hkv = k.shape[1], k.shape[2]
+    g = H // Hkv
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qf = q.float().transpose(1, 2)  # B H S D
+    kf = k.float().transpose(1, 2).repeat_interleave(g, dim=1)
+    vf = v.float().transpose(1, 2).repeat_interleave(g, dim=1)
+    s = torch.matmul(qf, kf.transpose(-1, -2)) * scale
+    if causal or window is not None:
+        qi = torch.arange(S, device=q.device)[:, None] + (T - S)
+        kj = torch.arange(T, device=q.device)[None, :]
+        allowed = torch.ones(S, T, dtype=torch.bool, device=q.device)
+        if causal:
+            allowed &= kj <= qi
+        if window is not None:
+            allowed &= kj >= qi - window
+        s = s.masked_fill(~allowed, float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0)
+    o = torch.matmul(p, vf)
+    return o.transpose(1, 2).to(q.dtype)
+
+
+def swiglu(gate_up: Tensor) -> Tensor:
+    gate, up = gate_up.chunk(2, dim=-1)
+    return F.silu(gate) * up
+
+
+def cross_entropy(logits: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None) -> Tensor:
+    """Unreduced token cross-entropy computed in fp32."""
+    lf = logits.float()
+    if softcap is not None:
+        lf = softcap * torch.tanh(lf / softcap)
+    return F.cross_entropy(lf.reshape(-1, lf.shape[-1]), targets.reshape(-1), ignore_index=ignore_index, reduction="none").reshape(
+        targets.shape
+    )
+
+
+def linear_cross_entropy(
+    hidden: Tensor,
+    weight: Tensor,
+    targets: Tensor,
+    *,
+    ignore_index: int = -100,
+    softcap: float | None = None,
+) -> Tensor:
+    logits = linear(hidden, weight)
+    return cross_entropy(logits, targets, ignore_index=ignore_index, softcap=softcap)
+
+
+def adamw_(
+    params: list[Tensor],
+    grads: list[Tensor],
+    exp_avgs: list[Tensor],
+    exp_avg_sqs: list[Tensor],
+    *,
+    step: int,
+    lr: float,
+    beta1: float,
+    beta2: float,
+    eps: float,
+    weight_decay: float,
+) -> None:
+    """AdamW in the FusedAdamW operation order (``priml/optimizers/fused_adamw.py:42-83``):
+    ``p *= 1 - lr*wd``; ``m = lerp(m, g, 1-b1)``; ``v = lerp(v, g*g, 1-b2)``;
+    ``p -= m / (sqrt(v / bias2) + eps) * (lr / bias1)`` -- all in fp32."""
+    bias1 = 1.0 - beta1**step
+    bias2 = 1.0 - beta2**step
+    with torch.no_grad():
+        for p, g, m, v in zip(params, grads, exp_avgs, exp_avg_sqs, strict=True):
+            g32 = g.float()
+            p32 = p if p.dtype == torch.float32 else p.float()
+            p32.mul_(1.0 - lr * weight_decay)
+            m.lerp_(g32, 1.0 - beta1)
+            v.lerp_(g32.square(), 1.0 - beta2)
+            denom = (v / bias2).sqrt() + eps
+            p32.sub_(m / denom * (lr / bias1))
+            if p32.data_ptr() != p.data_ptr():
+                p.copy_(p32)
+
+
+def grouped_swiglu_mlp(x_sorted: Tensor, up_w: Tensor, down_w: Tensor, offsets: Tensor) -> Tensor:
+    """Rows ``offsets[e]:offsets[e+1]`` through expert ``e``:
+    ``down_w[e] @ swiglu(up_w[e] @ x)``; ``up_w [E, 2H, C]``, ``down_w [E, C, H]``."""
+    bounds = offsets.tolist()
+    pieces = []
+    for e in range(up_w.shape[0]):
+        lo, hi = bounds[e], bounds[e + 1]
+        if hi > lo:
+            pieces.append(linear(swiglu(linear(x_sorted[lo:hi], up_w[e])), down_w[e]))
+    if not pieces:
+        return x_sorted.new_zeros(0, down_w.shape[1])
+    return torch.cat(pieces, dim=0)

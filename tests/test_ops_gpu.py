@@ -1,0 +1,186 @@
+"""Numerics of the sm_100a kernels against fp32 PyTorch references of the same op."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _native():
+    from priml_b200.ops import native
+
+    return native()
+
+
+def _rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float(), b.float()
+    return float((a.detach() - b.detach()).abs().max() / b.detach().abs().max().clamp_min(1e-6))
+
+
+LAYOUTS = [(False, False), (False, True), (True, False), (True, True)]
+SHAPES = [(128, 256, 64), (300, 520, 200), (1024, 2048, 512), (2048, 768, 1088)]
+
+
+@pytest.mark.parametrize("a_mn,b_mn", LAYOUTS)
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_gemm_layouts(a_mn: bool, b_mn: bool, m: int, n: int, k: int) -> None:
+    from priml_b200.ops.functional import gemm
+
+    if (a_mn and m % 8) or (b_mn and n % 8):
+        pytest.skip("an M/N-major operand needs its contiguous extent to be a multiple of 8 (16-byte TMA rows)")
+    torch.manual_seed(0)
+    a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(n, k, device="cuda", dtype=torch.bfloat16)
+    ref = a.float() @ b.float().T
+    a_in = a.T.contiguous() if a_mn else a
+    b_in = b.T.contiguous() if b_mn else b
+    out = gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn, out_dtype=torch.float32)
+    assert _rel_err(out, ref) < 2e-3
+    out16 = gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn)
+    assert _rel_err(out16, ref) < 1e-2
+    acc = torch.ones(m, n, device="cuda", dtype=torch.float32)
+    gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn, out=acc, accumulate=True)
+    assert _rel_err(acc, ref + 1) < 2e-3
+    torch.cuda.synchronize()
+    assert _native().read_status(True) == 0
+
+
+def test_gemm_strided_views() -> None:
+    from priml_b200.ops.functional import gemm
+
+    big = torch.randn(512, 3 * 256, device="cuda", dtype=torch.bfloat16)
+    a = big[:, 256:512]  # row stride 768
+    b = torch.randn(384, 256, device="cuda", dtype=torch.bfloat16)
+    out = gemm(a, b, out_dtype=torch.float32)
+    assert _rel_err(out, a.float() @ b.float().T) < 2e-3
+
+
+@pytest.mark.parametrize("m,h,k", [(256, 256, 128), (333, 384, 256), (1024, 1024, 512)])
+def test_gemm_swiglu(m: int, h: int, k: int) -> None:
+    torch.manual_seed(1)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(2 * h, k, device="cuda", dtype=torch.bfloat16) / math.sqrt(k)
+    hh = torch.empty(m, h, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(m, 2 * h, device="cuda", dtype=torch.bfloat16)
+    _native().gemm_swiglu(x, w, hh, gu)
+    ref_gu = x.float() @ w.float().T
+    g, u = ref_gu.chunk(2, dim=-1)
+    assert _rel_err(gu, ref_gu) < 1e-2
+    assert _rel_err(hh, F.silu(g) * u) < 2e-2
+
+
+def test_linear_autograd_matches_fp32() -> None:
+    from priml_b200.ops import functional as fn
+
+    torch.manual_seed(2)
+    x = torch.randn(4, 96, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(768, 512, device="cuda", dtype=torch.float32, requires_grad=True)
+    y = fn.linear(x, w)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().to(torch.bfloat16).float().requires_grad_()
+    yr = xr @ wr.T
+    yr.backward(gy.float())
+    assert _rel_err(y, yr) < 1e-2
+    assert _rel_err(x.grad, xr.grad) < 1e-2
+    assert _rel_err(w.grad, wr.grad) < 2e-3
+
+
+def test_rmsnorm_fwd_bwd() -> None:
+    from priml_b200.ops import functional as fn
+
+    torch.manual_seed(3)
+    for dtype in (torch.bfloat16, torch.float32):
+        x = torch.randn(37, 2048, device="cuda", dtype=dtype, requires_grad=True)
+        w = torch.randn(2048, device="cuda", dtype=torch.float32, requires_grad=True)
+        y = fn.rms_norm(x, w, 1e-5)
+        gy = torch.randn_like(y)
+        y.backward(gy)
+        xr = x.detach().float().requires_grad_()
+        wr = w.detach().requires_grad_()
+        yr = F.rms_norm(xr, (2048,), wr, 1e-5)
+        yr.backward(gy.float())
+        tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+        assert _rel_err(y, yr) < tol
+        assert _rel_err(x.grad, xr.grad) < tol * 2
+        assert _rel_err(w.grad, wr.grad) < 1e-3
+
+
+def test_rope_matches_reference() -> None:
+    from priml_b200.ops import functional as fn
+    from priml_b200.ops import reference
+
+    torch.manual_seed(4)
+    qkv = torch.randn(2, 64, 12, 64, device="cuda", dtype=torch.bfloat16)
+    q, k = qkv[:, :, :8], qkv[:, :, 8:10]
+    pos = torch.arange(64, device="cuda", dtype=torch.float32)
+    inv = 1.0 / (5e5 ** (torch.arange(0, 64, 2, device="cuda").float() / 64))
+    ang = pos[:, None] * inv[None, :]
+    cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
+    qo, ko = fn.rotary(q, k, cos, sin)
+    assert torch.equal(qo, reference.rotate_half(q, cos, sin))
+    assert torch.equal(ko, reference.rotate_half(k, cos, sin))
+
+
+def test_swiglu_and_ce() -> None:
+    from priml_b200.ops import functional as fn
+
+    torch.manual_seed(5)
+    gu = torch.randn(100, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    h = fn.swiglu(gu)
+    g, u = gu.detach().float().chunk(2, -1)
+    assert _rel_err(h, F.silu(g) * u) < 1e-2
+    h.sum().backward()
+    gr = gu.detach().float().requires_grad_()
+    a, b = gr.chunk(2, -1)
+    (F.silu(a) * b).sum().backward()
+    assert _rel_err(gu.grad, gr.grad) < 2e-2
+
+    hid = torch.randn(300, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(1000, 256, device="cuda") / 16).requires_grad_()
+    t = torch.randint(0, 1000, (300,), device="cuda")
+    t[5] = -100
+    loss = fn.linear_cross_entropy(hid, w, t)
+    loss.mean().backward()
+    hr = hid.detach().float().requires_grad_()
+    wr = w.detach().to(torch.bfloat16).float().requires_grad_()
+    logits = (hr @ wr.T).to(torch.bfloat16).float()
+    lr = F.cross_entropy(logits, t, reduction="none")
+    lr.mean().backward()
+    assert _rel_err(loss, lr) < 1e-2
+    assert _rel_err(hid.grad, hr.grad) < 3e-2
+    assert _rel_err(w.grad, wr.grad) < 3e-2
+
+
+def test_adamw_plan_matches_reference() -> None:
+    from priml_b200.ops import reference
+
+    torch.manual_seed(6)
+    shapes = [(1000,), (64, 300), (3,)]
+    ps = [torch.randn(s, device="cuda") for s in shapes]
+    gs = [torch.randn(s, device="cuda") for s in shapes]
+    ms = [torch.zeros(s, device="cuda") for s in shapes]
+    vs = [torch.zeros(s, device="cuda") for s in shapes]
+    shadows = [torch.empty(s, device="cuda", dtype=torch.bfloat16) for s in shapes]
+    rp = [p.clone() for p in ps]
+    rm = [m.clone() for m in ms]
+    rv = [v.clone() for v in vs]
+    plan = _native().MultiTensorPlan(ps, gs, ms, vs, shadows, 4096)
+    for step in (1, 2, 3):
+        b1 = 1 - 0.9**step
+        b2 = 1 - 0.95**step
+        plan.adamw(3e-4, 0.9, 0.95, 1e-8, 0.1, b1, b2, None)
+        reference.adamw_(rp, gs, rm, rv, step=step, lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1)
+    for p, r, s in zip(ps, rp, shadows, strict=True):
+        assert _rel_err(p, r) < 1e-5
+        assert torch.equal(s, p.to(torch.bfloat16))
+    norm, clip = plan.grad_norm_clip(1.0)
+    ref = torch.sqrt(sum((g.float() ** 2).sum() for g in gs))
+    assert abs(float(norm) - float(ref)) / float(ref) < 1e-4
+    assert abs(float(clip) - min(1.0, 1.0 / (float(ref) + 1e-6))) < 1e-6
