@@ -1,0 +1,306 @@
+"""Training-throughput benchmark: Llama-style 1B dense decoder, bf16, FSDP over N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (per GPU, weak scaling): micro-batch 4 x seq 4096 uniform random tokens
+in [0, 32768) (synthetic data, random-init weights: d_model 2048, 16 layers,
+32 q / 8 kv heads x 64, SwiGLU 8192, RMSNorm 1e-5, RoPE 5e5, vocab 32768,
+untied). Full training step: forward, fused LM loss, backward, global-norm
+clip, AdamW (fused kernel). bf16 compute, fp32 master weights and moments.
+
+Two timed phases, each exactly K steps after W untimed warm-up steps:
+
+* device-timed: CUDA events on the compute stream, bracketed by barrier +
+  synchronize on both sides, max over ranks -> ``value`` (tokens/s, whole job);
+* end-to-end through ``TrainStep`` (the public API): every step copies its
+  batch from pinned host memory and reads the loss back to the host -> ``e2e``.
+
+The model's working set (weights, optimizer state, activations: tens of GB)
+far exceeds the 126 MB L2, so no explicit flush is needed between steps.
+SM clocks and throttle reasons are sampled with nvidia-smi during the
+device-timed phase.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+BASELINE_TOKENS_PER_S: float | None = None  # BASELINE.md publishes no B200 / LLM-at-scale number
+
+
+def _parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mbs", type=int, default=4, help="micro-batch per GPU")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--out", type=str, default="")
+    return ap.parse_args()
+
+
+def _reference_unavailable() -> None:
+    print(
+        json.dumps(
+            {
+                "impl": "reference",
+                "unavailable": "pip install of the reference fails offline: its build backend (hatchling) is not in "
+                "the wheelhouse and its git-only dependency configgle cannot be fetched, so the package cannot be "
+                "installed or imported here",
+            }
+        ),
+        flush=True,
+    )
+
+
+class _ClockSampler:
+    """nvidia-smi sampling (200 ms) of SM clock and throttle reasons for this GPU."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+        self.proc: subprocess.Popen | None = None
+
+    def __enter__(self) -> _ClockSampler:
+        try:
+            self.fh = self.path.open("w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL,
+            )  # fmt: skip
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.fh.close()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        active = sorted({n for _, _, flags in rows for n, f in zip(names, flags, strict=True) if f.lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(r[0] for r in rows),
+            "sm_max_mhz": max(r[1] for r in rows),
+            "reasons": active,
+            "samples": len(rows),
+        }
+
+
+def main() -> None:
+    args = _parse()
+    if args.impl == "reference":
+        _reference_unavailable()
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from priml_b200 import cost
+    from priml_b200.data import SyntheticTokens
+    from priml_b200.loss import TokenCrossEntropy
+    from priml_b200.models.presets import dense_lm
+    from priml_b200.optimizers import FusedAdamW
+    from priml_b200.parallel.runtime import MultiProcess, SingleProcess
+    from priml_b200.parallel.strategies import FullySharded, NoParallel
+    from priml_b200.train import TrainStep
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    runtime = (MultiProcess.Config(mesh_topology={"dp": -1}, timeout_s=300.0) if world > 1 else SingleProcess.Config()).make()
+    runtime.initialize()
+    rank = dist.get_rank() if world > 1 else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(1234 + rank)
+
+    shape = cost.DenseLMShape(d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
+                              ffn_hidden=8192, vocab=32768)  # fmt: skip
+    model_cfg = dense_lm(vocab=32768, d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
+                         ffn_hidden=8192, rope_theta=5e5)  # fmt: skip
+    parallel = (
+        FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True)
+        if world > 1
+        else NoParallel.Config()
+    )
+    step_cfg = TrainStep.Config(
+        model=model_cfg,
+        optimizer=FusedAdamW.Config(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1),
+        loss=TokenCrossEntropy.Config(),
+        parallelism=parallel,
+        dtype_autocast=torch.bfloat16,
+        gradient_clip_norm=1.0,
+        device_init="eager",
+    )
+    step = step_cfg.make()
+    if world == 1:
+        step.model.to(dev)
+    tokens_per_step = args.mbs * args.seq * world
+
+    # ------------------------------------------------------------------ device-timed phase
+    vocab = 32768
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    n_batches = args.warmup + args.steps
+    dev_batches = [
+        torch.randint(0, vocab, (args.mbs, args.seq + 1), device=dev, generator=g) for _ in range(min(n_batches, 4))
+    ]
+
+    def run_step(i: int) -> None:
+        seq = dev_batches[i % len(dev_batches)]
+        step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
+
+    for i in range(args.warmup):
+        run_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    from priml_b200.ops import native_available
+
+    status_ok = True
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _ClockSampler(torch.cuda.current_device()) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            run_step(args.warmup + i)
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = tokens_per_step / (ms_per_step / 1e3)
+    if native_available():
+        from priml_b200.ops.functional import check_status
+
+        status_ok = check_status() == 0
+
+    # ------------------------------------------------------------------ launch count (one extra untimed step)
+    launches = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            run_step(0)
+            torch.cuda.synchronize()
+        ours = [e for e in prof.events() if e.device_type.name == "CUDA" and "pb::" in e.name]
+        launches = len(ours) * args.steps
+    except Exception:  # noqa: BLE001
+        launches = None
+
+    # ------------------------------------------------------------------ end-to-end phase (public API)
+    e2e = None
+    if not args.no_e2e:
+        data = SyntheticTokens.Config(vocab_size=vocab, batch_size=args.mbs, seq_len=args.seq, seed=100 + rank,
+                                      steps_per_epoch=n_batches + 8).make()  # fmt: skip
+        it = iter(data.train_dataloader())
+        host_batches = [next(it) for _ in range(n_batches)]
+        h2d = sum(t.numel() * t.element_size() for t in host_batches[0].values())
+        for i in range(args.warmup):
+            out = step.train_step(**step.preprocess_batch(host_batches[i]))
+            float(out["loss"])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            out = step.train_step(**step.preprocess_batch(host_batches[args.warmup + i]))
+            float(out["loss"])  # device -> host read of the step's loss
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([el], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el = float(t.item())
+            dist.barrier()
+        e2e = {
+            "value": round(tokens_per_step * args.steps / el, 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": 4,
+            "ms_per_step": round(el * 1e3 / args.steps, 3),
+        }
+
+    fpt = cost.train_flops_per_token(shape, args.seq)
+    peaks = cost.load_peaks()
+    result = {
+        "metric": "train tokens/s per box at 1/2/4/8 B200 (device-timed, max over ranks); MFU",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 3),
+        "dtype": "bf16",
+        "data": "synthetic (uniform random tokens, random-init weights)",
+        "mfu": round(cost.mfu(value, fpt, world, peaks, sustained=True), 4),
+        "mfu_of": f"{peaks.source} sustained bf16 {peaks.bf16_tflops_sustained} TFLOP/s per GPU",
+        "flops_per_token": fpt,
+        "config": {
+            "model": f"llama-1b dense decoder (d2048 L{args.layers} 32q/8kv h64 swiglu8192 vocab32768 untied)",
+            "global_batch": args.mbs * world,
+            "micro_batch_per_gpu": args.mbs,
+            "seq_len": args.seq,
+            "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+            "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",
+        },
+        "clocks": clocks.summary(),
+        "gpu_launches": launches,
+        "kernel_status_ok": status_ok,
+        "e2e": e2e,
+    }
+    if rank == 0:
+        line = json.dumps(result)
+        print(line, flush=True)
+        if args.out:
+            Path(args.out).write_text(line + "\n")
+    del step
+    runtime.destroy()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

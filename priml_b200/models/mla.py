@@ -260,6 +260,25 @@ class MultiHeadLatentAttention(nn.Module):
 
         return DTensor.from_local(out, self._tp_mesh, [Shard(-1)], run_check=False)
 
+    def shard_heads_over(self, mesh: Any) -> None:
+        """Record this rank's head range for a head-parallel mesh."""
+        tp = mesh.size()
+        if self.heads % tp:
+            raise ValueError(f"heads={self.heads} not divisible by tp={tp}.")
+        self._tp_mesh = mesh
+        self._heads_local = self.heads // tp
+        self._head_offset = mesh.get_local_rank() * self._heads_local
+
+    def tensor_parallel_plan(self) -> dict[str, Any]:
+        from torch.distributed.tensor.parallel import ColwiseParallel, RowwiseParallel
+
+        plan: dict[str, Any] = {"o_proj": RowwiseParallel()}
+        if self.q_proj is not None:
+            plan["q_proj"] = ColwiseParallel()
+        else:
+            plan["q_b_proj"] = ColwiseParallel()
+        return plan
+
     def tensor_parallel_style(self) -> Any:
         """Head-parallel: q path and o_proj sharded over heads, latent replicated."""
         from priml_b200.parallel.tensor_parallel import MLAParallel

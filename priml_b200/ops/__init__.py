@@ -41,6 +41,8 @@ def use_native(*tensors: Tensor | None) -> bool:
     """True when these tensors should take the CUDA kernel path."""
     if os.environ.get("PRIML_B200_REFERENCE", "0") == "1":
         return False
+    if any(t is not None and type(t).__name__ == "DTensor" for t in tensors):
+        return False  # DTensor dispatch (tensor parallel on the decomposed path)
     return any(t is not None and t.is_cuda for t in tensors)
 
 
@@ -57,7 +59,7 @@ def _compute_dtype(x: Tensor) -> torch.dtype:
 
 def linear(x: Tensor, weight: Tensor, bias: Tensor | None = None) -> Tensor:
     """``x @ weight.T (+ bias)``; weight ``[N, K]`` in its master dtype."""
-    if use_native(x) and _compute_dtype(x) == torch.bfloat16:
+    if use_native(x, weight) and _compute_dtype(x) == torch.bfloat16:
         from priml_b200.ops import functional
 
         return functional.linear(x, weight, bias)

@@ -264,7 +264,7 @@ def attention_supported(q: Tensor, k: Tensor, v: Tensor) -> bool:
 
 def attention(q: Tensor, k: Tensor, v: Tensor, *, causal: bool, scale: float | None, window: int | None) -> Tensor:
     """``[B,S,H,D]`` flash attention with grouped KV heads."""
-    from priml_b200.ops import attention as attn_mod
+    from priml_b200.ops import flash as attn_mod
 
     return attn_mod.flash_attention(q, k, v, causal=causal, scale=scale, window=window)
 

@@ -27,6 +27,11 @@ from priml_b200.config import Fig
 __all__ = ["FusedAdamW"]
 
 
+def _local(t: Tensor) -> Tensor:
+    """The rank-local shard of a DTensor (FSDP2 / TP parameter), else ``t``."""
+    return t._local_tensor if hasattr(t, "_local_tensor") else t  # noqa: SLF001
+
+
 class FusedAdamW(Optimizer):
     class Config(Fig["Callable[..., FusedAdamW]"]):
         lr: float = 1e-3
@@ -60,7 +65,7 @@ class FusedAdamW(Optimizer):
             raise ValueError(f"Invalid weight_decay: {weight_decay}.")
         super().__init__(params, {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay})
         self.compile = compile
-        self._plans: dict[int, tuple[tuple, Any]] = {}
+        self._plans: dict[int, tuple[Any, ...]] = {}
         self.grad_scale: Tensor | None = None
         """Optional fp32 device scalar multiplying every gradient (clip coefficient)."""
 
@@ -73,44 +78,65 @@ class FusedAdamW(Optimizer):
             st["second_moment"] = torch.zeros_like(p, memory_format=torch.preserve_format)
         return st
 
-    def _native_group(self, gi: int, group: dict[str, Any], params: list[Tensor]) -> bool:
-        if not ops.native_available() or ops.reference_forced():
-            return False
-        if any(p.dtype != torch.float32 or not p.is_contiguous() or not p.is_cuda for p in params):
-            return False
-        grads = [p.grad for p in params]
+    def _plan(self, gi: int, params: list[Tensor]) -> Any:
+        """Cached device tensor table for group ``gi`` (rebuilt when any pointer moves)."""
+        if not params or not ops.native_available() or ops.reference_forced():
+            return None
+        lp = [_local(p) for p in params]
+        if any(p.dtype != torch.float32 or not p.is_contiguous() or not p.is_cuda for p in lp):
+            return None
+        grads = [_local(p.grad) if p.grad is not None else None for p in params]
         if any(g is None or not g.is_contiguous() or g.dtype not in (torch.float32, torch.bfloat16) for g in grads):
-            return False
+            return None
+        states = [self._state(p) for p in params]
+        ms = [_local(st["first_moment"]) for st in states]
+        vs = [_local(st["second_moment"]) for st in states]
+        shadows = []
+        for p in params:
+            cached = getattr(_local(p), "_pb_shadow", None) or getattr(p, "_pb_shadow", None)
+            shadows.append(cached[1] if cached is not None and cached[1].is_contiguous() else None)
+        key = tuple(
+            (p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), None if s is None else s.data_ptr(), g.dtype)
+            for p, g, m, v, s in zip(lp, grads, ms, vs, shadows, strict=True)
+        )
+        plan = self._plans.get(gi)
+        if plan is None or plan[0] != key:
+            plan = (key, ops.native().MultiTensorPlan([p.detach() for p in lp], grads, ms, vs, shadows, 65536), shadows)
+            self._plans[gi] = plan
+        return plan
+
+    def fused_grad_norm(self, max_norm: float) -> tuple[Tensor, Tensor] | None:
+        """Global gradient norm and clip coefficient as device scalars (no host sync)."""
+        sq = None
+        sharded = False
+        for gi, group in enumerate(self.param_groups):
+            params = [p for p in group["params"] if p.grad is not None]
+            if not params:
+                continue
+            plan = self._plan(gi, params)
+            if plan is None:
+                return None
+            sharded = sharded or any(hasattr(p, "_local_tensor") for p in params)
+            n, _ = plan[1].grad_norm_clip(1.0)
+            sq = n * n if sq is None else sq + n * n
+        if sq is None:
+            return None
+        if sharded and torch.distributed.is_available() and torch.distributed.is_initialized():
+            torch.distributed.all_reduce(sq)
+        norm = sq.sqrt()
+        return norm, (max_norm / (norm + 1e-6)).clamp(max=1.0)
+
+    def _native_group(self, gi: int, group: dict[str, Any], params: list[Tensor]) -> bool:
         from priml_b200.ops import functional as fn
 
+        plan = self._plan(gi, params)
+        if plan is None:
+            return False
         states = [self._state(p) for p in params]
         steps = {st["step"] for st in states}
         if len(steps) != 1:
             return False
-        shadows = []
-        for p in params:
-            cached = getattr(p, "_pb_shadow", None)
-            shadows.append(cached[1] if cached is not None and cached[1].is_contiguous() else None)
-        key = tuple(
-            (p.data_ptr(), g.data_ptr(), st["first_moment"].data_ptr(), st["second_moment"].data_ptr(),
-             None if s is None else s.data_ptr(), g.dtype)
-            for p, g, st, s in zip(params, grads, states, shadows, strict=True)
-        )  # fmt: skip
-        plan = self._plans.get(gi)
-        if plan is None or plan[0] != key:
-            native = ops.native()
-            plan = (
-                key,
-                native.MultiTensorPlan(
-                    [p.data for p in params],
-                    [g for g in grads],
-                    [st["first_moment"] for st in states],
-                    [st["second_moment"] for st in states],
-                    shadows,
-                    65536,
-                ),
-            )
-            self._plans[gi] = plan
+        shadows = plan[2]
         step = next(iter(steps)) + 1
         for st in states:
             st["step"] = step
@@ -121,7 +147,7 @@ class FusedAdamW(Optimizer):
         plan[1].adamw(group["lr"], b1, b2, group["eps"], group["weight_decay"], bias1, bias2, self.grad_scale)
         for p, s in zip(params, shadows, strict=True):
             if s is not None:
-                fn.mark_shadow_fresh(p)
+                fn.mark_shadow_fresh(_local(p))
         return True
 
     @torch.no_grad()
