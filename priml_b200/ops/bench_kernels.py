@@ -96,12 +96,74 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", type=str, default="")
     ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--attn-only", action="store_true")
+    ap.add_argument("--profile", type=str, default="")
     args = ap.parse_args()
-    rows = bench_gemms(args.tokens)
+    if args.profile:
+        profile_case(args.profile)
+        return
+    rows = bench_gemms(args.tokens) if not args.attn_only else []
+    rows += bench_attention()
     for r in rows:
         print(json.dumps(r))
     if args.json:
         Path(args.json).write_text(json.dumps(rows, indent=1))
+
+
+def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int = 64) -> list[dict]:
+    """Causal GQA attention fwd / fwd+bwd: ours vs torch SDPA (cuDNN / flash)."""
+    import math as _m
+
+    import torch.nn.functional as F
+
+    from priml_b200.ops.attention_fn import FlashAttnFn
+
+    q = torch.randn(b, s, h, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(b, s, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(b, s, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    do = torch.randn(b, s, h, d, device="cuda", dtype=torch.bfloat16)
+    sc = 1 / _m.sqrt(d)
+    flops_f = 4.0 * b * h * s * s * d / 2
+    rows = []
+
+    def ours_f():
+        return FlashAttnFn.apply(q, k, v, True, sc, -1)
+
+    def sdpa_f():
+        return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
+                                              enable_gqa=True)  # fmt: skip
+
+    for name, f in (("ours", ours_f), ("sdpa", sdpa_f)):
+        with torch.no_grad():
+            t_f = time_fn(f)
+        t_fb = time_fn(lambda f=f: torch.autograd.backward(f(), do if name == "ours" else do.transpose(1, 2)))
+        rows.append({"case": f"attn.{name}", "B": b, "S": s, "H": h, "Hkv": hkv, "D": d, "fwd_ms": round(t_f, 3),
+                     "fwd_tflops": round(flops_f / t_f / 1e9, 1), "fwdbwd_ms": round(t_fb, 3),
+                     "bwd_tflops": round(2.5 * flops_f / (t_fb - t_f) / 1e9, 1)})  # fmt: skip
+    return rows
+
+
+def profile_case(name: str) -> None:
+    """Run one small instance of a kernel a few times (for an external profiler)."""
+    from priml_b200.ops import native
+    from priml_b200.ops.attention_fn import FlashAttnFn
+
+    n = native()
+    if name == "gemm":
+        a = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
+        c = torch.empty(8192, 8192, device="cuda", dtype=torch.bfloat16)
+        for _ in range(3):
+            n.gemm(a, b, c, False, False, 0)
+    elif name in ("attn_fwd", "attn_bwd"):
+        q = torch.randn(1, 4096, 32, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        k = torch.randn(1, 4096, 8, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        v = torch.randn(1, 4096, 8, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        for _ in range(2):
+            o = FlashAttnFn.apply(q, k, v, True, 0.125, -1)
+            if name == "attn_bwd":
+                o.backward(torch.ones_like(o))
+    torch.cuda.synchronize()
 
 
 if __name__ == "__main__":

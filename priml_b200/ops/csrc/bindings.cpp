@@ -276,6 +276,53 @@ Tensor cast_bf16(const Tensor& x, c10::optional<Tensor> out) {
   return y;
 }
 
+pb::AttnTensor attn_view(const Tensor& t, const char* name) {
+  PB_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16, std::string(name) + " must be CUDA bf16");
+  PB_CHECK(t.dim() == 4, std::string(name) + " must be [B, S, H, D]");
+  PB_CHECK(t.stride(3) == 1 && t.stride(2) == t.size(3), std::string(name) + " needs contiguous heads x head_dim");
+  PB_CHECK((t.stride(1) * 2) % 16 == 0 && (t.stride(0) * 2) % 16 == 0, std::string(name) + " strides must be 16-byte aligned");
+  PB_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, std::string(name) + " must be 16-byte aligned");
+  return pb::AttnTensor{t.data_ptr(), static_cast<int>(t.size(0)), static_cast<int>(t.size(1)), t.stride(0), t.stride(1)};
+}
+
+// (o [B,S,H,D] bf16, lse [B,H,S] fp32)
+std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, double scale, bool causal,
+                             int64_t window) {
+  const int D = q.size(3), H = q.size(2), Hkv = k.size(2);
+  PB_CHECK(D == 64 || D == 128, "head dim must be 64 or 128");
+  PB_CHECK(v.size(3) == D && k.size(3) == D && H % Hkv == 0 && v.size(2) == Hkv, "q/k/v shapes");
+  PB_CHECK(k.size(0) == q.size(0) && v.size(1) == k.size(1), "batch / key lengths");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto o = torch::empty({q.size(0), q.size(1), H, D}, q.options());
+  // 128 floats of tail padding: the backward reads lse rows in 512-byte bulk copies.
+  const long long n_lse = q.size(0) * H * q.size(1);
+  auto lse = torch::empty({n_lse + 128}, q.options().dtype(torch::kFloat32)).narrow(0, 0, n_lse).view({q.size(0), H, q.size(1)});
+  if (q.numel() == 0) return {o, lse};
+  pb::attn_fwd(attn_view(q, "q"), attn_view(k, "k"), attn_view(v, "v"), attn_view(o, "o"), lse.data_ptr<float>(), H, Hkv,
+               D, static_cast<float>(scale), causal, static_cast<int>(window), status_ptr(), stream());
+  return {o, lse};
+}
+
+// (dq, dk, dv) in the layouts of q / k / v (contiguous).
+std::vector<Tensor> attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& dout,
+                             const Tensor& lse, double scale, bool causal, int64_t window) {
+  const int D = q.size(3), H = q.size(2), Hkv = k.size(2);
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto dq = torch::empty({q.size(0), q.size(1), H, D}, q.options());
+  auto dk = torch::empty({k.size(0), k.size(1), Hkv, D}, k.options());
+  auto dv = torch::empty({v.size(0), v.size(1), Hkv, D}, v.options());
+  const long long n_rows = q.size(0) * H * q.size(1);
+  auto delta = torch::empty({n_rows + 128}, q.options().dtype(torch::kFloat32)).narrow(0, 0, n_rows);
+  PB_CHECK(lse.is_contiguous() && lse.numel() == n_rows, "lse must be the forward's [B, H, S] output");
+  auto doc = dout.stride(3) == 1 && dout.stride(2) == D ? dout : dout.contiguous();
+  if (q.numel() == 0) return {dq, dk, dv};
+  pb::attn_bwd(attn_view(q, "q"), attn_view(k, "k"), attn_view(v, "v"), attn_view(o, "o"), attn_view(doc, "dout"),
+               lse.data_ptr<float>(), delta.data_ptr<float>(), attn_view(dq, "dq"), attn_view(dk, "dk"),
+               attn_view(dv, "dv"), H, Hkv, D, static_cast<float>(scale), causal, static_cast<int>(window),
+               status_ptr(), stream());
+  return {dq, dk, dv};
+}
+
 int64_t read_status(bool reset) {
   auto& s = status_tensor();
   const int64_t v = s.item<int>();
@@ -297,6 +344,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd", &ce_bwd);
+  m.def("attn_fwd", &attn_fwd, "flash attention forward (tcgen05)");
+  m.def("attn_bwd", &attn_bwd, "flash attention backward (tcgen05)");
   m.def("cast_bf16", &cast_bf16, py::arg("x"), py::arg("out") = py::none());
   m.def("read_status", &read_status, py::arg("reset") = true);
   py::class_<MultiTensorPlan>(m, "MultiTensorPlan")

@@ -65,6 +65,22 @@ void multi_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const long 
 // clip[0] = min(1, max_norm / (sqrt(sumsq[0]) + 1e-6)); norm[0] = sqrt(sumsq[0]).
 void clip_coef(const float* sumsq, float max_norm, float* clip, float* norm, cudaStream_t stream);
 
+// Attention operand: [batch, seq, heads, D] bf16 with arbitrary batch / token strides
+// (elements) and contiguous heads x D.
+struct AttnTensor {
+  void* ptr;
+  int batch;
+  int seq;
+  long long s_batch;
+  long long s_seq;
+};
+void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, float* lse, int H,
+              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream);
+void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o,
+              const AttnTensor& dout, const float* lse, float* delta, const AttnTensor& dq, const AttnTensor& dk,
+              const AttnTensor& dv, int H, int Hkv, int D, float scale, bool causal, int window, int* status,
+              cudaStream_t stream);
+
 // fp32 -> bf16 cast of n elements.
 void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);
 
