@@ -44,8 +44,7 @@ static void ensure_context() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (bound_dev != dev) {
-    cudaSetDevice(dev);
-    cudaFree(nullptr);
+    cudaSetDevice(dev);  // initializes the primary context and makes it current (CUDA >= 12)
     bound_dev = dev;
   }
 }
