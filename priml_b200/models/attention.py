@@ -136,6 +136,17 @@ class SdpaNaive(nn.Module):
         **kwargs: Any,
     ) -> Tensor:
         del kwargs
+        if type(q).__name__ == "DTensor":
+            # Tensor parallel (DTensor) path: plain masks replicate implicitly.
+            from torch.distributed.tensor.experimental import implicit_replication
+
+            with implicit_replication():
+                return self._attend(q, k, v, dropout_p, is_causal, attn_mask, window)
+        return self._attend(q, k, v, dropout_p, is_causal, attn_mask, window)
+
+    @staticmethod
+    def _attend(q: Tensor, k: Tensor, v: Tensor, dropout_p: float, is_causal: bool, attn_mask: Tensor | None,
+                window: int) -> Tensor:  # fmt: skip
         k, v = _expand_kv(q, k, v)
         if attn_mask is None:
             attn_mask = window_mask(q, k, window=window)

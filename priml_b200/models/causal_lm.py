@@ -118,21 +118,32 @@ class CausalLM(nn.Module):
             x = out[0] if isinstance(out, tuple) else out
         return self.final_norm(x)
 
-    def forward(self, tokens: Tensor, *args: Any, **kwargs: Any) -> Tensor:
-        del args, kwargs
-        return self.project_to_logits(self.hidden_states(tokens))
+    def forward(
+        self,
+        tokens: Tensor,
+        *args: Any,
+        targets: Tensor | None = None,
+        ignore_index: int = -100,
+        **kwargs: Any,
+    ) -> Tensor:
+        """Logits ``[B, S, V]``; with ``targets``, the unreduced next-token CE ``[B, S]``.
 
-    def token_loss(self, tokens: Tensor, targets: Tensor, *, ignore_index: int = -100) -> Tensor:
-        """Unreduced next-token cross-entropy ``[B, S]`` (fp32).
-
-        Uses the fused linear + CE path whenever the head is a plain linear map;
-        any other head (soft-capped, DTensor-sharded, ...) goes through logits.
+        The loss form never materializes logits when the head is a plain linear
+        map (fused linear + CE on CUDA). It goes through ``forward`` so wrappers
+        that hook ``__call__`` (FSDP unshard / reshard) see it.
         """
+        del args, kwargs
         h = self.hidden_states(tokens)
-        plain = self.tie_embeddings or type(self.lm_head) is Linear and self.lm_head.bias is None  # type: ignore[union-attr]
+        if targets is None:
+            return self.project_to_logits(h)
+        plain = self.tie_embeddings or (type(self.lm_head) is Linear and self.lm_head.bias is None)  # type: ignore[union-attr]
         if plain and not _is_dtensor(self.output_weight):
             return ops.linear_cross_entropy(h, self.output_weight, targets, ignore_index=ignore_index)
         return ops.cross_entropy(self.project_to_logits(h), targets, ignore_index=ignore_index)
+
+    def token_loss(self, tokens: Tensor, targets: Tensor, *, ignore_index: int = -100) -> Tensor:
+        """Unreduced next-token cross-entropy ``[B, S]`` (fp32); see :meth:`forward`."""
+        return self(tokens, targets=targets, ignore_index=ignore_index)
 
 
 def _is_dtensor(t: Tensor) -> bool:

@@ -1,0 +1,166 @@
+"""Distributed plumbing on CPU gloo ranks (no GPU): FSDP / DDP / TP / seeding / checkpoints."""
+
+from __future__ import annotations
+
+import tempfile
+
+import pytest
+import torch
+
+from priml_b200.testing import WorkerPool, run_ranks
+
+
+def _tiny_step_cfg(parallelism=None):  # noqa: ANN001, ANN202
+    from priml_b200.loss import TokenCrossEntropy
+    from priml_b200.models.presets import tiny_lm
+    from priml_b200.optimizers import FusedAdamW
+    from priml_b200.train import TrainStep
+
+    return TrainStep.Config(
+        model=tiny_lm(),
+        optimizer=FusedAdamW.Config(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1),
+        loss=TokenCrossEntropy.Config(),
+        parallelism=parallelism,
+    )
+
+
+def _batches(n: int, world: int) -> list[torch.Tensor]:
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, 512, (8 * world, 65), generator=g) for _ in range(n)]
+
+
+def _fsdp_losses(rank: int, world: int, steps: int) -> list[float]:
+    from priml_b200.parallel.strategies import FullySharded
+
+    torch.manual_seed(0)
+    step = _tiny_step_cfg(FullySharded.Config(device="cpu")).make()
+    losses = []
+    for seq in _batches(steps, world):
+        local = seq.chunk(world)[rank]
+        out = step.train_step(tokens=local[:, :-1], targets=local[:, 1:])
+        t = out["loss"].detach().clone()
+        torch.distributed.all_reduce(t)
+        losses.append(float(t) / world)
+    return losses
+
+
+def _single_losses(steps: int, world: int) -> list[float]:
+    torch.manual_seed(0)
+    step = _tiny_step_cfg().make()
+    losses = []
+    for seq in _batches(steps, world):
+        out = step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
+        losses.append(float(out["loss"]))
+    return losses
+
+
+def test_fsdp_world2_matches_single_process() -> None:
+    """The tiny fp32 LM trained as FSDP world_size=2 on gloo tracks the 1-process run."""
+    steps = 4
+    ranks = run_ranks(_fsdp_losses, 2, steps, mesh_shape={"dp": 2})
+    ref = _single_losses(steps, 2)
+    assert ranks[0] == ranks[1]
+    for a, b in zip(ranks[0], ref, strict=True):
+        assert abs(a - b) < 1e-4 * max(1.0, abs(b))
+
+
+def _ddp_grads(rank: int, world: int) -> float:
+    from priml_b200.parallel.strategies import DataParallel
+
+    torch.manual_seed(0)
+    step = _tiny_step_cfg(DataParallel.Config(device="cpu")).make()
+    seq = _batches(1, world)[0].chunk(world)[rank]
+    out = step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
+    return float(out["loss"])
+
+
+def test_ddp_world2_runs() -> None:
+    losses = run_ranks(_ddp_grads, 2, mesh_shape={"dp": 2})
+    assert all(5.0 < x < 8.0 for x in losses)
+
+
+def _tp_matches_dense(rank: int, world: int) -> float:
+    from torch.distributed.tensor import DTensor
+
+    from priml_b200.models import SdpaNaive, SelfAttention, SwiGLU, TransformerBlock
+    from priml_b200.parallel.runtime import global_device_mesh
+    from priml_b200.parallel.tensor_parallel import apply_tensor_parallel
+
+    torch.manual_seed(0)
+    cfg = TransformerBlock.Config(
+        32, attn=SelfAttention.Config(heads=4, num_heads_kv=2, causal=True, attn_kernel=SdpaNaive.Config()),
+        ffn=SwiGLU.Config(channels_hidden=64),
+    )  # fmt: skip
+    dense = cfg.make()
+    tp = cfg.make()
+    tp.load_state_dict(dense.state_dict())
+    apply_tensor_parallel(tp, global_device_mesh(), mesh_dim="tp")
+    x = torch.randn(2, 8, 32, generator=torch.Generator().manual_seed(1))
+    y_ref = dense(x)
+    y = tp(x)
+    y = y.full_tensor() if isinstance(y, DTensor) else y
+    return float((y - y_ref).abs().max())
+
+
+def test_tensor_parallel_block_matches_dense() -> None:
+    errs = run_ranks(_tp_matches_dense, 2, mesh_shape={"tp": 2})
+    assert max(errs) < 1e-5
+
+
+def _seed_agree(rank: int, world: int) -> int:
+    from priml_b200.math.seed import set_seed_distributed
+
+    return set_seed_distributed(None)
+
+
+def test_seed_broadcast_agrees_across_ranks() -> None:
+    with WorkerPool(2) as pool:
+        seeds = pool(_seed_agree)
+        seeds2 = pool(_seed_agree)
+    assert seeds[0] == seeds[1]
+    assert seeds2[0] == seeds2[1]
+
+
+def _dcp_roundtrip(rank: int, world: int, path: str) -> float:
+    from priml_b200.parallel.strategies import FullySharded
+    from priml_b200.train import Checkpointer
+
+    torch.manual_seed(0)
+    step = _tiny_step_cfg(FullySharded.Config(device="cpu")).make()
+    seq = _batches(1, world)[0].chunk(world)[rank]
+    step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
+
+    class _Holder:
+        def state_dict(self):  # noqa: ANN202
+            return {"step": step.state_dict()}
+
+        def load_state_dict(self, s):  # noqa: ANN001, ANN202
+            step.load_state_dict(s["step"])
+
+    ck = Checkpointer.Config(working_dir=path, save_every=1, allow_checkpoint_overwrite=True).make()
+    ck.save(_Holder(), 1)
+    before = float(next(iter(step.model.parameters())).full_tensor().sum())
+    with torch.no_grad():
+        for p in step.model.parameters():
+            p.zero_()
+    resumed = ck.load(_Holder(), guard=False)
+    after = float(next(iter(step.model.parameters())).full_tensor().sum())
+    assert resumed == 1
+    return abs(after - before)
+
+
+def test_sharded_checkpoint_roundtrip_world2() -> None:
+    with tempfile.TemporaryDirectory() as d:
+        diffs = run_ranks(_dcp_roundtrip, 2, d, mesh_shape={"dp": 2})
+    assert max(diffs) < 1e-6
+
+
+def _boom(rank: int, world: int) -> None:
+    if rank == 1:
+        raise ValueError("injected failure on rank 1")
+
+
+def test_worker_pool_reports_rank_failure() -> None:
+    """A rank that raises (host-side fault injection) is reported, not hung on."""
+    with pytest.raises(RuntimeError, match="injected failure"):
+        run_ranks(_boom, 2, timeout_s=20)
