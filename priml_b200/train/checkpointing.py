@@ -242,11 +242,13 @@ class Checkpointer:
             items = [(s, p) for s, p in items if s == self.config.resume_step]
             if not items:
                 raise FileNotFoundError(f"no complete checkpoint for step {self.config.resume_step} in {self.dir}")
+        self._unreadable: set[int] = set()
         for step, path in reversed(items):
             try:
                 state = self.storage.read(Path(path), target.state_dict())
             except Exception as exc:  # noqa: BLE001 -- fall back to an older checkpoint
                 log.warning("checkpoint %s unreadable (%s); trying an older one", path, exc)
+                self._unreadable.add(step)
                 continue
             target.load_state_dict(state)
             if guard:
@@ -259,7 +261,8 @@ class Checkpointer:
     def _guard_overwrite(self, start: int, max_steps: float) -> None:
         if self.config.allow_checkpoint_overwrite:
             return
-        later = [s for s, _ in self._list() if s > start]
+        bad = getattr(self, "_unreadable", set())
+        later = [s for s, _ in self._list() if s > start and s not in bad]
         if later and (max_steps == float("inf") or any(s <= max_steps for s in later)):
             raise RuntimeError(
                 f"checkpoints after step {start} exist in {self.dir} ({later[:4]}...); this run would overwrite "
