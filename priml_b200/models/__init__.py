@@ -23,6 +23,7 @@ from priml_b200.models.custom_types import (
     propagate_attr,
 )
 from priml_b200.models.embedding import Embedding, NarrowEmbedding
+from priml_b200.models.gated_delta_net import GatedDeltaNet
 from priml_b200.models.generate import generate
 from priml_b200.models.init import (
     call_init,
@@ -54,8 +55,31 @@ from priml_b200.models.rope import RoPE, RoPEMixed, YarnScaling, rotate_conjugat
 from priml_b200.models.special import Identity, ResidualMix, Sequential, Skip, SoftCap
 from priml_b200.models.swiglu import SwiGLU, SwiGLUReluSquared
 from priml_b200.models.transformer import TransformerBlock
+from priml_b200.models.value_gated_attention import ValueGatedAttention
+from priml_b200.models.vision import (
+    AdaLNZero,
+    Conv1d,
+    Conv2d,
+    Conv3d,
+    MLPMixerBlock,
+    MMDiTBlock,
+    Patchify,
+    PCAWhiteningConv2d,
+    Unpatchify,
+)
 
 __all__ = [
+    "ValueGatedAttention",
+    "Unpatchify",
+    "PCAWhiteningConv2d",
+    "Patchify",
+    "MMDiTBlock",
+    "MLPMixerBlock",
+    "GatedDeltaNet",
+    "Conv3d",
+    "Conv2d",
+    "Conv1d",
+    "AdaLNZero",
     "BatchNorm",
     "BatchNorm2d",
     "BatchRenorm",
