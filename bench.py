@@ -47,6 +47,8 @@ def _parse() -> argparse.Namespace:
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "single"], default="auto",
+                    help="auto: fused-collective sharding for N>1, single-GPU for N=1")
     ap.add_argument("--out", type=str, default="")
     return ap.parse_args()
 
@@ -137,6 +139,7 @@ def main() -> None:
     from priml_b200.models.presets import dense_lm
     from priml_b200.optimizers import FusedAdamW
     from priml_b200.parallel.runtime import MultiProcess, SingleProcess
+    from priml_b200.parallel.fused_fsdp import FusedFullySharded
     from priml_b200.parallel.strategies import FullySharded, NoParallel
     from priml_b200.train import TrainStep
 
@@ -153,11 +156,14 @@ def main() -> None:
                               ffn_hidden=8192, vocab=32768)  # fmt: skip
     model_cfg = dense_lm(vocab=32768, d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
                          ffn_hidden=8192, rope_theta=5e5)  # fmt: skip
-    parallel = (
-        FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True)
-        if world > 1
-        else NoParallel.Config()
-    )
+    strategy = args.strategy if args.strategy != "auto" else ("fused" if world > 1 else "single")
+    if strategy == "single" and world > 1:
+        raise SystemExit("--strategy single needs --gpus 1")
+    parallel = {
+        "fused": lambda: FusedFullySharded.Config(),
+        "fsdp2": lambda: FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True),
+        "single": lambda: NoParallel.Config(),
+    }[strategy]()
     step_cfg = TrainStep.Config(
         model=model_cfg,
         optimizer=FusedAdamW.Config(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1),
@@ -168,7 +174,7 @@ def main() -> None:
         device_init="eager",
     )
     step = step_cfg.make()
-    if world == 1:
+    if strategy == "single":
         step.model.to(dev)
     tokens_per_step = args.mbs * args.seq * world
 
@@ -286,6 +292,12 @@ def main() -> None:
             "micro_batch_per_gpu": args.mbs,
             "seq_len": args.seq,
             "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+            "strategy": {
+                "fused": "sharded fp32 master + Adam state, resident bf16 weights; reduce-scatter, clip, AdamW and "
+                "weight all-gather in hand-written NVLink peer-memory kernels",
+                "fsdp2": "torch FSDP2 fully_shard over NCCL (bf16 params, fp32 reduce)",
+                "single": "one GPU, fused AdamW",
+            }[strategy],
             "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",
         },
         "clocks": clocks.summary(),

@@ -5,6 +5,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstring>
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -330,6 +332,135 @@ int64_t read_status(bool reset) {
   return v;
 }
 
+
+// Peer-shared weight / gradient / signal buffers of one data-parallel rank plus
+// the fused collective launches over them (collective.cu). The buffers are
+// cudaMalloc'd (IPC needs an allocation base) and exposed as tensors that keep
+// the allocation alive; peer buffers are mapped with cudaIpcOpenMemHandle.
+class PeerGroup {
+ public:
+  PeerGroup(int64_t rank, int64_t world, int64_t param_elems, int64_t grad_elems)
+      : rank_(rank), world_(world), device_(at::cuda::current_device()) {
+    PB_CHECK(world >= 1 && world <= pb::kMaxRanks, "world size must be 1..8");
+    PB_CHECK(rank >= 0 && rank < world, "rank out of range");
+    local_ = std::make_shared<Local>();
+    local_->param = pb::sym_alloc(std::max<int64_t>(param_elems, 8) * 2);
+    local_->grad = pb::sym_alloc(std::max<int64_t>(grad_elems, 4) * 4);
+    local_->signal = pb::sym_alloc(pb::kSigWords * 8);
+    auto opts = torch::TensorOptions().device(torch::kCUDA, device_);
+    auto keep = local_;
+    param_ = torch::from_blob(local_->param, {param_elems}, [keep](void*) {}, opts.dtype(torch::kBFloat16));
+    grad_ = torch::from_blob(local_->grad, {grad_elems}, [keep](void*) {}, opts.dtype(torch::kFloat32));
+    signal_ = torch::from_blob(local_->signal, {pb::kSigWords}, [keep](void*) {}, opts.dtype(torch::kInt64));
+    std::memset(&table_, 0, sizeof(table_));
+  }
+
+  ~PeerGroup() {
+    for (void* p : opened_) pb::ipc_close(p);
+  }
+
+  py::bytes handles() const {
+    char buf[192];
+    pb::ipc_handle(local_->param, buf);
+    pb::ipc_handle(local_->grad, buf + 64);
+    pb::ipc_handle(local_->signal, buf + 128);
+    return py::bytes(buf, 192);
+  }
+
+  // `all` holds every rank's handles() in rank order.
+  void open(const std::vector<std::string>& all) {
+    PB_CHECK(static_cast<int64_t>(all.size()) == world_, "need one handle record per rank");
+    const c10::cuda::CUDAGuard guard(device_);
+    for (int64_t r = 0; r < world_; ++r) {
+      PB_CHECK(all[r].size() == 192, "bad handle record");
+      if (r == rank_) {
+        table_.param[r] = reinterpret_cast<unsigned long long>(local_->param);
+        table_.grad[r] = reinterpret_cast<unsigned long long>(local_->grad);
+        table_.signal[r] = reinterpret_cast<unsigned long long>(local_->signal);
+        continue;
+      }
+      void* p = pb::ipc_open(all[r].data());
+      void* g = pb::ipc_open(all[r].data() + 64);
+      void* s = pb::ipc_open(all[r].data() + 128);
+      opened_.insert(opened_.end(), {p, g, s});
+      table_.param[r] = reinterpret_cast<unsigned long long>(p);
+      table_.grad[r] = reinterpret_cast<unsigned long long>(g);
+      table_.signal[r] = reinterpret_cast<unsigned long long>(s);
+    }
+    opened_ok_ = true;
+  }
+
+  Tensor param() const { return param_; }
+  Tensor grad() const { return grad_; }
+  Tensor signal() const { return signal_; }
+
+  void reduce_scatter(int64_t bucket, int64_t bucket_off, int64_t shard, Tensor& out, Tensor& partial, int64_t epoch,
+                      double scale, double timeout_s) {
+    PB_CHECK(opened_ok_, "open() the peer group first");
+    PB_CHECK(out.is_contiguous() && out.scalar_type() == torch::kFloat32 && out.numel() == shard, "out shard");
+    PB_CHECK(partial.is_contiguous() && partial.scalar_type() == torch::kFloat32, "partial sums");
+    PB_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0 && bucket_off % 4 == 0, "16-byte alignment");
+    pb::rs_bucket(table_, rank_, world_, bucket, bucket_off, shard, out.data_ptr<float>(), partial.data_ptr<float>(),
+                  partial.numel(), static_cast<unsigned long long>(epoch), static_cast<float>(scale),
+                  static_cast<long long>(timeout_s * 1e9), status_ptr(), stream());
+  }
+
+  void norm_exchange(const Tensor& partial, int64_t epoch, double max_norm, Tensor& norm, Tensor& clip,
+                     double timeout_s) {
+    PB_CHECK(opened_ok_, "open() the peer group first");
+    pb::norm_exchange(table_, rank_, world_, partial.data_ptr<float>(), partial.numel(),
+                      static_cast<unsigned long long>(epoch), static_cast<float>(max_norm), norm.data_ptr<float>(),
+                      clip.data_ptr<float>(), static_cast<long long>(timeout_s * 1e9), status_ptr(), stream());
+  }
+
+  // segs: int64 [n, 3] = (local_off, gathered_off, group); hyper: 7 lists of per-group floats.
+  void adamw_scatter(const Tensor& segs, Tensor& master, Tensor& m1, Tensor& m2, const Tensor& grad,
+                     c10::optional<Tensor> clip, const std::vector<std::vector<double>>& hyper, int64_t blocks) {
+    PB_CHECK(opened_ok_, "open() the peer group first");
+    PB_CHECK(segs.is_cuda() && segs.scalar_type() == torch::kInt64 && segs.dim() == 2 && segs.size(1) == 3, "segments");
+    PB_CHECK(hyper.size() == 7, "hyper = [lr, beta1, beta2, eps, wd, bias1, bias2]");
+    const int64_t n = master.numel();
+    for (const Tensor* t : {static_cast<const Tensor*>(&master), static_cast<const Tensor*>(&m1), static_cast<const Tensor*>(&m2), &grad})
+      PB_CHECK(t->is_contiguous() && t->scalar_type() == torch::kFloat32 && t->numel() == n, "fp32 shard tensors");
+    pb::AdamHyper hp{};
+    float* dst[7] = {hp.lr, hp.beta1, hp.beta2, hp.eps, hp.wd, hp.bias1, hp.bias2};
+    for (int k = 0; k < 7; ++k) {
+      PB_CHECK(hyper[k].size() <= static_cast<size_t>(pb::kMaxGroups), "at most 8 parameter groups");
+      for (size_t g = 0; g < hyper[k].size(); ++g) dst[k][g] = static_cast<float>(hyper[k][g]);
+    }
+    pb::adamw_scatter(table_, world_, reinterpret_cast<const pb::ShardSegment*>(segs.data_ptr()), segs.size(0), n,
+                      master.data_ptr<float>(), m1.data_ptr<float>(), m2.data_ptr<float>(), grad.data_ptr<float>(),
+                      clip.has_value() ? clip->data_ptr<float>() : nullptr, hp, blocks, stream());
+  }
+
+  void barrier(int64_t target, double timeout_s) {
+    PB_CHECK(opened_ok_, "open() the peer group first");
+    pb::peer_barrier(reinterpret_cast<const unsigned long long*>(local_->signal) + pb::kSigDone,
+                     static_cast<unsigned long long>(target), static_cast<long long>(timeout_s * 1e9), status_ptr(),
+                     stream());
+  }
+
+ private:
+  struct Local {
+    void* param = nullptr;
+    void* grad = nullptr;
+    void* signal = nullptr;
+    ~Local() {
+      pb::sym_free(param);
+      pb::sym_free(grad);
+      pb::sym_free(signal);
+    }
+  };
+  int64_t rank_, world_;
+  int device_;
+  std::shared_ptr<Local> local_;
+  Tensor param_, grad_, signal_;
+  pb::PeerTable table_;
+  std::vector<void*> opened_;
+  bool opened_ok_ = false;
+};
+
+Tensor status_tensor_py() { return status_tensor(); }
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -348,6 +479,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd, "flash attention backward (tcgen05)");
   m.def("cast_bf16", &cast_bf16, py::arg("x"), py::arg("out") = py::none());
   m.def("read_status", &read_status, py::arg("reset") = true);
+  py::class_<PeerGroup>(m, "PeerGroup")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t>(), py::arg("rank"), py::arg("world"), py::arg("param_elems"),
+           py::arg("grad_elems"))
+      .def("handles", &PeerGroup::handles)
+      .def("open", &PeerGroup::open)
+      .def("param", &PeerGroup::param)
+      .def("grad", &PeerGroup::grad)
+      .def("signal", &PeerGroup::signal)
+      .def("reduce_scatter", &PeerGroup::reduce_scatter)
+      .def("norm_exchange", &PeerGroup::norm_exchange)
+      .def("adamw_scatter", &PeerGroup::adamw_scatter)
+      .def("barrier", &PeerGroup::barrier);
+  m.def("status_tensor", &status_tensor_py);
   py::class_<MultiTensorPlan>(m, "MultiTensorPlan")
       .def(py::init<std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>,
                     std::vector<c10::optional<Tensor>>, int64_t>())

@@ -84,4 +84,58 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
 // fp32 -> bf16 cast of n elements.
 void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);
 
+// ---------------------------------------------------------------- peer collectives
+// Sharded data parallelism over IPC-mapped peer memory (collective.cu).
+constexpr int kMaxRanks = 8;
+constexpr int kMaxBuckets = 256;
+// Signal array layout (unsigned long long words, one array per rank).
+constexpr int kSigReady = 0;                                  // [bucket][src] epoch flags
+constexpr int kSigNorm = kSigReady + kMaxBuckets * kMaxRanks;  // [epoch & 1][src] (epoch << 32 | sumsq bits)
+constexpr int kSigDone = kSigNorm + 2 * kMaxRanks;            // scatter-completion counter
+constexpr int kSigWords = 4096;
+
+// Base addresses of every rank's buffers, as seen from this rank.
+struct PeerTable {
+  unsigned long long grad[kMaxRanks];    // fp32 gradient buffers
+  unsigned long long param[kMaxRanks];   // bf16 weight copies
+  unsigned long long signal[kMaxRanks];  // signal arrays
+};
+
+// A run of the local shard whose elements map contiguously into the gathered
+// weight buffer and share one hyper-parameter group.
+struct ShardSegment {
+  long long local_off;
+  long long gathered_off;
+  int group;
+  int pad;
+};
+
+constexpr int kMaxGroups = 8;
+struct AdamHyper {
+  float lr[kMaxGroups];
+  float beta1[kMaxGroups];
+  float beta2[kMaxGroups];
+  float eps[kMaxGroups];
+  float wd[kMaxGroups];
+  float bias1[kMaxGroups];
+  float bias2[kMaxGroups];
+};
+
+void* sym_alloc(size_t bytes);
+void sym_free(void* p);
+void ipc_handle(void* p, char out[64]);
+void* ipc_open(const char handle[64]);
+void ipc_close(void* p);
+void rs_bucket(const PeerTable& t, int rank, int world, int bucket, long long bucket_off, long long shard, float* out,
+               float* partial, int blocks, unsigned long long epoch, float scale, long long timeout_ns, int* status,
+               cudaStream_t stream);
+void norm_exchange(const PeerTable& t, int rank, int world, const float* partial, int n_partial,
+                   unsigned long long epoch, float max_norm, float* norm_out, float* clip_out, long long timeout_ns,
+                   int* status, cudaStream_t stream);
+void adamw_scatter(const PeerTable& t, int world, const ShardSegment* segs, int nseg, long long n_local, float* master,
+                   float* m1, float* m2, const float* grad, const float* clip, const AdamHyper& hp, int blocks,
+                   cudaStream_t stream);
+void peer_barrier(const unsigned long long* done, unsigned long long target, long long timeout_ns, int* status,
+                  cudaStream_t stream);
+
 }  // namespace pb

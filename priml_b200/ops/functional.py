@@ -19,11 +19,13 @@ from torch import Tensor
 from priml_b200.ops._loader import native
 
 __all__ = [
+    "GradSink",
     "attention",
     "attention_supported",
     "bf16_shadow",
     "check_status",
     "gemm",
+    "grad_sink",
     "grouped_swiglu_mlp",
     "linear",
     "linear_cross_entropy",
@@ -31,6 +33,7 @@ __all__ = [
     "rms_norm",
     "rotary",
     "swiglu",
+    "wgrad",
 ]
 
 
@@ -74,6 +77,62 @@ def mark_shadow_fresh(param: Tensor) -> None:
         param._pb_shadow = (param._version, cached[1])  # noqa: SLF001
 
 
+class GradSink:
+    """fp32 destination of one parameter's gradient inside a flat buffer.
+
+    Sharded data parallelism registers one on each parameter
+    (``param._pb_grad_sink``); weight-gradient GEMMs then write their fp32
+    output straight into it (overwriting on the first contribution of an
+    accumulation window, accumulating afterwards) and hand autograd ``None``.
+    """
+
+    __slots__ = ("buf", "fresh")
+
+    def __init__(self, buf: Tensor) -> None:
+        self.buf = buf
+        self.fresh = False
+
+    def region(self, view: Tensor) -> Tensor:
+        """The part of the buffer that corresponds to ``view`` of the parameter."""
+        off = view.storage_offset() - _root(view).storage_offset()
+        return self.buf.as_strided(view.shape, view.stride(), self.buf.storage_offset() + off)
+
+    def begin(self, view: Tensor) -> bool:
+        """Prepare a write of ``view``'s gradient; returns True to accumulate, False to overwrite."""
+        if self.fresh:
+            return True
+        self.fresh = True
+        if view.numel() == self.buf.numel():
+            return False
+        self.buf.zero_()
+        return True
+
+    def deliver(self, view: Tensor, grad: Tensor) -> None:
+        region = self.region(view)
+        if self.begin(view):
+            region.add_(grad)
+        else:
+            region.copy_(grad)
+
+
+def grad_sink(weight: Tensor) -> GradSink | None:
+    return getattr(_root(weight), "_pb_grad_sink", None)
+
+
+def wgrad(weight: Tensor, dy2: Tensor, x2: Tensor, w_dtype: torch.dtype) -> Tensor | None:
+    """Weight gradient ``dy2^T x2`` (fp32 accumulate); written into the
+    parameter's :class:`GradSink` when it has one (returns None), else returned
+    in the weight's dtype."""
+    sink = grad_sink(weight)
+    if sink is not None and weight.is_contiguous():
+        acc = sink.begin(weight)
+        out = sink.region(weight).view(dy2.shape[1], x2.shape[1])
+        gemm(dy2, x2, a_mn=True, b_mn=True, out=out, accumulate=acc)
+        return None
+    dw = gemm(dy2, x2, a_mn=True, b_mn=True, out_dtype=torch.float32)
+    return dw if w_dtype == torch.float32 else dw.to(w_dtype)
+
+
 def check_status(reset: bool = True) -> int:
     """Error code of the last kernel wait that timed out on this device (0 = none)."""
     return int(native().read_status(reset))
@@ -112,6 +171,7 @@ class _Linear(torch.autograd.Function):
         if bias is not None:
             y.add_(bias.to(y.dtype))
         ctx.save_for_backward(x2, w16)
+        ctx.weight = weight if grad_sink(weight) is not None else None
         ctx.has_bias = bias is not None
         ctx.w_dtype = weight.dtype
         ctx.x_shape = x.shape
@@ -128,9 +188,7 @@ class _Linear(torch.autograd.Function):
             if ctx.x_dtype != torch.bfloat16:
                 dx = dx.to(ctx.x_dtype)
         if ctx.needs_input_grad[1]:
-            dw = gemm(dy2, x2, a_mn=True, b_mn=True, out_dtype=torch.float32)
-            if ctx.w_dtype != torch.float32:
-                dw = dw.to(ctx.w_dtype)
+            dw = wgrad(ctx.weight if ctx.weight is not None else w16, dy2, x2, ctx.w_dtype)
         if ctx.has_bias and ctx.needs_input_grad[2]:
             db = dy2.float().sum(0)
         return dx, dw, db
@@ -155,6 +213,7 @@ class _LinearSwiGLU(torch.autograd.Function):
         gu = torch.empty(x2.shape[0], two_h, device=x.device, dtype=torch.bfloat16)
         native().gemm_swiglu(x2, w16, h, gu)
         ctx.save_for_backward(x2, w16, gu)
+        ctx.weight = weight if grad_sink(weight) is not None else None
         ctx.w_dtype = weight.dtype
         ctx.x_shape = x.shape
         ctx.x_dtype = x.dtype
@@ -170,9 +229,7 @@ class _LinearSwiGLU(torch.autograd.Function):
             if ctx.x_dtype != torch.bfloat16:
                 dx = dx.to(ctx.x_dtype)
         if ctx.needs_input_grad[1]:
-            dw = gemm(dgu, x2, a_mn=True, b_mn=True, out_dtype=torch.float32)
-            if ctx.w_dtype != torch.float32:
-                dw = dw.to(ctx.w_dtype)
+            dw = wgrad(ctx.weight if ctx.weight is not None else w16, dgu, x2, ctx.w_dtype)
         return dx, dw
 
 
@@ -201,7 +258,11 @@ class _RMSNorm(torch.autograd.Function):
     def backward(ctx, dy: Tensor):  # type: ignore[override]
         x, weight, rstd = ctx.saved_tensors
         dx, dw = native().rmsnorm_bwd(dy, x, weight, rstd, ctx.x_f32)
-        if weight is not None and dw is not None and dw.dtype != weight.dtype:
+        sink = grad_sink(weight) if weight is not None and dw is not None else None
+        if sink is not None:
+            sink.deliver(weight, dw)
+            dw = None
+        elif weight is not None and dw is not None and dw.dtype != weight.dtype:
             dw = dw.to(weight.dtype)
         return dx, (dw if weight is not None else None), None, None
 
@@ -279,6 +340,7 @@ class _LinearCE(torch.autograd.Function):
         t = targets.reshape(-1)
         loss, lse = native().ce_fwd(logits, t, ignore_index)
         ctx.save_for_backward(h2, w16, logits, t, lse)
+        ctx.weight = weight if grad_sink(weight) is not None else None
         ctx.ignore_index = ignore_index
         ctx.h_shape = h.shape
         ctx.h_dtype = h.dtype
@@ -298,9 +360,7 @@ class _LinearCE(torch.autograd.Function):
             if ctx.h_dtype != torch.bfloat16:
                 dh = dh.to(ctx.h_dtype)
         if ctx.needs_input_grad[1]:
-            dw = gemm(logits, h2, a_mn=True, b_mn=True, out_dtype=torch.float32)
-            if ctx.w_dtype != torch.float32:
-                dw = dw.to(ctx.w_dtype)
+            dw = wgrad(ctx.weight if ctx.weight is not None else w16, logits, h2, ctx.w_dtype)
         return dh, dw, None, None
 
 

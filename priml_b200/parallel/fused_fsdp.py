@@ -1,0 +1,563 @@
+"""Fully-sharded data parallelism with the collectives fused into hand-written kernels.
+
+Counterpart of the FSDP train step (``priml/train/parallelism.py:197-377``
+``FullySharded`` and the fused AdamW step of
+``priml/optimizers/fused_adamw.py:42-244``), planned for 180 GB GPUs joined by
+NVSwitch instead of translated from FSDP's all-gather / reduce-scatter
+schedule:
+
+* **What is sharded.** The fp32 master weights and both Adam moments live 1/R
+  per rank (R = data-parallel world size) -- 12 of the 14 bytes per parameter
+  that FSDP's sharding saves. The bf16 compute weights stay resident on every
+  rank (2 bytes per parameter: 2.5 GB for a 1B model, 16 GB for 8B), so the
+  forward and backward never wait for a parameter all-gather.
+* **Gradients.** Every parameter's fp32 gradient lives in a flat,
+  peer-mapped buffer (CUDA IPC). Weight-gradient GEMMs write into it directly
+  from their epilogue (:class:`priml_b200.ops.functional.GradSink`); other
+  parameters arrive through a post-accumulate hook. Parameters are grouped in
+  buckets (one per transformer block, plus the layers before / after the
+  blocks) ordered as the backward pass produces them.
+* **Reduce-scatter, overlapped with backward.** When a bucket is complete its
+  ``rs_bucket`` kernel runs on a side stream: rank r sums slice r of the bucket
+  over all ranks' buffers with NVLink peer loads (fixed rank order, so results
+  are bitwise reproducible), scales by 1/R and writes its fp32 gradient shard
+  plus partial sums of squares for clipping.
+* **Optimizer + all-gather in one kernel.** ``optimizer.step()`` exchanges the
+  squared norm on device (clip coefficient without a host sync), then one
+  ``adamw_scatter`` kernel updates the local shard and stores the new bf16
+  weights into every rank's resident copy with NVLink peer stores, followed by
+  a bounded device barrier.
+
+Per step each rank moves ``(R-1)/R * 4`` bytes per parameter in (gradient
+slices) during the backward and ``(R-1)/R * 2`` bytes per parameter out (new
+weights) after it -- the same bytes as FSDP's reduce-scatter plus ONE
+all-gather, instead of two all-gathers (forward and backward).
+
+Without CUDA (or with ``PRIML_B200_REFERENCE=1``) the same layout runs with
+``torch.distributed`` collectives (all-reduce + all-gather); the CPU tests use
+that path on gloo ranks as the oracle for the plumbing.
+
+Checkpoints: ``model.state_dict()`` returns full fp32 master weights and the
+optimizer state the per-parameter ``step`` / ``first_moment`` /
+``second_moment`` entries of :class:`FusedAdamW`, gathered from the shards, so
+a checkpoint written under this strategy loads into an unsharded model.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Iterable
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+from torch.optim import Optimizer
+
+from priml_b200 import ops
+from priml_b200.config import Fig
+from priml_b200.ops.functional import GradSink
+from priml_b200.parallel.runtime import get_device, global_device_mesh
+from priml_b200.parallel.strategies import place
+
+__all__ = ["FusedFullySharded", "ShardedAdamW", "ShardedState"]
+
+_ALIGN = 64  # elements; every parameter and shard starts on a 256-byte boundary (fp32)
+_MAX_BUCKETS = 256
+_MAX_GROUPS = 8
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+@dataclass
+class _Entry:
+    param: nn.Parameter
+    offset: int
+    numel: int
+    shape: torch.Size
+    bucket: int
+
+
+@dataclass
+class _Bucket:
+    index: int
+    entries: list[_Entry] = field(default_factory=list)
+    offset: int = 0
+    numel: int = 0
+    shard: int = 0
+    local: int = 0
+
+
+def _bucket_units(model: nn.Module, params: list[nn.Parameter]) -> list[list[nn.Parameter]]:
+    """Parameter groups in the order the backward pass finishes them."""
+    pos = {id(p): i for i, p in enumerate(params)}
+    blocks = getattr(model, "blocks", None)
+    if isinstance(blocks, nn.ModuleList) and len(blocks) > 0:
+        seen: set[int] = set()
+        per_block = []
+        for blk in blocks:
+            ps = [p for p in dict.fromkeys(blk.parameters()) if id(p) in pos and id(p) not in seen]
+            seen.update(id(p) for p in ps)
+            per_block.append(ps)
+        first = min((pos[id(p)] for ps in per_block for p in ps), default=0)
+        pre = [p for p in params if id(p) not in seen and pos[id(p)] < first]
+        post = [p for p in params if id(p) not in seen and pos[id(p)] > first]
+        units = [post, *per_block[::-1], pre]
+    else:
+        seen = set()
+        units = []
+        for child in model.children():
+            ps = [p for p in dict.fromkeys(child.parameters()) if id(p) in pos and id(p) not in seen]
+            seen.update(id(p) for p in ps)
+            units.append(ps)
+        units.append([p for p in params if id(p) not in seen])
+        units = units[::-1]
+    return [u for u in units if u]
+
+
+class ShardedState:
+    """Flat layout, peer buffers and per-step bookkeeping of one model."""
+
+    def __init__(self, model: nn.Module, config: FusedFullySharded.Config, device: torch.device,
+                 group: Any = None) -> None:  # fmt: skip
+        self.config = config
+        self.group = group
+        self.dist = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if self.dist else 1
+        self.rank = dist.get_rank(group) if self.dist else 0
+        if self.world > 8:
+            raise ValueError("FusedFullySharded supports up to 8 ranks per group (one NVSwitch domain)")
+        self.device = device
+        self.native = device.type == "cuda" and ops.native_available() and not ops.reference_forced()
+
+        params = [p for p in dict.fromkeys(model.parameters()) if p.requires_grad]
+        units = _bucket_units(model, params)
+        if len(units) > _MAX_BUCKETS:
+            raise ValueError(f"{len(units)} buckets; at most {_MAX_BUCKETS} are supported")
+        self.buckets: list[_Bucket] = []
+        self.entries: list[_Entry] = []
+        cursor = local = 0
+        for bi, unit in enumerate(units):
+            b = _Bucket(index=bi, offset=cursor)
+            for p in unit:
+                cursor = _round_up(cursor, _ALIGN)
+                e = _Entry(param=p, offset=cursor, numel=p.numel(), shape=p.shape, bucket=bi)
+                b.entries.append(e)
+                self.entries.append(e)
+                cursor += p.numel()
+            b.numel = _round_up(cursor - b.offset, _ALIGN * self.world)
+            b.shard = b.numel // self.world
+            b.local = local
+            local += b.shard
+            cursor = b.offset + b.numel
+            self.buckets.append(b)
+        self.total = cursor
+        self.local_total = local
+
+        # Buffers: bf16 weights + fp32 gradients (peer-mapped on CUDA), fp32 shards.
+        if self.native:
+            self.peers = ops.native().PeerGroup(self.rank, self.world, self.total, self.total)
+            handles = self.peers.handles()
+            all_handles: list[Any] = [None] * self.world
+            if self.dist:
+                dist.all_gather_object(all_handles, handles, group=group)
+            else:
+                all_handles = [handles]
+            self.peers.open(all_handles)
+            self.param_buf: Tensor = self.peers.param()
+            self.grad_buf: Tensor = self.peers.grad()
+            self.comm_stream = torch.cuda.Stream(device=device)
+        else:
+            self.peers = None
+            self.param_buf = torch.zeros(self.total, dtype=torch.bfloat16, device=device)
+            self.grad_buf = torch.zeros(self.total, dtype=torch.float32, device=device)
+            self.comm_stream = None
+        flat = torch.zeros(self.total, dtype=torch.float32, device=device)
+        with torch.no_grad():
+            for e in self.entries:
+                flat[e.offset : e.offset + e.numel].copy_(e.param.detach().reshape(-1))
+            if self.dist and self.world > 1:
+                dist.broadcast(flat, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+            self.param_buf.copy_(flat)
+        self.master = torch.empty(self.local_total, dtype=torch.float32, device=device)
+        for b in self.buckets:
+            lo = b.offset + self.rank * b.shard
+            self.master[b.local : b.local + b.shard].copy_(flat[lo : lo + b.shard])
+        del flat
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.grad_shard = torch.zeros_like(self.master)
+        self.reduce_blocks = max(1, int(config.reduce_blocks))
+        self.partial = torch.zeros(len(self.buckets), self.reduce_blocks, dtype=torch.float32, device=device)
+        self.norm = torch.zeros(1, dtype=torch.float32, device=device)
+        self.clip = torch.ones(1, dtype=torch.float32, device=device)
+
+        # Replace every parameter by a bf16 view of the resident weight buffer.
+        self.sinks: list[GradSink] = []
+        mapping: dict[int, nn.Parameter] = {}
+        for idx, e in enumerate(self.entries):
+            newp = nn.Parameter(self.param_buf[e.offset : e.offset + e.numel].view(e.shape))
+            sink = GradSink(self.grad_buf[e.offset : e.offset + e.numel].view(e.shape))
+            newp._pb_grad_sink = sink  # type: ignore[attr-defined]
+            newp.register_post_accumulate_grad_hook(self._make_hook(idx, sink))
+            self.sinks.append(sink)
+            mapping[id(e.param)] = newp
+            e.param = newp
+        for mod in model.modules():
+            for name, p in list(mod._parameters.items()):  # noqa: SLF001
+                if p is not None and id(p) in mapping:
+                    mod._parameters[name] = mapping[id(p)]  # noqa: SLF001
+        self._param_index = {id(e.param): i for i, e in enumerate(self.entries)}
+
+        # Per-backward bookkeeping.
+        self.sync = True
+        self.epoch = 1
+        self.done_target = 0
+        self._armed = False
+        self._reset_backward()
+        self.reduced = False
+
+    # ------------------------------------------------------------------ backward
+    def _reset_backward(self) -> None:
+        self.pending = [len(b.entries) for b in self.buckets]
+        self.done = [False] * len(self.entries)
+        self.next_bucket = 0
+
+    def _make_hook(self, idx: int, sink: GradSink) -> Callable[[Tensor], None]:
+        def hook(p: Tensor) -> None:
+            if p.grad is not None:
+                sink.deliver(p, p.grad)
+                p.grad = None
+            self._param_done(idx)
+
+        return hook
+
+    def _param_done(self, idx: int) -> None:
+        if not self._armed:
+            self._armed = True
+            torch.autograd.Variable._execution_engine.queue_callback(self._end_backward)  # noqa: SLF001
+        if self.done[idx]:
+            return
+        self.done[idx] = True
+        b = self.entries[idx].bucket
+        self.pending[b] -= 1
+        if self.sync:
+            while self.next_bucket < len(self.buckets) and self.pending[self.next_bucket] == 0:
+                self._launch(self.buckets[self.next_bucket])
+                self.next_bucket += 1
+
+    def _end_backward(self) -> None:
+        self._armed = False
+        if self.sync:
+            while self.next_bucket < len(self.buckets):
+                self._launch(self.buckets[self.next_bucket])
+                self.next_bucket += 1
+            self.reduced = True
+        self._reset_backward()
+
+    def _launch(self, b: _Bucket) -> None:
+        for e in b.entries:  # parameters that received no gradient this window
+            sink = e.param._pb_grad_sink  # type: ignore[attr-defined]
+            if not sink.fresh:
+                sink.buf.zero_()
+                sink.fresh = True
+        out = self.grad_shard[b.local : b.local + b.shard]
+        if self.native:
+            ev = torch.cuda.Event()
+            ev.record()
+            self.comm_stream.wait_event(ev)
+            with torch.cuda.stream(self.comm_stream):
+                self.peers.reduce_scatter(b.index, b.offset, b.shard, out, self.partial[b.index], self.epoch,
+                                          1.0 / self.world, self.config.timeout_s)  # fmt: skip
+            return
+        full = self.grad_buf[b.offset : b.offset + b.numel].clone()
+        if self.dist and self.world > 1:
+            dist.all_reduce(full, group=self.group)
+        out.copy_(full[self.rank * b.shard : (self.rank + 1) * b.shard] / self.world)
+        self.partial[b.index].zero_()
+        self.partial[b.index, 0] = out.double().square().sum().float()
+
+    def set_requires_gradient_sync(self, flag: bool) -> None:
+        self.sync = bool(flag)
+
+    def zero_grad(self) -> None:
+        for s in self.sinks:
+            s.fresh = False
+        self.reduced = False
+
+    # ------------------------------------------------------------------ step
+    def segments(self, group_of: dict[int, int]) -> Tensor:
+        """(local_off, gathered_off, group) runs of the local shard, as an int64 table."""
+        rows: list[tuple[int, int, int]] = []
+        for b in self.buckets:
+            lo, hi = b.offset + self.rank * b.shard, b.offset + (self.rank + 1) * b.shard
+            starts = [(e.offset, group_of[self._param_index[id(e.param)]]) for e in b.entries]
+            current = starts[0][1]
+            for off, g in starts:  # the run containing `lo` belongs to the last parameter starting at or before it
+                if off <= lo:
+                    current = g
+            rows.append((b.local, lo, current))
+            for off, g in starts:
+                if lo < off < hi and g != current:
+                    rows.append((b.local + off - lo, off, g))
+                    current = g
+        return torch.tensor(rows, dtype=torch.int64, device=self.device).view(-1, 3)
+
+    def gather_full(self, local: Tensor) -> Tensor:
+        """Full flat fp32 tensor from every rank's concatenated local shards."""
+        full = torch.zeros(self.total, dtype=local.dtype, device=local.device)
+        for b in self.buckets:
+            mine = local[b.local : b.local + b.shard].contiguous()
+            if self.dist and self.world > 1:
+                parts = [torch.empty_like(mine) for _ in range(self.world)]
+                dist.all_gather(parts, mine, group=self.group)
+                full[b.offset : b.offset + b.numel].copy_(torch.cat(parts))
+            else:
+                full[b.offset : b.offset + b.numel].copy_(mine)
+        return full
+
+    def scatter_full(self, full: Tensor, local: Tensor) -> None:
+        for b in self.buckets:
+            lo = b.offset + self.rank * b.shard
+            local[b.local : b.local + b.shard].copy_(full[lo : lo + b.shard])
+
+
+class ShardedAdamW(Optimizer):
+    """AdamW over the shards of a :class:`ShardedState` (same arithmetic order
+    and state keys as :class:`priml_b200.optimizers.FusedAdamW`)."""
+
+    def __init__(self, state: ShardedState, param_groups: Iterable[dict[str, Any]]) -> None:
+        groups = [dict(g) for g in param_groups]
+        if len(groups) > _MAX_GROUPS:
+            raise ValueError(f"at most {_MAX_GROUPS} parameter groups are supported")
+        defaults = {k: groups[0][k] for k in ("lr", "betas", "eps", "weight_decay")}
+        super().__init__([{**g, "params": list(g["params"])} for g in groups], defaults)
+        self.sharded = state
+        group_of: dict[int, int] = {}
+        for gi, g in enumerate(self.param_groups):
+            for p in g["params"]:
+                idx = state._param_index.get(id(p))  # noqa: SLF001
+                if idx is None:
+                    raise ValueError("optimizer parameter is not managed by FusedFullySharded")
+                group_of[idx] = gi
+        for i in range(len(state.entries)):
+            group_of.setdefault(i, 0)
+        self._group_of = group_of
+        self._segments = state.segments(group_of)
+        self._group_index = self._element_groups() if not state.native else None
+        self.step_count = 0
+        self.grad_scale: Tensor | None = None
+        self._max_norm = 0.0
+        self._scatter_blocks = int(state.config.scatter_blocks) or 2 * (
+            torch.cuda.get_device_properties(state.device).multi_processor_count if state.native else 1
+        )
+        self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=state.native)
+        self._status_event: Any = None
+
+    def _element_groups(self) -> Tensor:
+        seg = self._segments.cpu().tolist()
+        idx = torch.zeros(self.sharded.local_total, dtype=torch.int64)
+        for i, (lo, _, g) in enumerate(seg):
+            hi = seg[i + 1][0] if i + 1 < len(seg) else self.sharded.local_total
+            idx[lo:hi] = g
+        return idx.to(self.sharded.device)
+
+    # ------------------------------------------------------------------ clip hook
+    def fused_grad_norm(self, max_norm: float) -> tuple[Tensor, Tensor]:
+        """Device scalars (global norm, clip coefficient), filled in by ``step()``."""
+        self._max_norm = float(max_norm)
+        return self.sharded.norm, self.sharded.clip
+
+    def _hyper(self) -> list[list[float]]:
+        cols: list[list[float]] = [[] for _ in range(7)]
+        for g in self.param_groups:
+            b1, b2 = g["betas"]
+            bias1 = 1.0 - b1**self.step_count
+            bias2 = 1.0 - b2**self.step_count
+            for col, val in zip(cols, (g["lr"], b1, b2, g["eps"], g["weight_decay"], bias1, bias2), strict=True):
+                col.append(float(val))
+        return cols
+
+    def _check_status(self) -> None:
+        if self._status_event is None:
+            return
+        self._status_event.synchronize()
+        code = int(self._status_host[0])
+        if code != 0:
+            raise RuntimeError(f"peer collective timed out (status {code}); a rank stopped or fell behind")
+
+    @torch.no_grad()
+    def step(self, closure: Callable[[], Any] | None = None) -> Any:
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        st = self.sharded
+        if not st.reduced:
+            raise RuntimeError("optimizer.step() before a synchronized backward pass")
+        self.step_count += 1
+        clipping = self.grad_scale is not None and math.isfinite(self._max_norm) and self._max_norm > 0
+        hyper = self._hyper()
+        if st.native:
+            self._check_status()
+            torch.cuda.current_stream().wait_stream(st.comm_stream)
+            st.peers.norm_exchange(st.partial.view(-1), st.epoch, self._max_norm if clipping else 0.0, st.norm,
+                                   st.clip, st.config.timeout_s)  # fmt: skip
+            st.peers.adamw_scatter(self._segments, st.master, st.exp_avg, st.exp_avg_sq, st.grad_shard,
+                                   st.clip if clipping else None, hyper, self._scatter_blocks)  # fmt: skip
+            st.done_target += st.world * self._scatter_blocks
+            st.peers.barrier(st.done_target, st.config.timeout_s)
+            self._status_host.copy_(ops.native().status_tensor(), non_blocking=True)
+            self._status_event = torch.cuda.Event()
+            self._status_event.record()
+        else:
+            self._reference_step(hyper, clipping)
+        st.epoch += 1
+        st.reduced = False
+        return loss
+
+    def _reference_step(self, hyper: list[list[float]], clipping: bool) -> None:
+        st = self.sharded
+        sq = st.partial.sum().reshape(1).double()
+        if st.dist and st.world > 1:
+            dist.all_reduce(sq, group=st.group)
+        st.norm.copy_(sq.sqrt().float())
+        if clipping:
+            st.clip.copy_((self._max_norm / (st.norm + 1e-6)).clamp(max=1.0))
+        else:
+            st.clip.fill_(1.0)
+        gi = self._group_index
+        lr, b1, b2, eps, wd, bias1, bias2 = (torch.tensor(c, dtype=torch.float32, device=st.device)[gi] for c in hyper)
+        g = st.grad_shard * st.clip
+        p = st.master * (1 - lr * wd)
+        st.exp_avg.lerp_(g, 1 - b1)
+        st.exp_avg_sq.lerp_(g * g, 1 - b2)
+        p -= st.exp_avg / ((st.exp_avg_sq / bias2).sqrt() + eps) * (lr / bias1)
+        st.master.copy_(p)
+        st.param_buf.copy_(st.gather_full(st.master))
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        del set_to_none
+        self.sharded.zero_grad()
+        for e in self.sharded.entries:
+            e.param.grad = None
+
+    # ------------------------------------------------------------------ state
+    def state_dict(self) -> dict[str, Any]:
+        st = self.sharded
+        m = st.gather_full(st.exp_avg)
+        v = st.gather_full(st.exp_avg_sq)
+        state: dict[int, dict[str, Any]] = {}
+        index = 0
+        groups = []
+        for g in self.param_groups:
+            ids = []
+            for p in g["params"]:
+                e = st.entries[st._param_index[id(p)]]  # noqa: SLF001
+                sl = slice(e.offset, e.offset + e.numel)
+                state[index] = {
+                    "step": self.step_count,
+                    "first_moment": m[sl].view(e.shape).clone(),
+                    "second_moment": v[sl].view(e.shape).clone(),
+                }
+                ids.append(index)
+                index += 1
+            groups.append({k: val for k, val in g.items() if k != "params"} | {"params": ids})
+        return {"state": state, "param_groups": groups}
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        st = self.sharded
+        m = torch.zeros(st.total, dtype=torch.float32, device=st.device)
+        v = torch.zeros_like(m)
+        index = 0
+        step = 0
+        for g, sg in zip(self.param_groups, state_dict["param_groups"], strict=True):
+            for k, val in sg.items():
+                if k != "params":
+                    g[k] = val
+            for p, pid in zip(g["params"], sg["params"], strict=True):
+                s = state_dict["state"].get(pid, state_dict["state"].get(str(pid)))
+                e = st.entries[st._param_index[id(p)]]  # noqa: SLF001
+                if s:
+                    m[e.offset : e.offset + e.numel].copy_(s["first_moment"].reshape(-1))
+                    v[e.offset : e.offset + e.numel].copy_(s["second_moment"].reshape(-1))
+                    step = int(s["step"])
+                index += 1
+        st.scatter_full(m, st.exp_avg)
+        st.scatter_full(v, st.exp_avg_sq)
+        self.step_count = step
+
+
+def _install_state_dict_hooks(model: nn.Module, state: ShardedState) -> None:
+    """``state_dict`` returns fp32 master weights; ``load_state_dict`` refreshes the shards."""
+    names: dict[int, str] = {}
+    for name, p in model.named_parameters(remove_duplicate=False):
+        names.setdefault(id(p), name)
+
+    def save_hook(module: nn.Module, sd: dict[str, Any], prefix: str, local_metadata: Any) -> None:
+        del module, local_metadata
+        full = state.gather_full(state.master)
+        for e in state.entries:
+            key = prefix + names[id(e.param)]
+            if key in sd:
+                sd[key] = full[e.offset : e.offset + e.numel].view(e.shape).clone()
+
+    def load_hook(module: nn.Module, sd: dict[str, Any], prefix: str, *args: Any) -> None:
+        del module, args
+        full = state.gather_full(state.master)
+        for e in state.entries:
+            key = prefix + names[id(e.param)]
+            if key in sd:
+                full[e.offset : e.offset + e.numel].copy_(sd[key].reshape(-1).to(full.device, torch.float32))
+        state.scatter_full(full, state.master)
+
+    model.register_state_dict_post_hook(save_hook)
+    model.register_load_state_dict_pre_hook(load_hook)
+
+
+class FusedFullySharded:
+    """Strategy: shard optimizer state, keep bf16 weights resident, fuse the
+    gradient reduce-scatter and the weight all-gather into kernels."""
+
+    class Config(Fig["FusedFullySharded"]):
+        device: torch.device | str | None = "auto"
+        mesh_dim: str = "dp"
+        reduce_blocks: int = 24
+        """CTAs per bucket reduce-scatter (they share SMs with the backward GEMMs)."""
+        scatter_blocks: int = 0
+        """CTAs of the optimizer + all-gather kernel; 0 = two per SM."""
+        timeout_s: float = 60.0
+        """Bound on every cross-rank wait inside the kernels."""
+
+    def __init__(self, config: Config | None = None) -> None:
+        self.config = config or FusedFullySharded.Config()
+        self.device = get_device(self.config.device)
+        self.state: ShardedState | None = None
+
+    def _group(self) -> Any:
+        mesh = global_device_mesh()
+        if mesh is not None and self.config.mesh_dim in (mesh.mesh_dim_names or ()):
+            return mesh[self.config.mesh_dim].get_group()
+        return None
+
+    def __call__(self, model: nn.Module) -> nn.Module:
+        dev = self.device
+        if dev.type == "cuda" and torch.cuda.is_available():
+            dev = torch.device("cuda", torch.cuda.current_device())
+        model = place(model, dev)
+        self.state = ShardedState(model, self.config, dev, self._group())
+        _install_state_dict_hooks(model, self.state)
+        model.set_requires_gradient_sync = self.state.set_requires_gradient_sync  # type: ignore[assignment]
+        return model
+
+    def build_optimizer(self, make: Callable[..., Any], model: nn.Module) -> Optimizer:
+        from priml_b200.optimizers import FusedAdamW
+
+        assert self.state is not None, "apply the strategy to the model first"
+        base = make([p for p in model.parameters() if p.requires_grad])
+        if not isinstance(base, FusedAdamW):
+            raise TypeError(f"FusedFullySharded fuses AdamW into its all-gather; got {type(base).__name__}")
+        return ShardedAdamW(self.state, base.param_groups)

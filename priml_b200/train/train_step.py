@@ -127,7 +127,10 @@ class TrainStep:
             model = config.activation_memoization.make()(model)
         self.model: nn.Module = model
         self.device = next((p.device for p in model.parameters()), getattr(strategy, "device", torch.device("cpu")))
-        self.optimizer = self.build_optimizer(model)
+        if hasattr(strategy, "build_optimizer"):
+            self.optimizer = strategy.build_optimizer(config.optimizer.make(), model)
+        else:
+            self.optimizer = self.build_optimizer(model)
         for g in self.optimizer.param_groups:
             g.setdefault("initial_lr", g["lr"])
         self.schedule: Callable[[float], float] = config.learning_rate_scheduler.make()
@@ -227,9 +230,7 @@ class TrainStep:
     # ------------------------------------------------------------------ update
     def _clip(self) -> Tensor | None:
         c = self.config.gradient_clip_norm
-        from priml_b200.optimizers import FusedAdamW
-
-        if isinstance(self.optimizer, FusedAdamW):
+        if hasattr(self.optimizer, "fused_grad_norm"):
             if math.isinf(c):
                 self.optimizer.grad_scale = None
                 return None
@@ -255,6 +256,9 @@ class TrainStep:
 
     def train_step(self, **batch: Any) -> TrainStepOutput:
         """Forward + backward on one micro-batch; steps when the window closes."""
+        sync = getattr(self.model, "set_requires_gradient_sync", None)
+        if callable(sync) and self.config.accumulate_grad_batches > 1:
+            sync(self.accumulation_steps + 1 >= self.config.accumulate_grad_batches)
         with self.timer_forward:
             losses = self.compute_loss(**batch)
             loss = losses["loss"]
