@@ -25,9 +25,8 @@
 // Synchronization uses a small signal array per rank (also IPC-mapped):
 // monotone epoch flags written with st.release.sys and read with
 // ld.acquire.sys. Every wait is bounded by globaltimer; a wait that runs out
-// records kTimeoutPeer in the status word and the kernel returns. No load here
-// uses TMA or cluster multicast; peers are read and written with plain
-// 16-byte global accesses.
+// records kTimeoutPeer in the status word and the kernel returns. Peer memory
+// is read and written only with plain 16-byte global loads and stores.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -56,8 +55,8 @@ __device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsig
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Spin until *flag >= target (or, with `hi_match`, until the high word equals
-// target). Returns the value seen, or 0 after recording a timeout.
+// Spin until *flag >= target; false (after recording kTimeoutPeer) when the
+// bound runs out first.
 __device__ bool wait_flag_ge(const unsigned long long* flag, unsigned long long target, long long timeout_ns,
                              int* status) {
   const unsigned long long t0 = globaltimer();
