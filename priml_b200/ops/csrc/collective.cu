@@ -90,23 +90,28 @@ __device__ __forceinline__ float lerp_t(float a, float b, float w) {
   return w < 0.5f ? fmaf(w, b - a, a) : b - (b - a) * (1.f - w);
 }
 
-__global__ void __launch_bounds__(512) rs_bucket_kernel(PeerTable t, int rank, int world, int bucket,
-                                                         long long bucket_off, long long shard, float* __restrict__ out,
+// W = world size (compile-time, so the peer loads are fully unrolled); each
+// thread keeps U float4 chunks x W peers (8 to 16) independent 16-byte loads
+// in flight, enough to cover NVLink latency with a few dozen CTAs.
+template <int W>
+__global__ void __launch_bounds__(256, 2) rs_bucket_kernel(PeerTable t, int rank, int bucket, long long bucket_off,
+                                                         long long shard, float* __restrict__ out,
                                                          float* __restrict__ partial, unsigned long long epoch,
                                                          float scale, long long timeout_ns, int* status) {
+  constexpr int U = W <= 2 ? 8 / W : (W >= 16 ? 1 : 16 / W);
   __shared__ int ok;
   __shared__ float red[32];
   if (threadIdx.x == 0) {
     // This rank's gradients for the bucket are complete (stream order): say so
     // to every peer, then wait until every peer has said the same.
     __threadfence_system();
-    for (int p = 0; p < world; ++p) {
+    for (int p = 0; p < W; ++p) {
       auto* sig = reinterpret_cast<unsigned long long*>(t.signal[p]);
       st_release_sys(sig + kSigReady + bucket * kMaxRanks + rank, epoch);
     }
     auto* mine = reinterpret_cast<const unsigned long long*>(t.signal[rank]);
     int good = 1;
-    for (int p = 0; p < world && good; ++p)
+    for (int p = 0; p < W && good; ++p)
       good = wait_flag_ge(mine + kSigReady + bucket * kMaxRanks + p, epoch, timeout_ns, status) ? 1 : 0;
     ok = good;
   }
@@ -115,27 +120,40 @@ __global__ void __launch_bounds__(512) rs_bucket_kernel(PeerTable t, int rank, i
   if (ok) {
     const long long base = bucket_off + static_cast<long long>(rank) * shard;
     const long long n4 = shard >> 2;
-    for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < n4;
-         c += static_cast<long long>(gridDim.x) * blockDim.x) {
-      float4 v[kMaxRanks];
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const float4* src[W];
 #pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < world) v[p] = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(t.grad[p]) + base) + c);
-      float4 s = v[0];
+    for (int p = 0; p < W; ++p) src[p] = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(t.grad[p]) + base);
+    for (long long c0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c0 < n4; c0 += U * stride) {
+      float4 v[U][W];
 #pragma unroll
-      for (int p = 1; p < kMaxRanks; ++p)
-        if (p < world) {
-          s.x += v[p].x;
-          s.y += v[p].y;
-          s.z += v[p].z;
-          s.w += v[p].w;
+      for (int u = 0; u < U; ++u) {
+        const long long c = c0 + u * stride;
+        if (c < n4) {
+#pragma unroll
+          for (int p = 0; p < W; ++p) v[u][p] = __ldcg(src[p] + c);
         }
-      s.x *= scale;
-      s.y *= scale;
-      s.z *= scale;
-      s.w *= scale;
-      reinterpret_cast<float4*>(out)[c] = s;
-      acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long c = c0 + u * stride;
+        if (c < n4) {
+          float4 s = v[u][0];
+#pragma unroll
+          for (int p = 1; p < W; ++p) {
+            s.x += v[u][p].x;
+            s.y += v[u][p].y;
+            s.z += v[u][p].z;
+            s.w += v[u][p].w;
+          }
+          s.x *= scale;
+          s.y *= scale;
+          s.z *= scale;
+          s.w *= scale;
+          reinterpret_cast<float4*>(out)[c] = s;
+          acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+        }
+      }
     }
   }
   const float tot = block_sum(acc, red);
@@ -289,8 +307,24 @@ void rs_bucket(const PeerTable& t, int rank, int world, int bucket, long long bu
                cudaStream_t stream) {
   if (world > kMaxRanks || bucket >= kMaxBuckets || (shard & 3) != 0)
     throw std::invalid_argument("rs_bucket: world / bucket / shard alignment out of range");
-  rs_bucket_kernel<<<blocks, 512, 0, stream>>>(t, rank, world, bucket, bucket_off, shard, out, partial, epoch, scale,
-                                               timeout_ns, status);
+#define PB_RS_CASE(W)                                                                                  \
+  case W:                                                                                              \
+    rs_bucket_kernel<W><<<blocks, 256, 0, stream>>>(t, rank, bucket, bucket_off, shard, out, partial, epoch, scale, \
+                                                    timeout_ns, status);                               \
+    break;
+  switch (world) {
+    PB_RS_CASE(1)
+    PB_RS_CASE(2)
+    PB_RS_CASE(3)
+    PB_RS_CASE(4)
+    PB_RS_CASE(5)
+    PB_RS_CASE(6)
+    PB_RS_CASE(7)
+    PB_RS_CASE(8)
+    default:
+      throw std::invalid_argument("rs_bucket: world size must be 1..8");
+  }
+#undef PB_RS_CASE
   check(cudaGetLastError(), "rs_bucket launch");
 }
 

@@ -51,7 +51,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--params", type=float, default=1.24e9)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--reduce-blocks", type=int, default=24)
+    ap.add_argument("--reduce-blocks", type=int, default=48)
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))

@@ -525,7 +525,7 @@ class FusedFullySharded:
     class Config(Fig["FusedFullySharded"]):
         device: torch.device | str | None = "auto"
         mesh_dim: str = "dp"
-        reduce_blocks: int = 24
+        reduce_blocks: int = 48
         """CTAs per bucket reduce-scatter (they share SMs with the backward GEMMs)."""
         scatter_blocks: int = 0
         """CTAs of the optimizer + all-gather kernel; 0 = two per SM."""
