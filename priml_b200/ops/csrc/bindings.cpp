@@ -318,10 +318,13 @@ std::vector<Tensor> attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, 
   PB_CHECK(lse.is_contiguous() && lse.numel() == n_rows, "lse must be the forward's [B, H, S] output");
   auto doc = dout.stride(3) == 1 && dout.stride(2) == D ? dout : dout.contiguous();
   if (q.numel() == 0) return {dq, dk, dv};
+  // D = 64 runs the fused dK/dV/dQ kernel, which bulk-reduces dQ into fp32 scratch.
+  Tensor dq_acc;
+  if (D == 64) dq_acc = torch::empty({n_rows * D}, q.options().dtype(torch::kFloat32));
   pb::attn_bwd(attn_view(q, "q"), attn_view(k, "k"), attn_view(v, "v"), attn_view(o, "o"), attn_view(doc, "dout"),
                lse.data_ptr<float>(), delta.data_ptr<float>(), attn_view(dq, "dq"), attn_view(dk, "dk"),
                attn_view(dv, "dv"), H, Hkv, D, static_cast<float>(scale), causal, static_cast<int>(window),
-               status_ptr(), stream());
+               status_ptr(), stream(), dq_acc.defined() ? dq_acc.data_ptr<float>() : nullptr);
   return {dq, dk, dv};
 }
 

@@ -15,6 +15,9 @@ int device_sm_count();
 void make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
                        int box_inner, int box_outer);
 // 3-D bf16 tensor map (inner, mid, outer) with element strides for mid/outer.
+// 2-D fp32 map without swizzle (bulk reduce targets).
+void make_tmap_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
+                      int box_inner, int box_outer);
 void make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long inner, long long mid, long long outer,
                        long long mid_stride, long long outer_stride, int box_inner, int box_mid, bool swizzle128);
 
@@ -76,10 +79,12 @@ struct AttnTensor {
 };
 void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, float* lse, int H,
               int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream);
+// dq_acc: optional fp32 scratch of B*H*S*D floats; with it (and D == 64) the
+// backward runs as one fused kernel that bulk-reduces dQ partials into it.
 void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o,
               const AttnTensor& dout, const float* lse, float* delta, const AttnTensor& dq, const AttnTensor& dk,
               const AttnTensor& dv, int H, int Hkv, int D, float scale, bool causal, int window, int* status,
-              cudaStream_t stream);
+              cudaStream_t stream, float* dq_acc = nullptr);
 
 // fp32 -> bf16 cast of n elements.
 void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);
