@@ -46,7 +46,11 @@ __global__ void attn_delta_kernel(const AttnParams p) {
   }
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-  if ((threadIdx.x & 31) == 0) p.delta[(static_cast<long long>(b) * p.H + h) * p.S + q] = acc;
+  if ((threadIdx.x & 31) == 0) {
+    const long long idx = (static_cast<long long>(b) * p.H + h) * p.S + q;
+    p.delta[idx] = acc;
+    if (p.nlse2 != nullptr) p.nlse2[idx] = -p.lse[idx] * kLog2e;
+  }
 }
 
 // ============================================================================ dK dV
@@ -613,7 +617,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_ready[s], 8);
+      mbar_init(&p_ready[s], 4);
       mbar_init(&dq_full[s], 1);
       mbar_init(&dq_empty[s], 2);
     }
@@ -651,12 +655,12 @@ __global__ void __launch_bounds__(384, 1)
       const long long row = (static_cast<long long>(b) * p.H + h) * p.S + q0;
       if (bulk_vec) {
         mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes + 2 * kLT * 4);
-        bulk_load(vec, p.lse + row, kLT * 4, &in_full[st]);
+        bulk_load(vec, p.nlse2 + row, kLT * 4, &in_full[st]);
         bulk_load(vec + kLT, p.delta + row, kLT * 4, &in_full[st]);
       } else {
         for (int r = 0; r < kLT; ++r) {
           const bool in = q0 + r < p.S;
-          vec[r] = in ? p.lse[row + r] : 0.f;
+          vec[r] = in ? p.nlse2[row + r] : 0.f;
           vec[kLT + r] = in ? p.delta[row + r] : 0.f;
         }
         mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes);
@@ -757,86 +761,93 @@ __global__ void __launch_bounds__(384, 1)
     }
     if (lane == 0) tma_store_wait_all();
   } else if (warp >= 4) {
-    // 8 compute warps: lane quarter w % 4 (32 key rows), one 32-query half of each step.
+    // 8 softmax warps in two groups of four (one warp per TMEM lane quarter):
+    // group g takes the steps i with i % 2 == g (TMEM / dS^T buffer g), so one
+    // group computes while the other waits on TMEM or barriers. Each warp covers
+    // 32 key rows x 64 queries in two 32-column halves.
     const int quarter = warp & 3;
-    const int half = (warp - 4) >> 2;
+    const int grp = (warp - 4) >> 2;
     const int kr = quarter * 32 + lane;  // key row
     const int key = k0 + kr;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int c0 = half * 32;
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int i = 0; i < n_steps; ++i) {
+    for (int i = grp; i < n_steps; i += 2) {
       const int st = i % NS;
       const int q0 = (qt_lo + i % nq) * kLT;
       if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s_full[grp], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t tS = tmem + lane_off + (i & 1) * kLT;
-      const uint32_t tP = tmem + lane_off + 128 + (i & 1) * kLT;
-      uint32_t sv[32], dv[32];
-      tmem_ld_32x32b_x32(tS + c0, sv);
-      tmem_ld_32x32b_x32(tP + c0, dv);
-      const float4* lse4 = reinterpret_cast<const float4*>(sVec + st * 2 * kLT + c0);
-      const float4* dl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kLT + kLT + c0);
-      float nl[32], dl[32];
+      const uint32_t tS = tmem + lane_off + grp * kLT;
+      const uint32_t tP = tS + 128;
+      uint8_t* row = sDS + grp * SM::kDSBytes + kr * 128;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = half * 32;
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tS + c0, sv);
+        tmem_ld_32x32b_x32(tP + c0, dv);
+        const float4* nl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kLT + c0);
+        const float4* dl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kLT + kLT + c0);
+        float nl[32], dl[32];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const float4 a = lse4[t], d = dl4[t];
-        nl[4 * t] = -a.x * kLog2e;
-        nl[4 * t + 1] = -a.y * kLog2e;
-        nl[4 * t + 2] = -a.z * kLog2e;
-        nl[4 * t + 3] = -a.w * kLog2e;
-        dl[4 * t] = d.x;
-        dl[4 * t + 1] = d.y;
-        dl[4 * t + 2] = d.z;
-        dl[4 * t + 3] = d.w;
-      }
-      tmem_wait_ld();
-      const bool need_mask = (p.causal && k0 + kTile - 1 > off + q0 + c0) || (k0 + kTile > p.T) ||
-                             (q0 + c0 + 32 > p.S) || (p.window >= 0 && k0 < off + q0 + c0 + 31 - p.window);
-      uint32_t pk[16], dk[16];
-      if (!need_mask) {
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * t]), sl2, nl[2 * t]));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * t + 1]), sl2, nl[2 * t + 1]));
-          pk[t] = pack_bf16x2(p0, p1);
-          dk[t] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * t]) - dl[2 * t]),
-                              p1 * (__uint_as_float(dv[2 * t + 1]) - dl[2 * t + 1]));
+        for (int t = 0; t < 8; ++t) {
+          const float4 a = nl4[t], d = dl4[t];
+          nl[4 * t] = a.x;
+          nl[4 * t + 1] = a.y;
+          nl[4 * t + 2] = a.z;
+          nl[4 * t + 3] = a.w;
+          dl[4 * t] = d.x;
+          dl[4 * t + 1] = d.y;
+          dl[4 * t + 2] = d.z;
+          dl[4 * t + 3] = d.w;
         }
-      } else {
+        tmem_wait_ld();
+        const bool need_mask = (p.causal && k0 + kTile - 1 > off + q0 + c0) || (k0 + kTile > p.T) ||
+                               (q0 + c0 + 32 > p.S) || (p.window >= 0 && k0 < off + q0 + c0 + 31 - p.window);
+        uint32_t pk[16], dk[16];
+        if (!need_mask) {
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          float pr[2], ds[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int qi = 2 * t + e;
-            const bool vis = visible(p, q0 + c0 + qi, key);
-            const float pv = vis ? fast_exp2(fmaf(__uint_as_float(sv[qi]), sl2, nl[qi])) : 0.f;
-            pr[e] = pv;
-            ds[e] = vis ? pv * (__uint_as_float(dv[qi]) - dl[qi]) : 0.f;
+          for (int t = 0; t < 16; ++t) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * t]), sl2, nl[2 * t]));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * t + 1]), sl2, nl[2 * t + 1]));
+            pk[t] = pack_bf16x2(p0, p1);
+            dk[t] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * t]) - dl[2 * t]),
+                                p1 * (__uint_as_float(dv[2 * t + 1]) - dl[2 * t + 1]));
           }
-          pk[t] = pack_bf16x2(pr[0], pr[1]);
-          dk[t] = pack_bf16x2(ds[0], ds[1]);
-        }
-      }
-      tmem_st_32x32b_x16(tS + c0, pk);  // inside this half's own S columns
-      tmem_st_32x32b_x16(tP + c0, dk);
-      // dS^T row `kr`, queries [c0, c0 + 32): four 16-byte chunks of the 128B-swizzled row.
-      uint8_t* row = sDS + (i & 1) * SM::kDSBytes + kr * 128;
+        } else {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int chunk = (c0 >> 3) + t;
-        *reinterpret_cast<uint4*>(row + ((chunk ^ (kr & 7)) << 4)) =
-            make_uint4(dk[4 * t], dk[4 * t + 1], dk[4 * t + 2], dk[4 * t + 3]);
+          for (int t = 0; t < 16; ++t) {
+            float pr[2], ds[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int qi = 2 * t + e;
+              const bool vis = visible(p, q0 + c0 + qi, key);
+              const float pv = vis ? fast_exp2(fmaf(__uint_as_float(sv[qi]), sl2, nl[qi])) : 0.f;
+              pr[e] = pv;
+              ds[e] = vis ? pv * (__uint_as_float(dv[qi]) - dl[qi]) : 0.f;
+            }
+            pk[t] = pack_bf16x2(pr[0], pr[1]);
+            dk[t] = pack_bf16x2(ds[0], ds[1]);
+          }
+        }
+        tmem_st_32x32b_x16(tS + c0, pk);  // inside this half's own S columns
+        tmem_st_32x32b_x16(tP + c0, dk);
+        // dS^T row `kr`, queries [c0, c0 + 32): four 16-byte chunks of the 128B-swizzled row.
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int chunk = (c0 >> 3) + t;
+          *reinterpret_cast<uint4*>(row + ((chunk ^ (kr & 7)) << 4)) =
+              make_uint4(dk[4 * t], dk[4 * t + 1], dk[4 * t + 2], dk[4 * t + 3]);
+        }
       }
       fence_proxy_async_smem();
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[i & 1]);
+      if (lane == 0) mbar_arrive(&p_ready[grp]);
     }
+    const int half = grp;  // epilogue: group g writes d columns [32 g, 32 g + 32)
     if (ok && n_steps > 0) ok = mbar_wait(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
     tc_fence_after();
     // TMEM loads are warp-collective: every lane executes them; only stores are predicated.
@@ -935,8 +946,11 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.dk_ss = dk.s_seq;
   p.dk_sh = D;
   p.status = status;
+  const bool fused = D == 64 && dq_acc != nullptr;
   {
     const long long rows = static_cast<long long>(p.B) * p.S * p.H;
+    // The fused kernel reads -lse * log2(e), written next to delta (delta holds 2 * (rows + 128) floats).
+    p.nlse2 = fused ? delta + rows + 128 : nullptr;
     attn_delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(p);
   }
   CUtensorMap mq128, mdo128, mq64, mdo64, mk128, mv128, mk64, mv64;
@@ -950,7 +964,7 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   make_bshd_map(&mv64, v, Hkv, D, kLT);
   const int grid_kv = ((p.T + kTile - 1) / kTile) * p.B * p.Hkv;
   const int grid_q = ((p.S + kTile - 1) / kTile) * p.B * p.H;
-  if (D == 64 && dq_acc != nullptr) {
+  if (fused) {
     const long long n_acc = static_cast<long long>(p.B) * p.H * p.S * D;
     cudaMemsetAsync(dq_acc, 0, n_acc * sizeof(float), stream);
     CUtensorMap mdq;

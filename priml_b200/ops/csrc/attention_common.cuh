@@ -30,6 +30,7 @@ struct AttnParams {
   long long o_sb, o_ss, o_sh;
   float* lse;        // [B, H, S]
   float* delta;      // [B, H, S]
+  float* nlse2;      // optional [B, H, S] output of the delta kernel: -lse * log2(e)
   const void* dout;  // [B, S, H, D]
   long long do_sb, do_ss, do_sh;
   void* dq;  // [B, S, H, D] bf16 out
