@@ -544,15 +544,21 @@ __global__ void __launch_bounds__(320, 1)
 
 
 // ============================================================================ fused dK dV dQ (D = 64)
-// One CTA per (b, kv head, 128-key tile), the loop of attn_dkdv_kernel, plus
-// dQ: after the softmax warps turn S^T / dP^T into P^T / dS^T they also store
-// dS^T (bf16, 128B-swizzled, queries contiguous) in shared memory, and the MMA
-// warp issues dQ^T = K^T dS^T (M = 128: rows 0-63 read V as filler, rows
-// 64-127 read K; N = 64 queries; K = 128 keys) into one of two TMEM buffers.
-// Two epilogue warps (TMEM lanes 64-127 = d) move each dQ^T tile through
-// shared memory and bulk-reduce-add it (fp32, in L2) into dq_acc [B, H, S, D];
-// a final kernel scales and converts dq_acc to bf16. exp() runs once per score
-// and the backward needs five GEMMs instead of seven.
+// One CTA per (b, kv head, 128-key tile) loops over every (query head, 64-query
+// tile) step of its GQA group:
+//   * K and V rows are copied into TMEM once and serve as the A operands of
+//     S^T = K Q^T and dP^T = V dO^T (two TMEM buffer pairs, one step ahead);
+//   * eight softmax warps in two ping-pong groups of four turn S^T / dP^T into
+//     P^T / dS^T (bf16, back into TMEM) and also store dS^T in shared memory
+//     (128B-swizzled, queries contiguous);
+//   * the MMA warp issues dV += P^T dO, dK += dS^T Q (A from TMEM) and
+//     dQ^T = K^T dS^T (M = 128: rows 0-63 read V as filler, rows 64-127 read K;
+//     N = 64 queries; K = 128 keys);
+//   * two epilogue warps (TMEM lanes 64-127 = d) move each dQ^T tile through
+//     shared memory and bulk-reduce-add it (fp32, performed in L2) into
+//     dq_acc [B, H, S, D]; a last kernel scales and converts dq_acc to bf16.
+// exp() runs once per score and the backward needs five GEMMs instead of the
+// seven of the two-kernel variant.
 struct FusedSmem {
   static constexpr int kStages = 3;
   static constexpr int kKVBytes = kChunkBytes;   // [128 keys][64 d]
@@ -585,9 +591,10 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* in_empty = in_full + NS;   // [NS]
   uint64_t* s_full = in_empty + NS;    // [2]
   uint64_t* p_ready = s_full + 2;      // [2]
-  uint64_t* dq_full = p_ready + 2;     // [2]
-  uint64_t* dq_empty = dq_full + 2;    // [2]
-  uint64_t* mm_done = dq_empty + 2;
+  uint64_t* dq_full = p_ready + 2;
+  uint64_t* dq_empty = dq_full + 1;
+  uint64_t* kv_tmem = dq_empty + 1;    // K and V copied into TMEM
+  uint64_t* mm_done = kv_tmem + 1;
   uint64_t* acc_final = mm_done + 1;
   uint64_t* drain = acc_final + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -618,9 +625,10 @@ __global__ void __launch_bounds__(384, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_ready[s], 4);
-      mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_empty[s], 2);
     }
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 2);
+    mbar_init(kv_tmem, 8);
     mbar_init(mm_done, 1);
     mbar_init(acc_final, 1);
     mbar_init(drain, 1);
@@ -635,10 +643,14 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // cols: S^T [0,64) [64,128); dP^T [128,192) [192,256); dV [256,320); dK [320,384); dQ^T [384,448) [448,512)
+  // cols: S^T [0,64) [64,128); dP^T [128,192) [192,256); dV [256,320); dK [320,384); dQ^T [384,448);
+  // K [448,480) and V [480,512) as bf16 pairs: the A operands of S^T = K Q^T and dP^T = V dO^T stay in
+  // TMEM for the whole CTA, so those MMAs read only Q / dO from shared memory.
   const uint32_t tdV = tmem + 256;
   const uint32_t tdK = tmem + 320;
   const uint32_t tdQ = tmem + 384;
+  const uint32_t tK = tmem + 448;
+  const uint32_t tV = tmem + 480;
 
   if (warp == 0 && lane == 0) {
     bool ok = true;
@@ -673,9 +685,10 @@ __global__ void __launch_bounds__(384, 1)
     constexpr uint32_t idesc_ss = make_idesc_bf16(128, kLT, false, false);  // [128 keys x 64 q]
     constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, false, true);   // [128 keys x D]
     constexpr uint32_t idesc_dq = make_idesc_bf16(128, kLT, true, true);   // [128 (V|K) x 64 q]
-    bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag);
+    bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag) &&
+              mbar_wait(kv_tmem, 0, p.status, kTimeoutMma, abort_flag);
     tc_fence_after();
-    const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+    const uint32_t v_base = smem_u32(sV);
     auto issue_scores = [&](int i) -> bool {
       const int st = i % NS;
       if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutMma, abort_flag)) return false;
@@ -685,11 +698,10 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t tS = tmem + (i & 1) * kLT;
       const uint32_t tP = tmem + 128 + (i & 1) * kLT;
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        umma_f16(tS, kmajor_desc(k_base, kk), kmajor_desc(q_base, kk, kLChunk), idesc_ss, kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        umma_f16(tP, kmajor_desc(v_base, kk), kmajor_desc(do_base, kk, kLChunk), idesc_ss, kk > 0);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        umma_f16_tmem_a(tS, tK + kk * 8, kmajor_desc(q_base, kk, kLChunk), idesc_ss, kk > 0);
+        umma_f16_tmem_a(tP, tV + kk * 8, kmajor_desc(do_base, kk, kLChunk), idesc_ss, kk > 0);
+      }
       umma_commit(&s_full[i & 1]);
       return true;
     };
@@ -703,21 +715,25 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t do_base = smem_u32(sDO + st * SM::kQBytes);
       const uint32_t tS = tmem + (i & 1) * kLT;
       const uint32_t tP = tmem + 128 + (i & 1) * kLT;
-#pragma unroll
-      for (int kk = 0; kk < kLT / 16; ++kk)
-        umma_f16_tmem_a(tdV, tS + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(do_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
-#pragma unroll
-      for (int kk = 0; kk < kLT / 16; ++kk)
-        umma_f16_tmem_a(tdK, tP + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(q_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
-      // dQ^T buffer i&1 was last read by the epilogue warps at step i-2.
-      if (!mbar_wait(&dq_empty[i & 1], ((i >> 1) & 1) ^ 1u, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
+      // dQ^T was last read by the epilogue warps at step i-1.
+      if (!mbar_wait(dq_empty, (i & 1) ^ 1u, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t ds_base = smem_u32(sDS + (i & 1) * SM::kDSBytes);
+      const uint32_t tQ = tdQ;
+      // dV, dK and the first half of dQ^T interleaved (three independent accumulators), then
+      // the rest of dQ^T.
 #pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk)
-        umma_f16(tdQ + (i & 1) * kLT, make_sw128_desc(v_base + kk * 2048, SM::kKVBytes, 1024),
-                 make_sw128_desc(ds_base + kk * 2048, SM::kDSBytes, 1024), idesc_dq, kk > 0);
-      umma_commit(&dq_full[i & 1]);
+      for (int kk = 0; kk < kLT / 16; ++kk) {
+        umma_f16_tmem_a(tdV, tS + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(do_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
+        umma_f16_tmem_a(tdK, tP + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(q_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
+        umma_f16(tQ, make_sw128_desc(v_base + kk * 2048, SM::kKVBytes, 1024),
+                   make_sw128_desc(ds_base + kk * 2048, SM::kDSBytes, 1024), idesc_dq, kk > 0);
+      }
+#pragma unroll
+      for (int kk = kLT / 16; kk < kTile / 16; ++kk)
+        umma_f16(tQ, make_sw128_desc(v_base + kk * 2048, SM::kKVBytes, 1024),
+                 make_sw128_desc(ds_base + kk * 2048, SM::kDSBytes, 1024), idesc_dq, true);
+      umma_commit(dq_full);
       umma_commit(&in_empty[st]);
       umma_commit(mm_done);
       // Buffer pair i&1 (TMEM S/dP and shared dS^T) is rewritten at step i+2.
@@ -734,16 +750,16 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < n_steps; ++i) {
       const int h = hk * g + i / nq;
       const int q0 = (qt_lo + i % nq) * kLT;
-      if (!mbar_wait(&dq_full[i & 1], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait(dq_full, i & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
-      tmem_ld_32x32b_x32(tdQ + lane_off + (i & 1) * kLT, v0);
-      tmem_ld_32x32b_x32(tdQ + lane_off + (i & 1) * kLT + 32, v1);
+      tmem_ld_32x32b_x32(tdQ + lane_off, v0);
+      tmem_ld_32x32b_x32(tdQ + lane_off + 32, v1);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&dq_empty[i & 1]);
+        mbar_arrive(dq_empty);
         bulk_wait_read_1();  // the reduce issued two steps ago no longer reads this staging buffer
       }
       __syncwarp();
@@ -771,8 +787,26 @@ __global__ void __launch_bounds__(384, 1)
     const int key = k0 + kr;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = p.scale_log2;
-    bool ok = true;
-    for (int i = grp; i < n_steps; i += 2) {
+    bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutEpilogue, abort_flag);
+    {
+      // Row kr of K (group 0) or V (group 1): eight swizzled 16-byte chunks -> 32 TMEM columns.
+      const uint8_t* src = (grp == 0 ? sK : sV) + kr * 128;
+      uint32_t w[32];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 x = *reinterpret_cast<const uint4*>(src + ((c ^ (kr & 7)) << 4));
+        w[4 * c] = x.x;
+        w[4 * c + 1] = x.y;
+        w[4 * c + 2] = x.z;
+        w[4 * c + 3] = x.w;
+      }
+      tmem_st_32x32b_x32((grp == 0 ? tK : tV) + lane_off, w);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(kv_tmem);
+    }
+    for (int i = grp; i < n_steps && ok; i += 2) {
       const int st = i % NS;
       const int q0 = (qt_lo + i % nq) * kLT;
       if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
