@@ -19,6 +19,8 @@
 //               global (bf16 / fp32 / fp32 accumulate / fused SwiGLU).
 // The double-buffered accumulator lets the epilogue of tile i overlap the MMAs
 // of tile i+1. Tiles are visited in GROUP_M-grouped order for L2 reuse.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -58,6 +60,110 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   const int r = tile - g * group;
   mb = first_m + r % gm;
   nb = r / gm;
+}
+
+// Store one accumulator row slice (this thread's TMEM lane) of output tile column block `nb`.
+template <int BN, int EPI>
+__device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_row, int row, int nb) {
+  const bool row_ok = row < p.M;
+  if constexpr (EPI == 3) {
+    const int H = p.num_n_half;
+    const int h0 = nb * (BN / 2);
+    __nv_bfloat16* hout = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
+    __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(p.aux)) +
+                        static_cast<long long>(row) * (2LL * H);
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(t_row + c, g);
+      tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+      tmem_wait_ld();
+      const int col = h0 + c;
+      if (row_ok && col < H) {
+        uint32_t hv[16], gv[16], uv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
+          const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
+          // Round gate/up to bf16 first so forward and backward see the same values.
+          const __nv_bfloat162 gb = __floats2bfloat162_rn(g0, g1);
+          const __nv_bfloat162 ub = __floats2bfloat162_rn(u0, u1);
+          const float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
+          const float s0 = gf.x / (1.f + __expf(-gf.x)), s1 = gf.y / (1.f + __expf(-gf.y));
+          hv[j] = pack_bf16x2(s0 * uf.x, s1 * uf.y);
+          gv[j] = *reinterpret_cast<const uint32_t*>(&gb);
+          uv[j] = *reinterpret_cast<const uint32_t*>(&ub);
+        }
+        if (col + 32 <= H) {
+          uint4* hp = reinterpret_cast<uint4*>(hout + col);
+          uint4* gp = reinterpret_cast<uint4*>(gu + col);
+          uint4* up = reinterpret_cast<uint4*>(gu + H + col);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            hp[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+            gp[q] = make_uint4(gv[4 * q], gv[4 * q + 1], gv[4 * q + 2], gv[4 * q + 3]);
+            up[q] = make_uint4(uv[4 * q], uv[4 * q + 1], uv[4 * q + 2], uv[4 * q + 3]);
+          }
+        } else {
+          const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(hv);
+          const __nv_bfloat16* gb2 = reinterpret_cast<const __nv_bfloat16*>(gv);
+          const __nv_bfloat16* ub2 = reinterpret_cast<const __nv_bfloat16*>(uv);
+          for (int j = 0; j < 32 && col + j < H; ++j) {
+            hout[col + j] = hb[j];
+            gu[col + j] = gb2[j];
+            gu[H + col + j] = ub2[j];
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_row + c, v);
+      tmem_wait_ld();
+      const int col = nb * BN + c;
+      if (!row_ok || col >= p.N) continue;
+      const bool full_chunk = col + 32 <= p.N;
+      if constexpr (EPI == 0) {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+        if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+          uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        } else {
+          const __nv_bfloat16* pb16 = reinterpret_cast<const __nv_bfloat16*>(pk);
+          for (int j = 0; j < 32 && col + j < p.N; ++j) out[j] = pb16[j];
+        }
+      } else {
+        float* out = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+        if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+          float4* o4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 a = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                   __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+            if constexpr (EPI == 2) {
+              const float4 o = o4[q];
+              a.x += o.x;
+              a.y += o.y;
+              a.z += o.z;
+              a.w += o.w;
+            }
+            o4[q] = a;
+          }
+        } else {
+          for (int j = 0; j < 32 && col + j < p.N; ++j) {
+            const float a = __uint_as_float(v[j]);
+            out[j] = EPI == 2 ? out[j] + a : a;
+          }
+        }
+      }
+    }
+  }
 }
 
 // EPI: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += acc),
@@ -221,106 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int row = mb * BM + wq * 32 + lane;
-      const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * BN;
-      if constexpr (EPI == 3) {
-        const int H = p.num_n_half;
-        const int h0 = nb * (BN / 2);
-        __nv_bfloat16* hout = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
-        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(p.aux)) +
-                            static_cast<long long>(row) * (2LL * H);
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(t_row + c, g);
-          tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
-          tmem_wait_ld();
-          const int col = h0 + c;
-          if (row_ok && col < H) {
-            uint32_t hv[16], gv[16], uv[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
-              const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
-              // Round gate/up to bf16 first so forward and backward see the same values.
-              const __nv_bfloat162 gb = __floats2bfloat162_rn(g0, g1);
-              const __nv_bfloat162 ub = __floats2bfloat162_rn(u0, u1);
-              const float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
-              const float s0 = gf.x / (1.f + __expf(-gf.x)), s1 = gf.y / (1.f + __expf(-gf.y));
-              hv[j] = pack_bf16x2(s0 * uf.x, s1 * uf.y);
-              gv[j] = *reinterpret_cast<const uint32_t*>(&gb);
-              uv[j] = *reinterpret_cast<const uint32_t*>(&ub);
-            }
-            if (col + 32 <= H) {
-              uint4* hp = reinterpret_cast<uint4*>(hout + col);
-              uint4* gp = reinterpret_cast<uint4*>(gu + col);
-              uint4* up = reinterpret_cast<uint4*>(gu + H + col);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                hp[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
-                gp[q] = make_uint4(gv[4 * q], gv[4 * q + 1], gv[4 * q + 2], gv[4 * q + 3]);
-                up[q] = make_uint4(uv[4 * q], uv[4 * q + 1], uv[4 * q + 2], uv[4 * q + 3]);
-              }
-            } else {
-              const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(hv);
-              const __nv_bfloat16* gb2 = reinterpret_cast<const __nv_bfloat16*>(gv);
-              const __nv_bfloat16* ub2 = reinterpret_cast<const __nv_bfloat16*>(uv);
-              for (int j = 0; j < 32 && col + j < H; ++j) {
-                hout[col + j] = hb[j];
-                gu[col + j] = gb2[j];
-                gu[H + col + j] = ub2[j];
-              }
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c, v);
-          tmem_wait_ld();
-          const int col = nb * BN + c;
-          if (!row_ok || col >= p.N) continue;
-          const bool full_chunk = col + 32 <= p.N;
-          if constexpr (EPI == 0) {
-            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col;
-            uint32_t pk[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-            if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-              uint4* o4 = reinterpret_cast<uint4*>(out);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) o4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-            } else {
-              const __nv_bfloat16* pb16 = reinterpret_cast<const __nv_bfloat16*>(pk);
-              for (int j = 0; j < 32 && col + j < p.N; ++j) out[j] = pb16[j];
-            }
-          } else {
-            float* out = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
-            if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-              float4* o4 = reinterpret_cast<float4*>(out);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                float4 a = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                       __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
-                if constexpr (EPI == 2) {
-                  const float4 o = o4[q];
-                  a.x += o.x;
-                  a.y += o.y;
-                  a.z += o.z;
-                  a.w += o.w;
-                }
-                o4[q] = a;
-              }
-            } else {
-              for (int j = 0; j < 32 && col + j < p.N; ++j) {
-                const float a = __uint_as_float(v[j]);
-                out[j] = EPI == 2 ? out[j] + a : a;
-              }
-            }
-          }
-        }
-      }
+      store_acc_row<BN, EPI>(p, t_row, row, nb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -350,7 +358,248 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, i
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
 }
 
+
+// ---------------------------------------------------------------------------- 2-CTA tiles
+// A CTA pair (cluster of 2 on neighbouring SMs) computes one 256 x 256 output
+// tile with M = 256 tcgen05 MMAs: CTA r holds A rows [128 r, 128 r + 128) and B
+// rows (N) [128 r, 128 r + 128) of every K stage and receives D rows
+// [128 r, 128 r + 128) in its own TMEM. Per SM this streams 32 KB of operands
+// per 64-deep K step instead of the 48 KB of a 1-CTA 128 x 256 tile, for the
+// same MMA time -- the 1-CTA kernel is bound by that feed, not by the tensor core.
+//   * both CTAs TMA-load their halves; the completion bytes of both land on
+//     CTA 0's `full` barrier (CTA 0 expects the pair's total);
+//   * CTA 0's MMA thread issues the MMAs and commits `empty` / `tfull` to its own
+//     barriers; CTA 0's producer and epilogue relay those two signals to CTA 1
+//     with remote mbarrier arrives;
+//   * both CTAs' epilogues read their own TMEM and arrive on CTA 0's `tempty`;
+//   * TMEM is allocated and freed by warp 1 of both CTAs (cta_group::2).
+constexpr int kPairStages = 6;
+struct PairCfg {
+  static constexpr int kABytes = 128 * BK * 2;  // this CTA's 128 rows of A
+  static constexpr int kBBytes = 128 * BK * 2;  // this CTA's 128 rows (N) of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSmemBytes = kPairStages * kStageBytes + 1024 + 256;
+};
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  constexpr int S = kPairStages;
+  constexpr int TM = 256, TN = 256;  // pair tile
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + S * PairCfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * PairCfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* peer_done = drain + 1;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(peer_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (p.M + TM - 1) / TM;
+  const int num_n = (p.N + TN - 1) / TN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain, 1);
+    mbar_init(peer_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits of both CTAs visible before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    const uint32_t full0 = cluster_addr(full, 0);
+    const uint32_t empty1 = cluster_addr(empty, 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * TM + 128 * static_cast<int>(rank);
+      const int n0 = nb * TN + 128 * static_cast<int>(rank);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutProducer, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (leader) {
+          // The MMAs that read the previous fill of this stage are done: free CTA 1's copy too.
+          if (issued >= S) mbar_arrive_cluster(empty1 + 8u * stage);
+          mbar_arrive_expect_tx(&full[stage], 2 * PairCfg::kStageBytes);
+        }
+        const uint32_t bar = full0 + 8u * stage;
+        uint8_t* a_dst = smA + stage * PairCfg::kABytes;
+        uint8_t* b_dst = smB + stage * PairCfg::kBBytes;
+        const int k0 = kb * BK;
+        if constexpr (A_MN) {
+          tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
+          tma_load_2d_pair(a_dst + BK * 128, &tmA, bar, m0 + 64, k0);
+        } else {
+          tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+        }
+        if constexpr (EPI == 3) {
+          // Pair tile columns [0, 128) = gate rows h0.., [128, 256) = up rows H + h0..
+          const int h0 = nb * (TN / 2);
+          tma_load_2d_pair(b_dst, &tmB, bar, k0, leader ? h0 : p.num_n_half + h0);
+        } else if constexpr (B_MN) {
+          tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
+          tma_load_2d_pair(b_dst + BK * 128, &tmB, bar, n0 + 64, k0);
+        } else {
+          tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
+        }
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && leader) {
+      // Drain: the pair's loads already issued complete on this CTA's barriers.
+      for (int i = 0; i < min(issued, S); ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&full[stage], phase, p.status, kTimeoutDrain, nullptr);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    if (leader) {
+      // ------------------------------------------------------------ MMA issuer (CTA 0)
+      constexpr uint32_t idesc = make_idesc_bf16(TM, TN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
+        const int b = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[b], acc_phase ^ 1u, p.status, kTimeoutMma, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * TN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * PairCfg::kABytes);
+          const uint32_t b_base = smem_u32(smB + stage * PairCfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sw128_desc(a_base + kk * 2048, BK * 128, 1024)
+                                     : make_sw128_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = (B_MN && EPI != 3) ? make_sw128_desc(b_base + kk * 2048, BK * 128, 1024)
+                                                   : make_sw128_desc(b_base + kk * 32, 16, 1024);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+          }
+          umma_commit_pair(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit_pair(&tfull[b]);
+      }
+      umma_commit_pair(drain);
+      mbar_wait(drain, 0, p.status, kTimeoutDrain, nullptr);
+      mbar_arrive_cluster(cluster_addr(peer_done, 1));  // CTA 1 may free its TMEM now
+    } else {
+      // CTA 1 frees its TMEM only after CTA 0's MMAs (which write it) are complete.
+      mbar_wait(peer_done, 0, p.status, kTimeoutDrain, nullptr);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int wq = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t tempty0 = cluster_addr(tempty, 0);
+    const uint32_t tfull1 = cluster_addr(tfull, 1);
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int b = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (leader && warp == 2 && lane == 0) mbar_arrive_cluster(tfull1 + 8u * b);  // relay to CTA 1
+      tc_fence_after();
+      const int row = mb * TM + 128 * static_cast<int>(rank) + wq * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TN;
+      store_acc_row<TN, EPI>(p, t_row, row, nb);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * b);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no remote arrive may target a CTA that has exited
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmemBytes);
+    configured = true;
+  }
+  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  kern<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(ta, tb, p);
+}
 }  // namespace
+
+// 2-CTA tiles are on unless PRIML_B200_GEMM_PAIR=0 (kept for A/B measurements of the two tilings).
+static bool pair_gemm_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("PRIML_B200_GEMM_PAIR");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
 
 // Public entry. Layout flags: a_mn = A stored [K, M]; b_mn = B stored [K, N].
 // lda / ldb are the row strides (elements) of A and B as stored.
@@ -359,30 +608,44 @@ void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long
                cudaStream_t stream) {
   const int num_sms = device_sm_count();
   CUtensorMap ta, tb;
-  // A tile: 128 (M) x 64 (K).
+  GemmParams p{M, N, K, C, ldc, aux, status, swiglu_h};
+  // 2-CTA 256 x 256 tiles once the problem has enough of them; 1-CTA 128 x 256 otherwise.
+  const bool pair = M >= 256 && N >= 256 && pair_gemm_enabled();
+  // A tile: 128 (M) x 64 (K) per CTA in both kernels.
   if (a_mn) {
     make_tmap_2d_bf16(&ta, A, /*inner=*/M, /*outer=*/K, lda, /*box_inner=*/64, /*box_outer=*/BK);
   } else {
     make_tmap_2d_bf16(&ta, A, K, M, lda, 64, BM);
   }
-  GemmParams p{M, N, K, C, ldc, aux, status, swiglu_h};
   if (epi == 3) {
     // B = up_proj weight [2H, K] (K-major); tile rows are split gate / up.
     make_tmap_2d_bf16(&tb, B, K, 2 * swiglu_h, ldb, 64, 128);
-    launch<256, false, false, 3>(ta, tb, p, num_sms, stream);
+    if (pair) {
+      launch_pair<false, false, 3>(ta, tb, p, num_sms, stream);
+    } else {
+      launch<256, false, false, 3>(ta, tb, p, num_sms, stream);
+    }
     return;
   }
   constexpr int BN = 256;
   if (b_mn) {
     make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, BK);
   } else {
-    make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, BN);
+    make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, pair ? 128 : BN);
   }
-#define PB_DISPATCH(AM, BMJ)                                   \
-  switch (epi) {                                               \
-    case 0: launch<BN, AM, BMJ, 0>(ta, tb, p, num_sms, stream); break; \
-    case 1: launch<BN, AM, BMJ, 1>(ta, tb, p, num_sms, stream); break; \
-    default: launch<BN, AM, BMJ, 2>(ta, tb, p, num_sms, stream); break; \
+#define PB_DISPATCH(AM, BMJ)                                                                  \
+  if (pair) {                                                                                 \
+    switch (epi) {                                                                            \
+      case 0: launch_pair<AM, BMJ, 0>(ta, tb, p, num_sms, stream); break;                     \
+      case 1: launch_pair<AM, BMJ, 1>(ta, tb, p, num_sms, stream); break;                     \
+      default: launch_pair<AM, BMJ, 2>(ta, tb, p, num_sms, stream); break;                    \
+    }                                                                                         \
+  } else {                                                                                    \
+    switch (epi) {                                                                            \
+      case 0: launch<BN, AM, BMJ, 0>(ta, tb, p, num_sms, stream); break;                      \
+      case 1: launch<BN, AM, BMJ, 1>(ta, tb, p, num_sms, stream); break;                      \
+      default: launch<BN, AM, BMJ, 2>(ta, tb, p, num_sms, stream); break;                     \
+    }                                                                                         \
   }
   if (!a_mn && !b_mn) {
     PB_DISPATCH(false, false)
