@@ -146,6 +146,12 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
                : "memory");
 }
 
+// Same, for an mbarrier named by a shared::cluster address (e.g. the peer CTA's).
+__device__ __forceinline__ void umma_commit_pair_to(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 // 2-D TMA load into this CTA's shared memory whose completion bytes are counted on an
 // mbarrier of the pair's CTA 0 (shared::cluster address).
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t cluster_bar, int x,

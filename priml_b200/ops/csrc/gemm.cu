@@ -368,12 +368,11 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, i
 // same MMA time -- the 1-CTA kernel is bound by that feed, not by the tensor core.
 //   * both CTAs TMA-load their halves; the completion bytes of both land on
 //     CTA 0's `full` barrier (CTA 0 expects the pair's total);
-//   * CTA 0's MMA thread issues the MMAs and commits `empty` / `tfull` to its own
-//     barriers; CTA 0's producer and epilogue relay those two signals to CTA 1
-//     with remote mbarrier arrives;
+//   * CTA 0's MMA thread issues the MMAs and commits `empty` / `tfull` to the
+//     barriers of both CTAs (one commit per CTA);
 //   * both CTAs' epilogues read their own TMEM and arrive on CTA 0's `tempty`;
 //   * TMEM is allocated and freed by warp 1 of both CTAs (cta_group::2).
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 7;
 struct PairCfg {
   static constexpr int kABytes = 128 * BK * 2;  // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * BK * 2;  // this CTA's 128 rows (N) of B
@@ -440,7 +439,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     const uint32_t full0 = cluster_addr(full, 0);
-    const uint32_t empty1 = cluster_addr(empty, 1);
     int stage = 0;
     uint32_t phase = 0;
     int issued = 0;
@@ -455,11 +453,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (leader) {
-          // The MMAs that read the previous fill of this stage are done: free CTA 1's copy too.
-          if (issued >= S) mbar_arrive_cluster(empty1 + 8u * stage);
-          mbar_arrive_expect_tx(&full[stage], 2 * PairCfg::kStageBytes);
-        }
+        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * PairCfg::kStageBytes);
         const uint32_t bar = full0 + 8u * stage;
         uint8_t* a_dst = smA + stage * PairCfg::kABytes;
         uint8_t* b_dst = smB + stage * PairCfg::kBBytes;
@@ -501,6 +495,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (leader) {
       // ------------------------------------------------------------ MMA issuer (CTA 0)
       constexpr uint32_t idesc = make_idesc_bf16(TM, TN, A_MN, B_MN);
+      const uint32_t empty1 = cluster_addr(empty, 1);
+      const uint32_t tfull1 = cluster_addr(tfull, 1);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -531,12 +527,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
           }
           umma_commit_pair(&empty[stage]);
+          umma_commit_pair_to(empty1 + 8u * stage);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) umma_commit_pair(&tfull[b]);
+        if (ok) {
+          umma_commit_pair(&tfull[b]);
+          umma_commit_pair_to(tfull1 + 8u * b);
+        }
       }
       umma_commit_pair(drain);
       mbar_wait(drain, 0, p.status, kTimeoutDrain, nullptr);
@@ -549,7 +549,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int wq = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t tempty0 = cluster_addr(tempty, 0);
-    const uint32_t tfull1 = cluster_addr(tfull, 1);
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
       int mb, nb;
@@ -557,7 +556,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
-      if (leader && warp == 2 && lane == 0) mbar_arrive_cluster(tfull1 + 8u * b);  // relay to CTA 1
       tc_fence_after();
       const int row = mb * TM + 128 * static_cast<int>(rank) + wq * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TN;
