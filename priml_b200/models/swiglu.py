@@ -102,6 +102,10 @@ class SwiGLU(nn.Module):
             w = self.up_proj.weight
             fusable = self.norm is None and self.act is nn.functional.silu and self.up_proj.bias is None
             if fusable and not isinstance(w, _DTensorType()) and ops.use_native(x):
+                down = self.down_proj
+                wd = getattr(down, "weight", None)
+                if type(down) is Linear and getattr(down, "bias", None) is None and not isinstance(wd, _DTensorType()):
+                    return ops.swiglu_mlp(x, w, wd)
                 return self.down_proj(ops.linear_swiglu(x, w))
             gate, up = self.up_proj(x).chunk(2, dim=-1)
         if self.norm is None:

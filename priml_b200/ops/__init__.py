@@ -33,6 +33,7 @@ __all__ = [
     "rms_norm",
     "rotary",
     "swiglu",
+    "swiglu_mlp",
     "use_native",
 ]
 
@@ -110,6 +111,21 @@ def linear_swiglu(x: Tensor, up_weight: Tensor) -> Tensor:
 
         return functional.linear_swiglu(x, up_weight)
     return swiglu(linear(x, up_weight))
+
+
+def swiglu_mlp(x: Tensor, up_weight: Tensor, down_weight: Tensor) -> Tensor:
+    """``down(silu(x Wg^T) * (x Wu^T))`` for ``up_weight = [Wg; Wu]`` ([2H, C]) and ``down_weight`` [C_out, H]."""
+    if (
+        use_native(x)
+        and _compute_dtype(x) == torch.bfloat16
+        and up_weight.shape[0] % 16 == 0
+        and x.shape[-1] % 8 == 0
+        and down_weight.shape[0] % 8 == 0
+    ):
+        from priml_b200.ops import functional
+
+        return functional.swiglu_mlp(x, up_weight, down_weight)
+    return linear(swiglu(linear(x, up_weight)), down_weight)
 
 
 def swiglu(gate_up: Tensor) -> Tensor:

@@ -28,25 +28,33 @@ constexpr int kLChunk = kLT * 128;  // one [64 rows][64 d] swizzled chunk = 8 KB
 
 // ============================================================================ delta
 __global__ void attn_delta_kernel(const AttnParams p) {
-  // One warp per (b, q, h) row: delta = sum_d dO * O.
-  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  // D / 8 threads per (b, q, h) row, one 16-byte load of O and dO each: delta = sum_d dO * O.
+  const int tpr = p.D / 8;
+  const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long row = t / tpr;
+  const int part = static_cast<int>(t % tpr);
   const long long total = static_cast<long long>(p.B) * p.S * p.H;
-  if (row >= total) return;
-  const int h = static_cast<int>(row % p.H);
-  const long long bq = row / p.H;
-  const int q = static_cast<int>(bq % p.S);
-  const int b = static_cast<int>(bq / p.S);
-  const __nv_bfloat16* o = static_cast<const __nv_bfloat16*>(p.o) + b * p.o_sb + q * p.o_ss + h * p.o_sh;
-  const __nv_bfloat16* d = static_cast<const __nv_bfloat16*>(p.dout) + b * p.do_sb + q * p.do_ss + h * p.do_sh;
   float acc = 0.f;
-  for (int i = (threadIdx.x & 31) * 2; i < p.D; i += 64) {
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(o + i));
-    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(d + i));
-    acc += a.x * c.x + a.y * c.y;
-  }
+  int b = 0, q = 0, h = 0;
+  if (row < total) {
+    h = static_cast<int>(row % p.H);
+    const long long bq = row / p.H;
+    q = static_cast<int>(bq % p.S);
+    b = static_cast<int>(bq / p.S);
+    const uint4 a = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.o) + b * p.o_sb + q * p.o_ss +
+                                                    h * p.o_sh + part * 8);
+    const uint4 c = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.dout) + b * p.do_sb +
+                                                    q * p.do_ss + h * p.do_sh + part * 8);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-  for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-  if ((threadIdx.x & 31) == 0) {
+    for (int j = 0; j < 4; ++j) {
+      const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[j]));
+      const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&cw[j]));
+      acc += x.x * y.x + x.y * y.y;
+    }
+  }
+  for (int s = tpr / 2; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+  if (row < total && part == 0) {
     const long long idx = (static_cast<long long>(b) * p.H + h) * p.S + q;
     p.delta[idx] = acc;
     if (p.nlse2 != nullptr) p.nlse2[idx] = -p.lse[idx] * kLog2e;
@@ -985,7 +993,8 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
     const long long rows = static_cast<long long>(p.B) * p.S * p.H;
     // The fused kernel reads -lse * log2(e), written next to delta (delta holds 2 * (rows + 128) floats).
     p.nlse2 = fused ? delta + rows + 128 : nullptr;
-    attn_delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(p);
+    const long long threads = rows * (D / 8);
+    attn_delta_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p);
   }
   CUtensorMap mq128, mdo128, mq64, mdo64, mk128, mv128, mk64, mv64;
   make_bshd_map(&mq128, q, H, D, kTile);

@@ -88,6 +88,25 @@ void gemm_swiglu(const Tensor& X, const Tensor& W, Tensor& H, Tensor& GU) {
                 two_h, K, 3, GU.data_ptr(), two_h / 2, status_ptr(), stream());
 }
 
+// DGU [M, 2H] = SwiGLU backward of GU [M, 2H] for dh = DY [M, C] @ WD [C, H], computed in the
+// GEMM epilogue (dh never reaches memory).
+void gemm_swiglu_bwd(const Tensor& DY, const Tensor& WD, const Tensor& GU, Tensor& DGU) {
+  check_cuda(DY, "DY");
+  PB_CHECK(DY.scalar_type() == torch::kBFloat16 && WD.scalar_type() == torch::kBFloat16 &&
+               GU.scalar_type() == torch::kBFloat16 && DGU.scalar_type() == torch::kBFloat16,
+           "bf16 tensors");
+  const int M = DY.size(0), C = DY.size(1), H = WD.size(1);
+  PB_CHECK(WD.size(0) == C, "WD must be [C, H]");
+  PB_CHECK(GU.is_contiguous() && DGU.is_contiguous() && GU.size(0) == M && GU.size(1) == 2 * H &&
+               DGU.size(0) == M && DGU.size(1) == 2 * H,
+           "GU / DGU must be contiguous [M, 2H]");
+  PB_CHECK(H % 8 == 0, "H must be a multiple of 8");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(DY.device());
+  pb::gemm_bf16(DY.data_ptr(), row_stride(DY), false, WD.data_ptr(), row_stride(WD), true, DGU.data_ptr(), DGU.stride(0),
+                M, H, C, 4, GU.data_ptr(), H, status_ptr(), stream());
+}
+
 std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const c10::optional<Tensor>& w, double eps, bool out_f32) {
   check_cuda(x, "x");
   PB_CHECK(x.is_contiguous(), "x must be contiguous");
@@ -472,6 +491,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM: C (op)= A B^T", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epi"));
   m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 GEMM with fused SwiGLU epilogue");
+  m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, "tcgen05 GEMM dy @ W_down with the SwiGLU backward in the epilogue");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rope", &rope);

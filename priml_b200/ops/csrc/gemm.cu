@@ -20,6 +20,7 @@
 // The double-buffered accumulator lets the epilogue of tile i overlap the MMAs
 // of tile i+1. Tiles are visited in GROUP_M-grouped order for L2 reuse.
 #include <cstdlib>
+#include <stdexcept>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -116,6 +117,63 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
         }
       }
     }
+  } else if constexpr (EPI == 4) {
+    // Accumulator = dh (N = H); aux = saved [gate | up] pre-activation [M, 2H]; C = dgu [M, 2H].
+    // dh is rounded to bf16 first, as the unfused path stores it.
+    const int H = p.num_n_half;
+    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + static_cast<long long>(row) * (2LL * H);
+    __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_row + c, v);
+      tmem_wait_ld();
+      const int col = nb * BN + c;
+      if (!row_ok || col >= H) continue;
+      const int n = min(32, H - col);
+      uint32_t gw[16], uw[16], dg[16], du[16];
+      if (n == 32) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 a = reinterpret_cast<const uint4*>(gu + col)[q];
+          const uint4 b = reinterpret_cast<const uint4*>(gu + H + col)[q];
+          gw[4 * q] = a.x, gw[4 * q + 1] = a.y, gw[4 * q + 2] = a.z, gw[4 * q + 3] = a.w;
+          uw[4 * q] = b.x, uw[4 * q + 1] = b.y, uw[4 * q + 2] = b.z, uw[4 * q + 3] = b.w;
+        }
+      } else {
+        const uint16_t* g16 = reinterpret_cast<const uint16_t*>(gu + col);
+        const uint16_t* u16 = reinterpret_cast<const uint16_t*>(gu + H + col);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int a = 2 * j, b2 = 2 * j + 1;
+          gw[j] = (a < n ? g16[a] : 0u) | ((b2 < n ? static_cast<uint32_t>(g16[b2]) : 0u) << 16);
+          uw[j] = (a < n ? u16[a] : 0u) | ((b2 < n ? static_cast<uint32_t>(u16[b2]) : 0u) << 16);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[j]));
+        const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[j]));
+        const float2 d = __bfloat1622float2(__floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
+        const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+        du[j] = pack_bf16x2(d.x * (g.x * s0), d.y * (g.y * s1));
+        dg[j] = pack_bf16x2(d.x * u.x * s0 * (1.f + g.x * (1.f - s0)), d.y * u.y * s1 * (1.f + g.y * (1.f - s1)));
+      }
+      if (n == 32) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          reinterpret_cast<uint4*>(dgu + col)[q] = make_uint4(dg[4 * q], dg[4 * q + 1], dg[4 * q + 2], dg[4 * q + 3]);
+          reinterpret_cast<uint4*>(dgu + H + col)[q] = make_uint4(du[4 * q], du[4 * q + 1], du[4 * q + 2], du[4 * q + 3]);
+        }
+      } else {
+        const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(dg);
+        const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(du);
+        for (int j = 0; j < n; ++j) {
+          dgu[col + j] = gb[j];
+          dgu[H + col + j] = ub[j];
+        }
+      }
+    }
   } else {
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
@@ -167,6 +225,7 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
 }
 
 // EPI: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += acc),
+//      4 = SwiGLU backward: acc = dh, aux = [gate | up] -> C = [dgate | dup] (bf16 [M, 2H]),
 //      3 = fused SwiGLU: the BN columns hold [gate(BN/2) | up(BN/2)] of the same
 //          hidden units; writes bf16 h = silu(gate) * up into C[M, H] and the raw
 //          pre-activation [gate | up] into aux-out (bf16 [M, 2H]) for backward.
@@ -626,6 +685,17 @@ void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long
     return;
   }
   constexpr int BN = 256;
+  if (epi == 4) {
+    // dgu = swiglu'(gu) * (dy @ W_down): A = dy (K-major), B = W_down stored [K, N = H].
+    if (a_mn || !b_mn) throw std::invalid_argument("gemm epilogue 4 needs A K-major and B N-major");
+    make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, BK);
+    if (pair) {
+      launch_pair<false, true, 4>(ta, tb, p, num_sms, stream);
+    } else {
+      launch<BN, false, true, 4>(ta, tb, p, num_sms, stream);
+    }
+    return;
+  }
   if (b_mn) {
     make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, BK);
   } else {

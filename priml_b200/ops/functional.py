@@ -33,6 +33,7 @@ __all__ = [
     "rms_norm",
     "rotary",
     "swiglu",
+    "swiglu_mlp",
     "wgrad",
 ]
 
@@ -235,6 +236,51 @@ class _LinearSwiGLU(torch.autograd.Function):
 
 def linear_swiglu(x: Tensor, weight: Tensor) -> Tensor:
     return _LinearSwiGLU.apply(x, weight)
+
+
+class _SwiGLUMLP(torch.autograd.Function):
+    """``down(silu(x Wg^T) * (x Wu^T))`` as one autograd node: the forward fuses
+    the activation into the up-projection epilogue, the backward fuses the
+    SwiGLU derivative into the epilogue of ``dy @ W_down`` (dh never exists)."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, w_up: Tensor, w_down: Tensor) -> Tensor:  # type: ignore[override]
+        x2 = _as_bf16_2d(x)
+        wu = bf16_shadow(w_up)
+        wd = bf16_shadow(w_down)
+        two_h = wu.shape[0]
+        h = torch.empty(x2.shape[0], two_h // 2, device=x.device, dtype=torch.bfloat16)
+        gu = torch.empty(x2.shape[0], two_h, device=x.device, dtype=torch.bfloat16)
+        native().gemm_swiglu(x2, wu, h, gu)
+        y = gemm(h, wd)
+        ctx.save_for_backward(x2, wu, wd, gu, h)
+        ctx.w_up = w_up if grad_sink(w_up) is not None else None
+        ctx.w_down = w_down if grad_sink(w_down) is not None else None
+        ctx.dtypes = (w_up.dtype, w_down.dtype)
+        ctx.x_shape = x.shape
+        ctx.x_dtype = x.dtype
+        return y.view(*x.shape[:-1], wd.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        x2, wu, wd, gu, h = ctx.saved_tensors
+        dy2 = _as_bf16_2d(dy)
+        dgu = torch.empty_like(gu)
+        native().gemm_swiglu_bwd(dy2, wd, gu, dgu)
+        dx = dwu = dwd = None
+        if ctx.needs_input_grad[2]:
+            dwd = wgrad(ctx.w_down if ctx.w_down is not None else wd, dy2, h, ctx.dtypes[1])
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dgu, wu, b_mn=True).view(ctx.x_shape)
+            if ctx.x_dtype != torch.bfloat16:
+                dx = dx.to(ctx.x_dtype)
+        if ctx.needs_input_grad[1]:
+            dwu = wgrad(ctx.w_up if ctx.w_up is not None else wu, dgu, x2, ctx.dtypes[0])
+        return dx, dwu, dwd
+
+
+def swiglu_mlp(x: Tensor, w_up: Tensor, w_down: Tensor) -> Tensor:
+    return _SwiGLUMLP.apply(x, w_up, w_down)
 
 
 # --------------------------------------------------------------------------- elementwise

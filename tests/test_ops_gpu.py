@@ -184,3 +184,27 @@ def test_adamw_plan_matches_reference() -> None:
     ref = torch.sqrt(sum((g.float() ** 2).sum() for g in gs))
     assert abs(float(norm) - float(ref)) / float(ref) < 1e-4
     assert abs(float(clip) - min(1.0, 1.0 / (float(ref) + 1e-6))) < 1e-6
+
+
+@pytest.mark.parametrize("m,c,h", [(256, 256, 512), (300, 384, 264), (1024, 512, 1024)])
+def test_swiglu_mlp_fused_fwd_bwd(m: int, c: int, h: int) -> None:
+    """Up-projection + SwiGLU + down-projection with both epilogue fusions vs fp32 autograd."""
+    from priml_b200.ops import functional as fn
+
+    torch.manual_seed(0)
+    x = torch.randn(m, c, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    wu = (torch.randn(2 * h, c, device="cuda") / math.sqrt(c)).requires_grad_()
+    wd = (torch.randn(c, h, device="cuda") / math.sqrt(h)).requires_grad_()
+    y = fn.swiglu_mlp(x, wu, wd)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_()
+    wur = wu.detach().clone().requires_grad_()
+    wdr = wd.detach().clone().requires_grad_()
+    g, u = (xr @ wur.t()).chunk(2, dim=-1)
+    yr = (F.silu(g) * u) @ wdr.t()
+    yr.backward(dy.float())
+    assert _rel_err(y, yr) < 2e-2
+    assert _rel_err(x.grad, xr.grad) < 3e-2
+    assert _rel_err(wu.grad, wur.grad) < 3e-2
+    assert _rel_err(wd.grad, wdr.grad) < 3e-2
