@@ -245,14 +245,14 @@ def main() -> None:
         h2d = sum(t.numel() * t.element_size() for t in host_batches[0].values())
         for i in range(args.warmup):
             out = step.train_step(**step.preprocess_batch(host_batches[i]))
-            float(out["loss"])
+            float(step.last_loss)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         t0 = time.perf_counter()
         for i in range(args.steps):
             out = step.train_step(**step.preprocess_batch(host_batches[args.warmup + i]))
-            float(out["loss"])  # device -> host read of the step's loss
+            float(step.last_loss)  # device -> host read of the step's loss
         torch.cuda.synchronize()
         el = time.perf_counter() - t0
         if world > 1:

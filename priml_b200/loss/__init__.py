@@ -118,20 +118,24 @@ class DiffusionLoss:
 
 
 class AdversarialLoss:
-    """Non-saturating GAN loss on logits: generator ``softplus(-d)``, discriminator
-    ``softplus(-d_real) + softplus(d_fake)``."""
+    """Generator loss of a GAN step (``priml/loss/gan.py:19-90``), per sample:
+    ``adversarial_weight * BCE(D(G(z)), 1) + content_weight * mean |G(z) - real|``."""
 
     class Config(Fig["AdversarialLoss"]):
-        role: str = "generator"
+        adversarial_weight: float = 1.0
+        content_weight: float = 100.0
 
     def __init__(self, config: Config) -> None:
-        self.role = config.role
+        self.adversarial_weight = config.adversarial_weight
+        self.content_weight = config.content_weight
 
-    def __call__(self, prediction: Tensor, **batch: Any) -> LossOutput:
-        if self.role == "generator":
-            return {"loss": F.softplus(-prediction.float())}
-        fake = batch["fake_logits"].float()
-        return {"loss": F.softplus(-prediction.float()) + F.softplus(fake)}
+    def __call__(self, model_output: Tensor, *, fake_logits: Tensor, fake_media: Tensor, real_media: Tensor,
+                 **batch: Any) -> LossOutput:  # fmt: skip
+        del model_output, batch
+        # BCE against "real" labels on logits is softplus(-logit)
+        adversarial = F.softplus(-fake_logits.float()).flatten(1).mean(1)
+        content = (fake_media.float() - real_media.float()).abs().flatten(1).mean(1)
+        return {"loss": self.adversarial_weight * adversarial + self.content_weight * content}
 
 
 def categorical_entropy(logits: Tensor, dim: int = -1) -> Tensor:

@@ -175,8 +175,8 @@ class TrainLoop:
         return hit
 
     def _log(self, out: dict[str, Any], dt: float) -> None:
-        keys = sorted(k for k, v in out.items() if isinstance(v, torch.Tensor))
-        vals = torch.stack([out[k].float().reshape(()) for k in keys])
+        keys = sorted(k for k, v in out.items() if isinstance(v, torch.Tensor) and k != "model" and v.is_floating_point())
+        vals = torch.stack([out[k].detach().float().mean() for k in keys])
         if _dist():
             dist.all_reduce(vals)
             vals = vals / dist.get_world_size()
@@ -203,7 +203,7 @@ class TrainLoop:
             m.reset()
         for i, batch in enumerate(self.dataset.eval_dataloader()):
             batch = self.step.preprocess_batch(batch)
-            out = self.step.call_eval(**batch)
+            out = self.step.eval_loss(**batch)
             if i < self.config.eval_warmup_batches:
                 continue
             v = out["loss"].float().mean()

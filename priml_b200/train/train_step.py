@@ -218,14 +218,49 @@ class TrainStep:
         with self._autocast():
             return self.loss_fn(out, **batch)
 
-    @torch.no_grad()
-    def call_eval(self, **batch: Any) -> dict[str, Tensor]:
-        with self.timer_eval:
+    def _forward(self, batch: dict[str, Any]) -> Any:
+        if "media" in batch:
+            return self.model(batch["media"])
+        if "tokens" in batch:
+            return self.model(batch["tokens"])
+        return self.model(**batch)
+
+    def call_eval(self, *args: Any, **batch: Any) -> Any:
+        """Model output in eval mode under ``inference_mode``, autocast and the EMA
+        weights (``ema.apply_to``); the previous train/eval mode is restored."""
+        was_training = self.model.training
+        self.model.eval()
+        try:
+            with self.timer_eval, torch.inference_mode(), self.ema.apply_to(self.model), self._autocast():
+                return self.model(*args, **batch) if args else self._forward(batch)
+        finally:
+            self.model.train(was_training)
+
+    def _loss_from(self, output: Any, batch: dict[str, Any]) -> dict[str, Any]:
+        with self._autocast():
+            result = dict(self.loss_fn(output, **batch))
+        result["model"] = output
+        return result
+
+    def train_loss(self, **batch: Any) -> TrainStepOutput:
+        """Loss in train mode, without backprop."""
+        with torch.no_grad():
+            if isinstance(self.loss_fn, TokenCrossEntropy) and hasattr(self.model, "token_loss"):
+                self.model.train()
+                return TrainStepOutput(self.compute_loss(**batch))
+            return TrainStepOutput(self._loss_from(self(**batch), batch))
+
+    def eval_loss(self, **batch: Any) -> TrainStepOutput:
+        """Loss in eval mode with the EMA weights (the evaluation path of the train loop)."""
+        if isinstance(self.loss_fn, TokenCrossEntropy) and hasattr(self.model, "token_loss"):
+            was_training = self.model.training
             self.model.eval()
             try:
-                return self.compute_loss(**batch)
+                with self.timer_eval, torch.inference_mode(), self.ema.apply_to(self.model), self._autocast():
+                    return TrainStepOutput(self.loss_fn.fused(self.model, **batch))
             finally:
-                self.model.train()
+                self.model.train(was_training)
+        return TrainStepOutput(self._loss_from(self.call_eval(**batch), batch))
 
     # ------------------------------------------------------------------ update
     def _clip(self) -> Tensor | None:
@@ -277,11 +312,12 @@ class TrainStep:
             self.accumulation_steps = 0
             self.accumulated_samples = 0
             stepped = True
-        self.last_loss = (loss.detach().float().mean())
-        out = TrainStepOutput(loss=self.last_loss, num_samples=n, stepped=stepped)
-        for k, v in losses.items():
-            if k != "loss":
-                out[k] = v.detach().float().mean()
+        self.last_loss = loss.detach().float().mean()
+        # Like the reference: the unreduced loss (and every other loss term) is returned;
+        # ``last_loss`` holds the scalar mean for logging.
+        out = TrainStepOutput({k: (v.detach() if isinstance(v, Tensor) else v) for k, v in losses.items()})
+        out["num_samples"] = n
+        out["stepped"] = stepped
         return out
 
     def on_epoch_end(self) -> None:

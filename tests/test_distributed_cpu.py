@@ -38,7 +38,7 @@ def _fsdp_losses(rank: int, world: int, steps: int) -> list[float]:
     for seq in _batches(steps, world):
         local = seq.chunk(world)[rank]
         out = step.train_step(tokens=local[:, :-1], targets=local[:, 1:])
-        t = out["loss"].detach().clone()
+        t = out["loss"].detach().float().mean()
         torch.distributed.all_reduce(t)
         losses.append(float(t) / world)
     return losses
@@ -50,7 +50,7 @@ def _single_losses(steps: int, world: int) -> list[float]:
     losses = []
     for seq in _batches(steps, world):
         out = step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
-        losses.append(float(out["loss"]))
+        losses.append(float(out["loss"].float().mean()))
     return losses
 
 
@@ -71,7 +71,7 @@ def _ddp_grads(rank: int, world: int) -> float:
     step = _tiny_step_cfg(DataParallel.Config(device="cpu")).make()
     seq = _batches(1, world)[0].chunk(world)[rank]
     out = step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
-    return float(out["loss"])
+    return float(out["loss"].float().mean())
 
 
 def test_ddp_world2_runs() -> None:

@@ -87,7 +87,7 @@ def _losses(parallelism, world: int = 1, rank: int = 0, steps: int = 4) -> list[
         seq = torch.randint(0, 1024, (4, 257), device="cuda", generator=g)
         local = seq.chunk(world)[rank]
         o = step.train_step(tokens=local[:, :-1], targets=local[:, 1:])
-        t = o["loss"].detach().clone()
+        t = o["loss"].detach().float().mean()
         if world > 1:
             torch.distributed.all_reduce(t)
         out.append(float(t) / world)
