@@ -119,3 +119,4 @@ class SyntheticTokens:
     def load_state_dict(self, s: dict[str, Any]) -> None:
         self._step = int(s.get("step", 0))
         self.timer_epoch.load_state_dict(s.get("timer_epoch", {}))
+from priml_b200.data import augmentation_gpu, environment  # noqa: E402, F401

@@ -484,6 +484,32 @@ class PeerGroup {
 };
 
 Tensor status_tensor_py() { return status_tensor(); }
+// images [B, C, H, W] (fp32 / bf16 / uint8, contiguous) -> [B, C, crop, crop].
+Tensor augment_pad_crop_flip_cutout(const Tensor& images, int64_t crop, int64_t pad, int64_t mode, double fill,
+                                    const Tensor& dy, const Tensor& dx, c10::optional<Tensor> flip, const Tensor& cy,
+                                    const Tensor& cx, int64_t cut) {
+  check_cuda(images, "images");
+  PB_CHECK(images.dim() == 4 && images.is_contiguous(), "images must be contiguous [B, C, H, W]");
+  const int B = images.size(0), C = images.size(1), H = images.size(2), W = images.size(3);
+  int dtype = -1;
+  if (images.scalar_type() == torch::kFloat32) dtype = 0;
+  if (images.scalar_type() == torch::kBFloat16) dtype = 1;
+  if (images.scalar_type() == torch::kUInt8) dtype = 2;
+  PB_CHECK(dtype >= 0, "images must be fp32, bf16 or uint8");
+  for (const Tensor* t : {&dy, &dx, &cy, &cx})
+    PB_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->numel() == B, "offsets must be int32 [B]");
+  if (flip.has_value()) PB_CHECK(flip->scalar_type() == torch::kUInt8 && flip->numel() == B, "flip must be uint8 [B]");
+  PB_CHECK(crop <= H + 2 * pad && crop <= W + 2 * pad, "crop larger than the padded image");
+  const c10::cuda::CUDAGuard guard(images.device());
+  auto out = torch::empty({B, C, crop, crop}, images.options());
+  pb::pad_crop_flip_cutout(images.data_ptr(), out.data_ptr(), dtype, B, C, H, W, static_cast<int>(crop),
+                           static_cast<int>(pad), static_cast<int>(mode), static_cast<float>(fill),
+                           dy.data_ptr<int32_t>(), dx.data_ptr<int32_t>(),
+                           flip.has_value() ? flip->data_ptr<uint8_t>() : nullptr, cy.data_ptr<int32_t>(),
+                           cx.data_ptr<int32_t>(), static_cast<int>(cut), stream());
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -516,6 +542,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("adamw_scatter", &PeerGroup::adamw_scatter)
       .def("barrier", &PeerGroup::barrier);
   m.def("status_tensor", &status_tensor_py);
+  m.def("augment_pad_crop_flip_cutout", &augment_pad_crop_flip_cutout, "fused pad + random crop + flip + cutout");
   py::class_<MultiTensorPlan>(m, "MultiTensorPlan")
       .def(py::init<std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>,
                     std::vector<c10::optional<Tensor>>, int64_t>())

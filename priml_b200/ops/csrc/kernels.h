@@ -144,4 +144,10 @@ void adamw_scatter(const PeerTable& t, int world, const ShardSegment* segs, int 
 void peer_barrier(const unsigned long long* done, unsigned long long target, long long timeout_ns, int* status,
                   cudaStream_t stream);
 
+// ---------------------------------------------------------------- augmentation
+// dtype: 0 fp32, 1 bf16, 2 uint8; mode: 0 constant, 1 replicate, 2 reflect. flip may be null.
+void pad_crop_flip_cutout(const void* in, void* out, int dtype, int B, int C, int H, int W, int crop, int pad,
+                          int mode, float fill, const int32_t* dy, const int32_t* dx, const uint8_t* flip,
+                          const int32_t* cy, const int32_t* cx, int cut, cudaStream_t stream);
+
 }  // namespace pb

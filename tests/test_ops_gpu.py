@@ -208,3 +208,17 @@ def test_swiglu_mlp_fused_fwd_bwd(m: int, c: int, h: int) -> None:
     assert _rel_err(x.grad, xr.grad) < 3e-2
     assert _rel_err(wu.grad, wur.grad) < 3e-2
     assert _rel_err(wd.grad, wdr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("mode", ["reflect", "replicate", "constant"])
+def test_fused_augmentation_matches_torch_path(dtype: torch.dtype, mode: str) -> None:
+    from priml_b200.data.augmentation_gpu import draw, pad_crop_flip
+
+    torch.manual_seed(0)
+    img = torch.randn(16, 3, 32, 32, device="cuda").to(dtype)
+    d = draw(16, 32, 32, 4, None, img.device)
+    fused = pad_crop_flip(img, 32, pad=4, pad_mode=mode, cutout_size=8, draws=d)
+    ref = pad_crop_flip(img.cpu().float(), 32, pad=4, pad_mode=mode, cutout_size=8,
+                        draws=type(d)(*(t.cpu() if t is not None else None for t in d)))  # fmt: skip
+    assert torch.equal(fused.float().cpu(), ref.to(dtype).float())

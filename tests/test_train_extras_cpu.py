@@ -101,3 +101,25 @@ def test_protocols_progress_and_results(tmp_path) -> None:  # noqa: ANN001
     assert format_summary(read_metrics(m), ["eval/loss"]) == "loss=2.0"
     assert summarize(["--path", str(m)]) == 0
     assert summarize(["--path", str(tmp_path / "missing.json")]) == 1
+
+
+def test_augmentation_torch_path() -> None:
+    from priml_b200.data.augmentation_gpu import AugmentDraws, cutout, flip_lr, pad_crop_flip, random_crop
+
+    torch.manual_seed(0)
+    img = torch.arange(2 * 3 * 6 * 6, dtype=torch.float32).reshape(2, 3, 6, 6)
+    z = torch.zeros(2, dtype=torch.int32)
+    ident = AugmentDraws(z + 2, z + 2, None, z, z)
+    assert torch.equal(pad_crop_flip(img, 6, pad=2, draws=ident), img)
+    flipped = AugmentDraws(z + 2, z + 2, torch.ones(2, dtype=torch.uint8), z, z)
+    assert torch.equal(pad_crop_flip(img, 6, pad=2, draws=flipped), img.flip(-1))
+    shifted = AugmentDraws(z, z, None, z, z)
+    out = pad_crop_flip(img, 6, pad=2, pad_mode="constant", draws=shifted)
+    assert torch.equal(out[..., 2:, 2:], img[..., :4, :4]) and float(out[..., :2, :].abs().sum()) == 0.0
+    cut = AugmentDraws(z + 2, z + 2, None, z + 1, z + 2)
+    c = pad_crop_flip(img, 6, pad=2, cutout_size=3, draws=cut)
+    assert float(c[:, :, 1:4, 2:5].abs().sum()) == 0.0 and torch.equal(c[:, :, 0], img[:, :, 0])
+    rnd = pad_crop_flip(torch.rand(8, 3, 32, 32), 32, pad=4, cutout_size=8)
+    assert rnd.shape == (8, 3, 32, 32) and rnd.is_contiguous()
+    assert random_crop(torch.rand(4, 3, 10, 10), 8).shape == (4, 3, 8, 8)
+    assert flip_lr(img).shape == img.shape and cutout(img, 2).shape == img.shape
