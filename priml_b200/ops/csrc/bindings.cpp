@@ -484,6 +484,147 @@ class PeerGroup {
 };
 
 Tensor status_tensor_py() { return status_tensor(); }
+// Tensor-parallel group of the fused all-gather GEMM / GEMM reduce-scatter (tp_gemm.cu):
+// IPC-mapped A-shard buffer, receive slots and signal words of every rank, plus the
+// host-side epochs and counter targets of the two operations.
+class TpGroup {
+ public:
+  TpGroup(int64_t rank, int64_t world, int64_t shard_elems, int64_t slot_elems, int64_t max_chunks, double timeout_s)
+      : rank_(rank), world_(world), timeout_ns_(static_cast<long long>(timeout_s * 1e9)),
+        device_(at::cuda::current_device()) {
+    PB_CHECK(world >= 1 && world <= pb::kMaxRanks, "world size must be 1..8");
+    local_ = std::make_shared<Local>();
+    local_->shard = pb::sym_alloc(std::max<int64_t>(shard_elems, 8) * 2);
+    local_->slots = pb::sym_alloc(std::max<int64_t>(slot_elems, 8) * 2);
+    local_->signal = pb::sym_alloc(pb::kSigWords * 8);
+    auto opts = torch::TensorOptions().device(torch::kCUDA, device_);
+    auto keep = local_;
+    shard_ = torch::from_blob(local_->shard, {shard_elems}, [keep](void*) {}, opts.dtype(torch::kBFloat16));
+    flags_ = torch::zeros({2 * std::max<int64_t>(max_chunks, 1)}, opts.dtype(torch::kInt32));
+    std::memset(&base_, 0, sizeof(base_));
+    slot_bytes_ = std::max<int64_t>(slot_elems, 8) * 2;
+  }
+  ~TpGroup() {
+    for (void* p : opened_) pb::ipc_close(p);
+  }
+  py::bytes handles() const {
+    char buf[192];
+    pb::ipc_handle(local_->shard, buf);
+    pb::ipc_handle(local_->slots, buf + 64);
+    pb::ipc_handle(local_->signal, buf + 128);
+    return py::bytes(buf, 192);
+  }
+  void open(const std::vector<std::string>& all) {
+    PB_CHECK(static_cast<int64_t>(all.size()) == world_, "need one handle record per rank");
+    const c10::cuda::CUDAGuard guard(device_);
+    for (int64_t r = 0; r < world_; ++r) {
+      if (r == rank_) {
+        base_.peer_a[r] = reinterpret_cast<unsigned long long>(local_->shard);
+        base_.slots[r] = reinterpret_cast<unsigned long long>(local_->slots);
+        base_.signal[r] = reinterpret_cast<unsigned long long>(local_->signal);
+        continue;
+      }
+      void* a = pb::ipc_open(all[r].data());
+      void* sl = pb::ipc_open(all[r].data() + 64);
+      void* sg = pb::ipc_open(all[r].data() + 128);
+      opened_.insert(opened_.end(), {a, sl, sg});
+      base_.peer_a[r] = reinterpret_cast<unsigned long long>(a);
+      base_.slots[r] = reinterpret_cast<unsigned long long>(sl);
+      base_.signal[r] = reinterpret_cast<unsigned long long>(sg);
+    }
+    opened_ok_ = true;
+  }
+  Tensor shard() const { return shard_; }
+
+  // Wait (on the stream) until every peer has finished reading this rank's previous shard.
+  void wait_shard_free() {
+    PB_CHECK(opened_ok_, "open() first");
+    if (ag_target_ == 0) return;
+    pb::tp_wait(local_->signal, pb::kTpSigAgDone, ag_target_, timeout_ns_, status_ptr(), stream());
+  }
+
+  // C [world*m_shard, N] = AllGather(shard[:m_shard*K]) @ B^T ; B [N, K] (b_mn: [K, N]); a_full [world*m_shard, K].
+  void ag_gemm(const Tensor& B, bool b_mn, int64_t m_shard, int64_t K, Tensor& C, Tensor& a_full) {
+    PB_CHECK(opened_ok_, "open() first");
+    const int64_t N = b_mn ? B.size(1) : B.size(0);
+    PB_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "B has the wrong K");
+    PB_CHECK(m_shard % 128 == 0 && m_shard * K <= shard_.numel(), "m_shard must be a multiple of 128 and fit the shard buffer");
+    PB_CHECK(C.is_contiguous() && C.size(0) == m_shard * world_ && C.size(1) == N && C.scalar_type() == torch::kBFloat16, "C");
+    PB_CHECK(a_full.is_contiguous() && a_full.numel() >= m_shard * world_ * K && a_full.scalar_type() == torch::kBFloat16, "a_full");
+    const int64_t chunks = (world_ - 1) * (m_shard / 128);
+    PB_CHECK(2 * chunks <= flags_.numel(), "too many chunks for the flag buffer");
+    pb::TpGemmParams p = base_;
+    p.N = N;
+    p.K = K;
+    p.m_shard = m_shard;
+    p.rank = rank_;
+    p.world = world_;
+    p.epoch = ++ag_epoch_;
+    p.timeout_ns = timeout_ns_;
+    p.status = status_ptr();
+    p.C = C.data_ptr();
+    p.ldc = N;
+    p.a_full = a_full.data_ptr();
+    p.chunk_flags = reinterpret_cast<unsigned int*>(flags_.data_ptr<int32_t>());
+    const int grid = pb::tp_gemm_grid(m_shard * world_, N);
+    pb::tp_ag_gemm(p, local_->shard, B.data_ptr(), row_stride(B), b_mn, grid, stream());
+    ag_target_ += static_cast<unsigned long long>((world_ - 1) * grid * 2);
+  }
+
+  // out [m_shard, N] = rows of this rank of sum_ranks(A @ B^T); A [world*m_shard, K]; B [N, K] (b_mn: [K, N]).
+  void gemm_rs(const Tensor& A, const Tensor& B, bool b_mn, Tensor& out) {
+    PB_CHECK(opened_ok_, "open() first");
+    const int64_t M = A.size(0), K = A.size(1);
+    const int64_t N = b_mn ? B.size(1) : B.size(0);
+    PB_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "B has the wrong K");
+    PB_CHECK(M % (128 * world_) == 0, "rows must be a multiple of 128 * world");
+    const int64_t m_shard = M / world_;
+    PB_CHECK(world_ * m_shard * N * 2 <= static_cast<int64_t>(slot_bytes()), "receive slots too small");
+    PB_CHECK(out.is_contiguous() && out.size(0) == m_shard && out.size(1) == N && out.scalar_type() == torch::kBFloat16, "out");
+    pb::TpGemmParams p = base_;
+    p.N = N;
+    p.K = K;
+    p.m_shard = m_shard;
+    p.rank = rank_;
+    p.world = world_;
+    p.epoch = ++rs_epoch_;
+    p.timeout_ns = timeout_ns_;
+    p.status = status_ptr();
+    p.reduce_grid = kReduceGrid;
+    const int grid = pb::tp_gemm_grid(M, N);
+    rs_target_ += static_cast<unsigned long long>(world_ * grid);
+    pb::tp_gemm_rs(p, A.data_ptr(), row_stride(A), B.data_ptr(), row_stride(B), b_mn, out.data_ptr(), N, grid,
+                   kReduceGrid, rs_target_, stream());
+  }
+
+  int64_t slot_bytes() const { return slot_bytes_; }
+  void set_slot_bytes(int64_t b) { slot_bytes_ = b; }
+
+ private:
+  static constexpr int kReduceGrid = 296;
+  struct Local {
+    void* shard = nullptr;
+    void* slots = nullptr;
+    void* signal = nullptr;
+    ~Local() {
+      pb::sym_free(shard);
+      pb::sym_free(slots);
+      pb::sym_free(signal);
+    }
+  };
+  int64_t rank_, world_;
+  long long timeout_ns_;
+  int device_;
+  std::shared_ptr<Local> local_;
+  Tensor shard_, flags_;
+  pb::TpGemmParams base_;
+  std::vector<void*> opened_;
+  bool opened_ok_ = false;
+  long long ag_epoch_ = 0, rs_epoch_ = 0;
+  unsigned long long ag_target_ = 0, rs_target_ = 0;
+  int64_t slot_bytes_ = 0;
+};
+
 // images [B, C, H, W] (fp32 / bf16 / uint8, contiguous) -> [B, C, crop, crop].
 Tensor augment_pad_crop_flip_cutout(const Tensor& images, int64_t crop, int64_t pad, int64_t mode, double fill,
                                     const Tensor& dy, const Tensor& dx, c10::optional<Tensor> flip, const Tensor& cy,
@@ -542,6 +683,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("adamw_scatter", &PeerGroup::adamw_scatter)
       .def("barrier", &PeerGroup::barrier);
   m.def("status_tensor", &status_tensor_py);
+  py::class_<TpGroup>(m, "TpGroup")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, double>(), py::arg("rank"), py::arg("world"),
+           py::arg("shard_elems"), py::arg("slot_elems"), py::arg("max_chunks"), py::arg("timeout_s") = 60.0)
+      .def("handles", &TpGroup::handles)
+      .def("open", &TpGroup::open)
+      .def("shard", &TpGroup::shard)
+      .def("wait_shard_free", &TpGroup::wait_shard_free)
+      .def("ag_gemm", &TpGroup::ag_gemm)
+      .def("gemm_rs", &TpGroup::gemm_rs)
+      .def("set_slot_bytes", &TpGroup::set_slot_bytes);
   m.def("augment_pad_crop_flip_cutout", &augment_pad_crop_flip_cutout, "fused pad + random crop + flip + cutout");
   py::class_<MultiTensorPlan>(m, "MultiTensorPlan")
       .def(py::init<std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>,

@@ -150,4 +150,34 @@ void pad_crop_flip_cutout(const void* in, void* out, int dtype, int B, int C, in
                           int mode, float fill, const int32_t* dy, const int32_t* dx, const uint8_t* flip,
                           const int32_t* cy, const int32_t* cx, int cut, cudaStream_t stream);
 
+// ---------------------------------------------------------------- tensor-parallel GEMMs (tp_gemm.cu)
+// Signal-array words (same IPC-mapped signal layout as the data-parallel group).
+constexpr int kTpSigAgDone = kSigDone + 1;  // peers finished reading this rank's A shard
+constexpr int kTpSigRsDone = kSigDone + 2;  // peers finished storing partials into this rank's slots
+constexpr int kTpSigRsFree = kSigDone + 3;  // owners finished reducing (slots reusable)
+constexpr int kTpSigAgReady = kSigDone + 4;  // [src rank]: epoch whose A shard the source has written
+
+struct TpGemmParams {
+  int N, K, m_shard, rank, world;
+  long long epoch;       // 1, 2, ... per call of the same kind
+  long long timeout_ns;
+  int* status;
+  void* C;               // all-gather GEMM output [world * m_shard, N]
+  long long ldc;
+  void* a_full;          // local gather buffer [world * m_shard, K]
+  unsigned int* chunk_flags;  // [2 * (world - 1) * m_shard / 128]: epoch of each chunk's two copy halves
+  int reduce_grid;
+  unsigned long long peer_a[kMaxRanks];  // every rank's A shard buffer
+  unsigned long long slots[kMaxRanks];   // every rank's receive slots [world, m_shard, N]
+  unsigned long long signal[kMaxRanks];
+};
+
+int tp_gemm_grid(int M, int N);
+void tp_ag_gemm(const TpGemmParams& p, const void* a_shard, const void* B, long long ldb, bool b_mn, int grid,
+                cudaStream_t stream);
+void tp_gemm_rs(const TpGemmParams& p, const void* A, long long lda, const void* B, long long ldb, bool b_mn, void* out,
+                long long ldo, int grid, int reduce_grid, unsigned long long done_target, cudaStream_t stream);
+void tp_wait(const void* signal_local, int word, unsigned long long target, long long timeout_ns, int* status,
+             cudaStream_t stream);
+
 }  // namespace pb
