@@ -47,8 +47,9 @@ def _parse() -> argparse.Namespace:
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "single"], default="auto",
-                    help="auto: fused-collective sharding for N>1, single-GPU for N=1")
+    ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "tp", "single"], default="auto",
+                    help="auto: fused-collective sharding for N>1, single-GPU for N=1; "
+                    "tp: sequence-parallel tensor parallelism on the fused NVLink GEMMs")
     ap.add_argument("--out", type=str, default="")
     return ap.parse_args()
 
@@ -140,13 +141,15 @@ def main() -> None:
     from priml_b200.optimizers import FusedAdamW
     from priml_b200.parallel.runtime import MultiProcess, SingleProcess
     from priml_b200.parallel.fused_fsdp import FusedFullySharded
+    from priml_b200.parallel.tp_fused import FusedSequenceParallel
     from priml_b200.parallel.strategies import FullySharded, NoParallel
     from priml_b200.train import TrainStep
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    runtime = (MultiProcess.Config(mesh_topology={"dp": -1}, timeout_s=300.0) if world > 1 else SingleProcess.Config()).make()
+    axis = "tp" if args.strategy == "tp" else "dp"
+    runtime = (MultiProcess.Config(mesh_topology={axis: -1}, timeout_s=300.0) if world > 1 else SingleProcess.Config()).make()
     runtime.initialize()
     rank = dist.get_rank() if world > 1 else 0
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -162,6 +165,7 @@ def main() -> None:
     parallel = {
         "fused": lambda: FusedFullySharded.Config(),
         "fsdp2": lambda: FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True),
+        "tp": lambda: FusedSequenceParallel.Config(),
         "single": lambda: NoParallel.Config(),
     }[strategy]()
     step_cfg = TrainStep.Config(
@@ -291,11 +295,13 @@ def main() -> None:
             "global_batch": args.mbs * world,
             "micro_batch_per_gpu": args.mbs,
             "seq_len": args.seq,
-            "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+            "parallelism": (f"tp{world}-sp" if strategy == "tp" else f"fsdp{world}") if world > 1 else "single-gpu",
             "strategy": {
                 "fused": "sharded fp32 master + Adam state, resident bf16 weights; reduce-scatter, clip, AdamW and "
                 "weight all-gather in hand-written NVLink peer-memory kernels",
                 "fsdp2": "torch FSDP2 fully_shard over NCCL (bf16 params, fp32 reduce)",
+                "tp": "sequence-parallel tensor parallelism: all-gather GEMM and GEMM reduce-scatter fused over "
+                "NVLink peer memory; replicated grads averaged once per step",
                 "single": "one GPU, fused AdamW",
             }[strategy],
             "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",

@@ -101,7 +101,7 @@ class SwiGLU(nn.Module):
         else:
             w = self.up_proj.weight
             fusable = self.norm is None and self.act is nn.functional.silu and self.up_proj.bias is None
-            if fusable and not isinstance(w, _DTensorType()) and ops.use_native(x):
+            if fusable and type(self.up_proj) is Linear and not isinstance(w, _DTensorType()) and ops.use_native(x):
                 down = self.down_proj
                 wd = getattr(down, "weight", None)
                 if type(down) is Linear and getattr(down, "bias", None) is None and not isinstance(wd, _DTensorType()):

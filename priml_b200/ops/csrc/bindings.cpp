@@ -500,7 +500,7 @@ class TpGroup {
     auto opts = torch::TensorOptions().device(torch::kCUDA, device_);
     auto keep = local_;
     shard_ = torch::from_blob(local_->shard, {shard_elems}, [keep](void*) {}, opts.dtype(torch::kBFloat16));
-    flags_ = torch::zeros({2 * std::max<int64_t>(max_chunks, 1)}, opts.dtype(torch::kInt32));
+    flags_ = torch::zeros({std::max<int64_t>(max_chunks, 1)}, opts.dtype(torch::kInt32));
     std::memset(&base_, 0, sizeof(base_));
     slot_bytes_ = std::max<int64_t>(slot_elems, 8) * 2;
   }
@@ -552,7 +552,7 @@ class TpGroup {
     PB_CHECK(C.is_contiguous() && C.size(0) == m_shard * world_ && C.size(1) == N && C.scalar_type() == torch::kBFloat16, "C");
     PB_CHECK(a_full.is_contiguous() && a_full.numel() >= m_shard * world_ * K && a_full.scalar_type() == torch::kBFloat16, "a_full");
     const int64_t chunks = (world_ - 1) * (m_shard / 128);
-    PB_CHECK(2 * chunks <= flags_.numel(), "too many chunks for the flag buffer");
+    PB_CHECK(chunks <= flags_.numel(), "too many chunks for the flag buffer");
     pb::TpGemmParams p = base_;
     p.N = N;
     p.K = K;

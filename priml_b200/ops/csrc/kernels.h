@@ -165,7 +165,7 @@ struct TpGemmParams {
   void* C;               // all-gather GEMM output [world * m_shard, N]
   long long ldc;
   void* a_full;          // local gather buffer [world * m_shard, K]
-  unsigned int* chunk_flags;  // [2 * (world - 1) * m_shard / 128]: epoch of each chunk's two copy halves
+  unsigned int* chunk_flags;  // [(world - 1) * m_shard / 128]: pieces copied per chunk (zeroed before each launch)
   int reduce_grid;
   unsigned long long peer_a[kMaxRanks];  // every rank's A shard buffer
   unsigned long long slots[kMaxRanks];   // every rank's receive slots [world, m_shard, N]

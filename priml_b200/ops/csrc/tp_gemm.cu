@@ -3,20 +3,24 @@
 //
 //   tp_ag_gemm   C[M, N] = AllGather_rows(A_shard) @ B^T
 //     One cooperative launch (every CTA resident). Besides the TMA producer,
-//     the MMA issuer and four epilogue warps, each CTA runs two copy warps that
-//     pull 128-row chunks of the peers' A shards over NVLink (16-byte peer
-//     loads) into a local gather buffer and publish a per-chunk flag. Tiles
-//     are visited own shard first, then the peers' shards in copy order; the
-//     producer loads a peer tile only after its chunk flag is set (bounded
-//     wait), so the copy overlaps the GEMM tile by tile. When a CTA's copy
-//     warps are done they bump a counter on every source rank: a rank may
-//     overwrite its shard buffer once all peers have finished reading it.
+//     the MMA issuer and four epilogue warps, each CTA runs two copy warps.
+//     The peers' shards are cut into 16-row pieces (contiguous bytes); the
+//     copy warps of all CTAs pull them over NVLink (16-byte peer loads, 16 in
+//     flight per lane) into a local gather buffer in consumption order and
+//     count each finished piece on its 128-row chunk (then copy this rank's
+//     own rows, so the gathered buffer is complete for the weight gradient). Tiles are visited own
+//     shard first, then the peers' shards in copy order; the producer loads
+//     a peer tile only once its chunk is complete (bounded wait), so the copy
+//     overlaps the GEMM tile by tile. A rank announces its shard on every
+//     peer at kernel start, and the copy warps finish by counting themselves
+//     on every source rank, which may then overwrite its shard buffer.
 //   tp_gemm_rs   C_shard = ReduceScatter_rows(A @ B^T)
-//     The epilogue stores each bf16 partial row straight into the owner
-//     rank's receive slot for this rank (16-byte peer stores) and each CTA
-//     then bumps a completion counter on every rank; tp_rs_reduce waits for
-//     all ranks' stores and sums the slots in rank order (fp32), then frees
-//     the slots for the next call with a counter on every peer.
+//     The epilogue stages each 64-column slice of its partial rows in shared
+//     memory and every lane bulk-stores its row (128 contiguous bytes) into
+//     the owner rank's receive slot for this rank over NVLink; each CTA then
+//     counts itself on every rank. tp_rs_reduce waits for all ranks' stores
+//     and sums the slots in rank order (fp32), then frees the slots for the
+//     next call with a counter on every peer.
 // B is K-major ([N, K]) or N-major ([K, N]); A is K-major. Every cross-rank
 // wait is bounded by globaltimer and reports kTimeoutPeer.
 #include <cuda_runtime.h>
@@ -33,13 +37,15 @@ namespace {
 
 constexpr int TBM = 128, TBN = 256, TBK = 64, TSTAGES = 4;
 constexpr int kTpABytes = TBM * TBK * 2, kTpBBytes = TBN * TBK * 2, kTpStage = kTpABytes + kTpBBytes;
-constexpr int kTpSmem = TSTAGES * kTpStage + 1024 + 256;
+constexpr int kOutCols = 64;                         // columns per staged epilogue slice
+constexpr int kOutPitch = kOutCols * 2 + 16;         // padded row pitch of the staging buffer (bytes)
+constexpr int kOutWarpBytes = 32 * kOutPitch;        // one epilogue warp's 32 rows
+constexpr int kPieceRows = 16;                       // rows per all-gather copy piece
+constexpr int kPiecesPerChunk = TBM / kPieceRows;
+constexpr int kTpSmem = TSTAGES * kTpStage + 1024 + 256 + 4 * kOutWarpBytes;
 
 __device__ __forceinline__ void red_add_release_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_gpu_u32(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -90,6 +96,7 @@ __global__ void __launch_bounds__(MODE == 0 ? 256 : 192, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* stage_out = smem + S * kTpStage + 256;  // [4 warps][32 rows][kOutPitch]
 
   const int warp = warp_id(), lane = lane_id();
   const int bps = p.m_shard / TBM;               // 128-row blocks per shard
@@ -134,9 +141,8 @@ __global__ void __launch_bounds__(MODE == 0 ? 256 : 192, 1)
       const int mb = real_mblock(vm, bps, p.rank, p.world);
       const bool own = MODE == 1 || vm < bps;
       if (MODE == 0 && !own) {
-        const unsigned int* flag = p.chunk_flags + 2 * (vm - bps);  // one epoch flag per copy warp
-        const unsigned int target = static_cast<unsigned int>(p.epoch);
-        if (!bounded_until([&] { return (ld_acquire_gpu_u32(flag) >= target && ld_acquire_gpu_u32(flag + 1) >= target) ||
+        const unsigned int* flag = p.chunk_flags + (vm - bps);  // pieces copied (reset before the launch)
+        if (!bounded_until([&] { return ld_acquire_gpu_u32(flag) >= static_cast<unsigned int>(kPiecesPerChunk) ||
                                         *abort_flag; },
                            p.timeout_ns, p.status) || *abort_flag) {
           *abort_flag = 1;
@@ -245,43 +251,70 @@ __global__ void __launch_bounds__(MODE == 0 ? 256 : 192, 1)
       tc_fence_after();
       const int row = mb * TBM + wq * 32 + lane;  // < M always (M = world * m_shard, m_shard % 128 == 0)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TBN;
-      __nv_bfloat16* dst;
-      if (MODE == 0) {
-        dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
-      } else {
-        const int owner = row / p.m_shard, lr = row - owner * p.m_shard;
-        dst = reinterpret_cast<__nv_bfloat16*>(p.slots[owner]) +
-              (static_cast<long long>(p.rank) * p.m_shard + lr) * p.N;
-      }
+      if constexpr (MODE == 0) {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
-      for (int c = 0; c < TBN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + c, v);
-        tmem_wait_ld();
-        const int col = nb * TBN + c;
-        if (col >= p.N || *abort_flag) continue;
-        uint32_t pk[16];
+        for (int c = 0; c < TBN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c, v);
+          tmem_wait_ld();
+          const int col = nb * TBN + c;
+          if (col >= p.N || *abort_flag) continue;
+          uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        if (col + 32 <= p.N) {
-          uint4* o4 = reinterpret_cast<uint4*>(dst + col);
+          for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          if (col + 32 <= p.N) {
+            uint4* o4 = reinterpret_cast<uint4*>(dst + col);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) o4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        } else {
-          const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(pk);
-          for (int j = 0; j < 32 && col + j < p.N; ++j) dst[col + j] = hb[j];
+            for (int q = 0; q < 4; ++q) o4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          } else {
+            const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(pk);
+            for (int j = 0; j < 32 && col + j < p.N; ++j) dst[col + j] = hb[j];
+          }
+        }
+      } else {
+        // Partial row -> the owner's slot for this rank: stage 64 columns, then one
+        // 128-byte bulk store per lane (each lane only touches its own staged row).
+        const int owner = row / p.m_shard, lr = row - owner * p.m_shard;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.slots[owner]) +
+                             (static_cast<long long>(p.rank) * p.m_shard + lr) * p.N;
+        uint8_t* my_row = stage_out + wq * kOutWarpBytes + lane * kOutPitch;
+#pragma unroll 1
+        for (int c = 0; c < TBN; c += kOutCols) {
+          uint32_t v[64];
+          tmem_ld_32x32b_x32(t_row + c, *reinterpret_cast<uint32_t(*)[32]>(v));
+          tmem_ld_32x32b_x32(t_row + c + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          tmem_wait_ld();
+          const int col = nb * TBN + c;
+          if (col >= p.N || *abort_flag) continue;
+          tma_store_wait_read();  // the previous slice has left the staging row
+          uint4* s4 = reinterpret_cast<uint4*>(my_row);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            s4[q] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * q]), __uint_as_float(v[8 * q + 1])),
+                               pack_bf16x2(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
+                               pack_bf16x2(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
+                               pack_bf16x2(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+          fence_proxy_async_smem();
+          bulk_store(dst + col, my_row, static_cast<uint32_t>(min(kOutCols, p.N - col)) * 2u);  // N % 8 == 0
+          tma_store_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
     }
-    if (MODE == 1) __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    if (MODE == 1) {
+      // this thread's bulk stores are complete, then ordered before the CTA counts itself done
+      tma_store_wait_all();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __threadfence_system();
+    }
   } else if (MODE == 0 && warp >= 6) {
     // ------------------------------------------------------------ copy warps (all-gather)
-    const int cw = warp - 6;  // 0 or 1: alternate rows of each chunk
-    const int chunks = (p.world - 1) * bps;
-    const long long row_u4 = static_cast<long long>(p.K) / 8;  // 16-byte words per row
+    const int cw = warp - 6;
+    const int pieces = (p.world - 1) * bps * kPiecesPerChunk;  // in consumption order: chunk j, piece q
+    const long long piece_u4 = static_cast<long long>(kPieceRows) * p.K / 8;  // 16-byte words per piece
     if (blockIdx.x == 0 && cw == 0 && lane == 0) {
       // This rank's shard for this epoch is in place (stream order): tell every peer.
       __threadfence_system();
@@ -290,47 +323,45 @@ __global__ void __launch_bounds__(MODE == 0 ? 256 : 192, 1)
                            static_cast<unsigned long long>(p.epoch));
     }
     const unsigned long long* ready = reinterpret_cast<const unsigned long long*>(p.signal[p.rank]) + kTpSigAgReady;
-    bool copy_ok = true;
-    for (int j = blockIdx.x; j < chunks && copy_ok; j += gridDim.x) {
-      const int vm = bps + j;
-      const int mb = real_mblock(vm, bps, p.rank, p.world);
+    int ready_rank = p.rank;  // the source whose announcement this warp has already seen (own shard: in place)
+    // Pieces [0, pieces) come from the peers and gate GEMM tiles; the last bps * kPiecesPerChunk
+    // fill in this rank's own rows of the gathered output (read by the caller, not by the GEMM).
+    const int total = pieces + bps * kPiecesPerChunk;
+    for (int w = cw * gridDim.x + blockIdx.x; w < total; w += 2 * gridDim.x) {
+      const bool own = w >= pieces;
+      const int j = own ? -1 : w / kPiecesPerChunk;
+      const int piece = own ? (w - pieces) % kPiecesPerChunk : w - j * kPiecesPerChunk;
+      const int mb = own ? p.rank * bps + (w - pieces) / kPiecesPerChunk : real_mblock(bps + j, bps, p.rank, p.world);
       const int src_rank = mb / bps;
-      if (lane == 0)
-        copy_ok = bounded_until([&] { return ld_acquire_sys_u64(ready + src_rank) >= static_cast<unsigned long long>(p.epoch) ||
-                                             *abort_flag; },
-                                p.timeout_ns, p.status) && !*abort_flag;
-      copy_ok = __shfl_sync(0xffffffffu, copy_ok, 0);
-      if (!copy_ok) {
-        *abort_flag = 1;
-        break;
+      if (src_rank != ready_rank) {
+        bool ok = true;
+        if (lane == 0)
+          ok = bounded_until([&] { return ld_acquire_sys_u64(ready + src_rank) >= static_cast<unsigned long long>(p.epoch) ||
+                                          *abort_flag; },
+                             p.timeout_ns, p.status) && !*abort_flag;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          *abort_flag = 1;
+          break;
+        }
+        ready_rank = src_rank;
       }
-      const uint4* src = reinterpret_cast<const uint4*>(p.peer_a[src_rank]) + static_cast<long long>(mb - src_rank * bps) * TBM * row_u4;
-      uint4* dst = reinterpret_cast<uint4*>(p.a_full) + static_cast<long long>(mb) * TBM * row_u4;
-      const long long words = TBM * row_u4;
-      // this warp copies the rows r = cw, cw + 2, ...: word w of row r
-      constexpr int U = 8;
-      for (long long base = 0; base < words / 2; base += 32 * U) {
+      const long long row0 = static_cast<long long>(mb - src_rank * bps) * TBM + piece * kPieceRows;
+      const uint4* src = reinterpret_cast<const uint4*>(p.peer_a[src_rank]) + row0 * (p.K / 8);
+      uint4* dst = reinterpret_cast<uint4*>(p.a_full) + (static_cast<long long>(mb) * TBM + piece * kPieceRows) * (p.K / 8);
+      constexpr int U = 16;
+      for (long long base = lane; base < piece_u4; base += 32 * U) {
         uint4 buf[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const long long idx = base + u * 32 + lane;  // index within this warp's half
-          if (idx < words / 2) {
-            const long long r = 2 * (idx / row_u4) + cw, w = idx % row_u4;
-            buf[u] = __ldcg(src + r * row_u4 + w);
-          }
-        }
+        for (int u = 0; u < U; ++u)
+          if (base + 32 * u < piece_u4) buf[u] = __ldcg(src + base + 32 * u);
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const long long idx = base + u * 32 + lane;
-          if (idx < words / 2) {
-            const long long r = 2 * (idx / row_u4) + cw, w = idx % row_u4;
-            dst[r * row_u4 + w] = buf[u];
-          }
-        }
+        for (int u = 0; u < U; ++u)
+          if (base + 32 * u < piece_u4) dst[base + 32 * u] = buf[u];
       }
+      if (own) continue;
       __threadfence();
       __syncwarp();
-      if (lane == 0) st_release_gpu_u32(p.chunk_flags + 2 * j + cw, static_cast<unsigned int>(p.epoch));
+      if (lane == 0) atomicAdd(p.chunk_flags + j, 1u);
     }
     // Done reading the peers' shards for this epoch: tell every rank.
     __threadfence_system();
@@ -444,6 +475,8 @@ int tp_gemm_grid(int M, int N) {
 void tp_ag_gemm(const TpGemmParams& p, const void* a_shard, const void* B, long long ldb, bool b_mn, int grid,
                 cudaStream_t stream) {
   if (p.m_shard % TBM != 0 || p.K % 8 != 0) throw std::invalid_argument("tp_ag_gemm: m_shard % 128 and K % 8");
+  const int chunks = (p.world - 1) * (p.m_shard / TBM);
+  if (chunks > 0) check(cudaMemsetAsync(p.chunk_flags, 0, sizeof(unsigned int) * chunks, stream), "tp chunk flags reset");
   const long long M = static_cast<long long>(p.m_shard) * p.world;
   CUtensorMap a_own, a_full, tb;
   make_tmap_2d_bf16(&a_own, a_shard, p.K, p.m_shard, p.K, 64, TBM);
