@@ -157,7 +157,8 @@ class GroupedSwiGLUExperts(nn.Module):
                 self.down_proj[e].copy_(tpl.down_proj.weight)
 
     def forward(self, x_sorted: Tensor, offsets: Tensor) -> Tensor:
-        """Rows ``offsets[e]:offsets[e+1]`` of ``x_sorted`` go through expert ``e``."""
+        """Rows ``offsets[e]:offsets[e+1]`` of ``x_sorted`` go through expert ``e`` (on CUDA the
+        segments start on multiples of 128: ``priml_b200.ops.grouped.padded_dispatch_plan``)."""
         return ops.grouped_swiglu_mlp(x_sorted, self.up_proj, self.down_proj, offsets)
 
 
@@ -252,12 +253,8 @@ class MoE(nn.Module):
         return y.reshape(*shape[:-1], self.channels_out)
 
     def _dispatch_grouped(self, xf: Tensor, weights: Tensor, indices: Tensor) -> Tensor:
-        order, tok, offsets = moe_dispatch_plan(indices, self.num_experts)
-        x_sorted = xf.index_select(0, tok)
-        y_sorted = self.experts(x_sorted, offsets)
-        w_sorted = weights.reshape(-1)[order].unsqueeze(-1).to(y_sorted.dtype)
-        y = xf.new_zeros(xf.shape[0], self.channels_out, dtype=y_sorted.dtype)
-        return y.index_add_(0, tok, y_sorted * w_sorted)
+        # padded device-side dispatch -> grouped expert GEMMs -> weighted combine (no host sync)
+        return ops.grouped_swiglu_experts(xf, weights, indices, self.experts.up_proj, self.experts.down_proj)
 
     def _dispatch_loop(self, xf: Tensor, weights: Tensor, indices: Tensor) -> Tensor:
         order, tok, offsets = moe_dispatch_plan(indices, self.num_experts)

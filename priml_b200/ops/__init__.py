@@ -22,6 +22,7 @@ __all__ = [
     "adamw_",
     "attention",
     "cross_entropy",
+    "grouped_swiglu_experts",
     "grouped_swiglu_mlp",
     "linear",
     "linear_cross_entropy",
@@ -158,12 +159,20 @@ def linear_cross_entropy(
 
 
 def grouped_swiglu_mlp(x_sorted: Tensor, up_w: Tensor, down_w: Tensor, offsets: Tensor) -> Tensor:
-    """Grouped SwiGLU experts over expert-sorted rows (device-side offsets)."""
-    if use_native(x_sorted) and _compute_dtype(x_sorted) == torch.bfloat16:
-        from priml_b200.ops import functional
+    """Grouped SwiGLU experts over expert segments ``offsets[e]:offsets[e+1]`` (device-side
+    offsets; on CUDA the segments must start on multiples of 128, as the padded plan lays them out)."""
+    if use_native(x_sorted):
+        from priml_b200.ops import grouped
 
-        return functional.grouped_swiglu_mlp(x_sorted, up_w, down_w, offsets)
+        return grouped.grouped_swiglu_mlp(x_sorted, up_w, down_w, offsets)
     return reference.grouped_swiglu_mlp(x_sorted, up_w, down_w, offsets)
+
+
+def grouped_swiglu_experts(x: Tensor, weights: Tensor, indices: Tensor, up_w: Tensor, down_w: Tensor) -> Tensor:
+    """Routed SwiGLU experts: padded device-side dispatch, grouped expert MLP, weighted combine."""
+    from priml_b200.ops import grouped
+
+    return grouped.grouped_swiglu_experts(x, weights, indices, up_w, down_w)
 
 
 def adamw_(

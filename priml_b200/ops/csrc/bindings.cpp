@@ -107,6 +107,61 @@ void gemm_swiglu_bwd(const Tensor& DY, const Tensor& WD, const Tensor& GU, Tenso
                 M, H, C, 4, GU.data_ptr(), H, status_ptr(), stream());
 }
 
+// Grouped expert GEMM (grouped_gemm.cu) over 128-row-aligned expert segments; offsets: int32 [experts + 1].
+// mode 0: A [rows, K]; B stacked per expert: [experts * b_rows, K] (K-major) or [experts * b_rows, N] (b_mn);
+//         epi 3: B = up weights [experts * 2H, K], C = h [rows, H], aux = gu [rows, 2H] (written);
+//         epi 4: B = down weights [experts * C, H] (b_mn), aux = gu (read), C = dgu [rows, 2H].
+// mode 1: A [rows, out_rows], B [rows, N] -> C [experts * out_rows, N] fp32 (epi 1 store, 2 accumulate).
+void grouped_gemm(const Tensor& A, const Tensor& B, Tensor& C, const Tensor& offsets, bool b_mn, int64_t epi,
+                  int64_t mode, int64_t b_rows, const c10::optional<Tensor>& aux, int64_t swiglu_h) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  check_cuda(offsets, "offsets");
+  PB_CHECK(A.scalar_type() == torch::kBFloat16 && B.scalar_type() == torch::kBFloat16, "A and B must be bf16");
+  PB_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.is_contiguous(), "offsets must be contiguous int32");
+  PB_CHECK(C.is_contiguous(), "C must be contiguous");
+  const int experts = static_cast<int>(offsets.numel()) - 1;
+  const int rows = A.size(0);
+  int N = 0, K = 0, out_rows = 0;
+  if (mode == 1) {
+    out_rows = A.size(1);
+    N = B.size(1);
+    K = rows;
+    PB_CHECK(B.size(0) == rows, "A and B must have the same rows");
+    PB_CHECK(C.size(0) == static_cast<int64_t>(experts) * out_rows && C.size(1) == N && C.scalar_type() == torch::kFloat32,
+             "C must be fp32 [experts * out_rows, N]");
+  } else {
+    K = A.size(1);
+    if (epi == 3) {
+      N = 2 * swiglu_h;
+      PB_CHECK(!b_mn && B.size(1) == K && b_rows == 2 * swiglu_h, "epi 3: B = up weights [experts * 2H, K]");
+      PB_CHECK(C.size(0) == rows && C.size(1) == swiglu_h && aux.has_value() && aux->is_contiguous() &&
+                   aux->size(0) == rows && aux->size(1) == 2 * swiglu_h,
+               "epi 3: C = h [rows, H], aux = gu [rows, 2H]");
+    } else if (b_mn) {
+      N = B.size(1);
+      PB_CHECK(b_rows == K, "B N-major: rows per expert must equal K");
+    } else {
+      N = b_rows;
+      PB_CHECK(B.size(1) == K, "B K-major: [experts * N, K]");
+    }
+    if (epi == 4) {
+      PB_CHECK(b_mn && N == swiglu_h && aux.has_value() && aux->size(1) == 2 * swiglu_h && C.size(1) == 2 * swiglu_h,
+               "epi 4: B = down weights (N-major), aux = gu, C = dgu [rows, 2H]");
+    } else if (epi != 3) {
+      PB_CHECK(C.size(0) == rows && C.size(1) == N, "C must be [rows, N]");
+    }
+    PB_CHECK(B.size(0) == static_cast<int64_t>(experts) * b_rows, "B must stack experts * b_rows rows");
+  }
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard guard(A.device());
+  pb::grouped_gemm_bf16(A.data_ptr(), row_stride(A), B.data_ptr(), row_stride(B), b_mn, C.data_ptr(), C.stride(0), rows,
+                        N, K, offsets.data_ptr<int>(), experts, static_cast<int>(b_rows), static_cast<int>(mode),
+                        out_rows, static_cast<int>(epi), aux.has_value() ? aux->data_ptr() : nullptr,
+                        static_cast<int>(swiglu_h), status_ptr(), stream());
+}
+
 std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const c10::optional<Tensor>& w, double eps, bool out_f32) {
   check_cuda(x, "x");
   PB_CHECK(x.is_contiguous(), "x must be contiguous");
@@ -655,6 +710,9 @@ Tensor augment_pad_crop_flip_cutout(const Tensor& images, int64_t crop, int64_t 
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "priml_b200 sm_100a kernels";
+  m.def("grouped_gemm", &grouped_gemm, "grouped expert tcgen05 GEMM over device offsets", py::arg("A"), py::arg("B"),
+        py::arg("C"), py::arg("offsets"), py::arg("b_mn"), py::arg("epi"), py::arg("mode"), py::arg("b_rows"),
+        py::arg("aux") = py::none(), py::arg("swiglu_h") = 0);
   m.def("gemm", &gemm, "tcgen05 GEMM: C (op)= A B^T", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epi"));
   m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 GEMM with fused SwiGLU epilogue");

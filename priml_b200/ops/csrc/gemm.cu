@@ -23,206 +23,12 @@
 #include <stdexcept>
 
 #include "common.cuh"
+#include "gemm_common.cuh"
 #include "kernels.h"
 
 namespace pb {
 
 namespace {
-
-constexpr int BM = 128;
-constexpr int BK = 64;
-constexpr int GROUP_M = 16;
-constexpr int kThreads = 192;
-
-template <int BN>
-struct GemmCfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
-  static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-};
-
-struct GemmParams {
-  int M, N, K;
-  void* C;
-  long long ldc;
-  const void* aux;       // SwiGLU: unused; residual add: [M, ldc] bf16
-  int* status;
-  int num_n_half;        // fused SwiGLU: H (gate/up split point in B rows)
-};
-
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
-  const int group = GROUP_M * num_n;
-  const int g = tile / group;
-  const int first_m = g * GROUP_M;
-  const int gm = min(num_m - first_m, GROUP_M);
-  const int r = tile - g * group;
-  mb = first_m + r % gm;
-  nb = r / gm;
-}
-
-// Store one accumulator row slice (this thread's TMEM lane) of output tile column block `nb`.
-template <int BN, int EPI>
-__device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_row, int row, int nb) {
-  const bool row_ok = row < p.M;
-  if constexpr (EPI == 3) {
-    const int H = p.num_n_half;
-    const int h0 = nb * (BN / 2);
-    __nv_bfloat16* hout = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
-    __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(p.aux)) +
-                        static_cast<long long>(row) * (2LL * H);
-#pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 32) {
-      uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(t_row + c, g);
-      tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
-      tmem_wait_ld();
-      const int col = h0 + c;
-      if (row_ok && col < H) {
-        uint32_t hv[16], gv[16], uv[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
-          const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
-          // Round gate/up to bf16 first so forward and backward see the same values.
-          const __nv_bfloat162 gb = __floats2bfloat162_rn(g0, g1);
-          const __nv_bfloat162 ub = __floats2bfloat162_rn(u0, u1);
-          const float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
-          const float s0 = gf.x / (1.f + __expf(-gf.x)), s1 = gf.y / (1.f + __expf(-gf.y));
-          hv[j] = pack_bf16x2(s0 * uf.x, s1 * uf.y);
-          gv[j] = *reinterpret_cast<const uint32_t*>(&gb);
-          uv[j] = *reinterpret_cast<const uint32_t*>(&ub);
-        }
-        if (col + 32 <= H) {
-          uint4* hp = reinterpret_cast<uint4*>(hout + col);
-          uint4* gp = reinterpret_cast<uint4*>(gu + col);
-          uint4* up = reinterpret_cast<uint4*>(gu + H + col);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            hp[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
-            gp[q] = make_uint4(gv[4 * q], gv[4 * q + 1], gv[4 * q + 2], gv[4 * q + 3]);
-            up[q] = make_uint4(uv[4 * q], uv[4 * q + 1], uv[4 * q + 2], uv[4 * q + 3]);
-          }
-        } else {
-          const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(hv);
-          const __nv_bfloat16* gb2 = reinterpret_cast<const __nv_bfloat16*>(gv);
-          const __nv_bfloat16* ub2 = reinterpret_cast<const __nv_bfloat16*>(uv);
-          for (int j = 0; j < 32 && col + j < H; ++j) {
-            hout[col + j] = hb[j];
-            gu[col + j] = gb2[j];
-            gu[H + col + j] = ub2[j];
-          }
-        }
-      }
-    }
-  } else if constexpr (EPI == 4) {
-    // Accumulator = dh (N = H); aux = saved [gate | up] pre-activation [M, 2H]; C = dgu [M, 2H].
-    // dh is rounded to bf16 first, as the unfused path stores it.
-    const int H = p.num_n_half;
-    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + static_cast<long long>(row) * (2LL * H);
-    __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c, v);
-      tmem_wait_ld();
-      const int col = nb * BN + c;
-      if (!row_ok || col >= H) continue;
-      const int n = min(32, H - col);
-      uint32_t gw[16], uw[16], dg[16], du[16];
-      if (n == 32) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 a = reinterpret_cast<const uint4*>(gu + col)[q];
-          const uint4 b = reinterpret_cast<const uint4*>(gu + H + col)[q];
-          gw[4 * q] = a.x, gw[4 * q + 1] = a.y, gw[4 * q + 2] = a.z, gw[4 * q + 3] = a.w;
-          uw[4 * q] = b.x, uw[4 * q + 1] = b.y, uw[4 * q + 2] = b.z, uw[4 * q + 3] = b.w;
-        }
-      } else {
-        const uint16_t* g16 = reinterpret_cast<const uint16_t*>(gu + col);
-        const uint16_t* u16 = reinterpret_cast<const uint16_t*>(gu + H + col);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int a = 2 * j, b2 = 2 * j + 1;
-          gw[j] = (a < n ? g16[a] : 0u) | ((b2 < n ? static_cast<uint32_t>(g16[b2]) : 0u) << 16);
-          uw[j] = (a < n ? u16[a] : 0u) | ((b2 < n ? static_cast<uint32_t>(u16[b2]) : 0u) << 16);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[j]));
-        const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[j]));
-        const float2 d = __bfloat1622float2(__floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
-        const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
-        du[j] = pack_bf16x2(d.x * (g.x * s0), d.y * (g.y * s1));
-        dg[j] = pack_bf16x2(d.x * u.x * s0 * (1.f + g.x * (1.f - s0)), d.y * u.y * s1 * (1.f + g.y * (1.f - s1)));
-      }
-      if (n == 32) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          reinterpret_cast<uint4*>(dgu + col)[q] = make_uint4(dg[4 * q], dg[4 * q + 1], dg[4 * q + 2], dg[4 * q + 3]);
-          reinterpret_cast<uint4*>(dgu + H + col)[q] = make_uint4(du[4 * q], du[4 * q + 1], du[4 * q + 2], du[4 * q + 3]);
-        }
-      } else {
-        const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(dg);
-        const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(du);
-        for (int j = 0; j < n; ++j) {
-          dgu[col + j] = gb[j];
-          dgu[H + col + j] = ub[j];
-        }
-      }
-    }
-  } else {
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c, v);
-      tmem_wait_ld();
-      const int col = nb * BN + c;
-      if (!row_ok || col >= p.N) continue;
-      const bool full_chunk = col + 32 <= p.N;
-      if constexpr (EPI == 0) {
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col;
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-          uint4* o4 = reinterpret_cast<uint4*>(out);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) o4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        } else {
-          const __nv_bfloat16* pb16 = reinterpret_cast<const __nv_bfloat16*>(pk);
-          for (int j = 0; j < 32 && col + j < p.N; ++j) out[j] = pb16[j];
-        }
-      } else {
-        float* out = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
-        if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-          float4* o4 = reinterpret_cast<float4*>(out);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 a = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                   __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
-            if constexpr (EPI == 2) {
-              const float4 o = o4[q];
-              a.x += o.x;
-              a.y += o.y;
-              a.z += o.z;
-              a.w += o.w;
-            }
-            o4[q] = a;
-          }
-        } else {
-          for (int j = 0; j < 32 && col + j < p.N; ++j) {
-            const float a = __uint_as_float(v[j]);
-            out[j] = EPI == 2 ? out[j] + a : a;
-          }
-        }
-      }
-    }
-  }
-}
 
 // EPI: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += acc),
 //      4 = SwiGLU backward: acc = dh, aux = [gate | up] -> C = [dgate | dup] (bf16 [M, 2H]),

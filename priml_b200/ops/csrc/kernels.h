@@ -26,6 +26,13 @@ void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long
                long long ldc, int M, int N, int K, int epi, const void* aux, int swiglu_h, int* status,
                cudaStream_t stream);
 
+// Grouped expert GEMM over 128-row-aligned expert segments (device offsets [experts + 1]).
+// mode 0: C[r] = A[r] @ B_e^T (B stacked per expert, b_rows rows each; epi 0, 1, 3, 4);
+// mode 1: C[e * out_rows + m, n] = sum_{r in e} A[r, m] B[r, n] (epi 1 or 2).
+void grouped_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, bool b_mn, void* C, long long ldc,
+                       int rows, int N, int K, const int* offsets, int experts, int b_rows, int mode, int out_rows,
+                       int epi, const void* aux, int swiglu_h, int* status, cudaStream_t stream);
+
 // RMSNorm over the last dim C of R rows. x: bf16 or fp32 (x_f32 selects), y: bf16 or fp32.
 void rmsnorm_fwd(const void* x, bool x_f32, const float* w, void* y, bool y_f32, float* rstd, int R, int C, float eps,
                  cudaStream_t stream);

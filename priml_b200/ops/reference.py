@@ -133,13 +133,17 @@ def adamw_(
 
 def grouped_swiglu_mlp(x_sorted: Tensor, up_w: Tensor, down_w: Tensor, offsets: Tensor) -> Tensor:
     """Rows ``offsets[e]:offsets[e+1]`` through expert ``e``:
-    ``down_w[e] @ swiglu(up_w[e] @ x)``; ``up_w [E, 2H, C]``, ``down_w [E, C, H]``."""
+    ``down_w[e] @ swiglu(up_w[e] @ x)``; ``up_w [E, 2H, C]``, ``down_w [E, C, H]``.
+    Rows past ``offsets[E]`` (padding of a padded buffer) come out zero."""
     bounds = offsets.tolist()
     pieces = []
     for e in range(up_w.shape[0]):
         lo, hi = bounds[e], bounds[e + 1]
         if hi > lo:
             pieces.append(linear(swiglu(linear(x_sorted[lo:hi], up_w[e])), down_w[e]))
+    tail = x_sorted.shape[0] - bounds[-1]  # rows past the last segment (padded buffers)
+    if tail > 0:
+        pieces.append(x_sorted.new_zeros(tail, down_w.shape[1]))
     if not pieces:
         return x_sorted.new_zeros(0, down_w.shape[1])
     return torch.cat(pieces, dim=0)

@@ -222,3 +222,42 @@ def test_fused_augmentation_matches_torch_path(dtype: torch.dtype, mode: str) ->
     ref = pad_crop_flip(img.cpu().float(), 32, pad=4, pad_mode=mode, cutout_size=8,
                         draws=type(d)(*(t.cpu() if t is not None else None for t in d)))  # fmt: skip
     assert torch.equal(fused.float().cpu(), ref.to(dtype).float())
+
+
+@pytest.mark.parametrize("t,k,e,c,h", [(300, 2, 6, 256, 256), (1000, 6, 16, 512, 384)])
+def test_grouped_swiglu_experts_fwd_bwd(t: int, k: int, e: int, c: int, h: int) -> None:
+    import torch.nn.functional as F
+
+    from priml_b200.ops import native
+    from priml_b200.ops.grouped import grouped_swiglu_experts
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(t, c, device="cuda", generator=g).to(torch.bfloat16).requires_grad_()
+    up = (torch.randn(e, 2 * h, c, device="cuda", generator=g) / c**0.5).requires_grad_()
+    down = (torch.randn(e, c, h, device="cuda", generator=g) / h**0.5).requires_grad_()
+    idx = torch.randint(0, e - 1, (t, k), device="cuda", generator=g)  # the last expert gets no rows
+    w = torch.rand(t, k, device="cuda", generator=g)
+    y = grouped_swiglu_experts(x, w, idx, up, down)
+    gy = torch.randn(t, c, device="cuda", generator=g).to(torch.bfloat16)
+    dx, dup, ddown = torch.autograd.grad(y, (x, up, down), gy)
+    # fp32 oracle over the same bf16-rounded operands
+    xf, upf, downf = x.detach().float(), up.detach().to(torch.bfloat16).float(), down.detach().to(torch.bfloat16).float()
+    xf.requires_grad_()
+    upf.requires_grad_()
+    downf.requires_grad_()
+    ref = torch.zeros(t, c, device="cuda")
+    for ei in range(e):
+        sel = (idx == ei).nonzero()
+        if sel.numel() == 0:
+            continue
+        ti, j = sel[:, 0], sel[:, 1]
+        gate, u = F.linear(xf[ti], upf[ei]).chunk(2, dim=-1)
+        out = F.linear(F.silu(gate) * u, downf[ei]) * w[ti, j].unsqueeze(-1)
+        ref = ref.index_add(0, ti, out)
+    rx, rup, rdown = torch.autograd.grad(ref, (xf, upf, downf), gy.float())
+    assert _rel_err(y, ref) < 2e-2
+    assert _rel_err(dx, rx) < 3e-2
+    assert _rel_err(dup, rup) < 3e-2
+    assert _rel_err(ddown, rdown) < 3e-2
+    assert float(dup[e - 1].abs().max()) == 0.0 and float(ddown[e - 1].abs().max()) == 0.0
+    assert int(native().read_status(True)) == 0
