@@ -279,19 +279,22 @@ class MoE(nn.Module):
 
 
 def _split_expert_keys(module: nn.Module, state: dict[str, Any], prefix: str, local_metadata: Any) -> None:
-    del module, local_metadata
+    del local_metadata
+    base = getattr(module.experts, "expert_offset", 0)  # expert parallelism: this rank's first global expert
     for name in ("up_proj", "down_proj"):
         key = f"{prefix}experts.{name}"
         if key in state:
             stacked = state.pop(key)
             for e in range(stacked.shape[0]):
-                state[f"{prefix}experts.{e}.{name}.weight"] = stacked[e]
+                state[f"{prefix}experts.{base + e}.{name}.weight"] = stacked[e]
 
 
 def _stack_expert_keys(module: nn.Module, state: dict[str, Any], prefix: str, *args: Any) -> None:
     del args
-    n = module.num_experts  # type: ignore[attr-defined]
+    ex = module.experts  # type: ignore[attr-defined]
+    base = getattr(ex, "expert_offset", 0)
+    n = ex.num_experts
     for name in ("up_proj", "down_proj"):
-        keys = [f"{prefix}experts.{e}.{name}.weight" for e in range(n)]
+        keys = [f"{prefix}experts.{base + e}.{name}.weight" for e in range(n)]
         if all(k in state for k in keys):
             state[f"{prefix}experts.{name}"] = torch.stack([state.pop(k) for k in keys])

@@ -1,6 +1,7 @@
 """Model presets for the benchmark workloads.
 
 * ``tiny_lm``      vocab 512, d 128, 2 layers, 4 heads x 32, SwiGLU 512, RoPE 1e4 (fp32 CPU check).
+* ``tiny_moe_lm``  tiny_lm with MoE FFNs: 8 routed SwiGLU experts x 128 (top-2 softmax) + 1 shared.
 * ``llama_1b``     d 2048, 16 layers, 32 q / 8 kv heads x 64, SwiGLU 8192, RMSNorm 1e-5,
                    RoPE 5e5, vocab 32768, untied, init N(0, 0.02).
 * ``llama3_8b``    d 4096, 32 layers, 32 / 8 heads x 128, SwiGLU 14336, RoPE 5e5, vocab 128256.
@@ -24,7 +25,7 @@ from priml_b200.models.rope import RoPE
 from priml_b200.models.swiglu import SwiGLU
 from priml_b200.models.transformer import TransformerBlock
 
-__all__ = ["dense_lm", "llama3_8b", "llama_1b", "mla_moe", "tiny_lm"]
+__all__ = ["dense_lm", "llama3_8b", "llama_1b", "mla_moe", "tiny_lm", "tiny_moe_lm"]
 
 
 def dense_lm(
@@ -74,6 +75,22 @@ def dense_lm(
 def tiny_lm() -> CausalLM.Config:
     return dense_lm(vocab=512, d_model=128, n_layers=2, n_heads=4, n_kv_heads=4, head_dim=32, ffn_hidden=512,
                     rope_theta=1e4, norm_eps=1e-6, init_std=None)  # fmt: skip
+
+
+def tiny_moe_lm(*, num_experts: int = 8, top_k: int = 2, aux_loss_weight: float = 0.0) -> CausalLM.Config:
+    block = TransformerBlock.Config(
+        attn=SelfAttention.Config(heads=4, channels_head=32, causal=True, rope=RoPE.Config(32, base=1e4)),
+        ffn=MoE.Config(
+            router=Router.Config(num_experts=num_experts, top_k=top_k, scoring_func="softmax"),
+            expert=SwiGLU.Config(channels_hidden=128),
+            num_shared_experts=1,
+            shared_expert=SwiGLU.Config(channels_hidden=128),
+            aux_loss_weight=aux_loss_weight,
+        ),
+        norm1=RMSNorm.Config(eps=1e-6),
+        norm2=RMSNorm.Config(eps=1e-6),
+    )
+    return CausalLM.Config(512, channels=128, num_layers=2, block=block, final_norm=RMSNorm.Config(eps=1e-6))
 
 
 def llama_1b(*, checkpoint: bool = False) -> CausalLM.Config:

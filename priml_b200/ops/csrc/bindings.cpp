@@ -680,6 +680,166 @@ class TpGroup {
   int64_t slot_bytes_ = 0;
 };
 
+// Expert-parallel row exchange (ep.cu): two symmetric row buffers per rank,
+// 0 = rows travelling to the expert owners, 1 = rows travelling back to their sources.
+class EpGroup {
+ public:
+  static constexpr int kDoneWord = 64, kFreeWord = 66;  // + buffer id
+
+  EpGroup(int64_t rank, int64_t world, int64_t recv_rows, int64_t back_rows, int64_t cols, double timeout_s)
+      : rank_(rank), world_(world), cols_(cols), timeout_ns_(static_cast<long long>(timeout_s * 1e9)),
+        device_(at::cuda::current_device()) {
+    PB_CHECK(world >= 1 && world <= pb::kMaxRanks, "world size must be 1..8");
+    PB_CHECK(cols % 8 == 0, "channels must be a multiple of 8");
+    rows_[0] = std::max<int64_t>(recv_rows, 1);
+    rows_[1] = std::max<int64_t>(back_rows, 1);
+    local_ = std::make_shared<Local>();
+    for (int b = 0; b < 2; ++b) {
+      local_->rows[b] = pb::sym_alloc(rows_[b] * cols * 2);
+      local_->meta[b] = pb::sym_alloc(rows_[b] * 4);
+    }
+    local_->signal = pb::sym_alloc(pb::kSigWords * 8);
+    counters_ = torch::zeros({2}, torch::TensorOptions().device(torch::kCUDA, device_).dtype(torch::kInt32));
+  }
+  ~EpGroup() {
+    for (void* p : opened_) pb::ipc_close(p);
+  }
+  py::bytes handles() const {
+    char buf[320];
+    pb::ipc_handle(local_->rows[0], buf);
+    pb::ipc_handle(local_->meta[0], buf + 64);
+    pb::ipc_handle(local_->rows[1], buf + 128);
+    pb::ipc_handle(local_->meta[1], buf + 192);
+    pb::ipc_handle(local_->signal, buf + 256);
+    return py::bytes(buf, 320);
+  }
+  void open(const std::vector<std::string>& all) {
+    PB_CHECK(static_cast<int64_t>(all.size()) == world_, "need one handle record per rank");
+    const c10::cuda::CUDAGuard guard(device_);
+    for (int64_t r = 0; r < world_; ++r) {
+      void* ptr[5];
+      if (r == rank_) {
+        ptr[0] = local_->rows[0], ptr[1] = local_->meta[0], ptr[2] = local_->rows[1], ptr[3] = local_->meta[1];
+        ptr[4] = local_->signal;
+      } else {
+        for (int i = 0; i < 5; ++i) {
+          ptr[i] = pb::ipc_open(all[r].data() + 64 * i);
+          opened_.push_back(ptr[i]);
+        }
+      }
+      for (int b = 0; b < 2; ++b) {
+        peer_rows_[b][r] = reinterpret_cast<unsigned long long>(ptr[2 * b]);
+        peer_meta_[b][r] = reinterpret_cast<unsigned long long>(ptr[2 * b + 1]);
+      }
+      peer_sig_[r] = reinterpret_cast<unsigned long long>(ptr[4]);
+    }
+    opened_ok_ = true;
+  }
+
+  // rows i of src (or src[gather[i]]) -> buffer b of rank dest_rank[i], row dest_row[i] (-1 rank: skipped).
+  void scatter(int64_t b, const Tensor& src, const c10::optional<Tensor>& gather, const Tensor& dest_rank,
+               const Tensor& dest_row, const c10::optional<Tensor>& meta) {
+    PB_CHECK(opened_ok_ && (b == 0 || b == 1), "open() first; buffer 0 or 1");
+    check_cuda(src, "src");
+    PB_CHECK(src.scalar_type() == torch::kBFloat16 && src.dim() == 2 && src.size(1) == cols_ && src.stride(1) == 1,
+             "src must be bf16 [rows, channels]");
+    PB_CHECK(dest_rank.scalar_type() == torch::kInt32 && dest_row.scalar_type() == torch::kInt64 &&
+                 dest_rank.is_contiguous() && dest_row.is_contiguous() && dest_rank.numel() == dest_row.numel(),
+             "dest_rank int32 / dest_row int64, contiguous, same length");
+    const int64_t rows = dest_rank.numel();
+    if (gather.has_value()) {
+      PB_CHECK(gather->scalar_type() == torch::kInt64 && gather->is_contiguous() && gather->numel() == rows, "gather");
+    } else {
+      PB_CHECK(src.size(0) >= rows, "src has too few rows");
+    }
+    if (meta.has_value()) PB_CHECK(meta->scalar_type() == torch::kInt32 && meta->numel() == rows, "meta");
+    pb::EpScatterParams p{};
+    p.src = reinterpret_cast<const __nv_bfloat16*>(src.data_ptr());
+    p.ld_src = src.stride(0);
+    p.gather = gather.has_value() ? reinterpret_cast<const long long*>(gather->data_ptr<int64_t>()) : nullptr;
+    p.dest_rank = dest_rank.data_ptr<int>();
+    p.dest_row = reinterpret_cast<const long long*>(dest_row.data_ptr<int64_t>());
+    p.meta = meta.has_value() ? meta->data_ptr<int>() : nullptr;
+    p.rows = rows;
+    p.cols = static_cast<int>(cols_);
+    for (int r = 0; r < world_; ++r) {
+      p.buf[r] = peer_rows_[b][r];
+      p.meta_buf[r] = peer_meta_[b][r];
+      p.signal[r] = peer_sig_[r];
+    }
+    p.done_word = kDoneWord + static_cast<int>(b);
+    p.free_word = kFreeWord + static_cast<int>(b);
+    p.rank = static_cast<int>(rank_);
+    p.world = static_cast<int>(world_);
+    p.epoch = ++epoch_[b];
+    p.block_counter = reinterpret_cast<unsigned int*>(counters_.data_ptr<int>()) + b;
+    p.timeout_ns = timeout_ns_;
+    p.status = status_ptr();
+    const c10::cuda::CUDAGuard guard(device_);
+    pb::ep_scatter(p, stream());
+  }
+  // Wait (on the stream) until every rank has finished this epoch's scatter into our buffer b.
+  void wait(int64_t b) {
+    pb::tp_wait(local_->signal, kDoneWord + static_cast<int>(b), static_cast<unsigned long long>(epoch_[b]) * world_,
+                timeout_ns_, status_ptr(), stream());
+  }
+  // First seg_start[segs] rows of our buffer b -> dst (segment padding zeroed, meta -1).
+  void collect(int64_t b, Tensor& dst, const c10::optional<Tensor>& meta_dst, const Tensor& seg_start,
+               const Tensor& totals) {
+    PB_CHECK(dst.scalar_type() == torch::kBFloat16 && dst.is_contiguous() && dst.size(1) == cols_ &&
+                 dst.size(0) <= rows_[b],
+             "dst must be contiguous bf16 [rows <= capacity, channels]");
+    PB_CHECK(seg_start.scalar_type() == torch::kInt32 && totals.scalar_type() == torch::kInt32 &&
+                 seg_start.numel() == totals.numel() + 1,
+             "seg_start int32 [segs + 1], totals int32 [segs]");
+    if (meta_dst.has_value()) PB_CHECK(meta_dst->scalar_type() == torch::kInt32 && meta_dst->numel() >= dst.size(0), "meta_dst");
+    pb::ep_collect(local_->rows[b], static_cast<const int*>(local_->meta[b]), dst.data_ptr(),
+                   meta_dst.has_value() ? meta_dst->data_ptr<int>() : nullptr, seg_start.data_ptr<int>(),
+                   totals.data_ptr<int>(), static_cast<int>(totals.numel()), static_cast<int>(cols_), dst.size(0),
+                   stream());
+  }
+  // This rank has consumed its buffer b: peers may write the next epoch.
+  void release(int64_t b) {
+    pb::EpSignalParams p{};
+    for (int r = 0; r < world_; ++r) p.signal[r] = peer_sig_[r];
+    p.word = kFreeWord + static_cast<int>(b);
+    p.world = static_cast<int>(world_);
+    pb::ep_signal(p, stream());
+  }
+  // Our buffer b as a tensor (rows x channels), for consumers that read it in place.
+  Tensor rows(int64_t b) const {
+    auto keep = local_;
+    return torch::from_blob(local_->rows[b], {rows_[b], cols_}, [keep](void*) {},
+                            torch::TensorOptions().device(torch::kCUDA, device_).dtype(torch::kBFloat16));
+  }
+
+ private:
+  struct Local {
+    void* rows[2] = {nullptr, nullptr};
+    void* meta[2] = {nullptr, nullptr};
+    void* signal = nullptr;
+    ~Local() {
+      for (int b = 0; b < 2; ++b) {
+        pb::sym_free(rows[b]);
+        pb::sym_free(meta[b]);
+      }
+      pb::sym_free(signal);
+    }
+  };
+  int64_t rank_, world_, cols_;
+  long long timeout_ns_;
+  int device_;
+  int64_t rows_[2];
+  std::shared_ptr<Local> local_;
+  Tensor counters_;
+  unsigned long long peer_rows_[2][pb::kMaxRanks] = {};
+  unsigned long long peer_meta_[2][pb::kMaxRanks] = {};
+  unsigned long long peer_sig_[pb::kMaxRanks] = {};
+  std::vector<void*> opened_;
+  bool opened_ok_ = false;
+  long long epoch_[2] = {0, 0};
+};
+
 // images [B, C, H, W] (fp32 / bf16 / uint8, contiguous) -> [B, C, crop, crop].
 Tensor augment_pad_crop_flip_cutout(const Tensor& images, int64_t crop, int64_t pad, int64_t mode, double fill,
                                     const Tensor& dy, const Tensor& dx, c10::optional<Tensor> flip, const Tensor& cy,
@@ -741,6 +901,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("adamw_scatter", &PeerGroup::adamw_scatter)
       .def("barrier", &PeerGroup::barrier);
   m.def("status_tensor", &status_tensor_py);
+  py::class_<EpGroup>(m, "EpGroup")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, double>(), py::arg("rank"), py::arg("world"),
+           py::arg("recv_rows"), py::arg("back_rows"), py::arg("cols"), py::arg("timeout_s") = 60.0)
+      .def("handles", &EpGroup::handles)
+      .def("open", &EpGroup::open)
+      .def("scatter", &EpGroup::scatter, py::arg("b"), py::arg("src"), py::arg("gather"), py::arg("dest_rank"),
+           py::arg("dest_row"), py::arg("meta"))
+      .def("wait", &EpGroup::wait)
+      .def("collect", &EpGroup::collect, py::arg("b"), py::arg("dst"), py::arg("meta_dst"), py::arg("seg_start"),
+           py::arg("totals"))
+      .def("release", &EpGroup::release)
+      .def("rows", &EpGroup::rows);
   py::class_<TpGroup>(m, "TpGroup")
       .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, double>(), py::arg("rank"), py::arg("world"),
            py::arg("shard_elems"), py::arg("slot_elems"), py::arg("max_chunks"), py::arg("timeout_s") = 60.0)

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -178,6 +179,35 @@ struct TpGemmParams {
   unsigned long long slots[kMaxRanks];   // every rank's receive slots [world, m_shard, N]
   unsigned long long signal[kMaxRanks];
 };
+
+// ---------------------------------------------------------------- expert-parallel exchange (ep.cu)
+struct EpScatterParams {
+  const __nv_bfloat16* src;
+  long long ld_src;                 // row stride of src (elements)
+  const long long* gather;          // optional: row i reads src[gather[i]]
+  const int* dest_rank;             // [rows], -1 = skip
+  const long long* dest_row;        // [rows]
+  const int* meta;                  // optional metadata word per row
+  long long rows;
+  int cols;                         // channels (multiple of 8)
+  unsigned long long buf[kMaxRanks];       // every rank's receive rows
+  unsigned long long meta_buf[kMaxRanks];  // every rank's receive metadata
+  unsigned long long signal[kMaxRanks];    // every rank's signal words (u64)
+  int done_word, free_word;         // signal words: rows of this buffer written / buffer consumed
+  int rank, world;
+  long long epoch;                  // 1, 2, ... per buffer
+  unsigned int* block_counter;      // local, zero between launches
+  long long timeout_ns;
+  int* status;
+};
+struct EpSignalParams {
+  unsigned long long signal[kMaxRanks];
+  int word, world;
+};
+void ep_scatter(const EpScatterParams& p, cudaStream_t stream);
+void ep_collect(const void* buf, const int* meta, void* dst, int* meta_dst, const int* seg_start, const int* totals,
+                int segs, int cols, long long cap, cudaStream_t stream);
+void ep_signal(const EpSignalParams& p, cudaStream_t stream);
 
 int tp_gemm_grid(int M, int N);
 void tp_ag_gemm(const TpGemmParams& p, const void* a_shard, const void* B, long long ldb, bool b_mn, int grid,
