@@ -741,8 +741,9 @@ class EpGroup {
                const Tensor& dest_row, const c10::optional<Tensor>& meta) {
     PB_CHECK(opened_ok_ && (b == 0 || b == 1), "open() first; buffer 0 or 1");
     check_cuda(src, "src");
-    PB_CHECK(src.scalar_type() == torch::kBFloat16 && src.dim() == 2 && src.size(1) == cols_ && src.stride(1) == 1,
-             "src must be bf16 [rows, channels]");
+    PB_CHECK(src.scalar_type() == torch::kBFloat16 && src.dim() == 2 && src.size(1) == cols_ && src.stride(1) == 1 &&
+                 src.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0,
+             "src must be bf16 [rows, channels] with 16-byte aligned rows");
     PB_CHECK(dest_rank.scalar_type() == torch::kInt32 && dest_row.scalar_type() == torch::kInt64 &&
                  dest_rank.is_contiguous() && dest_row.is_contiguous() && dest_rank.numel() == dest_row.numel(),
              "dest_rank int32 / dest_row int64, contiguous, same length");
@@ -762,6 +763,7 @@ class EpGroup {
     p.meta = meta.has_value() ? meta->data_ptr<int>() : nullptr;
     p.rows = rows;
     p.cols = static_cast<int>(cols_);
+    p.dest_cap = rows_[b];
     for (int r = 0; r < world_; ++r) {
       p.buf[r] = peer_rows_[b][r];
       p.meta_buf[r] = peer_meta_[b][r];

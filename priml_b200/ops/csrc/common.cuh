@@ -22,6 +22,7 @@ enum : int {
   kTimeoutEpilogue = 3,
   kTimeoutDrain = 4,
   kTimeoutPeer = 5,
+  kBadIndex = 6,  // a row index outside its buffer was refused
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

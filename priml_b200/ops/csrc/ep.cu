@@ -66,6 +66,10 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const EpScatterParams p
       if (dr < 0) continue;
       const long long srow = p.gather != nullptr ? p.gather[i] : i;
       const long long drow = p.dest_row[i];
+      if (dr >= p.world || drow < 0 || drow >= p.dest_cap) {  // never write outside a peer's buffer
+        if (lane == 0) record_error(p.status, kBadIndex);
+        continue;
+      }
       const uint4* s = reinterpret_cast<const uint4*>(p.src + srow * p.ld_src);
       uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.buf[dr]) + drow * p.cols);
       for (int w = lane; w < words; w += 32) d[w] = __ldg(s + w);

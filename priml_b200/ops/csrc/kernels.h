@@ -190,6 +190,7 @@ struct EpScatterParams {
   const int* meta;                  // optional metadata word per row
   long long rows;
   int cols;                         // channels (multiple of 8)
+  long long dest_cap;               // rows of every rank's receive buffer (rows at or past it are refused)
   unsigned long long buf[kMaxRanks];       // every rank's receive rows
   unsigned long long meta_buf[kMaxRanks];  // every rank's receive metadata
   unsigned long long signal[kMaxRanks];    // every rank's signal words (u64)

@@ -114,6 +114,11 @@ class EpComm:
         from priml_b200.ops import native
 
         want = (max(recv, self._cap[0]), max(back, self._cap[1]), cols)
+        # Every rank must size (and later fill) its buffers alike: the plan assumes equal token counts.
+        seen: list[Any] = [None] * self.world
+        dist.all_gather_object(seen, want, group=self.group)
+        if any(s != want for s in seen):
+            raise ValueError(f"expert parallelism needs the same tokens per MoE call on every rank; got {seen}")
         if self._g is not None:
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
