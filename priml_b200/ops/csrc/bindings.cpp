@@ -162,6 +162,41 @@ void grouped_gemm(const Tensor& A, const Tensor& B, Tensor& C, const Tensor& off
                         static_cast<int>(swiglu_h), status_ptr(), stream());
 }
 
+// MXFP8 quantization of bf16 x [R, K]: returns (q uint8, scales uint8 in the blocked layout).
+// transpose = false: q [R, K], 32-element blocks along K; true: q [K, R], blocks along R.
+std::vector<Tensor> mx_quantize(const Tensor& x, bool transpose) {
+  check_cuda(x, "x");
+  PB_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x must be bf16 [R, K], rows contiguous");
+  const int64_t R = x.size(0), K = x.size(1);
+  auto opts = torch::TensorOptions().device(x.device()).dtype(torch::kUInt8);
+  Tensor q = transpose ? torch::empty({K, R}, opts) : torch::empty({R, K}, opts);
+  Tensor sf = torch::empty({pb::mx_scale_bytes(transpose ? K : R, transpose ? R : K)}, opts);
+  if (R == 0 || K == 0) return {q, sf};
+  const c10::cuda::CUDAGuard guard(x.device());
+  pb::mx_quantize(x.data_ptr(), row_stride(x), q.data_ptr(), sf.data_ptr(), static_cast<int>(R), static_cast<int>(K),
+                  transpose, stream());
+  return {q, sf};
+}
+
+// C [M, N] (op)= MX(A [M, K]) @ MX(B [N, K])^T; epi 0 bf16, 1 fp32, 2 fp32 +=.
+void mx_gemm(const Tensor& A, const Tensor& sfa, const Tensor& B, const Tensor& sfb, Tensor& C, int64_t epi) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  PB_CHECK(A.scalar_type() == torch::kUInt8 && B.scalar_type() == torch::kUInt8 && A.is_contiguous() && B.is_contiguous(),
+           "A and B must be contiguous uint8 (fp8 E4M3 bytes)");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  PB_CHECK(B.size(1) == K && K % 32 == 0, "A [M, K] and B [N, K] with K a multiple of 32");
+  PB_CHECK(sfa.numel() >= pb::mx_scale_bytes(M, K) && sfb.numel() >= pb::mx_scale_bytes(N, K), "scale buffers too small");
+  PB_CHECK(C.dim() == 2 && C.size(0) == M && C.size(1) == N && C.is_contiguous(), "C must be contiguous [M, N]");
+  if (epi == 0) PB_CHECK(C.scalar_type() == torch::kBFloat16, "epi 0 writes bf16");
+  if (epi == 1 || epi == 2) PB_CHECK(C.scalar_type() == torch::kFloat32, "epi 1/2 write fp32");
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(A.device());
+  pb::mx_gemm(A.data_ptr(), sfa.data_ptr(), B.data_ptr(), sfb.data_ptr(), C.data_ptr(), N, static_cast<int>(M),
+              static_cast<int>(N), static_cast<int>(K), static_cast<int>(epi), status_ptr(), stream());
+}
+
 std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const c10::optional<Tensor>& w, double eps, bool out_f32) {
   check_cuda(x, "x");
   PB_CHECK(x.is_contiguous(), "x must be contiguous");
@@ -872,6 +907,9 @@ Tensor augment_pad_crop_flip_cutout(const Tensor& images, int64_t crop, int64_t 
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "priml_b200 sm_100a kernels";
+  m.def("mx_quantize", &mx_quantize, "MXFP8 quantization (E4M3 + E8M0 per 32)", py::arg("x"), py::arg("transpose"));
+  m.def("mx_gemm", &mx_gemm, "block-scaled MXFP8 tcgen05 GEMM", py::arg("A"), py::arg("sfa"), py::arg("B"), py::arg("sfb"),
+        py::arg("C"), py::arg("epi"));
   m.def("grouped_gemm", &grouped_gemm, "grouped expert tcgen05 GEMM over device offsets", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("offsets"), py::arg("b_mn"), py::arg("epi"), py::arg("mode"), py::arg("b_rows"),
         py::arg("aux") = py::none(), py::arg("swiglu_h") = 0);

@@ -19,6 +19,8 @@ void make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long inner, long
 // 2-D fp32 map without swizzle (bulk reduce targets).
 void make_tmap_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
                       int box_inner, int box_outer);
+void make_tmap_2d_u8(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
+                     int box_inner, int box_outer);
 void make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long inner, long long mid, long long outer,
                        long long mid_stride, long long outer_stride, int box_inner, int box_mid, bool swizzle128);
 
@@ -33,6 +35,13 @@ void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long
 void grouped_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, bool b_mn, void* C, long long ldc,
                        int rows, int N, int K, const int* offsets, int experts, int b_rows, int mode, int out_rows,
                        int epi, const void* aux, int swiglu_h, int* status, cudaStream_t stream);
+
+// MXFP8 (mxfp8.cu): E4M3 elements with one E8M0 scale per 32 along the contraction dim, scales
+// in the blocked layout of mx_scale_bytes(rows, k) bytes.
+long long mx_scale_bytes(long long rows, long long k);
+void mx_quantize(const void* x, long long ldx, void* q, void* sf, int R, int K, bool transpose, cudaStream_t stream);
+void mx_gemm(const void* A, const void* sfa, const void* B, const void* sfb, void* C, long long ldc, int M, int N, int K,
+             int epi, int* status, cudaStream_t stream);
 
 // RMSNorm over the last dim C of R rows. x: bf16 or fp32 (x_f32 selects), y: bf16 or fp32.
 void rmsnorm_fwd(const void* x, bool x_f32, const float* w, void* y, bool y_f32, float* rstd, int R, int C, float eps,

@@ -21,11 +21,14 @@ from priml_b200.train.profiling import PhaseTimer, TorchProfiling
 from priml_b200.train.tracker import AsyncTracker, FileTracker, NoTracker, TensorBoardTracker, TrackerList, WandbTracker
 from priml_b200.train.train_loop import EvalTimeLimitError, TrainLoop
 from priml_b200.train.progress import write_progress
+from priml_b200.train.quantization import Float8ModelQuantization, NoModelQuantization
 from priml_b200.train.results import format_summary, read_metrics, summarize
 from priml_b200.train.train_step import TrainStep, TrainStepOutput
 from priml_b200.train.train_step_gan import GANTrainStep
 
 __all__ = [
+    "Float8ModelQuantization",
+    "NoModelQuantization",
     "GANTrainStep",
     "format_summary",
     "read_metrics",
