@@ -92,15 +92,77 @@ def bench_gemms(tokens: int = 16384) -> list[dict]:
     return rows
 
 
+def _scaled_mm_mx(qa: torch.Tensor, sa: torch.Tensor, qb: torch.Tensor, sb: torch.Tensor) -> Callable[[], object] | None:
+    """cuBLASLt MXFP8 through torch._scaled_mm on the same bytes (the library baseline), if this torch has it."""
+    try:
+        a8, b8 = qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn)
+        sa8, sb8 = sa.view(torch.float8_e8m0fnu), sb.view(torch.float8_e8m0fnu)
+
+        def run() -> object:
+            return torch._scaled_mm(a8, b8.t(), scale_a=sa8, scale_b=sb8, out_dtype=torch.bfloat16)  # noqa: SLF001
+
+        run()
+        torch.cuda.synchronize()
+        return run
+    except Exception:  # noqa: BLE001 -- unsupported build / layout: no baseline
+        return None
+
+
+def bench_mx(tokens: int = 16384) -> list[dict]:
+    """MXFP8 GEMMs (operands pre-quantized) on the forward-shaped Llama-1B GEMMs, vs our bf16 GEMM
+    and cuBLASLt MXFP8; plus the quantizer's bandwidth."""
+    from priml_b200.ops import native
+
+    peak_tf, peak_gbs = _peaks()
+    n = native()
+    rows = []
+    for name, m, nn, k, a_mn, b_mn in gemm_cases(tokens):
+        if a_mn or b_mn:
+            continue  # every MX GEMM reads K-major operands (transposed ones are quantized transposed)
+        a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(nn, k, device="cuda", dtype=torch.bfloat16)
+        qa, sa = n.mx_quantize(a, False)
+        qb, sb = n.mx_quantize(b, False)
+        c = torch.empty(m, nn, device="cuda", dtype=torch.bfloat16)
+        mx = time_fn(lambda: n.mx_gemm(qa, sa, qb, sb, c, 0))
+        bf = time_fn(lambda: n.gemm(a, b, c, False, False, 0))
+        lib = _scaled_mm_mx(qa, sa, qb, sb)
+        lib_ms = time_fn(lib) if lib is not None else None
+        quant = time_fn(lambda: n.mx_quantize(a, False))
+        flops = 2.0 * m * nn * k
+        rows.append(
+            {
+                "case": f"mx.{name}",
+                "M": m, "N": nn, "K": k,
+                "mx_ms": round(mx, 4),
+                "mx_tflops": round(flops / mx / 1e9, 1),
+                "frac_of_2x_measured_bf16": round(flops / mx / 1e9 / (2 * peak_tf), 3),
+                "frac_of_nominal_fp8_4500": round(flops / mx / 1e9 / 4500.0, 3),
+                "our_bf16_ms": round(bf, 4),
+                "speedup_vs_our_bf16": round(bf / mx, 3),
+                "cublaslt_mxfp8_ms": None if lib_ms is None else round(lib_ms, 4),
+                "quantize_ms": round(quant, 4),
+                "quantize_frac_of_measured_hbm": round((m * k * 3 + m * k / 32) / quant / 1e6 / peak_gbs, 3),
+            }
+        )  # fmt: skip
+        del a, b, qa, qb, c
+    return rows
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", type=str, default="")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--attn-only", action="store_true")
     ap.add_argument("--profile", type=str, default="")
+    ap.add_argument("--mx", action="store_true", help="MXFP8 GEMMs and quantizers only")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)
+        return
+    if args.mx:
+        for r in bench_mx(args.tokens):
+            print(json.dumps(r))
         return
     rows = bench_gemms(args.tokens) if not args.attn_only else []
     rows += bench_attention()
@@ -155,6 +217,14 @@ def profile_case(name: str) -> None:
         c = torch.empty(8192, 8192, device="cuda", dtype=torch.bfloat16)
         for _ in range(3):
             n.gemm(a, b, c, False, False, 0)
+    elif name == "mx_gemm":
+        a = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
+        c = torch.empty(8192, 8192, device="cuda", dtype=torch.bfloat16)
+        qa, sa = n.mx_quantize(a, False)
+        qb, sb = n.mx_quantize(b, False)
+        for _ in range(3):
+            n.mx_gemm(qa, sa, qb, sb, c, 0)
     elif name in ("attn_fwd", "attn_bwd"):
         q = torch.randn(1, 4096, 32, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         k = torch.randn(1, 4096, 8, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
