@@ -122,13 +122,16 @@ def adamw_(
         for p, g, m, v in zip(params, grads, exp_avgs, exp_avg_sqs, strict=True):
             g32 = g.float()
             p32 = p if p.dtype == torch.float32 else p.float()
+            m32 = m if m.dtype == torch.float32 else m.float()  # moments of narrow parameters update in fp32
+            v32 = v if v.dtype == torch.float32 else v.float()
             p32.mul_(1.0 - lr * weight_decay)
-            m.lerp_(g32, 1.0 - beta1)
-            v.lerp_(g32.square(), 1.0 - beta2)
-            denom = (v / bias2).sqrt() + eps
-            p32.sub_(m / denom * (lr / bias1))
-            if p32.data_ptr() != p.data_ptr():
-                p.copy_(p32)
+            m32.lerp_(g32, 1.0 - beta1)
+            v32.lerp_(g32.square(), 1.0 - beta2)
+            denom = (v32 / bias2).sqrt() + eps
+            p32.sub_(m32 / denom * (lr / bias1))
+            for lo, hi in ((p, p32), (m, m32), (v, v32)):
+                if hi.data_ptr() != lo.data_ptr():
+                    lo.copy_(hi)
 
 
 def grouped_swiglu_mlp(x_sorted: Tensor, up_w: Tensor, down_w: Tensor, offsets: Tensor) -> Tensor:

@@ -165,7 +165,7 @@ class TrainLoop:
         c = self.config
         if not math.isfinite(c.max_time):
             return False
-        used = time.perf_counter() - self._t_start if c.max_time_kind == "wall" else self.train_seconds
+        used = time.perf_counter() - self._t_start if c.max_time_kind == "wall" else self._train_elapsed()
         hit = used >= c.max_time
         if _dist():
             dev = self.step.device if self.step.device.type == "cuda" else torch.device("cpu")
@@ -206,6 +206,8 @@ class TrainLoop:
             out = self.step.eval_loss(**batch)
             if i < self.config.eval_warmup_batches:
                 continue
+            for m in self.metrics.values():
+                m.update(out.get("model"), **batch)
             v = out["loss"].float().mean()
             total = v if total is None else total + v
             n += 1
@@ -221,7 +223,8 @@ class TrainLoop:
                 t = t / dist.get_world_size()
             res["eval/total_loss"] = float(t)
         for k, m in self.metrics.items():
-            res[f"eval/{k}"] = float(m.compute())
+            for key, value in m.compute().items():
+                res[f"eval/{k}_{key}" if k else f"eval/{key}"] = float(value)
         self.eval_seconds += time.perf_counter() - t0
         if self.tracker is not None and res:
             self.tracker.log(res, self.global_step)
@@ -230,7 +233,8 @@ class TrainLoop:
 
     def _maybe_eval(self, *, is_final: bool = False) -> None:
         c = self.config
-        due = is_final or (math.isfinite(c.num_steps_eval) and self.global_step > 0 and self.global_step % int(c.num_steps_eval) == 0)
+        due = is_final or (math.isfinite(c.num_steps_eval) and c.num_steps_eval > 0 and self.global_step > 0
+                           and self.global_step % int(c.num_steps_eval) == 0)  # <= 0: only the final eval
         if due:
             self.eval()
 
@@ -244,13 +248,23 @@ class TrainLoop:
         finally:
             self._cleanup()
 
+    def _train_elapsed(self) -> float:
+        """Seconds the ``train`` time limit counts (a step with its own budget clock overrides this)."""
+        return self.train_seconds
+
+    def _on_batch_ready(self, fetch_time: float) -> None:
+        """Called with the seconds spent fetching each training batch (no-op by default)."""
+        del fetch_time
+
     def train(self) -> dict[str, float]:
         c = self.config
         it = iter(self.dataset.train_dataloader())
         window_t0 = time.perf_counter()
         while self.global_step < c.max_steps and self.epoch < c.max_epochs:
             try:
+                fetch_t0 = time.perf_counter()
                 batch = next(it)
+                self._on_batch_ready(time.perf_counter() - fetch_t0)
             except StopIteration:
                 self.epoch += 1
                 self.step.on_epoch_end()
