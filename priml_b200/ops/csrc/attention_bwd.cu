@@ -233,8 +233,8 @@ __global__ void __launch_bounds__(320, 1)
       const int st = i % NS;
       const int q0 = (qt_lo + i % nq) * kLT;
       // Acquire the lse / delta vectors (bulk copies or the producer's plain stores).
-      if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[i & 1], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t tS = tmem + lane_off + (i & 1) * kLT;
       const uint32_t tP = tmem + lane_off + 128 + (i & 1) * kLT;
@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[i & 1]);
     }
-    if (ok && n_steps > 0) ok = mbar_wait(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
+    if (ok && n_steps > 0) ok = mbar_wait_warp(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
     tc_fence_after();
     // TMEM loads are warp-collective: every lane executes them; only stores are predicated.
     const bool row_ok = key < p.T;
@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int k0 = (kt_lo + j) * kLT + c0;  // first key of this warp's half
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t tS = tmem + lane_off + (j & 1) * kLT;
       const uint32_t tP = tmem + lane_off + 128 + (j & 1) * kLT;
@@ -516,7 +516,7 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[j & 1]);
     }
-    if (ok && n_tiles > 0) ok = mbar_wait(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
+    if (ok && n_tiles > 0) ok = mbar_wait_warp(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
     tc_fence_after();
     __nv_bfloat16* dqr = static_cast<__nv_bfloat16*>(p.dq) + b * p.dq_sb + static_cast<long long>(q) * p.dq_ss + h * p.dq_sh;
 #pragma unroll
@@ -758,7 +758,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < n_steps; ++i) {
       const int h = hk * g + i / nq;
       const int q0 = (qt_lo + i % nq) * kLT;
-      if (!mbar_wait(dq_full, i & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(dq_full, i & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
       tmem_ld_32x32b_x32(tdQ + lane_off, v0);
@@ -795,7 +795,7 @@ __global__ void __launch_bounds__(384, 1)
     const int key = k0 + kr;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = p.scale_log2;
-    bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutEpilogue, abort_flag);
+    bool ok = mbar_wait_warp(kv_full, 0, p.status, kTimeoutEpilogue, abort_flag);
     {
       // Row kr of K (group 0) or V (group 1): eight swizzled 16-byte chunks -> 32 TMEM columns.
       const uint8_t* src = (grp == 0 ? sK : sV) + kr * 128;
@@ -817,8 +817,8 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = grp; i < n_steps && ok; i += 2) {
       const int st = i % NS;
       const int q0 = (qt_lo + i % nq) * kLT;
-      if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(&s_full[grp], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[grp], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t tS = tmem + lane_off + grp * kLT;
       const uint32_t tP = tS + 128;
@@ -890,7 +890,7 @@ __global__ void __launch_bounds__(384, 1)
       if (lane == 0) mbar_arrive(&p_ready[grp]);
     }
     const int half = grp;  // epilogue: group g writes d columns [32 g, 32 g + 32)
-    if (ok && n_steps > 0) ok = mbar_wait(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
+    if (ok && n_steps > 0) ok = mbar_wait_warp(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
     tc_fence_after();
     // TMEM loads are warp-collective: every lane executes them; only stores are predicated.
     const bool row_ok = key < p.T;

@@ -39,7 +39,21 @@ struct AttnParams {
   void* dv;
   long long dk_sb, dk_ss, dk_sh;
   int* status;
+  int* trace;  // optional progress record, 8 ints per CTA (stage, SM, producer / MMA / softmax tile), for diagnosis
 };
+
+__device__ __forceinline__ void trace_put(const AttnParams& p, int slot, int value) {
+  if (p.trace != nullptr) {
+    reinterpret_cast<volatile int*>(p.trace)[blockIdx.x * 8 + slot] = value;
+    __threadfence_system();
+  }
+}
+
+__device__ __forceinline__ int sm_id() {
+  int id;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
+  return id;
+}
 
 // Inclusive key range [lo, hi] visible to query rows [q0, q0 + rows).
 __device__ __forceinline__ void key_range(const AttnParams& p, int q0, int rows, int& lo, int& hi) {

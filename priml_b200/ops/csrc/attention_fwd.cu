@@ -75,6 +75,8 @@ __global__ void __launch_bounds__(192, 2)
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
+    trace_put(p, 0, 1);
+    trace_put(p, 1, sm_id());
     mbar_init(q_full, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(&k_full[s], 1);
@@ -99,6 +101,7 @@ __global__ void __launch_bounds__(192, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) trace_put(p, 0, 2);
   const uint32_t tmem = *tmem_slot;
   const uint32_t tO = tmem + 2 * kKT;  // S buffers at cols [0, 64) and [64, 128); O at [128, 128 + D)
 
@@ -111,15 +114,17 @@ __global__ void __launch_bounds__(192, 2)
     uint32_t ph = 0;
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int k0 = (kt_lo + j) * kKT;
-      if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; trace_put(p, 5, 1000 + j); break; }
       mbar_arrive_expect_tx(&k_full[st], SM::kKVBytes);
       load_tile(sK + st * SM::kKVBytes, &tmK, &k_full[st], hk * D, k0, b, D, kKChunk);
-      if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; trace_put(p, 5, 2000 + j); break; }
       mbar_arrive_expect_tx(&v_full[st], SM::kKVBytes);
       load_tile(sV + st * SM::kKVBytes, &tmV, &v_full[st], hk * D, k0, b, D, kKChunk);
       if (++st == NS) { st = 0; ph ^= 1u; }
+      trace_put(p, 2, j + 1);
     }
     if (!ok) mbar_wait(q_full, 0, p.status, kTimeoutDrain, nullptr);
+    trace_put(p, 2, 100 + (ok ? 1 : 0));
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- MMA
     constexpr uint32_t idesc_s = make_idesc_bf16(128, kKT, false, false);
@@ -130,7 +135,7 @@ __global__ void __launch_bounds__(192, 2)
     auto issue_s = [&](int j) -> bool {
       const int st = j % NS;
       const uint32_t ph = static_cast<uint32_t>((j / NS) & 1);
-      if (!mbar_wait(&k_full[st], ph, p.status, kTimeoutMma, abort_flag)) return false;
+      if (!mbar_wait(&k_full[st], ph, p.status, kTimeoutMma, abort_flag)) { trace_put(p, 6, 1000 + j); return false; }
       tc_fence_after();
       const uint32_t k_base = smem_u32(sK + st * SM::kKVBytes);
       const uint32_t tS = tmem + (j & 1) * kKT;
@@ -144,10 +149,10 @@ __global__ void __launch_bounds__(192, 2)
     if (ok && n_tiles > 0) ok = issue_s(0);
     for (int j = 0; j < n_tiles && ok; ++j) {
       if (j + 1 < n_tiles && !(ok = issue_s(j + 1))) break;
-      if (!mbar_wait(&p_ready[j & 1], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&p_ready[j & 1], (j >> 1) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; trace_put(p, 6, 2000 + j); break; }
       tc_fence_after();
       const int st = j % NS;
-      if (!mbar_wait(&v_full[st], (j / NS) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&v_full[st], (j / NS) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; trace_put(p, 6, 3000 + j); break; }
       tc_fence_after();
       const uint32_t v_base = smem_u32(sV + st * SM::kKVBytes);
       const uint32_t tP = tmem + (j & 1) * kKT;
@@ -157,8 +162,10 @@ __global__ void __launch_bounds__(192, 2)
       umma_commit(&v_empty[st]);
       umma_commit(pv_done);
       // P_j sits in score buffer j&1, which S_{j+2} overwrites next iteration.
-      if (!mbar_wait(pv_done, j & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(pv_done, j & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; trace_put(p, 6, 4000 + j); break; }
+      trace_put(p, 3, j + 1);
     }
+    trace_put(p, 3, 100 + (ok ? 1 : 0));
     umma_commit(o_final);
     umma_commit(drain);
     mbar_wait(drain, 0, p.status, kTimeoutDrain, nullptr);
@@ -174,7 +181,7 @@ __global__ void __launch_bounds__(192, 2)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int k0 = (kt_lo + j) * kKT;
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; if (lane == 0) trace_put(p, 7, 1000 + 100 * warp + j); break; }
       tc_fence_after();
       const uint32_t tS = tmem + lane_off + (j & 1) * kKT;
       uint32_t v[64];
@@ -195,25 +202,28 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < 64; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
       }
       const float mxs = mx * sl2;  // scale > 0: max commutes with scaling
-      if (mxs > m + kRescaleThreshold) {
-        if (j > 0 && m != -INFINITY) {
-          // O holds P V of earlier tiles: wait until the last of them landed.
-          if (!mbar_wait(pv_done, (j - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const float f = fast_exp2(m - mxs);
-          l *= f;
+      // Rows move their running max independently, but rescaling O uses warp-collective
+      // tcgen05.ld / st: the warp rescales together whenever any of its rows must, each
+      // row by its own factor (1 for rows whose max did not move).
+      const bool grow = mxs > m + kRescaleThreshold;
+      const bool scale_o = grow && j > 0 && m != -INFINITY;
+      if (__any_sync(0xffffffffu, scale_o)) {
+        // O holds P V of earlier tiles: wait until the last of them landed.
+        if (!mbar_wait_warp(pv_done, (j - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; if (lane == 0) trace_put(p, 7, 2000 + 100 * warp + j); break; }
+        tc_fence_after();
+        const float f = scale_o ? fast_exp2(m - mxs) : 1.f;
+        l *= f;
 #pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld_32x32b_x16(tO + lane_off + c * 16, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld_32x32b_x16(tO + lane_off + c * 16, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st_32x32b_x16(tO + lane_off + c * 16, o);
-          }
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st_32x32b_x16(tO + lane_off + c * 16, o);
         }
-        m = mxs;
       }
+      if (grow) m = mxs;
       const float neg_mu = m == -INFINITY ? 0.f : -m;
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
@@ -234,8 +244,10 @@ __global__ void __launch_bounds__(192, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[j & 1]);
+      if (threadIdx.x == 64) trace_put(p, 4, j + 1);
     }
-    if (ok && n_tiles > 0) ok = mbar_wait(o_final, 0, p.status, kTimeoutEpilogue, abort_flag);
+    if (threadIdx.x == 64) trace_put(p, 4, 100 + (ok ? 1 : 0));
+    if (ok && n_tiles > 0) ok = mbar_wait_warp(o_final, 0, p.status, kTimeoutEpilogue, abort_flag);
     tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + b * p.o_sb + static_cast<long long>(q) * p.o_ss + h * p.o_sh;
@@ -267,17 +279,20 @@ __global__ void __launch_bounds__(192, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) trace_put(p, 0, 3);
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem, 256);
+    if (lane == 0) trace_put(p, 0, 4);
   }
 }
 
 }  // namespace
 
 void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, float* lse, int H,
-              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream) {
+              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream, int* trace) {
   AttnParams p{};
+  p.trace = trace;
   p.B = q.batch;
   p.S = q.seq;
   p.T = k.seq;

@@ -398,7 +398,7 @@ pb::AttnTensor attn_view(const Tensor& t, const char* name) {
 
 // (o [B,S,H,D] bf16, lse [B,H,S] fp32)
 std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, double scale, bool causal,
-                             int64_t window) {
+                             int64_t window, const c10::optional<Tensor>& trace) {
   const int D = q.size(3), H = q.size(2), Hkv = k.size(2);
   PB_CHECK(D == 64 || D == 128, "head dim must be 64 or 128");
   PB_CHECK(v.size(3) == D && k.size(3) == D && H % Hkv == 0 && v.size(2) == Hkv, "q/k/v shapes");
@@ -410,7 +410,8 @@ std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, 
   auto lse = torch::empty({n_lse + 128}, q.options().dtype(torch::kFloat32)).narrow(0, 0, n_lse).view({q.size(0), H, q.size(1)});
   if (q.numel() == 0) return {o, lse};
   pb::attn_fwd(attn_view(q, "q"), attn_view(k, "k"), attn_view(v, "v"), attn_view(o, "o"), lse.data_ptr<float>(), H, Hkv,
-               D, static_cast<float>(scale), causal, static_cast<int>(window), status_ptr(), stream());
+               D, static_cast<float>(scale), causal, static_cast<int>(window), status_ptr(), stream(),
+               trace.has_value() ? trace->data_ptr<int>() : nullptr);
   return {o, lse};
 }
 
@@ -924,7 +925,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd", &ce_bwd);
-  m.def("attn_fwd", &attn_fwd, "flash attention forward (tcgen05)");
+  m.def("attn_fwd", &attn_fwd, "flash attention forward (tcgen05); trace: optional int32 [8 * CTAs] progress record",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("causal"), py::arg("window"),
+        py::arg("trace") = py::none());
   m.def("attn_bwd", &attn_bwd, "flash attention backward (tcgen05)");
   m.def("cast_bf16", &cast_bf16, py::arg("x"), py::arg("out") = py::none());
   m.def("read_status", &read_status, py::arg("reset") = true);

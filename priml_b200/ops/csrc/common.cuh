@@ -93,6 +93,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return true;
 }
 
+// The same wait for a whole warp that next issues warp-collective (.sync.aligned) instructions
+// such as tcgen05.ld / tcgen05.st: the lanes can disagree after a timeout (one lane's wait
+// expires just as another's completes), so the warp goes on only if every lane saw the phase,
+// and leaves together otherwise.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code,
+                                               volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, status, code, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- CTA pairs (2-CTA tcgen05)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(tile, num_m, num_n, mb, nb);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int row = mb * BM + wq * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * BN;
@@ -420,7 +420,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tile_coords(tile, num_m, num_n, mb, nb);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int row = mb * TM + 128 * static_cast<int>(rank) + wq * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TN;

@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const TileInfo t = tile_info<MODE>(tile, off, p, num_n);
       const int b = local & 1;
-      if (!mbar_wait(&tfull[b], (local >> 1) & 1, p.g.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(&tfull[b], (local >> 1) & 1, p.g.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int row = t.m0 + wq * 32 + lane;
       if (t.kb1 > t.kb0) {

@@ -95,7 +95,8 @@ struct AttnTensor {
   long long s_seq;
 };
 void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, float* lse, int H,
-              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream);
+              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream,
+              int* trace = nullptr);
 // dq_acc: optional fp32 scratch of B*H*S*D floats; with it (and D == 64) the
 // backward runs as one fused kernel that bulk-reduces dQ partials into it, and
 // `delta` must then hold 2 * (B*H*S + 128) floats.

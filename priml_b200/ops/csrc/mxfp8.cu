@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait(tfull, local & 1, p.g.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(tfull, local & 1, p.g.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int row = mb * BM + wq * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16);

@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(MODE == 0 ? 256 : 192, 1)
       const int vm = first + r % gm, nb = r / gm;
       const int mb = real_mblock(vm, bps, p.rank, p.world);
       const int b = local & 1;
-      if (!mbar_wait(&tfull[b], (local >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_warp(&tfull[b], (local >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int row = mb * TBM + wq * 32 + lane;  // < M always (M = world * m_shard, m_shard % 128 == 0)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TBN;

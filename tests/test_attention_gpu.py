@@ -66,3 +66,31 @@ def test_flash_attention_strided_v() -> None:
     q, k = q.contiguous(), k.contiguous()
     o = FlashAttnFn.apply(q, k, v, True, 1 / 8, -1)
     assert _err(o, _ref(q, k, v, True, 1 / 8, None)) < 2e-2
+
+
+@pytest.mark.parametrize("D,window", [(128, 256), (64, 256), (128, None), (64, 100)])
+def test_flash_attention_rows_rescale_independently(D: int, window) -> None:  # noqa: ANN001
+    """RMS-normalized q / k give scores of magnitude ~sqrt(D), so rows of one warp move their
+    running max at different tiles (windows make their first visible tile differ too)."""
+    from priml_b200.ops import native
+    from priml_b200.ops.attention_fn import FlashAttnFn
+
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q, k, v = (torch.randn(4, 512, 4, D, device="cuda", generator=g) for _ in range(3))
+    q = (q / q.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16).requires_grad_()
+    k = (k / k.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16).requires_grad_()
+    v = v.to(torch.bfloat16).requires_grad_()
+    scale = D**-0.5
+    o = FlashAttnFn.apply(q, k, v, True, scale, -1 if window is None else window)
+    go = torch.randn_like(o)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), go)
+    qf, kf, vf = (x.detach().float().requires_grad_() for x in (q, k, v))
+    idx = torch.arange(512, device="cuda")
+    off = idx[:, None] - idx[None, :]
+    mask = (off >= 0) & ((off <= window) if window is not None else True)
+    ref = torch.nn.functional.scaled_dot_product_attention(qf.transpose(1, 2), kf.transpose(1, 2), vf.transpose(1, 2),
+                                                           attn_mask=mask, scale=scale).transpose(1, 2)  # fmt: skip
+    rq, rk, rv = torch.autograd.grad(ref, (qf, kf, vf), go.float())
+    assert _rel(o, ref) < 2e-2
+    assert _rel(dq, rq) < 5e-2 and _rel(dk, rk) < 5e-2 and _rel(dv, rv) < 5e-2
+    assert int(native().read_status(True)) == 0
