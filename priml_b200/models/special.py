@@ -11,8 +11,8 @@ from typing import Any
 import torch
 from torch import Tensor, nn
 
-from priml_b200.config import Fig, Makeable
-from priml_b200.models.custom_types import ChannelsIn, ChannelsOut, propagate_attr
+from priml_b200.config import Fig, Makeable, copy_tree
+from priml_b200.models.custom_types import ChannelsIn, ChannelsOut, HasDepth, propagate_attr
 from priml_b200.models.linear import Linear
 
 __all__ = ["Identity", "ResidualMix", "Sequential", "Skip", "SoftCap"]
@@ -70,6 +70,8 @@ class Sequential(nn.Sequential):
         elements: list[Any] = field(default_factory=list)
         _: KW_ONLY
         channels_in: int = -1
+        repeat: int = 1
+        """Copies of ``elements`` to chain; with more than one, copy ``i`` gets ``depth = i``."""
 
         @property
         def channels_out(self) -> int:
@@ -80,6 +82,19 @@ class Sequential(nn.Sequential):
             return self.channels_in
 
         def finalize(self):  # noqa: ANN201
+            if self.repeat < 1:
+                raise ValueError(f"repeat must be >= 1; got {self.repeat}.")
+            if self.repeat > 1:
+                base = self.elements if isinstance(self.elements, list) else [self.elements]
+                flat = []
+                for i in range(self.repeat):
+                    for e in base:
+                        e = copy_tree(e)
+                        if isinstance(e, HasDepth):
+                            e.depth = i
+                        flat.append(e)
+                self.elements = flat
+                self.repeat = 1
             c = self.channels_in
             for e in self.elements:
                 if c != -1:

@@ -77,6 +77,13 @@ class SignSGD(Optimizer):
     With ``aggregate_distributed`` and more than one rank, rank-local gradient
     rows are all-gathered and summed before the sign (the reference's sparse
     distributed path, ``priml/optimizers/sign_sgd.py:220-349``).
+
+    A group flagged ``{"sparse_embedding": True}`` holds exactly three tensors
+    of a sparse embedding: the full ``[N, D]`` table (a buffer), the ``[B, D]``
+    gradient leaf holding the batch's rows, and the ``[B]`` row ids. Only the
+    rows named by the ids (summed over duplicates and, when aggregating, over
+    ranks) are read, decayed and written back; the table never has a dense
+    gradient (``priml/optimizers/sign_sgd.py:98-134``).
     """
 
     class Config(Fig["Callable[..., SignSGD]"]):
@@ -103,6 +110,11 @@ class SignSGD(Optimizer):
                 loss = closure()
         for g in self.param_groups:
             lr, wd = g["lr"], g["weight_decay"]
+            if g.get("sparse_embedding", False):
+                grad, ids, table = _sparse_parts(g["params"])
+                if grad is not None:
+                    _sparse_row_step(grad, ids, table, lr=lr, weight_decay=wd, aggregate=self.aggregate_distributed)
+                continue
             for p in g["params"]:
                 grad = p.grad
                 if grad is None:
@@ -117,6 +129,44 @@ class SignSGD(Optimizer):
                         p.mul_(1.0 - lr * wd)
                 p.add_(torch.sign(grad), alpha=-lr)
         return loss
+
+
+    @torch.no_grad()
+    def step_sparse_embedding(self, rows_grad: Tensor, row_ids: Tensor) -> None:
+        """Apply an explicit ``[B, D]`` row gradient for ``row_ids`` to every sparse-embedding group's table."""
+        for g in self.param_groups:
+            if g.get("sparse_embedding", False):
+                _, _, table = _sparse_parts(g["params"])
+                _sparse_row_step(rows_grad, row_ids, table, lr=g["lr"], weight_decay=g["weight_decay"],
+                                 aggregate=self.aggregate_distributed)  # fmt: skip
+
+
+def _sparse_parts(params: list[Tensor]) -> tuple[Tensor | None, Tensor, Tensor]:
+    """``(leaf.grad, ids, table)`` of a sparse-embedding group, told apart by role, not position."""
+    leaf = [p for p in params if p.requires_grad]
+    ids = [p for p in params if not p.requires_grad and p.ndim == 1]
+    table = [p for p in params if not p.requires_grad and p.ndim == 2]
+    if len(params) != 3 or len(leaf) != 1 or len(ids) != 1 or len(table) != 1:
+        raise ValueError("a sparse_embedding group holds [table (2-D), rows leaf (2-D, requires_grad), ids (1-D)].")
+    return leaf[0].grad, ids[0], table[0]
+
+
+def _sparse_row_step(rows_grad: Tensor, row_ids: Tensor, table: Tensor, *, lr: float, weight_decay: float,
+                     aggregate: bool) -> None:  # fmt: skip
+    if aggregate and _distributed():
+        world = dist.get_world_size()
+        all_rows = rows_grad.new_empty(world * rows_grad.shape[0], rows_grad.shape[1])
+        all_ids = row_ids.new_empty(world * row_ids.shape[0])
+        dist.all_gather_into_tensor(all_rows, rows_grad.contiguous())
+        dist.all_gather_into_tensor(all_ids, row_ids.contiguous())
+        rows_grad, row_ids = all_rows, all_ids
+    uniq, slot = torch.unique(row_ids.long(), return_inverse=True)
+    summed = rows_grad.new_zeros(uniq.numel(), rows_grad.shape[1]).index_add_(0, slot, rows_grad)
+    rows = table.index_select(0, uniq)
+    if weight_decay != 0.0:
+        rows.mul_(1.0 - lr * weight_decay)
+    rows.add_(torch.sign(summed).to(rows.dtype), alpha=-lr)
+    table.index_copy_(0, uniq, rows)
 
 
 def _gather_row_sum(grad: Tensor) -> Tensor:
