@@ -89,6 +89,34 @@ def bench_gemms(tokens: int = 16384) -> list[dict]:
             }
         )
         del a, b, c
+    # fused SwiGLU up-projections (h = silu(x Wg^T) * (x Wu^T), pre-activations kept for backward):
+    # the Llama-1B FFN and the 512-wide, K = 512 puzzle-solver FFN (384 x 81 tokens)
+    for name, m, h, k in (("up.swiglu", tokens, 8192, 2048), ("puzzle.up.swiglu", 31104, 1536, 512)):
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(2 * h, k, device="cuda", dtype=torch.bfloat16) * k**-0.5  # unit-scale pre-activations
+        hh = torch.empty(m, h, device="cuda", dtype=torch.bfloat16)
+        gu = torch.empty(m, 2 * h, device="cuda", dtype=torch.bfloat16)
+        ours = time_fn(lambda x=x, w=w, hh=hh, gu=gu: n.gemm_swiglu(x, w, hh, gu))
+        cub = time_fn(lambda x=x, w=w: torch.matmul(x, w.T))
+        flops = 2.0 * m * 2 * h * k
+        rows.append({"case": name, "M": m, "N": 2 * h, "K": k, "ours_ms": round(ours, 4),
+                     "ours_tflops": round(flops / ours / 1e9, 1),
+                     "frac_of_measured_peak": round(flops / ours / 1e9 / peak_tf, 3),
+                     "out_gb_per_s": round(m * 3 * h * 2 / ours / 1e6, 1),
+                     "cublas_ms": round(cub, 4), "speedup_vs_cublas": round(cub / ours, 3)})  # fmt: skip
+        del x, w, hh, gu
+    for name, m, nn, k in (("puzzle.qkv", 31104, 1536, 512), ("puzzle.down", 31104, 512, 1536)):
+        a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(nn, k, device="cuda", dtype=torch.bfloat16)
+        c = torch.empty(m, nn, device="cuda", dtype=torch.bfloat16)
+        ours = time_fn(lambda a=a, b=b, c=c: n.gemm(a, b, c, False, False, 0))
+        cub = time_fn(lambda a=a, b=b: torch.matmul(a, b.T))
+        flops = 2.0 * m * nn * k
+        rows.append({"case": name, "M": m, "N": nn, "K": k, "ours_ms": round(ours, 4),
+                     "ours_tflops": round(flops / ours / 1e9, 1),
+                     "frac_of_measured_peak": round(flops / ours / 1e9 / peak_tf, 3),
+                     "cublas_ms": round(cub, 4), "speedup_vs_cublas": round(cub / ours, 3)})  # fmt: skip
+        del a, b, c
     return rows
 
 
@@ -154,6 +182,7 @@ def main() -> None:
     ap.add_argument("--json", type=str, default="")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--attn-only", action="store_true")
+    ap.add_argument("--gemm-only", action="store_true")
     ap.add_argument("--profile", type=str, default="")
     ap.add_argument("--mx", action="store_true", help="MXFP8 GEMMs and quantizers only")
     args = ap.parse_args()
@@ -165,7 +194,8 @@ def main() -> None:
             print(json.dumps(r))
         return
     rows = bench_gemms(args.tokens) if not args.attn_only else []
-    rows += bench_attention()
+    if not args.gemm_only:
+        rows += bench_attention()
     for r in rows:
         print(json.dumps(r))
     if args.json:

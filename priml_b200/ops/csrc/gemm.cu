@@ -237,25 +237,135 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, i
 //     barriers of both CTAs (one commit per CTA);
 //   * both CTAs' epilogues read their own TMEM and arrive on CTA 0's `tempty`;
 //   * TMEM is allocated and freed by warp 1 of both CTAs (cta_group::2).
-constexpr int kPairStages = 7;
+// The pair kernel runs 10 warps: producer, MMA issuer and EIGHT epilogue warps. Two warps
+// share each TMEM lane quarter and split the tile's columns, so each SM sub-partition has two
+// epilogue warps to interleave (TMEM-load latency, conversion, SwiGLU math) and the epilogue
+// keeps up with the MMAs of a short-K tile (K = 512: about 2 us of tensor work per tile).
+constexpr int kPairThreads = 320;
+constexpr int kPairEpiWarps = 8;
+
+// TOUT: the epilogue stages each 32-column chunk in shared memory and writes it with a
+// bulk tensor store (bf16 / fp32) or bulk tensor reduce-add (fp32 +=), instead of one
+// 16-byte store per row and thread. A warp's 32 rows x 64 or 128 bytes leave as one
+// asynchronous copy, so the writes are full-line and run while the next chunk is loaded
+// from TMEM. One staging buffer per epilogue warp and output stream costs one or two
+// pipeline stages of shared memory.
+template <int EPI, bool TOUT>
 struct PairCfg {
+  static constexpr int kStages = !TOUT ? 7 : (EPI == 3 ? 5 : 6);
   static constexpr int kABytes = 128 * BK * 2;  // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * BK * 2;  // this CTA's 128 rows (N) of B
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kSmemBytes = kPairStages * kStageBytes + 1024 + 256;
+  // per epilogue warp: streams x (32 rows x 32 columns)
+  static constexpr int kChunkBytes = (EPI == 1 || EPI == 2) ? 4096 : 2048;
+  static constexpr int kStreams = EPI == 3 ? 3 : 1;
+  static constexpr int kStgPerWarp = TOUT ? kStreams * kChunkBytes : 0;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kPairEpiWarps * kStgPerWarp + 1024 + 256;
+  static_assert(kSmemBytes <= 232448, "pair GEMM shared memory exceeds the per-CTA limit");
 };
 
-template <bool A_MN, bool B_MN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+// TMA-store epilogue of one pair tile for this warp's 32 rows (row0 .. row0 + 31). Rows and
+// columns outside the output are clipped by the tensor maps, so no edge handling is needed.
+// Columns [c_lo, c_hi) of the accumulator (hidden units for the SwiGLU epilogue). The warp's
+// staging buffer is reused once the previous chunk's bulk stores have read it.
+template <int EPI>
+__device__ __forceinline__ void epilogue_tma_tile(uint32_t t_base, int row0, int nb, int c_lo, int c_hi,
+                                                  uint8_t* stg, int lane, const CUtensorMap* tmC,
+                                                  const CUtensorMap* tmG, const CUtensorMap* tmU) {
+  constexpr int TN = 256;
+  if constexpr (EPI == 3) {
+    const int h0 = nb * (TN / 2);
+#pragma unroll 1
+    for (int c = c_lo; c < c_hi; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(t_base + c, g);
+      tmem_ld_32x32b_x32(t_base + TN / 2 + c, u);
+      tmem_wait_ld();
+      uint32_t hv[16], gv[16], uv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        // gate / up rounded to bf16 first so forward and backward see the same values
+        const __nv_bfloat162 gb = __floats2bfloat162_rn(__uint_as_float(g[2 * j]), __uint_as_float(g[2 * j + 1]));
+        const __nv_bfloat162 ub = __floats2bfloat162_rn(__uint_as_float(u[2 * j]), __uint_as_float(u[2 * j + 1]));
+        const float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
+        const float s0 = gf.x * sigmoid_fast(gf.x), s1 = gf.y * sigmoid_fast(gf.y);
+        hv[j] = pack_bf16x2(s0 * uf.x, s1 * uf.y);
+        gv[j] = *reinterpret_cast<const uint32_t*>(&gb);
+        uv[j] = *reinterpret_cast<const uint32_t*>(&ub);
+      }
+      uint8_t* buf = stg;
+      if (lane == 0) tma_store_wait_read();  // the previous chunk's stores have read the buffer
+      __syncwarp();
+      stage_row<4>(buf + lane * 64, hv, lane);
+      stage_row<4>(buf + 2048 + lane * 64, gv, lane);
+      stage_row<4>(buf + 4096 + lane * 64, uv, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, buf, h0 + c, row0);
+        tma_store_2d(tmG, buf + 2048, h0 + c, row0);
+        tma_store_2d(tmU, buf + 4096, h0 + c, row0);
+        tma_store_commit();
+      }
+    }
+  } else if constexpr (EPI == 0) {
+#pragma unroll 1
+    for (int c = c_lo; c < c_hi; c += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_base + c, v);
+      tmem_wait_ld();
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+      uint8_t* buf = stg;
+      if (lane == 0) tma_store_wait_read();
+      __syncwarp();
+      stage_row<4>(buf + lane * 64, pk, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, buf, nb * TN + c, row0);
+        tma_store_commit();
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = c_lo; c < c_hi; c += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_base + c, v);
+      tmem_wait_ld();
+      uint8_t* buf = stg;
+      if (lane == 0) tma_store_wait_read();
+      __syncwarp();
+      stage_row<8>(buf + lane * 128, v, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (EPI == 2) {
+          tma_reduce_add_2d(tmC, buf, nb * TN + c, row0);
+        } else {
+          tma_store_2d(tmC, buf, nb * TN + c, row0);
+        }
+        tma_store_commit();
+      }
+    }
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI, bool TOUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmParams p) {
-  constexpr int S = kPairStages;
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmG,
+                     const __grid_constant__ CUtensorMap tmU, const GemmParams p) {
+  using Cfg = PairCfg<EPI, TOUT>;
+  constexpr int S = Cfg::kStages;
   constexpr int TM = 256, TN = 256;  // pair tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
-  uint8_t* smB = smem + S * PairCfg::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * PairCfg::kStageBytes);
+  uint8_t* smB = smem + S * Cfg::kABytes;
+  uint8_t* stg = smem + S * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg + kPairEpiWarps * Cfg::kStgPerWarp);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -282,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs
+      mbar_init(&tempty[b], 2 * kPairEpiWarps);  // epilogue warps of both CTAs
     }
     mbar_init(drain, 1);
     mbar_init(peer_done, 1);
@@ -290,6 +400,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if constexpr (TOUT) {
+      prefetch_tmap(&tmC);
+      if constexpr (EPI == 3) {
+        prefetch_tmap(&tmG);
+        prefetch_tmap(&tmU);
+      }
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_base_slot, 512);
@@ -318,10 +435,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * PairCfg::kStageBytes);
+        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
         const uint32_t bar = full0 + 8u * stage;
-        uint8_t* a_dst = smA + stage * PairCfg::kABytes;
-        uint8_t* b_dst = smB + stage * PairCfg::kBBytes;
+        uint8_t* a_dst = smA + stage * Cfg::kABytes;
+        uint8_t* b_dst = smB + stage * Cfg::kBBytes;
         const int k0 = kb * BK;
         if constexpr (A_MN) {
           tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
@@ -381,8 +498,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smA + stage * PairCfg::kABytes);
-          const uint32_t b_base = smem_u32(smB + stage * PairCfg::kBBytes);
+          const uint32_t a_base = smem_u32(smA + stage * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(smB + stage * Cfg::kBBytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t ad = A_MN ? make_sw128_desc(a_base + kk * 2048, BK * 128, 1024)
@@ -412,8 +529,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue (both CTAs)
-    const int wq = warp & 3;  // TMEM lane quarter this warp may access
+    const int wq = warp & 3;           // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    constexpr int kSpan = (EPI == 3 ? TN / 2 : TN) / 2;  // SwiGLU: a tile holds TN / 2 hidden units
+    const int c_lo = half * kSpan, c_hi = c_lo + kSpan;
     const uint32_t tempty0 = cluster_addr(tempty, 0);
+    uint8_t* my_stg = stg + (warp - 2) * Cfg::kStgPerWarp;
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
       int mb, nb;
@@ -422,12 +543,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_warp(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
-      const int row = mb * TM + 128 * static_cast<int>(rank) + wq * 32 + lane;
+      const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TN;
-      store_acc_row<TN, EPI>(p, t_row, row, nb);
+      if constexpr (TOUT) {
+        epilogue_tma_tile<EPI>(t_row, row0, nb, c_lo, c_hi, my_stg, lane, &tmC, &tmG, &tmU);
+      } else {
+        store_acc_row<TN, EPI>(p, t_row, row0 + lane, nb, c_lo, c_hi);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * b);
+    }
+    if constexpr (TOUT) {
+      if (lane == 0) tma_store_wait_all();  // shared staging is read and global writes are done before exit
+      __syncwarp();
     }
   }
 
@@ -441,17 +570,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
-void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, cudaStream_t stream) {
-  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+template <bool A_MN, bool B_MN, int EPI, bool TOUT>
+void launch_pair_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tg,
+                   const CUtensorMap& tu, const GemmParams& p, int num_sms, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, TOUT>;
+  using Cfg = PairCfg<EPI, TOUT>;
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmemBytes);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     configured = true;
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-  kern<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<2 * pairs, kPairThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, tg, tu, p);
+}
+
+// Output tensor maps of a TMA-store epilogue; false (and the per-row store epilogue) when the
+// output's base or row stride is not 16-byte aligned.
+bool make_out_maps(int epi, void* C, long long ldc, int M, int N, const void* aux, int swiglu_h, CUtensorMap* tc,
+                   CUtensorMap* tg, CUtensorMap* tu) {
+  const auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (!aligned(C)) return false;
+  if (epi == 0) {
+    if ((ldc * 2) % 16 != 0) return false;
+    make_tmap_2d_bf16_plain(tc, C, N, M, ldc, 32, 32);
+    return true;
+  }
+  if (epi == 1 || epi == 2) {
+    if ((ldc * 4) % 16 != 0) return false;
+    make_tmap_2d_f32(tc, C, N, M, ldc, 32, 32);
+    return true;
+  }
+  if (epi == 3) {
+    const long long H = swiglu_h;
+    if ((ldc * 2) % 16 != 0 || H % 8 != 0 || !aligned(aux)) return false;
+    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(aux);
+    make_tmap_2d_bf16_plain(tc, C, H, M, ldc, 32, 32);
+    make_tmap_2d_bf16_plain(tg, gu, H, M, 2 * H, 32, 32);
+    make_tmap_2d_bf16_plain(tu, gu + H, H, M, 2 * H, 32, 32);
+    return true;
+  }
+  return false;
+}
+
+// TMA-store epilogues are on unless PRIML_B200_GEMM_TMA_STORE=0 (kept for A/B measurements).
+bool tma_store_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("PRIML_B200_GEMM_TMA_STORE");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, cudaStream_t stream) {
+  CUtensorMap tc{}, tg{}, tu{};
+  if (tma_store_enabled() && make_out_maps(EPI, p.C, p.ldc, p.M, p.N, p.aux, p.num_n_half, &tc, &tg, &tu)) {
+    if constexpr (EPI == 4) {
+      launch_pair_k<A_MN, B_MN, EPI, false>(ta, tb, tc, tg, tu, p, num_sms, stream);
+    } else {
+      launch_pair_k<A_MN, B_MN, EPI, true>(ta, tb, tc, tg, tu, p, num_sms, stream);
+    }
+  } else {
+    launch_pair_k<A_MN, B_MN, EPI, false>(ta, tb, tc, tg, tu, p, num_sms, stream);
+  }
 }
 }  // namespace
 

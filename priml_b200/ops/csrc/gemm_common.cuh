@@ -41,9 +41,35 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   nb = r / gm;
 }
 
-// Store one accumulator row slice (this thread's TMEM lane) of output tile column block `nb`.
+// 1 / (1 + e^-x) with the hardware exponential and reciprocal approximations. Large negative
+// x gives an infinite denominator and a zero result, never the slow path of an IEEE divide.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// Write this lane's row of NCH 16-byte chunks (`words` = 4 * NCH 32-bit values) into a
+// dense row-major staging tile whose rows are NCH * 16 bytes apart. The chunk order is
+// rotated per lane (chunk i ^ s at step i) so that the eight lanes of one 128-bit store
+// phase hit distinct banks; the layout in memory is the plain row-major one.
+template <int NCH>
+__device__ __forceinline__ void stage_row(uint8_t* row_ptr, const uint32_t (&words)[4 * NCH], int lane) {
+  const int s = NCH == 8 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int c = i ^ s;
+    uint4 v = make_uint4(words[0], words[1], words[2], words[3]);
+#pragma unroll
+    for (int k = 1; k < NCH; ++k) {
+      if (c == k) v = make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+    }
+    *reinterpret_cast<uint4*>(row_ptr + c * 16) = v;
+  }
+}
+
+// Store one accumulator row slice (this thread's TMEM lane) of output tile column block `nb`,
+// accumulator columns [c_lo, c_hi) (hidden units [c_lo, c_hi) of the tile for the SwiGLU
+// epilogues 3 and 4; c_hi < 0 means the whole tile).
 template <int BN, int EPI>
-__device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_row, int row, int nb) {
+__device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_row, int row, int nb, int c_lo = 0,
+                                              int c_hi = -1) {
   const bool row_ok = row < p.M;
   if constexpr (EPI == 3) {
     const int H = p.num_n_half;
@@ -51,8 +77,9 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
     __nv_bfloat16* hout = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
     __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(p.aux)) +
                         static_cast<long long>(row) * (2LL * H);
+    if (c_hi < 0) c_hi = BN / 2;
 #pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 32) {
+    for (int c = c_lo; c < c_hi; c += 32) {
       uint32_t g[32], u[32];
       tmem_ld_32x32b_x32(t_row + c, g);
       tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
@@ -68,7 +95,7 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
           const __nv_bfloat162 gb = __floats2bfloat162_rn(g0, g1);
           const __nv_bfloat162 ub = __floats2bfloat162_rn(u0, u1);
           const float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
-          const float s0 = gf.x / (1.f + __expf(-gf.x)), s1 = gf.y / (1.f + __expf(-gf.y));
+          const float s0 = gf.x * sigmoid_fast(gf.x), s1 = gf.y * sigmoid_fast(gf.y);
           hv[j] = pack_bf16x2(s0 * uf.x, s1 * uf.y);
           gv[j] = *reinterpret_cast<const uint32_t*>(&gb);
           uv[j] = *reinterpret_cast<const uint32_t*>(&ub);
@@ -101,8 +128,9 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
     const int H = p.num_n_half;
     const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + static_cast<long long>(row) * (2LL * H);
     __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc;
+    if (c_hi < 0) c_hi = BN;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = c_lo; c < c_hi; c += 32) {
       uint32_t v[32];
       tmem_ld_32x32b_x32(t_row + c, v);
       tmem_wait_ld();
@@ -133,7 +161,7 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
         const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[j]));
         const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[j]));
         const float2 d = __bfloat1622float2(__floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
-        const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+        const float s0 = sigmoid_fast(g.x), s1 = sigmoid_fast(g.y);
         du[j] = pack_bf16x2(d.x * (g.x * s0), d.y * (g.y * s1));
         dg[j] = pack_bf16x2(d.x * u.x * s0 * (1.f + g.x * (1.f - s0)), d.y * u.y * s1 * (1.f + g.y * (1.f - s1)));
       }
@@ -153,8 +181,9 @@ __device__ __forceinline__ void store_acc_row(const GemmParams& p, uint32_t t_ro
       }
     }
   } else {
+    if (c_hi < 0) c_hi = BN;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = c_lo; c < c_hi; c += 32) {
       uint32_t v[32];
       tmem_ld_32x32b_x32(t_row + c, v);
       tmem_wait_ld();
