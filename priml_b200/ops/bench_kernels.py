@@ -105,6 +105,21 @@ def bench_gemms(tokens: int = 16384) -> list[dict]:
                      "out_gb_per_s": round(m * 3 * h * 2 / ours / 1e6, 1),
                      "cublas_ms": round(cub, 4), "speedup_vs_cublas": round(cub / ours, 3)})  # fmt: skip
         del x, w, hh, gu
+    # fused SwiGLU backward: dgu = swiglu'(gu) * (dy @ W_down), reading gu and writing dgu ([M, 2H] each)
+    for name, m, h, c in (("down.dgrad.swiglu", tokens, 8192, 2048), ("puzzle.down.dgrad.swiglu", 31104, 1536, 512)):
+        dy = torch.randn(m, c, device="cuda", dtype=torch.bfloat16)
+        wd = torch.randn(c, h, device="cuda", dtype=torch.bfloat16) * c**-0.5
+        gu = torch.randn(m, 2 * h, device="cuda", dtype=torch.bfloat16)
+        dgu = torch.empty(m, 2 * h, device="cuda", dtype=torch.bfloat16)
+        ours = time_fn(lambda dy=dy, wd=wd, gu=gu, dgu=dgu: n.gemm_swiglu_bwd(dy, wd, gu, dgu))
+        cub = time_fn(lambda dy=dy, wd=wd: torch.matmul(dy, wd))
+        flops = 2.0 * m * h * c
+        rows.append({"case": name, "M": m, "N": h, "K": c, "ours_ms": round(ours, 4),
+                     "ours_tflops": round(flops / ours / 1e9, 1),
+                     "frac_of_measured_peak": round(flops / ours / 1e9 / peak_tf, 3),
+                     "io_gb_per_s": round(m * 4 * h * 2 / ours / 1e6, 1),
+                     "cublas_ms": round(cub, 4), "speedup_vs_cublas": round(cub / ours, 3)})  # fmt: skip
+        del dy, wd, gu, dgu
     for name, m, nn, k in (("puzzle.qkv", 31104, 1536, 512), ("puzzle.down", 31104, 512, 1536)):
         a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
         b = torch.randn(nn, k, device="cuda", dtype=torch.bfloat16)
@@ -255,6 +270,14 @@ def profile_case(name: str) -> None:
         qb, sb = n.mx_quantize(b, False)
         for _ in range(3):
             n.mx_gemm(qa, sa, qb, sb, c, 0)
+    elif name == "swiglu_bwd":
+        # the SwiGLU-backward GEMM of a 512-wide FFN over 16384 tokens (K = 512: epilogue-bound)
+        dy = torch.randn(16384, 512, device="cuda", dtype=torch.bfloat16)
+        wd = torch.randn(512, 1536, device="cuda", dtype=torch.bfloat16) * 512**-0.5
+        gu = torch.randn(16384, 3072, device="cuda", dtype=torch.bfloat16)
+        dgu = torch.empty(16384, 3072, device="cuda", dtype=torch.bfloat16)
+        for _ in range(3):
+            n.gemm_swiglu_bwd(dy, wd, gu, dgu)
     elif name in ("attn_fwd", "attn_bwd"):
         q = torch.randn(1, 4096, 32, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         k = torch.randn(1, 4096, 8, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)

@@ -258,7 +258,7 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   // per epilogue warp: streams x (32 rows x 32 columns)
   static constexpr int kChunkBytes = (EPI == 1 || EPI == 2) ? 4096 : 2048;
-  static constexpr int kStreams = EPI == 3 ? 3 : 1;
+  static constexpr int kStreams = EPI == 3 ? 3 : (EPI == 4 ? 2 : 1);
   static constexpr int kStgPerWarp = TOUT ? kStreams * kChunkBytes : 0;
   static constexpr int kSmemBytes = kStages * kStageBytes + kPairEpiWarps * kStgPerWarp + 1024 + 256;
   static_assert(kSmemBytes <= 232448, "pair GEMM shared memory exceeds the per-CTA limit");
@@ -352,6 +352,77 @@ __device__ __forceinline__ void epilogue_tma_tile(uint32_t t_base, int row0, int
   }
 }
 
+// SwiGLU backward epilogue: the saved pre-activations [gate | up] of a 32 x 32 chunk are
+// fetched with coalesced 16-byte loads (lane l: rows l / 4 + 8 j, column group l % 4) one
+// chunk ahead, passed through the warp's staging buffer to the lane that owns each row, and
+// combined with dh from TMEM; dgate / dup leave through the same buffer as bulk tensor stores.
+__device__ __forceinline__ void swiglu_bwd_prefetch(const GemmParams& p, int row0, int col, int lane, uint4 (&g)[4],
+                                                    uint4 (&u)[4]) {
+  const int H = p.num_n_half;
+  const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux);
+  const int cc = col + (lane & 3) * 8;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = row0 + (lane >> 2) + 8 * j;
+    if (r < p.M && cc < H) {
+      const __nv_bfloat16* src = gu + static_cast<long long>(r) * (2LL * H) + cc;
+      g[j] = __ldg(reinterpret_cast<const uint4*>(src));
+      u[j] = __ldg(reinterpret_cast<const uint4*>(src + H));
+    } else {
+      g[j] = make_uint4(0u, 0u, 0u, 0u);
+      u[j] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+__device__ __forceinline__ void epilogue_swiglu_bwd_tile(const GemmParams& p, uint32_t t_base, int row0, int nb,
+                                                         int c_lo, int c_hi, uint8_t* stg, int lane, uint4 (&g)[4],
+                                                         uint4 (&u)[4], const CUtensorMap* tmDG,
+                                                         const CUtensorMap* tmDU) {
+  constexpr int TN = 256;
+#pragma unroll 1
+  for (int c = c_lo; c < c_hi; c += 32) {
+    const int col = nb * TN + c;
+    if (lane == 0) tma_store_wait_read();  // the previous chunk's stores have read the buffer
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int off = ((lane >> 2) + 8 * j) * 64 + (lane & 3) * 16;
+      *reinterpret_cast<uint4*>(stg + off) = g[j];
+      *reinterpret_cast<uint4*>(stg + 2048 + off) = u[j];
+    }
+    __syncwarp();
+    if (c + 32 < c_hi) swiglu_bwd_prefetch(p, row0, col + 32, lane, g, u);
+    uint32_t gw[16], uw[16];
+    load_row<4>(stg + lane * 64, gw, lane);
+    load_row<4>(stg + 2048 + lane * 64, uw, lane);
+    __syncwarp();
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(t_base + c, v);
+    tmem_wait_ld();
+    uint32_t dg[16], du[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[j]));
+      const float2 uf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[j]));
+      // dh rounded to bf16 first, as the unfused path stores it
+      const float2 d = __bfloat1622float2(__floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
+      const float s0 = sigmoid_fast(gf.x), s1 = sigmoid_fast(gf.y);
+      du[j] = pack_bf16x2(d.x * (gf.x * s0), d.y * (gf.y * s1));
+      dg[j] = pack_bf16x2(d.x * uf.x * s0 * (1.f + gf.x * (1.f - s0)), d.y * uf.y * s1 * (1.f + gf.y * (1.f - s1)));
+    }
+    stage_row<4>(stg + lane * 64, dg, lane);
+    stage_row<4>(stg + 2048 + lane * 64, du, lane);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmDG, stg, col, row0);
+      tma_store_2d(tmDU, stg + 2048, col, row0);
+      tma_store_commit();
+    }
+  }
+}
+
 template <bool A_MN, bool B_MN, int EPI, bool TOUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -402,10 +473,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     prefetch_tmap(&tmB);
     if constexpr (TOUT) {
       prefetch_tmap(&tmC);
-      if constexpr (EPI == 3) {
-        prefetch_tmap(&tmG);
-        prefetch_tmap(&tmU);
-      }
+      if constexpr (EPI == 3 || EPI == 4) prefetch_tmap(&tmG);
+      if constexpr (EPI == 3) prefetch_tmap(&tmU);
     }
   }
   if (warp == 1) {
@@ -541,11 +610,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       tile_coords(tile, num_m, num_n, mb, nb);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
+      [[maybe_unused]] uint4 pre_g[4], pre_u[4];
+      if constexpr (TOUT && EPI == 4) swiglu_bwd_prefetch(p, row0, nb * TN + c_lo, lane, pre_g, pre_u);
       if (!mbar_wait_warp(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
-      const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TN;
-      if constexpr (TOUT) {
+      if constexpr (TOUT && EPI == 4) {
+        epilogue_swiglu_bwd_tile(p, t_row, row0, nb, c_lo, c_hi, my_stg, lane, pre_g, pre_u, &tmC, &tmG);
+      } else if constexpr (TOUT) {
         epilogue_tma_tile<EPI>(t_row, row0, nb, c_lo, c_hi, my_stg, lane, &tmC, &tmG, &tmU);
       } else {
         store_acc_row<TN, EPI>(p, t_row, row0 + lane, nb, c_lo, c_hi);
@@ -610,6 +683,15 @@ bool make_out_maps(int epi, void* C, long long ldc, int M, int N, const void* au
     make_tmap_2d_bf16_plain(tu, gu + H, H, M, 2 * H, 32, 32);
     return true;
   }
+  if (epi == 4) {
+    // C = dgu [M, 2H]: dgate and dup views; aux = gu read with 16-byte loads
+    const long long H = swiglu_h;
+    if ((ldc * 2) % 16 != 0 || H % 8 != 0 || !aligned(aux)) return false;
+    __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(C);
+    make_tmap_2d_bf16_plain(tc, dgu, H, M, ldc, 32, 32);
+    make_tmap_2d_bf16_plain(tg, dgu + H, H, M, ldc, 32, 32);
+    return true;
+  }
   return false;
 }
 
@@ -626,11 +708,7 @@ template <bool A_MN, bool B_MN, int EPI>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, cudaStream_t stream) {
   CUtensorMap tc{}, tg{}, tu{};
   if (tma_store_enabled() && make_out_maps(EPI, p.C, p.ldc, p.M, p.N, p.aux, p.num_n_half, &tc, &tg, &tu)) {
-    if constexpr (EPI == 4) {
-      launch_pair_k<A_MN, B_MN, EPI, false>(ta, tb, tc, tg, tu, p, num_sms, stream);
-    } else {
-      launch_pair_k<A_MN, B_MN, EPI, true>(ta, tb, tc, tg, tu, p, num_sms, stream);
-    }
+    launch_pair_k<A_MN, B_MN, EPI, true>(ta, tb, tc, tg, tu, p, num_sms, stream);
   } else {
     launch_pair_k<A_MN, B_MN, EPI, false>(ta, tb, tc, tg, tu, p, num_sms, stream);
   }

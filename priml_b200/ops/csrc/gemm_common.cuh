@@ -64,6 +64,27 @@ __device__ __forceinline__ void stage_row(uint8_t* row_ptr, const uint32_t (&wor
   }
 }
 
+// Read this lane's row of NCH 16-byte chunks back from a dense row-major staging tile, in
+// the same bank-staggered order as stage_row.
+template <int NCH>
+__device__ __forceinline__ void load_row(const uint8_t* row_ptr, uint32_t (&words)[4 * NCH], int lane) {
+  const int s = NCH == 8 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int c = i ^ s;
+    const uint4 v = *reinterpret_cast<const uint4*>(row_ptr + c * 16);
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      if (c == k) {
+        words[4 * k] = v.x;
+        words[4 * k + 1] = v.y;
+        words[4 * k + 2] = v.z;
+        words[4 * k + 3] = v.w;
+      }
+    }
+  }
+}
+
 // Store one accumulator row slice (this thread's TMEM lane) of output tile column block `nb`,
 // accumulator columns [c_lo, c_hi) (hidden units [c_lo, c_hi) of the tile for the SwiGLU
 // epilogues 3 and 4; c_hi < 0 means the whole tile).
