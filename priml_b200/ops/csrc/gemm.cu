@@ -296,9 +296,9 @@ __device__ __forceinline__ void epilogue_tma_tile(uint32_t t_base, int row0, int
       uint8_t* buf = stg;
       if (lane == 0) tma_store_wait_read();  // the previous chunk's stores have read the buffer
       __syncwarp();
-      stage_row<4>(buf + lane * 64, hv, lane);
-      stage_row<4>(buf + 2048 + lane * 64, gv, lane);
-      stage_row<4>(buf + 4096 + lane * 64, uv, lane);
+      stage_row<4>(buf, lane, hv);
+      stage_row<4>(buf + 2048, lane, gv);
+      stage_row<4>(buf + 4096, lane, uv);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -320,7 +320,7 @@ __device__ __forceinline__ void epilogue_tma_tile(uint32_t t_base, int row0, int
       uint8_t* buf = stg;
       if (lane == 0) tma_store_wait_read();
       __syncwarp();
-      stage_row<4>(buf + lane * 64, pk, lane);
+      stage_row<4>(buf, lane, pk);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -337,7 +337,7 @@ __device__ __forceinline__ void epilogue_tma_tile(uint32_t t_base, int row0, int
       uint8_t* buf = stg;
       if (lane == 0) tma_store_wait_read();
       __syncwarp();
-      stage_row<8>(buf + lane * 128, v, lane);
+      stage_row<8>(buf, lane, v);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -387,15 +387,16 @@ __device__ __forceinline__ void epilogue_swiglu_bwd_tile(const GemmParams& p, ui
     __syncwarp();
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int off = ((lane >> 2) + 8 * j) * 64 + (lane & 3) * 16;
+      const int r = (lane >> 2) + 8 * j;
+      const int off = r * 64 + swz_chunk<4>(r, lane & 3) * 16;
       *reinterpret_cast<uint4*>(stg + off) = g[j];
       *reinterpret_cast<uint4*>(stg + 2048 + off) = u[j];
     }
     __syncwarp();
     if (c + 32 < c_hi) swiglu_bwd_prefetch(p, row0, col + 32, lane, g, u);
     uint32_t gw[16], uw[16];
-    load_row<4>(stg + lane * 64, gw, lane);
-    load_row<4>(stg + 2048 + lane * 64, uw, lane);
+    load_row<4>(stg, lane, gw);
+    load_row<4>(stg + 2048, lane, uw);
     __syncwarp();
     uint32_t v[32];
     tmem_ld_32x32b_x32(t_base + c, v);
@@ -411,8 +412,8 @@ __device__ __forceinline__ void epilogue_swiglu_bwd_tile(const GemmParams& p, ui
       du[j] = pack_bf16x2(d.x * (gf.x * s0), d.y * (gf.y * s1));
       dg[j] = pack_bf16x2(d.x * uf.x * s0 * (1.f + gf.x * (1.f - s0)), d.y * uf.y * s1 * (1.f + gf.y * (1.f - s1)));
     }
-    stage_row<4>(stg + lane * 64, dg, lane);
-    stage_row<4>(stg + 2048 + lane * 64, du, lane);
+    stage_row<4>(stg, lane, dg);
+    stage_row<4>(stg + 2048, lane, du);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
@@ -658,29 +659,30 @@ void launch_pair_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   kern<<<2 * pairs, kPairThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, tg, tu, p);
 }
 
-// Output tensor maps of a TMA-store epilogue; false (and the per-row store epilogue) when the
-// output's base or row stride is not 16-byte aligned.
+// Output tensor maps of a TMA-store epilogue (box 32 x 32, swizzled like the staging tiles:
+// 64-byte swizzle for bf16, 128-byte for fp32); false (and the per-row store epilogue) when
+// the output's base or row stride is not 16-byte aligned.
 bool make_out_maps(int epi, void* C, long long ldc, int M, int N, const void* aux, int swiglu_h, CUtensorMap* tc,
                    CUtensorMap* tg, CUtensorMap* tu) {
   const auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!aligned(C)) return false;
   if (epi == 0) {
     if ((ldc * 2) % 16 != 0) return false;
-    make_tmap_2d_bf16_plain(tc, C, N, M, ldc, 32, 32);
+    make_tmap_2d_bf16_sw64(tc, C, N, M, ldc, 32, 32);
     return true;
   }
   if (epi == 1 || epi == 2) {
     if ((ldc * 4) % 16 != 0) return false;
-    make_tmap_2d_f32(tc, C, N, M, ldc, 32, 32);
+    make_tmap_2d_f32_sw128(tc, C, N, M, ldc, 32, 32);
     return true;
   }
   if (epi == 3) {
     const long long H = swiglu_h;
     if ((ldc * 2) % 16 != 0 || H % 8 != 0 || !aligned(aux)) return false;
     const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(aux);
-    make_tmap_2d_bf16_plain(tc, C, H, M, ldc, 32, 32);
-    make_tmap_2d_bf16_plain(tg, gu, H, M, 2 * H, 32, 32);
-    make_tmap_2d_bf16_plain(tu, gu + H, H, M, 2 * H, 32, 32);
+    make_tmap_2d_bf16_sw64(tc, C, H, M, ldc, 32, 32);
+    make_tmap_2d_bf16_sw64(tg, gu, H, M, 2 * H, 32, 32);
+    make_tmap_2d_bf16_sw64(tu, gu + H, H, M, 2 * H, 32, 32);
     return true;
   }
   if (epi == 4) {
@@ -688,8 +690,8 @@ bool make_out_maps(int epi, void* C, long long ldc, int M, int N, const void* au
     const long long H = swiglu_h;
     if ((ldc * 2) % 16 != 0 || H % 8 != 0 || !aligned(aux)) return false;
     __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(C);
-    make_tmap_2d_bf16_plain(tc, dgu, H, M, ldc, 32, 32);
-    make_tmap_2d_bf16_plain(tg, dgu + H, H, M, ldc, 32, 32);
+    make_tmap_2d_bf16_sw64(tc, dgu, H, M, ldc, 32, 32);
+    make_tmap_2d_bf16_sw64(tg, dgu + H, H, M, ldc, 32, 32);
     return true;
   }
   return false;

@@ -45,43 +45,37 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 // x gives an infinite denominator and a zero result, never the slow path of an IEEE divide.
 __device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
-// Write this lane's row of NCH 16-byte chunks (`words` = 4 * NCH 32-bit values) into a
-// dense row-major staging tile whose rows are NCH * 16 bytes apart. The chunk order is
-// rotated per lane (chunk i ^ s at step i) so that the eight lanes of one 128-bit store
-// phase hit distinct banks; the layout in memory is the plain row-major one.
+// Epilogue staging tiles are 32 rows of NCH 16-byte chunks (NCH = 4: 64-byte bf16 rows,
+// NCH = 8: 128-byte fp32 rows) in the layout of the tensor maps' 64-byte / 128-byte swizzle:
+// chunk k of row r sits at chunk position k ^ ((r >> 1) & 3) (NCH = 4) or k ^ (r & 7)
+// (NCH = 8), i.e. address bits [4, 4 + log2 NCH) XOR bits [7, 7 + log2 NCH) of the offset.
+// Eight lanes writing or reading their own rows in one 128-bit phase then hit distinct banks,
+// and the data index stays a compile-time constant (only the address depends on the lane).
 template <int NCH>
-__device__ __forceinline__ void stage_row(uint8_t* row_ptr, const uint32_t (&words)[4 * NCH], int lane) {
-  const int s = NCH == 8 ? (lane & 7) : ((lane >> 1) & 3);
+__device__ __forceinline__ int swz_chunk(int row, int k) {
+  return NCH == 8 ? (k ^ (row & 7)) : (k ^ ((row >> 1) & 3));
+}
+
+template <int NCH>
+__device__ __forceinline__ void stage_row(uint8_t* tile, int row, const uint32_t (&words)[4 * NCH]) {
+  uint8_t* row_ptr = tile + row * (16 * NCH);
 #pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const int c = i ^ s;
-    uint4 v = make_uint4(words[0], words[1], words[2], words[3]);
-#pragma unroll
-    for (int k = 1; k < NCH; ++k) {
-      if (c == k) v = make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
-    }
-    *reinterpret_cast<uint4*>(row_ptr + c * 16) = v;
+  for (int k = 0; k < NCH; ++k) {
+    *reinterpret_cast<uint4*>(row_ptr + swz_chunk<NCH>(row, k) * 16) =
+        make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
   }
 }
 
-// Read this lane's row of NCH 16-byte chunks back from a dense row-major staging tile, in
-// the same bank-staggered order as stage_row.
 template <int NCH>
-__device__ __forceinline__ void load_row(const uint8_t* row_ptr, uint32_t (&words)[4 * NCH], int lane) {
-  const int s = NCH == 8 ? (lane & 7) : ((lane >> 1) & 3);
+__device__ __forceinline__ void load_row(const uint8_t* tile, int row, uint32_t (&words)[4 * NCH]) {
+  const uint8_t* row_ptr = tile + row * (16 * NCH);
 #pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const int c = i ^ s;
-    const uint4 v = *reinterpret_cast<const uint4*>(row_ptr + c * 16);
-#pragma unroll
-    for (int k = 0; k < NCH; ++k) {
-      if (c == k) {
-        words[4 * k] = v.x;
-        words[4 * k + 1] = v.y;
-        words[4 * k + 2] = v.z;
-        words[4 * k + 3] = v.w;
-      }
-    }
+  for (int k = 0; k < NCH; ++k) {
+    const uint4 v = *reinterpret_cast<const uint4*>(row_ptr + swz_chunk<NCH>(row, k) * 16);
+    words[4 * k] = v.x;
+    words[4 * k + 1] = v.y;
+    words[4 * k + 2] = v.z;
+    words[4 * k + 3] = v.w;
   }
 }
 

@@ -69,19 +69,34 @@ void make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long inner, long
                "2d");
 }
 
-void make_tmap_2d_bf16_plain(CUtensorMap* map, const void* base, long long inner, long long outer,
-                             long long row_stride, int box_inner, int box_outer) {
+static void encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int esize, const void* base, long long inner,
+                      long long outer, long long row_stride, int box_inner, int box_outer, CUtensorMapSwizzle swz,
+                      const char* what) {
   ensure_context();
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
-  if ((row_stride * 2) % 16 != 0) throw std::runtime_error("TMA row stride must be a multiple of 16 bytes");
+  if ((row_stride * esize) % 16 != 0) throw std::runtime_error("TMA row stride must be a multiple of 16 bytes");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * esize)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
   cuuint32_t estr[2] = {1, 1};
-  check_encode(encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-               "2d bf16 plain");
+  check_encode(encode_fn()(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+               what);
+}
+
+void make_tmap_2d_bf16_sw64(CUtensorMap* map, const void* base, long long inner, long long outer,
+                            long long row_stride, int box_inner, int box_outer) {
+  if (box_inner * 2 != 64) throw std::runtime_error("64-byte swizzle needs a 64-byte box row");
+  encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, inner, outer, row_stride, box_inner, box_outer,
+            CU_TENSOR_MAP_SWIZZLE_64B, "2d bf16 sw64");
+}
+
+void make_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, long long inner, long long outer,
+                            long long row_stride, int box_inner, int box_outer) {
+  if (box_inner * 4 != 128) throw std::runtime_error("128-byte swizzle needs a 128-byte box row");
+  encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, inner, outer, row_stride, box_inner, box_outer,
+            CU_TENSOR_MAP_SWIZZLE_128B, "2d f32 sw128");
 }
 
 void make_tmap_2d_u8(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,

@@ -15,9 +15,12 @@ int device_sm_count();
 // `row_stride` the stride (elements) between consecutive outer rows.
 void make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
                        int box_inner, int box_outer);
-// 2-D bf16 map without swizzle (dense row-major staging tiles, e.g. epilogue stores).
-void make_tmap_2d_bf16_plain(CUtensorMap* map, const void* base, long long inner, long long outer,
-                             long long row_stride, int box_inner, int box_outer);
+// 2-D maps for epilogue staging tiles: bf16 with 64-byte rows and 64-byte swizzle, fp32 with
+// 128-byte rows and 128-byte swizzle.
+void make_tmap_2d_bf16_sw64(CUtensorMap* map, const void* base, long long inner, long long outer,
+                            long long row_stride, int box_inner, int box_outer);
+void make_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, long long inner, long long outer,
+                            long long row_stride, int box_inner, int box_outer);
 // 3-D bf16 tensor map (inner, mid, outer) with element strides for mid/outer.
 // 2-D fp32 map without swizzle (bulk reduce targets).
 void make_tmap_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
