@@ -456,6 +456,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + BK - 1) / BK;
+  // Work unit u = (tile u / splits, K slice u % splits); slices accumulate through the
+  // fp32 reduce-add epilogue, so a few output tiles with a long K still fill every SM.
+  const int splits = p.splits;
+  const int num_units = num_tiles * splits;
+  const auto k_range = [&](int u, int& lo, int& hi) {
+    const int ks = u % splits;
+    lo = ks * num_kb / splits;
+    hi = (ks + 1) * num_kb / splits;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -495,12 +504,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint32_t phase = 0;
     int issued = 0;
     bool ok = true;
-    for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+    for (int u = pair; u < num_units && ok; u += num_pairs) {
+      int mb, nb, kb_lo, kb_hi;
+      tile_coords(u / splits, num_m, num_n, mb, nb);
+      k_range(u, kb_lo, kb_hi);
       const int m0 = mb * TM + 128 * static_cast<int>(rank);
       const int n0 = nb * TN + 128 * static_cast<int>(rank);
-      for (int kb = 0; kb < num_kb; ++kb) {
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutProducer, abort_flag)) {
           ok = false;
           break;
@@ -553,16 +563,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
+      for (int u = pair; u < num_units && ok; u += num_pairs, ++local) {
         const int b = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
         if (!mbar_wait(&tempty[b], acc_phase ^ 1u, p.status, kTimeoutMma, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * TN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kTimeoutMma, abort_flag)) {
             ok = false;
             break;
@@ -576,7 +588,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                      : make_sw128_desc(a_base + kk * 32, 16, 1024);
             const uint64_t bd = (B_MN && EPI != 3) ? make_sw128_desc(b_base + kk * 2048, BK * 128, 1024)
                                                    : make_sw128_desc(b_base + kk * 32, 16, 1024);
-            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+            umma_f16_pair(d_tmem, ad, bd, idesc, kb > kb_lo || kk > 0);
           }
           umma_commit_pair(&empty[stage]);
           umma_commit_pair_to(empty1 + 8u * stage);
@@ -606,9 +618,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const uint32_t tempty0 = cluster_addr(tempty, 0);
     uint8_t* my_stg = stg + (warp - 2) * Cfg::kStgPerWarp;
     int local = 0;
-    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+    for (int u = pair; u < num_units; u += num_pairs, ++local) {
       int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      tile_coords(u / splits, num_m, num_n, mb, nb);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
@@ -654,9 +666,37 @@ void launch_pair_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     configured = true;
   }
-  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
-  const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  const int units = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.splits;
+  const int pairs = units < num_sms / 2 ? units : num_sms / 2;
   kern<<<2 * pairs, kPairThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, tg, tu, p);
+}
+
+// Split-K factor for an fp32-output GEMM. A work unit costs 1/s of a full-K tile's MMAs plus
+// one tile epilogue (an fp32 reduce-add of 256 KB, modelled as 1024 / K of the MMA time), and
+// units run in waves of `pairs`: s minimizes ceil(tiles * s / pairs) * (1/s + 1024 / K) and is
+// kept only when that beats one slice by 5 % (at most 8 slices of at least 8 K blocks each).
+int choose_splits(const GemmParams& p, int num_sms) {
+  static const bool on = [] {
+    const char* e = std::getenv("PRIML_B200_GEMM_SPLITK");  // 0 disables (A/B measurements)
+    return e == nullptr || e[0] != '0';
+  }();
+  if (!on) return 1;
+  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int pairs = num_sms / 2;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const double epi = 1024.0 / static_cast<double>(p.K);
+  const auto cost = [&](int s) {
+    return static_cast<double>((tiles * s + pairs - 1) / pairs) * (1.0 / s + epi);
+  };
+  int best = 1;
+  double best_cost = cost(1);
+  for (int s = 2; s <= 8 && num_kb >= 8 * s; ++s) {
+    if (cost(s) < best_cost) {
+      best = s;
+      best_cost = cost(s);
+    }
+  }
+  return best_cost < 0.95 * cost(1) ? best : 1;
 }
 
 // Output tensor maps of a TMA-store epilogue (box 32 x 32, swizzled like the staging tiles:
@@ -707,9 +747,22 @@ bool tma_store_enabled() {
 }
 
 template <bool A_MN, bool B_MN, int EPI>
-void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, cudaStream_t stream) {
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, int num_sms, cudaStream_t stream) {
   CUtensorMap tc{}, tg{}, tu{};
+  p.splits = 1;
   if (tma_store_enabled() && make_out_maps(EPI, p.C, p.ldc, p.M, p.N, p.aux, p.num_n_half, &tc, &tg, &tu)) {
+    if constexpr (EPI == 1 || EPI == 2) {
+      const int splits = choose_splits(p, num_sms);
+      if (splits > 1) {
+        // K slices reduce-add into C: a plain store starts from zero
+        if (EPI == 1) {
+          cudaMemset2DAsync(p.C, static_cast<size_t>(p.ldc) * 4, 0, static_cast<size_t>(p.N) * 4, p.M, stream);
+        }
+        p.splits = splits;
+        launch_pair_k<A_MN, B_MN, 2, true>(ta, tb, tc, tg, tu, p, num_sms, stream);
+        return;
+      }
+    }
     launch_pair_k<A_MN, B_MN, EPI, true>(ta, tb, tc, tg, tu, p, num_sms, stream);
   } else {
     launch_pair_k<A_MN, B_MN, EPI, false>(ta, tb, tc, tg, tu, p, num_sms, stream);

@@ -29,6 +29,7 @@ struct GemmParams {
   const void* aux;       // SwiGLU: unused; residual add: [M, ldc] bf16
   int* status;
   int num_n_half;        // fused SwiGLU: H (gate/up split point in B rows)
+  int splits = 1;        // split-K factor (pair kernel, fp32 reduce-add epilogue only)
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {

@@ -23,7 +23,7 @@ def _rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
 
 
 LAYOUTS = [(False, False), (False, True), (True, False), (True, True)]
-SHAPES = [(128, 256, 64), (300, 520, 200), (1024, 2048, 512), (2048, 768, 1088), (300, 260, 96)]
+SHAPES = [(128, 256, 64), (300, 520, 200), (1024, 2048, 512), (2048, 768, 1088), (300, 260, 96), (264, 512, 8200)]
 
 
 @pytest.mark.parametrize("a_mn,b_mn", LAYOUTS)
