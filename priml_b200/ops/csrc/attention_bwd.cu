@@ -55,9 +55,10 @@ __global__ void attn_delta_kernel(const AttnParams p) {
   }
   for (int s = tpr / 2; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
   if (row < total && part == 0) {
-    const long long idx = (static_cast<long long>(b) * p.H + h) * p.S + q;
-    p.delta[idx] = acc;
-    if (p.nlse2 != nullptr) p.nlse2[idx] = -p.lse[idx] * kLog2e;
+    const long long bh = static_cast<long long>(b) * p.H + h;
+    const long long vidx = bh * p.vec_s + q;
+    p.delta[vidx] = acc;
+    if (p.nlse2 != nullptr) p.nlse2[vidx] = -p.lse[bh * p.S + q] * kLog2e;
   }
 }
 
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(320, 1)
   const int qt_hi = qhi < qlo ? qt_lo - 1 : qhi / kLT;
   const int nq = qt_hi >= qt_lo ? qt_hi - qt_lo + 1 : 0;
   const int n_steps = nq * g;  // (query head, 64-query tile) pairs
-  const bool bulk_vec = (p.S & 3) == 0;
+  const bool bulk_vec = (p.vec_s & 3) == 0;
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -621,7 +622,7 @@ __global__ void __launch_bounds__(384, 1)
   const int qt_hi = qhi < qlo ? qt_lo - 1 : qhi / kLT;
   const int nq = qt_hi >= qt_lo ? qt_hi - qt_lo + 1 : 0;
   const int n_steps = nq * g;  // (query head, 64-query tile) pairs
-  const bool bulk_vec = (p.S & 3) == 0;
+  const bool bulk_vec = (p.vec_s & 3) == 0;
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -672,7 +673,7 @@ __global__ void __launch_bounds__(384, 1)
       const int q0 = (qt_lo + i % nq) * kLT;
       if (!mbar_wait(&in_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
       float* vec = sVec + st * 2 * kLT;
-      const long long row = (static_cast<long long>(b) * p.H + h) * p.S + q0;
+      const long long row = (static_cast<long long>(b) * p.H + h) * p.vec_s + q0;
       if (bulk_vec) {
         mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes + 2 * kLT * 4);
         bulk_load(vec, p.nlse2 + row, kLT * 4, &in_full[st]);
@@ -991,8 +992,13 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   const bool fused = D == 64 && dq_acc != nullptr;
   {
     const long long rows = static_cast<long long>(p.B) * p.S * p.H;
-    // The fused kernel reads -lse * log2(e), written next to delta (delta holds 2 * (rows + 128) floats).
-    p.nlse2 = fused ? delta + rows + 128 : nullptr;
+    // The fused kernel reads delta and -lse * log2(e) in 64-row bulk copies, so their rows are
+    // padded to a multiple of 4 floats (16 bytes); delta holds 2 * (B * H * vec_s + 128) floats,
+    // zeroed when padding rows exist so that the padded queries read finite values.
+    p.vec_s = fused ? (p.S + 3) / 4 * 4 : p.S;
+    const long long n_vec = static_cast<long long>(p.B) * p.H * p.vec_s;
+    p.nlse2 = fused ? delta + n_vec + 128 : nullptr;
+    if (fused && p.vec_s != p.S) cudaMemsetAsync(delta, 0, 2 * (n_vec + 128) * sizeof(float), stream);
     const long long threads = rows * (D / 8);
     attn_delta_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p);
   }

@@ -31,6 +31,7 @@ struct AttnParams {
   float* lse;        // [B, H, S]
   float* delta;      // [B, H, S]
   float* nlse2;      // optional [B, H, S] output of the delta kernel: -lse * log2(e)
+  int vec_s;         // row stride of delta / nlse2 per (b, h): S, or S rounded up to 4 for 16-byte bulk reads
   const void* dout;  // [B, S, H, D]
   long long do_sb, do_ss, do_sh;
   void* dq;  // [B, S, H, D] bf16 out

@@ -424,8 +424,10 @@ std::vector<Tensor> attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, 
   auto dk = torch::empty({k.size(0), k.size(1), Hkv, D}, k.options());
   auto dv = torch::empty({v.size(0), v.size(1), Hkv, D}, v.options());
   const long long n_rows = q.size(0) * H * q.size(1);
-  // delta rows + 128 floats of padding; the fused D = 64 path also keeps -lse*log2(e) after them.
-  auto delta = torch::empty({(D == 64 ? 2 : 1) * (n_rows + 128)}, q.options().dtype(torch::kFloat32)).narrow(0, 0, n_rows);
+  // delta rows + 128 floats of padding; the fused D = 64 path pads each (b, h) row of delta to a
+  // multiple of 4 floats and keeps -lse*log2(e) after it in the same layout.
+  const long long n_vec = q.size(0) * H * ((q.size(1) + 3) / 4 * 4);
+  auto delta = torch::empty({D == 64 ? 2 * (n_vec + 128) : n_rows + 128}, q.options().dtype(torch::kFloat32));
   PB_CHECK(lse.is_contiguous() && lse.numel() == n_rows, "lse must be the forward's [B, H, S] output");
   auto doc = dout.stride(3) == 1 && dout.stride(2) == D ? dout : dout.contiguous();
   if (q.numel() == 0) return {dq, dk, dv};

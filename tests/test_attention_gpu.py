@@ -28,6 +28,8 @@ CASES = [
     (1, 256, 256, 4, 4, 64, False, None),
     (1, 512, 512, 2, 1, 64, True, 100),
     (1, 128, 384, 2, 2, 64, True, None),
+    (3, 81, 81, 8, 8, 64, False, None),  # sequence length not a multiple of 4 (padded delta rows)
+    (1, 917, 917, 2, 2, 64, False, None),
 ]
 
 
