@@ -9,6 +9,14 @@ in [0, 32768) (synthetic data, random-init weights: d_model 2048, 16 layers,
 untied). Full training step: forward, fused LM loss, backward, global-norm
 clip, AdamW (fused kernel). bf16 compute, fp32 master weights and moments.
 
+``--config`` selects another workload (default ``llama1b``, the one above):
+``llama3_8b`` (Llama-3-8B shape, seq 8192, micro-batch 1, dp x tp4 sequence-parallel
+TP on the fused NVLink GEMMs, block checkpointing), ``mla_moe`` (MLA + 64-expert
+MoE, seq 4096, micro-batch 2, expert parallel over all ranks) and
+``llama3_8b_mxfp8`` (the 8B shape with MXFP8 linear layers, micro-batch 2, fused
+sharding). ``--layers`` overrides the depth (a shallower model is a different,
+smaller workload and is reported as such in ``config.model``).
+
 Two timed phases, each exactly K steps after W untimed warm-up steps:
 
 * device-timed: CUDA events on the compute stream, bracketed by barrier +
@@ -33,6 +41,7 @@ import sys
 import tempfile
 import time
 from pathlib import Path
+from typing import Any
 
 BASELINE_TOKENS_PER_S: float | None = None  # BASELINE.md publishes no B200 / LLM-at-scale number
 
@@ -43,15 +52,36 @@ def _parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mbs", type=int, default=4, help="micro-batch per GPU")
-    ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--config", choices=sorted(_CONFIGS), default="llama1b",
+                    help="workload: llama1b (the default: Llama-1B, FSDP), llama3_8b (8B, dp x tp4 sequence-parallel "
+                    "TP, block checkpointing), mla_moe (MLA + 64-expert MoE, expert parallel over all ranks), "
+                    "llama3_8b_mxfp8 (8B with MXFP8 linear layers, fused sharding)")
+    ap.add_argument("--mbs", type=int, default=None, help="micro-batch per GPU (default: the config's)")
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default: the config's)")
+    ap.add_argument("--layers", type=int, default=None, help="decoder layers (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "tp", "single"], default="auto",
+    ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "tp", "ep", "single"], default="auto",
                     help="auto: fused-collective sharding for N>1, single-GPU for N=1; "
                     "tp: sequence-parallel tensor parallelism on the fused NVLink GEMMs")
     ap.add_argument("--out", type=str, default="")
     return ap.parse_args()
+
+
+# Per workload: default micro-batch, sequence length and depth, and the default parallel layout.
+_CONFIGS = {
+    "llama1b": {"mbs": 4, "seq": 4096, "layers": 16},
+    "llama3_8b": {"mbs": 1, "seq": 8192, "layers": 32},
+    "mla_moe": {"mbs": 2, "seq": 4096, "layers": 27},
+    "llama3_8b_mxfp8": {"mbs": 2, "seq": 8192, "layers": 32},
+}
+
+
+def _layout(strategy: str, world: int, tp: int) -> str:
+    if strategy == "tp":
+        return f"dp{world // tp}xtp{tp}-sp" if world // tp > 1 else f"tp{world}-sp"
+    if strategy == "ep":
+        return f"ep{world}"
+    return f"fsdp{world}"
 
 
 def _reference_unavailable() -> None:
@@ -137,37 +167,76 @@ def main() -> None:
     from priml_b200 import cost
     from priml_b200.data import SyntheticTokens
     from priml_b200.loss import TokenCrossEntropy
-    from priml_b200.models.presets import dense_lm
+    from priml_b200.models.presets import dense_lm, mla_moe
     from priml_b200.optimizers import FusedAdamW
     from priml_b200.parallel.runtime import MultiProcess, SingleProcess
     from priml_b200.parallel.fused_fsdp import FusedFullySharded
     from priml_b200.parallel.tp_fused import FusedSequenceParallel
+    from priml_b200.parallel.expert import ExpertParallel
     from priml_b200.parallel.strategies import FullySharded, NoParallel
     from priml_b200.train import TrainStep
+    from priml_b200.train.quantization import Float8ModelQuantization
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    axis = "tp" if args.strategy == "tp" else "dp"
-    runtime = (MultiProcess.Config(mesh_topology={axis: -1}, timeout_s=300.0) if world > 1 else SingleProcess.Config()).make()
+    for k, v in _CONFIGS[args.config].items():
+        if getattr(args, k) is None:
+            setattr(args, k, v)
+    strategy = args.strategy
+    if strategy == "auto":
+        strategy = {"llama3_8b": "tp", "mla_moe": "ep"}.get(args.config, "fused")
+        if world == 1:
+            strategy = "single"
+    if strategy == "single" and world > 1:
+        raise SystemExit("--strategy single needs --gpus 1")
+    # sequence-parallel TP groups of (up to) 4 GPUs, data parallel across them
+    tp = min(4, world) if strategy == "tp" else 1
+    if world % tp:
+        raise SystemExit(f"--gpus {world} is not a multiple of the tensor-parallel group {tp}")
+    mesh = {"dp": world // tp, "tp": tp} if strategy == "tp" and world // tp > 1 else {("tp" if strategy == "tp" else "dp"): -1}
+    runtime = (MultiProcess.Config(mesh_topology=mesh, timeout_s=300.0) if world > 1 else SingleProcess.Config()).make()
     runtime.initialize()
     rank = dist.get_rank() if world > 1 else 0
     dev = torch.device("cuda", torch.cuda.current_device())
-    torch.manual_seed(1234 + rank)
+    # the llama1b workload keeps its historical per-rank seed; the others build replicated weights from one seed
+    torch.manual_seed(1234 + rank if args.config == "llama1b" else 1234)
 
-    shape = cost.DenseLMShape(d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
-                              ffn_hidden=8192, vocab=32768)  # fmt: skip
-    model_cfg = dense_lm(vocab=32768, d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
-                         ffn_hidden=8192, rope_theta=5e5)  # fmt: skip
-    strategy = args.strategy if args.strategy != "auto" else ("fused" if world > 1 else "single")
-    if strategy == "single" and world > 1:
-        raise SystemExit("--strategy single needs --gpus 1")
+    quant: Any = None
+    if args.config == "llama1b":
+        shape: Any = cost.DenseLMShape(d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
+                                       ffn_hidden=8192, vocab=32768)  # fmt: skip
+        model_cfg = dense_lm(vocab=32768, d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
+                             ffn_hidden=8192, rope_theta=5e5)  # fmt: skip
+        model_name = f"llama-1b dense decoder (d2048 L{args.layers} 32q/8kv h64 swiglu8192 vocab32768 untied)"
+    elif args.config in ("llama3_8b", "llama3_8b_mxfp8"):
+        shape = cost.DenseLMShape(d_model=4096, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=128,
+                                  ffn_hidden=14336, vocab=128256)  # fmt: skip
+        model_cfg = dense_lm(vocab=128256, d_model=4096, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=128,
+                             ffn_hidden=14336, rope_theta=5e5, checkpoint=True)  # fmt: skip
+        model_name = (f"llama-3-8b dense decoder (d4096 L{args.layers} 32q/8kv h128 swiglu14336 vocab128256 untied, "
+                      "block checkpointing)")  # fmt: skip
+        if args.config == "llama3_8b_mxfp8":
+            quant = Float8ModelQuantization.Config(recipe="mxfp8")
+            model_name += ", MXFP8 (1x32 E8M0 scales, E4M3) MLP, output and head projections; fused QKV in bf16"
+    else:
+        shape = cost.MLAMoEShape(d_model=2048, n_layers=args.layers, n_heads=16, kv_lora_rank=512, qk_nope=128,
+                                 qk_rope=64, v_head=128, dense_hidden=10944, first_dense=1, n_experts=64, top_k=6,
+                                 expert_hidden=1408, n_shared=2, vocab=102400)  # fmt: skip
+        model_cfg = mla_moe(n_layers=args.layers)
+        model_name = (f"MLA + MoE decoder (d2048 L{args.layers}, 16 heads, kv_lora 512, first layer dense 10944, "
+                      "64 routed experts x 1408 top-6 + 2 shared, vocab 102400)")  # fmt: skip
+    vocab = shape.vocab
     parallel = {
         "fused": lambda: FusedFullySharded.Config(),
         "fsdp2": lambda: FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True),
         "tp": lambda: FusedSequenceParallel.Config(),
+        "ep": lambda: ExpertParallel.Config(),
         "single": lambda: NoParallel.Config(),
     }[strategy]()
+    step_kw: dict[str, Any] = {}
+    if quant is not None:
+        step_kw["model_quantization"] = quant
     step_cfg = TrainStep.Config(
         model=model_cfg,
         optimizer=FusedAdamW.Config(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1),
@@ -175,7 +244,8 @@ def main() -> None:
         parallelism=parallel,
         dtype_autocast=torch.bfloat16,
         gradient_clip_norm=1.0,
-        device_init="eager",
+        device_init="eager" if args.config == "llama1b" else "meta",
+        **step_kw,
     )
     step = step_cfg.make()
     if strategy == "single":
@@ -183,7 +253,6 @@ def main() -> None:
     tokens_per_step = args.mbs * args.seq * world
 
     # ------------------------------------------------------------------ device-timed phase
-    vocab = 32768
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     n_batches = args.warmup + args.steps
     dev_batches = [
@@ -285,23 +354,25 @@ def main() -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 3),
-        "dtype": "bf16",
+        "dtype": "bf16" if quant is None else "mxfp8 linear layers (bf16 attention, fp32 master)",
         "data": "synthetic (uniform random tokens, random-init weights)",
         "mfu": round(cost.mfu(value, fpt, world, peaks, sustained=True), 4),
         "mfu_of": f"{peaks.source} sustained bf16 {peaks.bf16_tflops_sustained} TFLOP/s per GPU",
         "flops_per_token": fpt,
         "config": {
-            "model": f"llama-1b dense decoder (d2048 L{args.layers} 32q/8kv h64 swiglu8192 vocab32768 untied)",
+            "model": model_name,
             "global_batch": args.mbs * world,
             "micro_batch_per_gpu": args.mbs,
             "seq_len": args.seq,
-            "parallelism": (f"tp{world}-sp" if strategy == "tp" else f"fsdp{world}") if world > 1 else "single-gpu",
+            "parallelism": _layout(strategy, world, tp) if world > 1 else "single-gpu",
             "strategy": {
                 "fused": "sharded fp32 master + Adam state, resident bf16 weights; reduce-scatter, clip, AdamW and "
                 "weight all-gather in hand-written NVLink peer-memory kernels",
                 "fsdp2": "torch FSDP2 fully_shard over NCCL (bf16 params, fp32 reduce)",
                 "tp": "sequence-parallel tensor parallelism: all-gather GEMM and GEMM reduce-scatter fused over "
                 "NVLink peer memory; replicated grads averaged once per step",
+                "ep": "expert parallelism: routed experts sharded over all ranks, token rows exchanged by "
+                "NVLink peer-memory dispatch / combine kernels around the grouped expert GEMM; the rest replicated",
                 "single": "one GPU, fused AdamW",
             }[strategy],
             "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 from functools import partial
 
+from priml_b200.config import copy_tree
 from priml_b200.models.attention import SelfAttention
 from priml_b200.models.causal_lm import CausalLM
 from priml_b200.models.embedding import Embedding
@@ -114,9 +115,9 @@ def mla_moe(*, n_layers: int = 27) -> CausalLM.Config:
         rope=RoPE.Config(64, base=1e4),
         init_weight=init,
     )
-    dense = TransformerBlock.Config(attn=attn, ffn=SwiGLU.Config(channels_hidden=10944, init_weight=init))
+    dense = TransformerBlock.Config(attn=copy_tree(attn), ffn=SwiGLU.Config(channels_hidden=10944, init_weight=init))
     moe = TransformerBlock.Config(
-        attn=attn,
+        attn=copy_tree(attn),
         ffn=MoE.Config(
             router=Router.Config(num_experts=64, top_k=6, scoring_func="softmax"),
             expert=SwiGLU.Config(channels_hidden=1408, init_weight=init),
@@ -124,11 +125,12 @@ def mla_moe(*, n_layers: int = 27) -> CausalLM.Config:
             shared_expert=SwiGLU.Config(channels_hidden=1408, init_weight=init),
         ),
     )
+    # one config tree per layer: finalization writes widths into each block's (and its attention's) config
     return CausalLM.Config(
         102400,
         channels=2048,
         num_layers=n_layers,
-        block=[dense] + [moe] * (n_layers - 1),
+        block=[dense] + [copy_tree(moe) for _ in range(n_layers - 1)],
         lm_head=Linear.Config(bias=False, shard="vocab", init_weight=init),
         embed=Embedding.Config(shard="vocab", init_weight=init),
     )
