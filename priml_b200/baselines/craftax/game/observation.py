@@ -1,0 +1,67 @@
+"""Symbolic observation of the Craftax game (``priml/baselines/craftax/game/observation.py``).
+
+Per visible tile of the 9 x 11 local view: a one-hot block (37 planes), a
+one-hot item (5), creature planes (5 classes x 8 species: passive, melee,
+ranged, mob projectile, player projectile) and a lit flag -- 83 planes, masked
+by the lit flag -- flattened, then 51 player features (square-rooted counts,
+tool levels, meters / 10, facing direction, armour, condition). 8,268 floats
+in all, the same layout as the reference so that trained networks read it.
+Tiles beyond the map edge read OUT_OF_BOUNDS. The overworld is always lit.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+from torch.nn import functional as F
+
+from priml_b200.baselines.craftax.game import constants as C
+from priml_b200.baselines.craftax.game.state import GameState
+
+__all__ = ["CHANNELS_PER_TILE", "observation_size", "render"]
+
+CHANNELS_PER_TILE = len(C.BlockType) + len(C.ItemType) + 5 * 8 + 1
+
+
+def observation_size(view: tuple[int, int] = C.OBS_DIM) -> int:
+    return view[0] * view[1] * CHANNELS_PER_TILE + C.INVENTORY_OBS_SIZE
+
+
+def _local(grid: Tensor, pos: Tensor, view: tuple[int, int], outside: int) -> Tensor:
+    vr, vc = view
+    pad = max(vr, vc)
+    padded = F.pad(grid, (pad, pad, pad, pad), value=outside)
+    r0 = pos[:, 0] - vr // 2 + pad
+    c0 = pos[:, 1] - vc // 2 + pad
+    rr = r0[:, None] + torch.arange(vr, device=grid.device)
+    cc = c0[:, None] + torch.arange(vc, device=grid.device)
+    e = torch.arange(grid.shape[0], device=grid.device)
+    return padded[e[:, None, None], rr[:, :, None], cc[:, None, :]]
+
+
+def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
+    vr, vc = view
+    blocks = _local(s.map, s.position, view, int(C.BlockType.OUT_OF_BOUNDS))
+    items = _local(s.item_map, s.position, view, int(C.ItemType.NONE))
+    mobs = torch.zeros(s.num_envs, vr, vc, 5 * 8, device=s.device)
+    corner = s.position - torch.tensor([vr // 2, vc // 2], device=s.device)
+    e = torch.arange(s.num_envs, device=s.device)
+    for creatures, plane in ((s.melee, 1), (s.passive, 0), (s.ranged, 2), (s.projectiles, 3)):
+        for slot in range(creatures.mask.shape[1]):
+            local = creatures.position[:, slot] - corner
+            seen = creatures.mask[:, slot] & (local[:, 0] >= 0) & (local[:, 0] < vr) & (local[:, 1] >= 0) & (local[:, 1] < vc)
+            r, c = local[:, 0].clamp(0, vr - 1), local[:, 1].clamp(0, vc - 1)
+            mobs[e, r, c, plane * 8] = torch.maximum(mobs[e, r, c, plane * 8], seen.float())
+    lit = torch.ones(s.num_envs, vr, vc, 1, device=s.device)
+    tiles = torch.cat([F.one_hot(blocks, len(C.BlockType)).float(), F.one_hot(items, len(C.ItemType)).float(), mobs], -1)
+    view_part = torch.cat([tiles * lit, lit], -1).flatten(1)
+    z = torch.zeros(s.num_envs, device=s.device)
+    counts = torch.stack([s.wood, s.stone, s.coal, s.iron, s.diamond, z, z, s.sapling, s.torches, s.arrows], -1).float()
+    tools = torch.stack([z, s.pickaxe.float() / 4.0, s.sword.float() / 4.0, z, z, z], -1)
+    potions = torch.zeros(s.num_envs, 6, device=s.device)
+    meters = torch.stack([s.health, s.food.float(), s.drink.float(), s.energy.float(), z, z, z, z, z], -1)
+    facing = F.one_hot((s.direction - 1).clamp(min=0), 4).float()
+    condition = torch.stack([s.light, s.sleeping.float(), z, z, z, z, z, z], -1)
+    player = torch.cat([counts.sqrt() / 10.0, tools, potions, meters / 10.0, facing, s.armour.float() / 2.0,
+                        torch.zeros(s.num_envs, 4, device=s.device), condition], -1)  # fmt: skip
+    return torch.cat([view_part, player], -1)

@@ -1,0 +1,149 @@
+"""Batched overworld state of the Craftax game (``priml/baselines/craftax/game/state.py``).
+
+Every field is a tensor with the worker (environment) axis first, so one rollout
+step is one batched tensor program on the device: no simulator process and no
+host round trip. ``select`` merges two states row by row (auto-reset) and
+``take`` gathers rows (dealing freshly generated worlds to finished workers).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, fields
+from typing import Any
+
+import torch
+from torch import Tensor
+
+from priml_b200.baselines.craftax.game import constants as C
+
+__all__ = ["Creatures", "GameState", "empty_state"]
+
+
+@dataclass(slots=True, kw_only=True)
+class Creatures:
+    """One class of creature: ``[envs, slots]`` records (``mask`` marks live slots)."""
+
+    position: Tensor  # [E, S, 2] int64 (row, column)
+    health: Tensor  # [E, S] float
+    mask: Tensor  # [E, S] bool
+    cooldown: Tensor  # [E, S] int32
+    direction: Tensor  # [E, S, 2] int64 (projectiles only)
+
+    @classmethod
+    def empty(cls, envs: int, slots: int, device: torch.device) -> Creatures:
+        return cls(position=torch.zeros(envs, slots, 2, dtype=torch.long, device=device),
+                   health=torch.zeros(envs, slots, device=device),
+                   mask=torch.zeros(envs, slots, dtype=torch.bool, device=device),
+                   cooldown=torch.zeros(envs, slots, dtype=torch.int32, device=device),
+                   direction=torch.zeros(envs, slots, 2, dtype=torch.long, device=device))  # fmt: skip
+
+
+_COUNTS = ("wood", "stone", "coal", "iron", "diamond", "sapling", "pickaxe", "sword", "arrows", "torches")
+
+
+@dataclass(slots=True, kw_only=True)
+class GameState:
+    map: Tensor  # [E, H, W] int64 BlockType
+    item_map: Tensor  # [E, H, W] int64 ItemType
+    position: Tensor  # [E, 2] int64
+    direction: Tensor  # [E] int64 Action of the last move (1..4)
+    health: Tensor  # [E] float
+    food: Tensor  # [E] int64
+    drink: Tensor
+    energy: Tensor
+    hunger: Tensor  # [E] float accumulators
+    thirst: Tensor
+    fatigue: Tensor
+    recover: Tensor
+    sleeping: Tensor  # [E] bool
+    wood: Tensor  # inventory counts [E] int64
+    stone: Tensor
+    coal: Tensor
+    iron: Tensor
+    diamond: Tensor
+    sapling: Tensor
+    pickaxe: Tensor  # tool level 0..4 (none, wood, stone, iron, diamond)
+    sword: Tensor
+    arrows: Tensor
+    torches: Tensor
+    armour: Tensor  # [E, 4] int64: 0 none, 1 iron, 2 diamond
+    passive: Creatures
+    melee: Creatures
+    ranged: Creatures
+    projectiles: Creatures
+    plant_position: Tensor  # [E, P, 2]
+    plant_age: Tensor  # [E, P] int64
+    plant_mask: Tensor  # [E, P] bool
+    achievements: Tensor  # [E, 67] bool
+    timestep: Tensor  # [E] int64
+    light: Tensor  # [E] float daylight
+
+    @property
+    def num_envs(self) -> int:
+        return int(self.timestep.shape[0])
+
+    @property
+    def device(self) -> torch.device:
+        return self.timestep.device
+
+    def _map(self, fn: Any, other: GameState) -> GameState:
+        out: dict[str, Any] = {}
+        for f in fields(self):
+            a, b = getattr(self, f.name), getattr(other, f.name)
+            if isinstance(a, Tensor):
+                out[f.name] = fn(a, b)
+            else:
+                out[f.name] = Creatures(**{g.name: fn(getattr(a, g.name), getattr(b, g.name)) for g in fields(a)})
+        return GameState(**out)
+
+    def select(self, replace: Tensor, other: GameState) -> GameState:
+        """Rows where ``replace`` is true come from ``other``."""
+        return self._map(lambda a, b: torch.where(replace.view(-1, *([1] * (a.dim() - 1))), b, a), other)
+
+    def take(self, rows: Tensor) -> GameState:
+        return self._map(lambda a, b: a[rows], self)
+
+    def state_dict(self) -> dict[str, Tensor]:
+        out: dict[str, Tensor] = {}
+        for f in fields(self):
+            v = getattr(self, f.name)
+            if isinstance(v, Tensor):
+                out[f.name] = v.clone()  # the rules update some fields in place
+            else:
+                for g in fields(v):
+                    out[f"{f.name}.{g.name}"] = getattr(v, g.name).clone()
+        return out
+
+    def load_state_dict(self, s: dict[str, Tensor]) -> None:
+        for k, v in s.items():
+            head, _, tail = k.partition(".")
+            if tail:
+                setattr(getattr(self, head), tail, v.clone())
+            else:
+                setattr(self, head, v.clone())
+
+
+def empty_state(envs: int, device: torch.device) -> GameState:
+    rows, cols = C.MAP_SIZE
+
+    def z(dtype: torch.dtype = torch.long, *shape: int) -> Tensor:
+        return torch.zeros(envs, *shape, dtype=dtype, device=device)
+
+    counts = {name: z() for name in _COUNTS}
+    return GameState(
+        map=z(torch.long, rows, cols), item_map=z(torch.long, rows, cols), position=z(torch.long, 2),
+        direction=torch.full((envs,), int(C.Action.DOWN), dtype=torch.long, device=device),
+        health=torch.full((envs,), float(C.MAX_METER), device=device),
+        food=torch.full((envs,), C.MAX_METER, dtype=torch.long, device=device),
+        drink=torch.full((envs,), C.MAX_METER, dtype=torch.long, device=device),
+        energy=torch.full((envs,), C.MAX_METER, dtype=torch.long, device=device),
+        hunger=z(torch.float32), thirst=z(torch.float32), fatigue=z(torch.float32), recover=z(torch.float32),
+        sleeping=z(torch.bool), armour=z(torch.long, 4),
+        passive=Creatures.empty(envs, C.MAX_PASSIVE_MOBS, device),
+        melee=Creatures.empty(envs, C.MAX_MELEE_MOBS, device),
+        ranged=Creatures.empty(envs, C.MAX_RANGED_MOBS, device),
+        projectiles=Creatures.empty(envs, 3, device),
+        plant_position=z(torch.long, C.MAX_GROWING_PLANTS, 2), plant_age=z(torch.long, C.MAX_GROWING_PLANTS),
+        plant_mask=z(torch.bool, C.MAX_GROWING_PLANTS), achievements=z(torch.bool, C.NUM_ACHIEVEMENTS),
+        timestep=z(), light=torch.ones(envs, device=device), **counts,
+    )  # fmt: skip

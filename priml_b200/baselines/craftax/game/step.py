@@ -1,0 +1,405 @@
+"""One batched step of the Craftax overworld (``priml/baselines/craftax/game/step.py``).
+
+Order of operations per step (every rule is a masked tensor update over all
+workers at once): sleeping workers act NOOP -> crafting -> DO on the facing tile
+(creatures first, then the block) -> placing -> movement -> creatures (move,
+attack, arrows) -> spawning / despawning -> plants -> survival meters ->
+achievements from the inventory -> reward.
+
+The rules are Crafter's and Craftax's published ones for the overworld (tool
+tiers for mining, crafting next to a table (and furnace), cows / zombies /
+skeletons, food / drink / energy / recovery counters, sleeping, saplings that
+ripen). Reward = newly unlocked achievements' rewards + 0.1 x the change in
+health. An episode ends when health reaches 0 or after 100,000 steps.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from priml_b200.baselines.craftax.game import constants as C
+from priml_b200.baselines.craftax.game.constants import Achievement as A
+from priml_b200.baselines.craftax.game.constants import Action as Act
+from priml_b200.baselines.craftax.game.constants import BlockType as B
+from priml_b200.baselines.craftax.game.constants import ItemType as I
+from priml_b200.baselines.craftax.game.state import Creatures, GameState
+from priml_b200.baselines.craftax.game.world import daylight
+
+__all__ = ["is_done", "step"]
+
+_DELTA = torch.zeros(len(Act), 2, dtype=torch.long)
+_DELTA[Act.LEFT] = torch.tensor([0, -1])
+_DELTA[Act.RIGHT] = torch.tensor([0, 1])
+_DELTA[Act.UP] = torch.tensor([-1, 0])
+_DELTA[Act.DOWN] = torch.tensor([1, 0])
+_SWORD_DAMAGE = torch.tensor([1.0, 2.0, 3.0, 5.0, 8.0])
+_PLANT_RIPE_AGE = 600
+_CAP = C.MAX_METER
+
+
+def _rows(s: GameState) -> Tensor:
+    return torch.arange(s.num_envs, device=s.device)
+
+
+def _in_bounds(pos: Tensor) -> Tensor:
+    rows, cols = C.MAP_SIZE
+    return (pos[..., 0] >= 0) & (pos[..., 0] < rows) & (pos[..., 1] >= 0) & (pos[..., 1] < cols)
+
+
+def _clamp(pos: Tensor) -> Tensor:
+    rows, cols = C.MAP_SIZE
+    return torch.stack([pos[..., 0].clamp(0, rows - 1), pos[..., 1].clamp(0, cols - 1)], -1)
+
+
+def _tile(grid: Tensor, pos: Tensor) -> Tensor:
+    """Block (or item) at ``pos`` [E, 2]; out-of-bounds positions read OUT_OF_BOUNDS."""
+    p = _clamp(pos)
+    v = grid[torch.arange(grid.shape[0], device=grid.device), p[:, 0], p[:, 1]]
+    return torch.where(_in_bounds(pos), v, torch.full_like(v, int(B.OUT_OF_BOUNDS)))
+
+
+def _set(grid: Tensor, pos: Tensor, value: Tensor | int, where: Tensor) -> Tensor:
+    p = _clamp(pos)
+    r = torch.arange(grid.shape[0], device=grid.device)
+    old = grid[r, p[:, 0], p[:, 1]]
+    new = torch.as_tensor(value, device=grid.device).expand_as(old).to(grid.dtype)
+    grid = grid.clone()
+    grid[r, p[:, 0], p[:, 1]] = torch.where(where & _in_bounds(pos), new, old)
+    return grid
+
+
+def _occupied(s: GameState, pos: Tensor) -> Tensor:
+    """``[E]`` true where a live creature (any class) stands at ``pos``."""
+    hit = torch.zeros(s.num_envs, dtype=torch.bool, device=s.device)
+    for mobs in (s.passive, s.melee, s.ranged):
+        hit |= ((mobs.position == pos[:, None]).all(-1) & mobs.mask).any(-1)
+    return hit
+
+
+def _near(s: GameState, block: B, radius: int = 1) -> Tensor:
+    r, c = s.position[:, 0], s.position[:, 1]
+    found = torch.zeros(s.num_envs, dtype=torch.bool, device=s.device)
+    for dr in range(-radius, radius + 1):
+        for dc in range(-radius, radius + 1):
+            found |= _tile(s.map, torch.stack([r + dr, c + dc], -1)) == int(block)
+    return found
+
+
+def _unlock(s: GameState, achievement: A, where: Tensor) -> None:
+    s.achievements[:, int(achievement)] |= where
+
+
+def _facing(s: GameState) -> Tensor:
+    return s.position + _DELTA.to(s.device)[s.direction]
+
+
+# ---------------------------------------------------------------- crafting
+def _craft(s: GameState, a: Tensor) -> None:
+    table = _near(s, B.CRAFTING_TABLE)
+    furnace = _near(s, B.FURNACE)
+
+    def make(act: Act, ok: Tensor, costs: dict[str, int]) -> Tensor:
+        do = (a == int(act)) & ok
+        for name, n in costs.items():
+            do &= getattr(s, name) >= n
+        for name, n in costs.items():
+            setattr(s, name, getattr(s, name) - n * do.long())
+        return do
+
+    for act, level, costs, ok in (
+        (Act.MAKE_WOOD_PICKAXE, 1, {"wood": 1}, table),
+        (Act.MAKE_STONE_PICKAXE, 2, {"wood": 1, "stone": 1}, table),
+        (Act.MAKE_IRON_PICKAXE, 3, {"wood": 1, "coal": 1, "iron": 1}, table & furnace),
+        (Act.MAKE_DIAMOND_PICKAXE, 4, {"wood": 1, "diamond": 3}, table),
+    ):
+        s.pickaxe = torch.where(make(act, ok & (s.pickaxe < level), costs), level, s.pickaxe)
+    for act, level, costs, ok in (
+        (Act.MAKE_WOOD_SWORD, 1, {"wood": 1}, table),
+        (Act.MAKE_STONE_SWORD, 2, {"wood": 1, "stone": 1}, table),
+        (Act.MAKE_IRON_SWORD, 3, {"wood": 1, "coal": 1, "iron": 1}, table & furnace),
+        (Act.MAKE_DIAMOND_SWORD, 4, {"wood": 1, "diamond": 2}, table),
+    ):
+        s.sword = torch.where(make(act, ok & (s.sword < level), costs), level, s.sword)
+    s.arrows = torch.clamp(s.arrows + 2 * make(Act.MAKE_ARROW, table, {"wood": 1, "stone": 1}).long(), max=99)
+    s.torches = torch.clamp(s.torches + 4 * make(Act.MAKE_TORCH, table, {"wood": 1, "coal": 1}).long(), max=99)
+    for act, tier, costs, ach in ((Act.MAKE_IRON_ARMOUR, 1, {"iron": 3, "coal": 3}, A.MAKE_IRON_ARMOUR),
+                                  (Act.MAKE_DIAMOND_ARMOUR, 2, {"diamond": 3}, A.MAKE_DIAMOND_ARMOUR)):  # fmt: skip
+        slot_free = s.armour < tier
+        do = make(act, table & furnace & slot_free.any(-1), costs)
+        first = torch.argmax(slot_free.long(), dim=-1)
+        upgraded = s.armour.clone()
+        upgraded[_rows(s), first] = tier
+        s.armour = torch.where(do[:, None], upgraded, s.armour)
+        _unlock(s, ach, do)
+
+
+# ---------------------------------------------------------------- DO
+def _hit_creatures(s: GameState, target: Tensor, doing: Tensor) -> Tensor:
+    """Damage the creature on ``target``; returns where a creature absorbed the action."""
+    damage = _SWORD_DAMAGE.to(s.device)[s.sword]
+    absorbed = torch.zeros_like(doing)
+    for mobs, ach in ((s.passive, A.EAT_COW), (s.melee, A.DEFEAT_ZOMBIE), (s.ranged, A.DEFEAT_SKELETON)):
+        at = (mobs.position == target[:, None]).all(-1) & mobs.mask & doing[:, None] & ~absorbed[:, None]
+        hit_any = at.any(-1)
+        mobs.health = mobs.health - at.float() * damage[:, None]
+        killed = at & (mobs.health <= 0)
+        mobs.mask = mobs.mask & ~killed
+        died = killed.any(-1)
+        if mobs is s.passive:  # eating a cow
+            s.food = torch.where(died, torch.clamp(s.food + 6, max=_CAP), s.food)
+            s.hunger = torch.where(died, torch.zeros_like(s.hunger), s.hunger)
+        _unlock(s, ach, died)
+        absorbed |= hit_any
+    return absorbed
+
+
+def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> None:
+    doing = a == int(Act.DO)
+    target = _facing(s)
+    doing = doing & ~_hit_creatures(s, target, doing)
+    block = _tile(s.map, target)
+
+    def mine(kind: B, tool: int, item: str) -> None:
+        ok = doing & (block == int(kind)) & (s.pickaxe >= tool)
+        setattr(s, item, torch.clamp(getattr(s, item) + ok.long(), max=_CAP))
+        s.map = _set(s.map, target, int(B.PATH), ok)
+
+    wood = doing & (block == int(B.TREE))
+    s.wood = torch.clamp(s.wood + wood.long(), max=_CAP)
+    mine(B.STONE, 1, "stone")
+    mine(B.COAL, 1, "coal")
+    mine(B.IRON, 2, "iron")
+    mine(B.DIAMOND, 3, "diamond")
+    sapling = doing & (block == int(B.GRASS)) & (torch.rand(s.num_envs, device=s.device, generator=generator) < 0.1)
+    s.sapling = torch.clamp(s.sapling + sapling.long(), max=_CAP)
+    drink = doing & (block == int(B.WATER))
+    s.drink = torch.where(drink, torch.clamp(s.drink + 1, max=_CAP), s.drink)
+    s.thirst = torch.where(drink, torch.zeros_like(s.thirst), s.thirst)
+    _unlock(s, A.COLLECT_DRINK, drink)
+    eat = doing & (block == int(B.RIPE_PLANT))
+    s.food = torch.where(eat, torch.clamp(s.food + 4, max=_CAP), s.food)
+    s.hunger = torch.where(eat, torch.zeros_like(s.hunger), s.hunger)
+    s.map = _set(s.map, target, int(B.PLANT), eat)
+    at_plant = (s.plant_position == target[:, None]).all(-1) & s.plant_mask & eat[:, None]
+    s.plant_age = torch.where(at_plant, torch.zeros_like(s.plant_age), s.plant_age)
+    _unlock(s, A.EAT_PLANT, eat)
+
+
+# ---------------------------------------------------------------- placing
+def _place(s: GameState, a: Tensor) -> None:
+    target = _facing(s)
+    block = _tile(s.map, target)
+    free = ~_occupied(s, target) & _in_bounds(target)
+    ground = (block == int(B.GRASS)) | (block == int(B.SAND)) | (block == int(B.PATH))
+
+    stone = (a == int(Act.PLACE_STONE)) & (s.stone >= 1) & free & (ground | (block == int(B.WATER)) | (block == int(B.LAVA)))
+    s.map = _set(s.map, target, int(B.STONE), stone)
+    s.stone = s.stone - stone.long()
+    _unlock(s, A.PLACE_STONE, stone)
+    table = (a == int(Act.PLACE_TABLE)) & (s.wood >= 1) & free & ground
+    s.map = _set(s.map, target, int(B.CRAFTING_TABLE), table)
+    s.wood = s.wood - table.long()
+    _unlock(s, A.PLACE_TABLE, table)
+    furnace = (a == int(Act.PLACE_FURNACE)) & (s.stone >= 1) & free & ground & _near(s, B.CRAFTING_TABLE)
+    s.map = _set(s.map, target, int(B.FURNACE), furnace)
+    s.stone = s.stone - furnace.long()
+    _unlock(s, A.PLACE_FURNACE, furnace)
+    slot_free = ~s.plant_mask
+    plant = (a == int(Act.PLACE_PLANT)) & (s.sapling >= 1) & free & (block == int(B.GRASS)) & slot_free.any(-1)
+    s.map = _set(s.map, target, int(B.PLANT), plant)
+    s.sapling = s.sapling - plant.long()
+    first = torch.argmax(slot_free.long(), dim=-1)
+    r = _rows(s)
+    pos, age, mask = s.plant_position.clone(), s.plant_age.clone(), s.plant_mask.clone()
+    pos[r, first] = torch.where(plant[:, None], target, pos[r, first])
+    age[r, first] = torch.where(plant, torch.zeros_like(age[r, first]), age[r, first])
+    mask[r, first] = mask[r, first] | plant
+    s.plant_position, s.plant_age, s.plant_mask = pos, age, mask
+    _unlock(s, A.PLACE_PLANT, plant)
+    torch_ok = (a == int(Act.PLACE_TORCH)) & (s.torches >= 1) & ground & (_tile(s.item_map, target) == int(I.NONE))
+    s.item_map = _set(s.item_map, target, int(I.TORCH), torch_ok)
+    s.torches = s.torches - torch_ok.long()
+    _unlock(s, A.PLACE_TORCH, torch_ok)
+
+
+# ---------------------------------------------------------------- movement
+def _move(s: GameState, a: Tensor) -> None:
+    moving = (a >= int(Act.LEFT)) & (a <= int(Act.DOWN))
+    s.direction = torch.where(moving, a, s.direction)
+    target = s.position + _DELTA.to(s.device)[a]
+    block = _tile(s.map, target)
+    ok = moving & _in_bounds(target) & ~_occupied(s, target)
+    ok &= (block == int(B.GRASS)) | (block == int(B.SAND)) | (block == int(B.PATH)) | (block == int(B.LAVA))
+    s.position = torch.where(ok[:, None], target, s.position)
+    s.health = torch.where(_tile(s.map, s.position) == int(B.LAVA), torch.zeros_like(s.health), s.health)
+
+
+# ---------------------------------------------------------------- creatures
+def _random_step(mobs: Creatures, generator: torch.Generator | None) -> Tensor:
+    e, k = mobs.mask.shape
+    choice = torch.randint(0, 5, (e, k), device=mobs.mask.device, generator=generator)  # 0 = stay
+    return _DELTA.to(mobs.mask.device)[choice]
+
+
+def _try_move(s: GameState, mobs: Creatures, step: Tensor, allowed: tuple[B, ...]) -> None:
+    for slot in range(mobs.mask.shape[1]):
+        pos = mobs.position[:, slot]
+        target = pos + step[:, slot]
+        block = _tile(s.map, target)
+        ok = mobs.mask[:, slot] & _in_bounds(target) & ~_occupied(s, target) & ~(target == s.position).all(-1)
+        ok &= torch.stack([block == int(b) for b in allowed]).any(0)
+        mobs.position[:, slot] = torch.where(ok[:, None], target, pos)
+
+
+def _armour_factor(s: GameState) -> Tensor:
+    return 1.0 - 0.1 * (s.armour == 1).sum(-1).float() - 0.2 * (s.armour == 2).sum(-1).float()
+
+
+def _creatures(s: GameState, generator: torch.Generator | None) -> None:
+    dev = s.device
+    # cows wander
+    _try_move(s, s.passive, _random_step(s.passive, generator), (B.GRASS, B.SAND, B.PATH))
+    # zombies chase when close, else wander; adjacent ones attack every 5 steps
+    offset = s.position[:, None] - s.melee.position
+    dist = offset.abs().sum(-1)
+    toward = torch.where((offset[..., 0].abs() >= offset[..., 1].abs())[..., None],
+                         torch.stack([offset[..., 0].sign(), torch.zeros_like(offset[..., 0])], -1),
+                         torch.stack([torch.zeros_like(offset[..., 1]), offset[..., 1].sign()], -1))  # fmt: skip
+    chase = (dist < 8) & (torch.rand(dist.shape, device=dev, generator=generator) < 0.8)
+    step = torch.where(chase[..., None], toward, _random_step(s.melee, generator))
+    _try_move(s, s.melee, step, (B.GRASS, B.SAND, B.PATH))
+    dist = (s.position[:, None] - s.melee.position).abs().sum(-1)
+    attack = s.melee.mask & (dist <= 1) & (s.melee.cooldown <= 0)
+    damage = torch.where(s.sleeping, torch.full_like(s.health, 7.0), torch.full_like(s.health, C.MELEE_DAMAGE))
+    s.health = s.health - attack.sum(-1).float() * damage * _armour_factor(s)
+    s.melee.cooldown = torch.where(attack, torch.full_like(s.melee.cooldown, 5), (s.melee.cooldown - 1).clamp(min=0))
+    # skeletons keep to the caves and shoot along rows / columns when the player is within 4 tiles
+    _try_move(s, s.ranged, _random_step(s.ranged, generator), (B.PATH,))
+    offset = s.position[:, None] - s.ranged.position
+    aligned = (offset == 0).any(-1) & (offset.abs().sum(-1) <= 4)
+    shoot = s.ranged.mask & aligned & (s.ranged.cooldown <= 0)
+    s.ranged.cooldown = torch.where(shoot, torch.full_like(s.ranged.cooldown, 4), (s.ranged.cooldown - 1).clamp(min=0))
+    proj = s.projectiles
+    for slot in range(s.ranged.mask.shape[1]):
+        want = shoot[:, slot]
+        free = ~proj.mask
+        first = torch.argmax(free.long(), -1)
+        put = want & free.any(-1)
+        r = _rows(s)
+        d = offset[:, slot].sign()
+        pos, dirn, mask = proj.position.clone(), proj.direction.clone(), proj.mask.clone()
+        pos[r, first] = torch.where(put[:, None], s.ranged.position[:, slot], pos[r, first])
+        dirn[r, first] = torch.where(put[:, None], d, dirn[r, first])
+        mask[r, first] = mask[r, first] | put
+        proj.position, proj.direction, proj.mask = pos, dirn, mask
+    # arrows fly one tile per step: they hurt the player they reach and stop at solid tiles
+    proj.position = proj.position + proj.direction * proj.mask[..., None].long()
+    hit = proj.mask & (proj.position == s.position[:, None]).all(-1)
+    s.health = s.health - hit.sum(-1).float() * C.ARROW_DAMAGE * _armour_factor(s)
+    blocked = torch.zeros_like(proj.mask)
+    for slot in range(proj.mask.shape[1]):
+        b = _tile(s.map, proj.position[:, slot])
+        blocked[:, slot] = ~((b == int(B.GRASS)) | (b == int(B.SAND)) | (b == int(B.PATH)) | (b == int(B.WATER)))
+    proj.mask = proj.mask & ~hit & ~blocked
+
+
+def _spawn(s: GameState, generator: torch.Generator | None) -> None:
+    dev, e = s.device, s.num_envs
+    rows, cols = C.MAP_SIZE
+    night = s.light < 0.5
+    for mobs, chance, allowed, min_dist, health in (
+        (s.passive, torch.full((e,), C.SPAWN_CHANCE["passive"], device=dev), B.GRASS, 3, C.PASSIVE_HEALTH),
+        (s.melee, torch.where(night, C.SPAWN_CHANCE["melee_night"], C.SPAWN_CHANCE["melee"]), B.GRASS, 6, C.MELEE_HEALTH),
+        (s.ranged, torch.full((e,), C.SPAWN_CHANCE["ranged"], device=dev), B.PATH, 4, C.RANGED_HEALTH),
+    ):  # fmt: skip
+        # despawn creatures that wandered far from the player
+        far = (mobs.position - s.position[:, None]).abs().max(-1).values > C.MOB_DESPAWN_DISTANCE
+        mobs.mask = mobs.mask & ~far
+        pos = torch.stack([(s.position[:, 0] + torch.randint(-9, 10, (e,), device=dev, generator=generator)).clamp(0, rows - 1),
+                           (s.position[:, 1] + torch.randint(-9, 10, (e,), device=dev, generator=generator)).clamp(0, cols - 1)], -1)  # fmt: skip
+        ok = torch.rand(e, device=dev, generator=generator) < chance
+        ok &= (_tile(s.map, pos) == int(allowed)) & ~_occupied(s, pos)
+        ok &= (pos - s.position).abs().sum(-1) >= min_dist
+        free = ~mobs.mask
+        ok &= free.any(-1)
+        first = torch.argmax(free.long(), -1)
+        r = _rows(s)
+        p, h, m, cd = mobs.position.clone(), mobs.health.clone(), mobs.mask.clone(), mobs.cooldown.clone()
+        p[r, first] = torch.where(ok[:, None], pos, p[r, first])
+        h[r, first] = torch.where(ok, torch.full_like(h[r, first], health), h[r, first])
+        m[r, first] = m[r, first] | ok
+        cd[r, first] = torch.where(ok, torch.zeros_like(cd[r, first]), cd[r, first])
+        mobs.position, mobs.health, mobs.mask, mobs.cooldown = p, h, m, cd
+
+
+def _plants(s: GameState) -> None:
+    s.plant_age = s.plant_age + s.plant_mask.long()
+    for slot in range(s.plant_mask.shape[1]):
+        pos = s.plant_position[:, slot]
+        here = _tile(s.map, pos)
+        live = s.plant_mask[:, slot] & ((here == int(B.PLANT)) | (here == int(B.RIPE_PLANT)))
+        s.plant_mask[:, slot] = live  # a plant trampled or removed stops growing
+        ripe = live & (s.plant_age[:, slot] >= _PLANT_RIPE_AGE) & (_tile(s.map, pos) == int(B.PLANT))
+        s.map = _set(s.map, pos, int(B.RIPE_PLANT), ripe)
+
+
+# ---------------------------------------------------------------- survival
+def _survive(s: GameState, a: Tensor) -> None:
+    start = (a == int(Act.SLEEP)) & (s.energy < _CAP)
+    s.sleeping = s.sleeping | start
+    slow = torch.where(s.sleeping, 0.5, 1.0)
+    s.hunger = s.hunger + slow
+    s.food = torch.where(s.hunger > 25, s.food - 1, s.food)
+    s.hunger = torch.where(s.hunger > 25, torch.zeros_like(s.hunger), s.hunger)
+    s.thirst = s.thirst + slow
+    s.drink = torch.where(s.thirst > 20, s.drink - 1, s.drink)
+    s.thirst = torch.where(s.thirst > 20, torch.zeros_like(s.thirst), s.thirst)
+    s.fatigue = torch.where(s.sleeping, torch.clamp(s.fatigue - 1, max=0.0), s.fatigue + 1)
+    s.energy = torch.where(s.fatigue > 30, s.energy - 1, s.energy)
+    s.energy = torch.where(s.fatigue < -10, s.energy + 1, s.energy)
+    s.fatigue = torch.where((s.fatigue > 30) | (s.fatigue < -10), torch.zeros_like(s.fatigue), s.fatigue)
+    fine = (s.food > 0) & (s.drink > 0) & ((s.energy > 0) | s.sleeping)
+    s.recover = s.recover + torch.where(fine, torch.where(s.sleeping, 2.0, 1.0), torch.where(s.sleeping, -0.5, -1.0))
+    s.health = torch.where(s.recover > 25, s.health + 1, s.health)
+    s.health = torch.where(s.recover < -15, s.health - 1, s.health)
+    s.recover = torch.where((s.recover > 25) | (s.recover < -15), torch.zeros_like(s.recover), s.recover)
+    woke = s.sleeping & (s.energy >= _CAP)
+    s.sleeping = s.sleeping & ~woke
+    _unlock(s, A.WAKE_UP, woke)
+    s.food, s.drink, s.energy = (x.clamp(0, _CAP) for x in (s.food, s.drink, s.energy))
+    s.health = s.health.clamp(max=float(_CAP))
+
+
+_THRESHOLDS = (("wood", 1, A.COLLECT_WOOD), ("stone", 1, A.COLLECT_STONE), ("coal", 1, A.COLLECT_COAL),
+               ("iron", 1, A.COLLECT_IRON), ("diamond", 1, A.COLLECT_DIAMOND), ("sapling", 1, A.COLLECT_SAPLING),
+               ("arrows", 1, A.MAKE_ARROW), ("torches", 1, A.MAKE_TORCH), ("pickaxe", 1, A.MAKE_WOOD_PICKAXE),
+               ("pickaxe", 2, A.MAKE_STONE_PICKAXE), ("pickaxe", 3, A.MAKE_IRON_PICKAXE),
+               ("pickaxe", 4, A.MAKE_DIAMOND_PICKAXE), ("sword", 1, A.MAKE_WOOD_SWORD), ("sword", 2, A.MAKE_STONE_SWORD),
+               ("sword", 3, A.MAKE_IRON_SWORD), ("sword", 4, A.MAKE_DIAMOND_SWORD))  # fmt: skip
+
+
+def step(s: GameState, action: Tensor, *, generator: torch.Generator | None = None) -> tuple[GameState, Tensor]:
+    """Advance every worker by one step; returns the state (updated in place) and the reward ``[E]``."""
+    before = s.achievements.clone()
+    health_before = s.health.clone()
+    a = torch.where(s.sleeping, torch.full_like(action, int(Act.NOOP)), action.long())
+    _craft(s, a)
+    _interact(s, a, generator)
+    _place(s, a)
+    _move(s, a)
+    _creatures(s, generator)
+    _spawn(s, generator)
+    _plants(s)
+    _survive(s, a)
+    for name, n, ach in _THRESHOLDS:
+        _unlock(s, ach, getattr(s, name) >= n)
+    newly = (s.achievements & ~before).float()
+    reward = (newly * C.ACHIEVEMENT_REWARD.to(s.device)).sum(-1) + 0.1 * (s.health - health_before)
+    s.timestep = s.timestep + 1
+    s.light = daylight(s.timestep)
+    return s, reward
+
+
+def is_done(s: GameState) -> Tensor:
+    return (s.health <= 0) | (s.timestep >= C.MAX_TIMESTEPS)

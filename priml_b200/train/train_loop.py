@@ -120,6 +120,8 @@ class TrainLoop:
         set_seed_local((seed + salt("data", self._axis_coord(c.mesh_dim_data_seed))) % (2**63) or 1)
         self.dataset = c.dataset.make()
         self.step.bind_epoch_timer(getattr(self.dataset, "timer_epoch", None))
+        if hasattr(self.dataset, "bind_step"):  # datasets that serve the learner's own policy (RL)
+            self.dataset.bind_step(self.step)
         self.checkpointing = c.checkpointing.make() if c.checkpointing is not None else None
         self.tracker = c.tracker.make() if c.tracker is not None else None
         self.profiling = c.profiling.make() if c.profiling is not None else None

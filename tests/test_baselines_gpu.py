@@ -125,3 +125,19 @@ def test_arc_transformer_step_on_cuda(monkeypatch) -> None:  # noqa: ANN001
     table = step.model.prefix.parts[0].weights
     assert float(table[ids].abs().sum()) > 0 and float(table[1].abs().sum()) == 0
     assert int(native().read_status(True)) == 0
+
+
+def test_craftax_ppo_update_on_cuda() -> None:
+    """The batched game, the 8,268-wide observation and a PPO update (bf16 tcgen05 GEMMs) on the device."""
+    from priml_b200.baselines.craftax import CraftaxEnv, CraftaxTrainStep
+    from priml_b200.ops import native
+
+    cfg = CraftaxTrainStep.Config()
+    cfg.env = CraftaxEnv.Config(num_envs=256, device="cuda", seed=0)
+    cfg.rollout_steps = 16
+    step = cfg.make()
+    assert step.env.device.type == "cuda"
+    out = [step.train_step() for _ in range(2)]
+    assert all(bool(torch.isfinite(o["loss"]).all()) for o in out)
+    assert math.isfinite(float(out[-1]["metrics"]["explained_variance"]))
+    assert int(native().read_status(True)) == 0

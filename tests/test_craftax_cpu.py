@@ -1,0 +1,203 @@
+"""Craftax on CPU: game rules, observation layout, environment resets, learners, metric, smoke ladder."""
+
+from __future__ import annotations
+
+import torch
+
+from priml_b200.baselines.craftax import (
+    ActorCritic,
+    CraftaxEnv,
+    CraftaxPQNTrainStep,
+    CraftaxRNNTrainStep,
+    CraftaxScore,
+    CraftaxTrainStep,
+)
+from priml_b200.baselines.craftax import experiments
+from priml_b200.baselines.craftax.game import constants as C
+from priml_b200.baselines.craftax.game import observation, world
+from priml_b200.baselines.craftax.game import step as rules
+from priml_b200.baselines.craftax.game.constants import Achievement as A
+from priml_b200.baselines.craftax.game.constants import Action as Act
+from priml_b200.baselines.craftax.game.constants import BlockType as B
+from priml_b200.baselines.craftax.metric import crafter_score_pct
+from priml_b200.parallel.strategies import NoParallel
+
+CPU = torch.device("cpu")
+
+
+def _world(n: int = 2, seed: int = 0):  # noqa: ANN202
+    s = world.generate(n, generator=torch.Generator().manual_seed(seed), device=CPU)
+    s.passive.mask[:] = False  # no creatures in the way of scripted tests
+    return s
+
+
+def _act(s, a: Act):  # noqa: ANN001, ANN202
+    return rules.step(s, torch.full((s.num_envs,), int(a)), generator=torch.Generator().manual_seed(1))
+
+
+def _face(s, block: B) -> None:  # noqa: ANN001
+    """Put ``block`` right of the player and face it."""
+    r, c = s.position[0].tolist()
+    s.map[:, r, c + 1] = int(block)
+    s.direction[:] = int(Act.RIGHT)
+
+
+def test_constants_and_observation_layout() -> None:
+    assert C.REWARD_CEILING == 226.0 and len(Act) == 43 and C.NUM_ACHIEVEMENTS == 67
+    s = _world()
+    o = observation.render(s)
+    assert o.shape == (2, 8268) == (2, observation.observation_size())
+    tiles = o[:, : 9 * 11 * observation.CHANNELS_PER_TILE].view(2, 9, 11, -1)
+    assert torch.all(tiles[:, 4, 5, int(B.GRASS)] == 1)  # the player stands on cleared grass at the centre
+    assert torch.all(tiles[..., -1] == 1)  # the overworld is lit
+    assert torch.allclose(tiles[..., : len(B)].sum(-1), torch.ones(2, 9, 11))
+
+
+def test_world_generation_is_seeded_and_has_resources() -> None:
+    a, b = _world(8, 3), _world(8, 3)
+    assert torch.equal(a.map, b.map)
+    counts = torch.bincount(a.map.flatten(), minlength=len(B))
+    for block in (B.GRASS, B.WATER, B.STONE, B.TREE, B.COAL, B.SAND):
+        assert counts[int(block)] > 0, block
+
+
+def test_tools_gate_mining_and_crafting_needs_a_table() -> None:
+    s = _world(1)
+    _face(s, B.TREE)
+    for _ in range(3):
+        s, r = _act(s, Act.DO)
+    assert int(s.wood) == 3 and bool(s.achievements[0, A.COLLECT_WOOD])
+    _face(s, B.STONE)
+    s, _ = _act(s, Act.DO)
+    assert int(s.stone) == 0  # no pickaxe yet
+    s, _ = _act(s, Act.MAKE_WOOD_PICKAXE)
+    assert int(s.pickaxe) == 0  # no table nearby
+    _face(s, B.GRASS)
+    s, reward = _act(s, Act.PLACE_TABLE)
+    assert bool(s.achievements[0, A.PLACE_TABLE]) and float(reward) >= 1.0
+    s, _ = _act(s, Act.MAKE_WOOD_PICKAXE)
+    assert int(s.pickaxe) == 1 and bool(s.achievements[0, A.MAKE_WOOD_PICKAXE])
+    _face(s, B.STONE)
+    s, _ = _act(s, Act.DO)
+    assert int(s.stone) == 1 and bool(s.achievements[0, A.COLLECT_STONE])
+    r, c = s.position[0].tolist()
+    assert int(s.map[0, r, c + 1]) == int(B.PATH)
+    _face(s, B.IRON)
+    s, _ = _act(s, Act.DO)
+    assert int(s.iron) == 0  # iron needs a stone pickaxe
+
+
+def test_water_drink_sleep_and_survival_meters() -> None:
+    s = _world(1)
+    s.drink[:] = 3
+    _face(s, B.WATER)
+    s, _ = _act(s, Act.DO)
+    assert int(s.drink) == 4 and bool(s.achievements[0, A.COLLECT_DRINK])
+    s.energy[:] = 5
+    s, _ = _act(s, Act.SLEEP)
+    assert bool(s.sleeping)
+    for _ in range(120):
+        if not bool(s.sleeping):
+            break
+        s.melee.mask[:] = False
+        s, _ = _act(s, Act.NOOP)
+    assert not bool(s.sleeping) and bool(s.achievements[0, A.WAKE_UP])
+    t = _world(1)
+    t.melee.mask[:] = False
+    for _ in range(30):
+        t.melee.mask[:] = False
+        t, _ = _act(t, Act.NOOP)
+    assert int(t.food) == C.MAX_METER - 1  # hunger crossed 25 once
+    assert int(t.drink) == C.MAX_METER - 1  # thirst crossed 20 once
+
+
+def test_cow_is_eaten_and_zombie_attacks() -> None:
+    s = _world(1)
+    r, c = s.position[0].tolist()
+    s.passive.mask[0, 0] = True
+    s.passive.position[0, 0] = torch.tensor([r, c + 1])
+    s.passive.health[0, 0] = 1.0
+    s.direction[:] = int(Act.RIGHT)
+    s.food[:] = 2
+    s, _ = _act(s, Act.DO)
+    assert bool(s.achievements[0, A.EAT_COW]) and int(s.food) == 8 and not bool(s.passive.mask[0, 0])
+    s.melee.mask[0, 0] = True
+    s.melee.position[0, 0] = torch.tensor([r + 1, c])
+    s.melee.health[0, 0] = 5.0
+    s.melee.cooldown[0, 0] = 0
+    h = float(s.health)
+    s, reward = _act(s, Act.NOOP)
+    assert float(s.health) < h and float(reward) < 0
+
+
+def test_env_auto_resets_and_state_round_trips() -> None:
+    env = CraftaxEnv.Config(num_envs=4, device="cpu", seed=0, optimistic_reset_ratio=2).make()
+    obs = env.reset()
+    assert obs.shape == (4, 8268)
+    env.state.health[1] = 0.0
+    t = env.step(torch.zeros(4, dtype=torch.long))
+    assert bool(t.done[1]) and not bool(t.done[0])
+    assert int(env.state.timestep[1]) == 0 and float(env.state.health[1]) == C.MAX_METER  # a fresh world
+    saved = env.state_dict()
+    a = env.step(torch.full((4,), int(Act.DO))).observation
+    env.load_state_dict(saved)
+    b = env.step(torch.full((4,), int(Act.DO))).observation
+    assert torch.equal(a, b)
+
+
+def _step_cfg(cls, **kw):  # noqa: ANN001, ANN202
+    c = cls.Config()
+    c.env = CraftaxEnv.Config(num_envs=4, device="cpu", seed=0)
+    c.parallelism = NoParallel.Config(device="cpu")
+    c.dtype_autocast = None
+    c.model.hidden_size = 32
+    c.rollout_steps = 8
+    c.num_minibatches = 2
+    c.num_epochs = 2
+    c.total_train_steps = 10
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c.make()
+
+
+def test_ppo_recurrent_ppo_and_pqn_update() -> None:
+    for cls in (CraftaxTrainStep, CraftaxRNNTrainStep, CraftaxPQNTrainStep):
+        step = _step_cfg(cls)
+        before = [p.detach().clone() for p in step.model.parameters()]
+        out = step.train_step()
+        assert torch.isfinite(out["loss"]).all() and out["stepped"], cls.__name__
+        assert any(not torch.equal(a, b) for a, b in zip(before, step.model.parameters(), strict=True))
+        step._lr()
+        assert step.global_step == 1 and abs(step.optimizer.param_groups[0]["lr"] - 3e-4 * 0.9) < 1e-12  # annealed
+        state = step.state_dict()
+        again = _step_cfg(cls)
+        again.load_state_dict(state)
+        assert again.global_step == 1
+
+
+def test_crafter_score_and_metric_plays_a_policy() -> None:
+    assert crafter_score_pct([0.0] * 5) == 0.0
+    assert abs(crafter_score_pct([100.0] * 3) - 100.0) < 1e-9
+    metric = CraftaxScore(CraftaxScore.Config(num_envs=3, steps=60, device="cpu"))
+    policy = ActorCritic.Config(hidden_size=16).make()
+    metric.update(None, policy=policy)
+    res = metric.compute()
+    assert "episodes" in res
+
+
+def test_experiment_chain_and_smoke_loop(tmp_path) -> None:  # noqa: ANN001
+    for exp in (experiments.exp000, experiments.exp001, experiments.exp002, experiments.exp003, experiments.exp011):
+        cfg = exp().copy_tree().finalize()
+        assert cfg.step.total_train_steps > 0
+    assert experiments.exp000().step.total_train_steps == 244
+    cfg = experiments.exp_smoke()
+    cfg.step.env.device = "cpu"
+    cfg.step.parallelism = NoParallel.Config(device="cpu")
+    cfg.step.dtype_autocast = None
+    cfg.step.model.hidden_size = 16
+    cfg.metrics["craftax"].device = "cpu"
+    cfg.base_dir = str(tmp_path)
+    loop = cfg.make()
+    loop.run()
+    assert loop.global_step == 3
+    assert "eval/craftax_episodes" in loop.last_eval or "eval/total_loss" in loop.last_eval
