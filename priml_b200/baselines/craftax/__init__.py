@@ -1,7 +1,7 @@
 """Craftax: open-ended RL in a 2-D survival game (``priml/baselines/craftax``).
 
 The game is a batched tensor program (``game/``); the learners are PPO,
-recurrent PPO and PQN. This build covers the overworld (floor 0): terrain,
+recurrent (GRU) PPO, gated Transformer-XL PPO and PQN. This build covers the overworld (floor 0): terrain,
 tools and crafting, cows / zombies / skeletons, survival meters, sleeping,
 plants and the overworld's achievements, with the full game's action space,
 achievement table (226-point ceiling) and 8,268-float observation layout.
@@ -9,8 +9,13 @@ achievement table (226-point ceiling) and 8,268-float observation layout.
 
 from priml_b200.baselines.craftax.env import CraftaxEnv
 from priml_b200.baselines.craftax.metric import CraftaxScore
-from priml_b200.baselines.craftax.model import ActorCritic, ActorCriticRNN, RecurrentQNetwork
-from priml_b200.baselines.craftax.train_step import CraftaxPQNTrainStep, CraftaxRNNTrainStep, CraftaxTrainStep
+from priml_b200.baselines.craftax.model import ActorCritic, ActorCriticGTrXL, ActorCriticRNN, RecurrentQNetwork
+from priml_b200.baselines.craftax.train_step import (
+    CraftaxGTrXLTrainStep,
+    CraftaxPQNTrainStep,
+    CraftaxRNNTrainStep,
+    CraftaxTrainStep,
+)
 
-__all__ = ["ActorCritic", "ActorCriticRNN", "CraftaxEnv", "CraftaxPQNTrainStep", "CraftaxRNNTrainStep",
-           "CraftaxScore", "CraftaxTrainStep", "RecurrentQNetwork"]
+__all__ = ["ActorCritic", "ActorCriticGTrXL", "ActorCriticRNN", "CraftaxEnv", "CraftaxGTrXLTrainStep",
+           "CraftaxPQNTrainStep", "CraftaxRNNTrainStep", "CraftaxScore", "CraftaxTrainStep", "RecurrentQNetwork"]

@@ -8,10 +8,10 @@ experiment  parent    change
 ``exp002``  exp001    a reset-aware GRU policy (recurrent PPO)
 ``exp003``  exp001    no policy at all: PQN with an LSTM Q-network
 ``exp011``  exp001    the 1B geometry at 100M interactions (a screening budget)
+``exp013``  exp001    a policy with memory, expensively: gated Transformer-XL
 ==========  ========  =========================================================
 
-``exp013`` (GTrXL memory) is not built. ``exp_smoke`` cuts exp000 to a few
-updates. Evaluation plays the policy in fresh worlds (:class:`CraftaxScore`).
+``exp_smoke`` cuts exp000 to a few updates. Evaluation plays the policy in fresh worlds (:class:`CraftaxScore`).
 """
 
 from __future__ import annotations
@@ -21,12 +21,17 @@ from typing import Any
 
 from priml_b200.baselines.craftax.data import CraftaxRollouts
 from priml_b200.baselines.craftax.metric import CraftaxScore
-from priml_b200.baselines.craftax.train_step import CraftaxPQNTrainStep, CraftaxRNNTrainStep, CraftaxTrainStep
+from priml_b200.baselines.craftax.train_step import (
+    CraftaxGTrXLTrainStep,
+    CraftaxPQNTrainStep,
+    CraftaxRNNTrainStep,
+    CraftaxTrainStep,
+)
 from priml_b200.config import Makes
 from priml_b200.parallel.runtime import SingleProcess
 from priml_b200.train.train_loop import TrainLoop
 
-__all__ = ["CraftaxTrainLoop", "exp000", "exp001", "exp002", "exp003", "exp011", "exp_smoke"]
+__all__ = ["CraftaxTrainLoop", "exp000", "exp001", "exp002", "exp003", "exp011", "exp013", "exp_smoke"]
 
 
 class CraftaxTrainLoop(Makes["TrainLoop"], TrainLoop.Config):
@@ -89,6 +94,17 @@ def exp011() -> CraftaxTrainLoop:
     cfg = exp001()
     cfg.experiment_name = "exp011"
     cfg.max_steps = cfg.step.total_train_steps = _updates(100_000_000, 1024, 64)
+    return cfg
+
+
+def exp013() -> CraftaxTrainLoop:
+    cfg = exp001()
+    cfg.experiment_name = "exp013"
+    gt = CraftaxGTrXLTrainStep.Config()
+    gt.env, gt.learning_rate = cfg.step.env, 2e-4
+    gt.total_train_steps = _updates(1_000_000_000, 1024, gt.rollout_steps)
+    cfg.step = gt
+    cfg.max_steps = gt.total_train_steps
     return cfg
 
 

@@ -14,6 +14,8 @@ return / 226 x 100) and checkpointable environment / generator state.
 * :class:`CraftaxRNNTrainStep` -- the same objective on a GRU policy; the
   recurrent state is carried across updates and minibatches are whole worker
   sequences replayed from the rollout's initial state.
+* :class:`CraftaxGTrXLTrainStep` -- the recurrent objective on a gated
+  Transformer-XL whose state is a per-layer memory of the last 128 inputs.
 * :class:`CraftaxPQNTrainStep` -- PQN (Gallici et al. 2024): epsilon-greedy
   rollouts from a recurrent Q-network, Peng's Q(lambda) targets from the
   rollout's own Q-values, squared error on the chosen actions' Q-values.
@@ -31,12 +33,18 @@ from torch.nn import functional as F
 from priml_b200.baselines.craftax.env import CraftaxEnv
 from priml_b200.baselines.craftax.game import constants as C
 from priml_b200.baselines.craftax.game.observation import observation_size
-from priml_b200.baselines.craftax.model import ActorCritic, ActorCriticRNN, RecurrentQNetwork, epsilon_at
+from priml_b200.baselines.craftax.model import (
+    ActorCritic,
+    ActorCriticGTrXL,
+    ActorCriticRNN,
+    RecurrentQNetwork,
+    epsilon_at,
+)
 from priml_b200.config import Makes, PartialConfig
 from priml_b200.math.advantage import explained_variance, generalized_advantage, q_lambda_targets
 from priml_b200.train.train_step import TrainStep, TrainStepOutput
 
-__all__ = ["CraftaxPQNTrainStep", "CraftaxRNNTrainStep", "CraftaxTrainStep", "ppo_terms"]
+__all__ = ["CraftaxGTrXLTrainStep", "CraftaxPQNTrainStep", "CraftaxRNNTrainStep", "CraftaxTrainStep", "ppo_terms"]
 
 
 def ppo_terms(logits: Tensor, actions: Tensor, old_log_prob: Tensor, value: Tensor, old_value: Tensor,
@@ -271,14 +279,24 @@ class CraftaxRNNTrainStep(_RolloutStep):
         super().__init__(config)
         self._hidden = self.model.initial_state(self._observation.shape[0], self.device)
 
+    @staticmethod
+    def _parts(state: Any) -> tuple[Tensor, ...]:
+        return tuple(state) if isinstance(state, tuple) else (state,)
+
+    def _pack(self, parts: tuple[Tensor, ...]) -> Any:
+        return parts if isinstance(self._hidden, tuple) else parts[0]
+
+    def _keep_dtype(self, state: Any) -> Any:
+        return self._pack(tuple(x.float() if x.is_floating_point() else x for x in self._parts(state)))
+
     @torch.no_grad()
     def collect(self) -> dict[str, Tensor]:
-        h0, prev_done0 = self._hidden.clone(), self._done.clone()
+        h0 = {f"h0_{i}": x.clone()[None] for i, x in enumerate(self._parts(self._hidden))}
         obs, pdone, act, logp, val, rew, done = [], [], [], [], [], [], []
         for _ in range(self.config.rollout_steps):
             with self._autocast():
                 self._hidden, logits, value = self.model.step(self._hidden, self._observation, self._done)
-            self._hidden = self._hidden.float()
+            self._hidden = self._keep_dtype(self._hidden)
             lp = logits.float().log_softmax(-1)
             a = torch.multinomial(lp.exp(), 1, generator=self._generator)[:, 0]
             obs.append(self._observation)
@@ -298,12 +316,13 @@ class CraftaxRNNTrainStep(_RolloutStep):
                                             last_value=last.float(), discount=self.config.discount,
                                             trace_decay=self.config.trace_decay)  # fmt: skip
         return {"observation": torch.stack(obs), "previous_done": torch.stack(pdone), "action": torch.stack(act),
-                "log_prob": torch.stack(logp), "value": value, "advantage": adv, "target": target,
-                "h0": h0[None], "d0": prev_done0[None]}  # fmt: skip
+                "log_prob": torch.stack(logp), "value": value, "advantage": adv, "target": target, **h0}  # fmt: skip
 
     def _loss(self, mb: dict[str, Tensor]) -> tuple[Tensor, dict[str, Tensor]]:
+        n = sum(1 for k in mb if k.startswith("h0_"))
+        state = self._pack(tuple(mb[f"h0_{i}"][0] for i in range(n)))
         with self._autocast():
-            _, logits, value = self.model.sequence(mb["h0"][0], mb["observation"], mb["previous_done"])
+            _, logits, value = self.model.sequence(state, mb["observation"], mb["previous_done"])
         c = self.config
         t = ppo_terms(logits, mb["action"], mb["log_prob"], value, mb["value"], mb["advantage"], mb["target"],
                       c.clip_epsilon)  # fmt: skip
@@ -331,6 +350,15 @@ class CraftaxRNNTrainStep(_RolloutStep):
     def load_state_dict(self, s: dict[str, Any]) -> None:
         super().load_state_dict(s)
         self._hidden = s["hidden"]
+
+
+class CraftaxGTrXLTrainStep(CraftaxRNNTrainStep):
+    """PPO on the gated Transformer-XL policy (``priml/baselines/craftax/gtrxl_train_step.py``): the
+    same recurrent machinery, with a memory of the last 128 inputs per layer as the carried state."""
+
+    class Config(Makes["CraftaxGTrXLTrainStep"], CraftaxRNNTrainStep.Config, kw_only=False):
+        model: Any = field(default_factory=ActorCriticGTrXL.Config)
+        rollout_steps: int = 128
 
 
 class CraftaxPQNTrainStep(_RolloutStep):

@@ -6,7 +6,9 @@ import torch
 
 from priml_b200.baselines.craftax import (
     ActorCritic,
+    ActorCriticGTrXL,
     CraftaxEnv,
+    CraftaxGTrXLTrainStep,
     CraftaxPQNTrainStep,
     CraftaxRNNTrainStep,
     CraftaxScore,
@@ -161,8 +163,12 @@ def _step_cfg(cls, **kw):  # noqa: ANN001, ANN202
 
 
 def test_ppo_recurrent_ppo_and_pqn_update() -> None:
-    for cls in (CraftaxTrainStep, CraftaxRNNTrainStep, CraftaxPQNTrainStep):
-        step = _step_cfg(cls)
+    for cls in (CraftaxTrainStep, CraftaxRNNTrainStep, CraftaxGTrXLTrainStep, CraftaxPQNTrainStep):
+        kw = {"rollout_steps": 8}
+        step = _step_cfg(cls, **kw)
+        if cls is CraftaxGTrXLTrainStep:
+            step = _step_cfg(cls, model=ActorCriticGTrXL.Config(embed_dim=32, num_heads=4, hidden_size=32,
+                                                                 memory_length=8))  # fmt: skip
         before = [p.detach().clone() for p in step.model.parameters()]
         out = step.train_step()
         assert torch.isfinite(out["loss"]).all() and out["stepped"], cls.__name__
@@ -170,7 +176,7 @@ def test_ppo_recurrent_ppo_and_pqn_update() -> None:
         step._lr()
         assert step.global_step == 1 and abs(step.optimizer.param_groups[0]["lr"] - 3e-4 * 0.9) < 1e-12  # annealed
         state = step.state_dict()
-        again = _step_cfg(cls)
+        again = _step_cfg(cls, model=step.config.model.copy_tree()) if cls is CraftaxGTrXLTrainStep else _step_cfg(cls)
         again.load_state_dict(state)
         assert again.global_step == 1
 
@@ -186,7 +192,8 @@ def test_crafter_score_and_metric_plays_a_policy() -> None:
 
 
 def test_experiment_chain_and_smoke_loop(tmp_path) -> None:  # noqa: ANN001
-    for exp in (experiments.exp000, experiments.exp001, experiments.exp002, experiments.exp003, experiments.exp011):
+    for exp in (experiments.exp000, experiments.exp001, experiments.exp002, experiments.exp003, experiments.exp011,
+                experiments.exp013):
         cfg = exp().copy_tree().finalize()
         assert cfg.step.total_train_steps > 0
     assert experiments.exp000().step.total_train_steps == 244
