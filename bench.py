@@ -43,7 +43,7 @@ import time
 from pathlib import Path
 from typing import Any
 
-BASELINE_TOKENS_PER_S: float | None = None  # BASELINE.md publishes no B200 / LLM-at-scale number
+BASELINE_TOKENS_PER_S: float | None = None  # the reference publishes no B200 or LLM-at-scale throughput
 
 
 def _parse() -> argparse.Namespace:

@@ -1,8 +1,8 @@
 """Muon and NorMuon (``priml/optimizers/muon.py:38-253``, ``priml/optimizers/normuon.py:55-407``).
 
 Both orthogonalize a momentum update with a bf16 polynomial iteration whose
-matmuls run on the tensor cores (cuBLAS-free on CUDA: the batched iteration goes
-through ``torch.baddbmm`` / ``@`` today; see the optimizer notes in DESIGN).
+matmuls run on the tensor cores as plain batched library GEMMs (``@`` on stacked
+``[N, R, C]`` buckets: one launch per product for the whole bucket).
 NorMuon stacks same-shape parameters and adds a per-row second-moment rescale
 and "cautious" weight decay. State keys match the reference (``momentum_buffer``;
 NorMuon keeps ``momentum_buffer`` / ``second_moment`` on the first parameter of
