@@ -164,3 +164,26 @@ def test_worker_pool_reports_rank_failure() -> None:
     """A rank that raises (host-side fault injection) is reported, not hung on."""
     with pytest.raises(RuntimeError, match="injected failure"):
         run_ranks(_boom, 2, timeout_s=20)
+
+
+def _sparse_sign_sgd(rank: int, world: int) -> list[float]:
+    from priml_b200.optimizers import SignSGD
+
+    table = torch.zeros(6, 2)
+    leaf = torch.zeros(2, 2, requires_grad=True)
+    ids = torch.tensor([rank, 4], dtype=torch.int32)  # row 4 is shared by both ranks
+    leaf.grad = torch.tensor([[1.0, -1.0], [1.0, 2.0]]) if rank == 0 else torch.tensor([[-1.0, -1.0], [-3.0, -1.0]])
+    opt = SignSGD([{"params": [table, leaf, ids], "sparse_embedding": True}], lr=0.5)
+    opt.step()
+    return table.flatten().tolist()
+
+
+def test_sparse_sign_sgd_sums_row_gradients_across_ranks() -> None:
+    """Each rank touches its own row and a shared one; the shared row steps on the SUM of the
+    ranks' gradients and every rank ends with the same table."""
+    a, b = run_ranks(_sparse_sign_sgd, 2, mesh_shape={"dp": 2})
+    assert a == b
+    t = torch.tensor(a).view(6, 2)
+    assert t[0].tolist() == [-0.5, 0.5] and t[1].tolist() == [0.5, 0.5]
+    assert t[4].tolist() == [0.5, -0.5]  # sign of (1 - 3, 2 - 1)
+    assert t[[2, 3, 5]].abs().sum() == 0
