@@ -203,6 +203,23 @@ MAX_RANGED_MOBS: Final = 2
 MAX_GROWING_PLANTS: Final = 10
 MOB_DESPAWN_DISTANCE: Final = 14
 
+LEVELS: Final = 2
+"""Floors built: 0 = overworld, 1 = dungeon (the game has nine)."""
+MONSTERS_KILLED_TO_CLEAR_LEVEL: Final = 8
+"""Kills on a floor before its ladder down opens."""
+LEVEL_ACHIEVEMENT: Final = (None, Achievement.ENTER_DUNGEON)
+SPECIES: Final = (0, 2)
+"""Creature species per floor (observation channel offset): overworld 0 (cow / zombie / skeleton),
+dungeon 2 (snail / orc soldier / orc mage)."""
+FLOOR_HEALTH: Final = ((3.0, 5.0, 3.0), (4.0, 7.0, 5.0))
+"""Fresh creature health per floor: (passive, melee, ranged)."""
+FLOOR_DAMAGE: Final = ((2.0, 2.0), (3.0, 3.0))
+"""Damage per floor: (melee hit, ranged projectile)."""
+FLOOR_SPAWN: Final = ((0.1, 0.02, 0.05, 0.1), (0.1, 0.06, 0.05, 0.06))
+"""Spawn probability per floor: (passive, melee by day, ranged, melee at night)."""
+KILL_ACHIEVEMENT: Final = ((Achievement.EAT_COW, Achievement.DEFEAT_ZOMBIE, Achievement.DEFEAT_SKELETON),
+                           (Achievement.EAT_SNAIL, Achievement.DEFEAT_ORC_SOLIDER, Achievement.DEFEAT_ORC_MAGE))  # fmt: skip
+
 # overworld creatures: passive = cow, melee = zombie, ranged = skeleton (tunnels only)
 PASSIVE_HEALTH: Final = 3.0
 MELEE_HEALTH: Final = 5.0

@@ -6,7 +6,9 @@ ranged, mob projectile, player projectile) and a lit flag -- 83 planes, masked
 by the lit flag -- flattened, then 51 player features (square-rooted counts,
 tool levels, meters / 10, facing direction, armour, condition). 8,268 floats
 in all, the same layout as the reference so that trained networks read it.
-Tiles beyond the map edge read OUT_OF_BOUNDS. The overworld is always lit.
+Tiles beyond the map edge read OUT_OF_BOUNDS. The overworld is always lit; in
+the dungeon a tile is seen within 3 tiles of the player or 4 of a torch (this
+build's light rule).
 """
 
 from __future__ import annotations
@@ -46,22 +48,32 @@ def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
     mobs = torch.zeros(s.num_envs, vr, vc, 5 * 8, device=s.device)
     corner = s.position - torch.tensor([vr // 2, vc // 2], device=s.device)
     e = torch.arange(s.num_envs, device=s.device)
-    for creatures, plane in ((s.melee, 1), (s.passive, 0), (s.ranged, 2), (s.projectiles, 3)):
+    species = torch.tensor(C.SPECIES, device=s.device)[s.level]
+    for creatures, plane, typed in ((s.melee, 1, True), (s.passive, 0, True), (s.ranged, 2, True),
+                                    (s.projectiles, 3, True), (s.shots, 4, False)):  # fmt: skip
+        channel = plane * 8 + (species if typed else torch.zeros_like(species))
         for slot in range(creatures.mask.shape[1]):
             local = creatures.position[:, slot] - corner
             seen = creatures.mask[:, slot] & (local[:, 0] >= 0) & (local[:, 0] < vr) & (local[:, 1] >= 0) & (local[:, 1] < vc)
             r, c = local[:, 0].clamp(0, vr - 1), local[:, 1].clamp(0, vc - 1)
-            mobs[e, r, c, plane * 8] = torch.maximum(mobs[e, r, c, plane * 8], seen.float())
-    lit = torch.ones(s.num_envs, vr, vc, 1, device=s.device)
+            mobs[e, r, c, channel] = torch.maximum(mobs[e, r, c, channel], seen.float())
+    # the surface is lit; below it the player sees 3 tiles around itself and 4 around a torch
+    rr = torch.arange(vr, device=s.device)[:, None] - vr // 2
+    cc = torch.arange(vc, device=s.device)[None, :] - vc // 2
+    near = (torch.maximum(rr.abs(), cc.abs()) <= 3).expand(s.num_envs, vr, vc)
+    torch_light = F.max_pool2d((items == int(C.ItemType.TORCH)).float()[:, None], 9, 1, 4)[:, 0] > 0
+    lit = ((s.level == 0)[:, None, None] | near | torch_light).float()[..., None]
     tiles = torch.cat([F.one_hot(blocks, len(C.BlockType)).float(), F.one_hot(items, len(C.ItemType)).float(), mobs], -1)
     view_part = torch.cat([tiles * lit, lit], -1).flatten(1)
     z = torch.zeros(s.num_envs, device=s.device)
     counts = torch.stack([s.wood, s.stone, s.coal, s.iron, s.diamond, z, z, s.sapling, s.torches, s.arrows], -1).float()
-    tools = torch.stack([z, s.pickaxe.float() / 4.0, s.sword.float() / 4.0, z, z, z], -1)
-    potions = torch.zeros(s.num_envs, 6, device=s.device)
-    meters = torch.stack([s.health, s.food.float(), s.drink.float(), s.energy.float(), z, z, z, z, z], -1)
+    tools = torch.stack([z, s.pickaxe.float() / 4.0, s.sword.float() / 4.0, z, z, s.bow.float()], -1)
+    potions = s.potions.float().sqrt() / 10.0
+    meters = torch.stack([s.health, s.food.float(), s.drink.float(), s.energy.float(), z, s.xp.float(),
+                          s.dexterity.float(), s.strength.float(), s.intelligence.float()], -1)  # fmt: skip
     facing = F.one_hot((s.direction - 1).clamp(min=0), 4).float()
-    condition = torch.stack([s.light, s.sleeping.float(), z, z, z, z, z, z], -1)
+    cleared = (s.kills[e, s.level] >= C.MONSTERS_KILLED_TO_CLEAR_LEVEL).float()
+    condition = torch.stack([s.light, s.sleeping.float(), z, z, z, s.level.float() / 10.0, cleared, z], -1)
     player = torch.cat([counts.sqrt() / 10.0, tools, potions, meters / 10.0, facing, s.armour.float() / 2.0,
                         torch.zeros(s.num_envs, 4, device=s.device), condition], -1)  # fmt: skip
     return torch.cat([view_part, player], -1)

@@ -1,4 +1,4 @@
-"""Batched overworld state of the Craftax game (``priml/baselines/craftax/game/state.py``).
+"""Batched state of the Craftax game (``priml/baselines/craftax/game/state.py``).
 
 Every field is a tensor with the worker (environment) axis first, so one rollout
 step is one batched tensor program on the device: no simulator process and no
@@ -77,6 +77,22 @@ class GameState:
     achievements: Tensor  # [E, 67] bool
     timestep: Tensor  # [E] int64
     light: Tensor  # [E] float daylight
+    # floors: `map` / `item_map` hold the current floor; the others wait in the floor stores
+    level: Tensor  # [E] int64
+    floor_map: Tensor  # [E, L, H, W]
+    floor_items: Tensor  # [E, L, H, W]
+    ladder_down: Tensor  # [E, L, 2]
+    ladder_up: Tensor  # [E, L, 2]
+    kills: Tensor  # [E, L] monsters defeated per floor
+    visited: Tensor  # [E, L] bool
+    bow: Tensor  # [E]
+    potions: Tensor  # [E, 6] red, green, blue, pink, cyan, yellow
+    potion_effect: Tensor  # [E, 6] hidden effect of each colour (a permutation per world)
+    xp: Tensor  # [E]
+    dexterity: Tensor  # [E] attributes 1..5
+    strength: Tensor
+    intelligence: Tensor
+    shots: Creatures  # the player's arrows in flight
 
     @property
     def num_envs(self) -> int:
@@ -145,5 +161,13 @@ def empty_state(envs: int, device: torch.device) -> GameState:
         projectiles=Creatures.empty(envs, 3, device),
         plant_position=z(torch.long, C.MAX_GROWING_PLANTS, 2), plant_age=z(torch.long, C.MAX_GROWING_PLANTS),
         plant_mask=z(torch.bool, C.MAX_GROWING_PLANTS), achievements=z(torch.bool, C.NUM_ACHIEVEMENTS),
-        timestep=z(), light=torch.ones(envs, device=device), **counts,
+        timestep=z(), light=torch.ones(envs, device=device),
+        level=z(), floor_map=z(torch.long, C.LEVELS, rows, cols), floor_items=z(torch.long, C.LEVELS, rows, cols),
+        ladder_down=z(torch.long, C.LEVELS, 2), ladder_up=z(torch.long, C.LEVELS, 2), kills=z(torch.long, C.LEVELS),
+        visited=z(torch.bool, C.LEVELS), bow=z(), potions=z(torch.long, 6),
+        potion_effect=torch.arange(6, device=device).expand(envs, 6).clone(), xp=z(),
+        dexterity=torch.ones(envs, dtype=torch.long, device=device),
+        strength=torch.ones(envs, dtype=torch.long, device=device),
+        intelligence=torch.ones(envs, dtype=torch.long, device=device),
+        shots=Creatures.empty(envs, 3, device), **counts,
     )  # fmt: skip

@@ -1,10 +1,12 @@
-"""One batched step of the Craftax overworld (``priml/baselines/craftax/game/step.py``).
+"""One batched step of the Craftax game, overworld and dungeon (``priml/baselines/craftax/game/step.py``).
 
 Order of operations per step (every rule is a masked tensor update over all
-workers at once): sleeping workers act NOOP -> crafting -> DO on the facing tile
-(creatures first, then the block) -> placing -> movement -> creatures (move,
-attack, arrows) -> spawning / despawning -> plants -> survival meters ->
-achievements from the inventory -> reward.
+workers at once): sleeping workers act NOOP -> ladders (descend needs 8 kills on
+the floor; creatures stay behind) -> crafting -> DO on the facing tile
+(creatures first, then the block: mining, chests, water / fountain, plants) ->
+placing -> potions, attribute level-ups and bow shots -> movement -> creatures
+(move, attack, projectiles) -> the player's arrows -> spawning / despawning ->
+plants -> survival meters -> achievements from the inventory -> reward.
 
 The rules are Crafter's and Craftax's published ones for the overworld (tool
 tiers for mining, crafting next to a table (and furnace), cows / zombies /
@@ -135,21 +137,28 @@ def _craft(s: GameState, a: Tensor) -> None:
 
 
 # ---------------------------------------------------------------- DO
-def _hit_creatures(s: GameState, target: Tensor, doing: Tensor) -> Tensor:
-    """Damage the creature on ``target``; returns where a creature absorbed the action."""
-    damage = _SWORD_DAMAGE.to(s.device)[s.sword]
+def _level_table(s: GameState, table: tuple, column: int) -> Tensor:
+    return torch.tensor([row[column] for row in table], device=s.device)[s.level]
+
+
+def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) -> Tensor:
+    """Damage the creature on ``target``; returns where a creature absorbed the blow."""
     absorbed = torch.zeros_like(doing)
-    for mobs, ach in ((s.passive, A.EAT_COW), (s.melee, A.DEFEAT_ZOMBIE), (s.ranged, A.DEFEAT_SKELETON)):
+    r = _rows(s)
+    for cls, mobs in enumerate((s.passive, s.melee, s.ranged)):
         at = (mobs.position == target[:, None]).all(-1) & mobs.mask & doing[:, None] & ~absorbed[:, None]
         hit_any = at.any(-1)
         mobs.health = mobs.health - at.float() * damage[:, None]
         killed = at & (mobs.health <= 0)
         mobs.mask = mobs.mask & ~killed
         died = killed.any(-1)
-        if mobs is s.passive:  # eating a cow
+        if cls == 0:  # eating the passive creature
             s.food = torch.where(died, torch.clamp(s.food + 6, max=_CAP), s.food)
             s.hunger = torch.where(died, torch.zeros_like(s.hunger), s.hunger)
-        _unlock(s, ach, died)
+        else:
+            s.kills[r, s.level] = s.kills[r, s.level] + died.long()
+        ach = torch.tensor([int(row[cls]) for row in C.KILL_ACHIEVEMENT], device=s.device)[s.level]
+        s.achievements[r, ach] |= died
         absorbed |= hit_any
     return absorbed
 
@@ -157,7 +166,8 @@ def _hit_creatures(s: GameState, target: Tensor, doing: Tensor) -> Tensor:
 def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> None:
     doing = a == int(Act.DO)
     target = _facing(s)
-    doing = doing & ~_hit_creatures(s, target, doing)
+    damage = _SWORD_DAMAGE.to(s.device)[s.sword] * (1.0 + 0.25 * (s.strength - 1).float())
+    doing = doing & ~_hit_creatures(s, target, doing, damage)
     block = _tile(s.map, target)
 
     def mine(kind: B, tool: int, item: str) -> None:
@@ -173,7 +183,10 @@ def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> Non
     mine(B.DIAMOND, 3, "diamond")
     sapling = doing & (block == int(B.GRASS)) & (torch.rand(s.num_envs, device=s.device, generator=generator) < 0.1)
     s.sapling = torch.clamp(s.sapling + sapling.long(), max=_CAP)
-    drink = doing & (block == int(B.WATER))
+    chest = doing & (block == int(B.CHEST))
+    _open_chest(s, chest, generator)
+    s.map = _set(s.map, target, int(B.PATH), chest)
+    drink = doing & ((block == int(B.WATER)) | (block == int(B.FOUNTAIN)))
     s.drink = torch.where(drink, torch.clamp(s.drink + 1, max=_CAP), s.drink)
     s.thirst = torch.where(drink, torch.zeros_like(s.thirst), s.thirst)
     _unlock(s, A.COLLECT_DRINK, drink)
@@ -184,6 +197,97 @@ def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> Non
     at_plant = (s.plant_position == target[:, None]).all(-1) & s.plant_mask & eat[:, None]
     s.plant_age = torch.where(at_plant, torch.zeros_like(s.plant_age), s.plant_age)
     _unlock(s, A.EAT_PLANT, eat)
+
+
+def _open_chest(s: GameState, opening: Tensor, generator: torch.Generator | None) -> None:
+    """Loot (this build's table): 1-4 arrows, and each with probability 1/2: 1-2 torches, a potion
+    of a random colour, 1 iron; 1 diamond with probability 1/10. The first chest on a floor below
+    the surface also holds a bow if the player has none."""
+    dev, n = s.device, s.num_envs
+
+    def roll(p: float) -> Tensor:
+        return opening & (torch.rand(n, device=dev, generator=generator) < p)
+
+    s.arrows = torch.clamp(s.arrows + opening.long() * torch.randint(1, 5, (n,), device=dev, generator=generator), max=99)
+    s.torches = torch.clamp(s.torches + roll(0.5).long() * torch.randint(1, 3, (n,), device=dev, generator=generator), max=99)
+    colour = torch.randint(0, 6, (n,), device=dev, generator=generator)
+    got = roll(0.5)
+    s.potions[_rows(s), colour] = s.potions[_rows(s), colour] + got.long()
+    s.iron = torch.clamp(s.iron + roll(0.5).long(), max=_CAP)
+    s.diamond = torch.clamp(s.diamond + roll(0.1).long(), max=_CAP)
+    bow = opening & (s.bow == 0) & (s.level > 0)
+    s.bow = s.bow + bow.long()
+    _unlock(s, A.OPEN_CHEST, opening)
+    _unlock(s, A.FIND_BOW, bow)
+
+
+_POTION_ACTIONS = (Act.DRINK_POTION_RED, Act.DRINK_POTION_GREEN, Act.DRINK_POTION_BLUE, Act.DRINK_POTION_PINK,
+                   Act.DRINK_POTION_CYAN, Act.DRINK_POTION_YELLOW)  # fmt: skip
+
+
+def _abilities(s: GameState, a: Tensor) -> None:
+    r = _rows(s)
+    for colour, act in enumerate(_POTION_ACTIONS):
+        drink = (a == int(act)) & (s.potions[:, colour] >= 1)
+        s.potions[:, colour] = s.potions[:, colour] - drink.long()
+        effect = s.potion_effect[:, colour]
+        # this build's effects: heal 8 / hurt 3 / energy +8 / energy -3 / drink +8 / drink -3
+        s.health = torch.where(drink & (effect == 0), s.health + 8, torch.where(drink & (effect == 1), s.health - 3, s.health))
+        s.energy = torch.where(drink & (effect == 2), s.energy + 8, torch.where(drink & (effect == 3), s.energy - 3, s.energy))
+        s.drink = torch.where(drink & (effect == 4), s.drink + 8, torch.where(drink & (effect == 5), s.drink - 3, s.drink))
+        _unlock(s, A.DRINK_POTION, drink)
+    for act, name in ((Act.LEVEL_UP_DEXTERITY, "dexterity"), (Act.LEVEL_UP_STRENGTH, "strength"),
+                      (Act.LEVEL_UP_INTELLIGENCE, "intelligence")):  # fmt: skip
+        up = (a == int(act)) & (s.xp >= 1) & (getattr(s, name) < 5)
+        setattr(s, name, getattr(s, name) + up.long())
+        s.xp = s.xp - up.long()
+    # a bow shot: an arrow leaves the facing tile and flies one tile per step
+    shoot = (a == int(Act.SHOOT_ARROW)) & (s.bow >= 1) & (s.arrows >= 1) & ~s.shots.mask.all(-1)
+    first = torch.argmax((~s.shots.mask).long(), -1)
+    d = _DELTA.to(s.device)[s.direction]
+    pos, dirn, mask = s.shots.position.clone(), s.shots.direction.clone(), s.shots.mask.clone()
+    pos[r, first] = torch.where(shoot[:, None], s.position, pos[r, first])
+    dirn[r, first] = torch.where(shoot[:, None], d, dirn[r, first])
+    mask[r, first] = mask[r, first] | shoot
+    s.shots.position, s.shots.direction, s.shots.mask = pos, dirn, mask
+    s.arrows = s.arrows - shoot.long()
+    _unlock(s, A.FIRE_BOW, shoot)
+
+
+def _fly_shots(s: GameState) -> None:
+    shots = s.shots
+    shots.position = shots.position + shots.direction * shots.mask[..., None].long()
+    damage = torch.full((s.num_envs,), 2.0, device=s.device) * (1.0 + 0.25 * (s.dexterity - 1).float())
+    for slot in range(shots.mask.shape[1]):
+        live = shots.mask[:, slot]
+        hit = _hit_creatures(s, shots.position[:, slot], live, damage)
+        b = _tile(s.map, shots.position[:, slot])
+        passable = (b == int(B.GRASS)) | (b == int(B.SAND)) | (b == int(B.PATH)) | (b == int(B.WATER)) | (b == int(B.LAVA))
+        shots.mask[:, slot] = live & ~hit & passable
+
+
+def _change_floor(s: GameState, a: Tensor) -> None:
+    here = _tile(s.item_map, s.position)
+    r, lvl = _rows(s), s.level
+    cleared = s.kills[r, lvl] >= C.MONSTERS_KILLED_TO_CLEAR_LEVEL
+    down = (a == int(Act.DESCEND)) & (here == int(I.LADDER_DOWN)) & cleared & (lvl < C.LEVELS - 1)
+    up = (a == int(Act.ASCEND)) & (here == int(I.LADDER_UP)) & (lvl > 0)
+    move = down | up
+    if not bool(move.any()):
+        return
+    s.floor_map[r, lvl] = torch.where(move[:, None, None], s.map, s.floor_map[r, lvl])
+    s.floor_items[r, lvl] = torch.where(move[:, None, None], s.item_map, s.floor_items[r, lvl])
+    new = lvl + down.long() - up.long()
+    s.map = torch.where(move[:, None, None], s.floor_map[r, new], s.map)
+    s.item_map = torch.where(move[:, None, None], s.floor_items[r, new], s.item_map)
+    s.position = torch.where(down[:, None], s.ladder_up[r, new], torch.where(up[:, None], s.ladder_down[r, new], s.position))
+    s.level = new
+    for mobs in (s.passive, s.melee, s.ranged, s.projectiles, s.shots):  # creatures stay behind (and despawn)
+        mobs.mask = mobs.mask & ~move[:, None]
+    first = move & ~s.visited[r, new]
+    s.visited[r, new] |= move
+    s.xp = s.xp + first.long()
+    _unlock(s, A.ENTER_DUNGEON, move & (new == 1))
 
 
 # ---------------------------------------------------------------- placing
@@ -271,7 +375,8 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     _try_move(s, s.melee, step, (B.GRASS, B.SAND, B.PATH))
     dist = (s.position[:, None] - s.melee.position).abs().sum(-1)
     attack = s.melee.mask & (dist <= 1) & (s.melee.cooldown <= 0)
-    damage = torch.where(s.sleeping, torch.full_like(s.health, 7.0), torch.full_like(s.health, C.MELEE_DAMAGE))
+    melee_hit = _level_table(s, C.FLOOR_DAMAGE, 0)
+    damage = torch.where(s.sleeping, torch.full_like(s.health, 7.0), melee_hit)
     s.health = s.health - attack.sum(-1).float() * damage * _armour_factor(s)
     s.melee.cooldown = torch.where(attack, torch.full_like(s.melee.cooldown, 5), (s.melee.cooldown - 1).clamp(min=0))
     # skeletons keep to the caves and shoot along rows / columns when the player is within 4 tiles
@@ -296,7 +401,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     # arrows fly one tile per step: they hurt the player they reach and stop at solid tiles
     proj.position = proj.position + proj.direction * proj.mask[..., None].long()
     hit = proj.mask & (proj.position == s.position[:, None]).all(-1)
-    s.health = s.health - hit.sum(-1).float() * C.ARROW_DAMAGE * _armour_factor(s)
+    s.health = s.health - hit.sum(-1).float() * _level_table(s, C.FLOOR_DAMAGE, 1) * _armour_factor(s)
     blocked = torch.zeros_like(proj.mask)
     for slot in range(proj.mask.shape[1]):
         b = _tile(s.map, proj.position[:, slot])
@@ -308,39 +413,44 @@ def _spawn(s: GameState, generator: torch.Generator | None) -> None:
     dev, e = s.device, s.num_envs
     rows, cols = C.MAP_SIZE
     night = s.light < 0.5
-    for mobs, chance, allowed, min_dist, health in (
-        (s.passive, torch.full((e,), C.SPAWN_CHANCE["passive"], device=dev), B.GRASS, 3, C.PASSIVE_HEALTH),
-        (s.melee, torch.where(night, C.SPAWN_CHANCE["melee_night"], C.SPAWN_CHANCE["melee"]), B.GRASS, 6, C.MELEE_HEALTH),
-        (s.ranged, torch.full((e,), C.SPAWN_CHANCE["ranged"], device=dev), B.PATH, 4, C.RANGED_HEALTH),
+    surface = s.level == 0
+    melee_chance = torch.where(night & surface, _level_table(s, C.FLOOR_SPAWN, 3), _level_table(s, C.FLOOR_SPAWN, 1))
+    grass_or_path = torch.where(surface, int(B.GRASS), int(B.PATH))
+    for cls, mobs, chance, tile, min_dist in (
+        (0, s.passive, _level_table(s, C.FLOOR_SPAWN, 0), grass_or_path, 3),
+        (1, s.melee, melee_chance, grass_or_path, 6),
+        (2, s.ranged, _level_table(s, C.FLOOR_SPAWN, 2), torch.full_like(s.level, int(B.PATH)), 4),
     ):  # fmt: skip
-        # despawn creatures that wandered far from the player
         far = (mobs.position - s.position[:, None]).abs().max(-1).values > C.MOB_DESPAWN_DISTANCE
         mobs.mask = mobs.mask & ~far
         pos = torch.stack([(s.position[:, 0] + torch.randint(-9, 10, (e,), device=dev, generator=generator)).clamp(0, rows - 1),
                            (s.position[:, 1] + torch.randint(-9, 10, (e,), device=dev, generator=generator)).clamp(0, cols - 1)], -1)  # fmt: skip
         ok = torch.rand(e, device=dev, generator=generator) < chance
-        ok &= (_tile(s.map, pos) == int(allowed)) & ~_occupied(s, pos)
+        ok &= (_tile(s.map, pos) == tile) & ~_occupied(s, pos) & ~(pos == s.position).all(-1)
         ok &= (pos - s.position).abs().sum(-1) >= min_dist
         free = ~mobs.mask
         ok &= free.any(-1)
         first = torch.argmax(free.long(), -1)
         r = _rows(s)
+        health = _level_table(s, C.FLOOR_HEALTH, cls)
         p, h, m, cd = mobs.position.clone(), mobs.health.clone(), mobs.mask.clone(), mobs.cooldown.clone()
         p[r, first] = torch.where(ok[:, None], pos, p[r, first])
-        h[r, first] = torch.where(ok, torch.full_like(h[r, first], health), h[r, first])
+        h[r, first] = torch.where(ok, health, h[r, first])
         m[r, first] = m[r, first] | ok
         cd[r, first] = torch.where(ok, torch.zeros_like(cd[r, first]), cd[r, first])
         mobs.position, mobs.health, mobs.mask, mobs.cooldown = p, h, m, cd
 
 
 def _plants(s: GameState) -> None:
-    s.plant_age = s.plant_age + s.plant_mask.long()
+    """Saplings grow on the surface; they wait (not ageing) while the player is below."""
+    surface = s.level == 0
+    s.plant_age = s.plant_age + (s.plant_mask & surface[:, None]).long()
     for slot in range(s.plant_mask.shape[1]):
         pos = s.plant_position[:, slot]
         here = _tile(s.map, pos)
-        live = s.plant_mask[:, slot] & ((here == int(B.PLANT)) | (here == int(B.RIPE_PLANT)))
-        s.plant_mask[:, slot] = live  # a plant trampled or removed stops growing
-        ripe = live & (s.plant_age[:, slot] >= _PLANT_RIPE_AGE) & (_tile(s.map, pos) == int(B.PLANT))
+        live = s.plant_mask[:, slot] & (~surface | (here == int(B.PLANT)) | (here == int(B.RIPE_PLANT)))
+        s.plant_mask[:, slot] = live  # a plant removed stops growing
+        ripe = live & surface & (s.plant_age[:, slot] >= _PLANT_RIPE_AGE) & (here == int(B.PLANT))
         s.map = _set(s.map, pos, int(B.RIPE_PLANT), ripe)
 
 
@@ -367,7 +477,7 @@ def _survive(s: GameState, a: Tensor) -> None:
     woke = s.sleeping & (s.energy >= _CAP)
     s.sleeping = s.sleeping & ~woke
     _unlock(s, A.WAKE_UP, woke)
-    s.food, s.drink, s.energy = (x.clamp(0, _CAP) for x in (s.food, s.drink, s.energy))
+    s.food, s.drink, s.energy = (x.clamp(0, _CAP) for x in (s.food, s.drink, s.energy))  # potions may overshoot
     s.health = s.health.clamp(max=float(_CAP))
 
 
@@ -384,11 +494,14 @@ def step(s: GameState, action: Tensor, *, generator: torch.Generator | None = No
     before = s.achievements.clone()
     health_before = s.health.clone()
     a = torch.where(s.sleeping, torch.full_like(action, int(Act.NOOP)), action.long())
+    _change_floor(s, a)
     _craft(s, a)
     _interact(s, a, generator)
     _place(s, a)
+    _abilities(s, a)
     _move(s, a)
     _creatures(s, generator)
+    _fly_shots(s)
     _spawn(s, generator)
     _plants(s)
     _survive(s, a)

@@ -11,7 +11,11 @@ the last), all batched over worlds. Four fields decide the tiles:
 * ``forest`` high -> dense trees on grass, sparse trees elsewhere.
 
 The player starts at the map centre on a cleared 3 x 3 patch of grass; a few
-cows are placed on grass. The day length is 300 steps and
+cows are placed on grass and a ladder down lies on grass 6-12 steps away. The
+dungeon below is this build's own layout: walls with eight rectangular rooms
+joined by L-shaped corridors, chests in about half the rooms, a fountain, the
+ladder up in the first room and the ladder down (blocked: the deeper floors
+are not built) in the last. The day length is 300 steps and
 ``daylight = 1 - |cos(pi * (t / 300 mod 1 + 0.3))|^3`` (Crafter's cycle: the
 episode starts in the morning).
 """
@@ -26,6 +30,7 @@ from torch.nn import functional as F
 
 from priml_b200.baselines.craftax.game import constants as C
 from priml_b200.baselines.craftax.game.constants import BlockType as B
+from priml_b200.baselines.craftax.game.constants import ItemType as I
 from priml_b200.baselines.craftax.game.state import GameState, empty_state
 
 __all__ = ["daylight", "generate", "value_noise"]
@@ -89,6 +94,28 @@ def generate(envs: int, *, generator: torch.Generator | None, device: torch.devi
     s.map = m
     s.position = torch.tensor([r0, c0], device=device).expand(envs, 2).clone()
 
+    # ladder down to the dungeon on a grass tile 6..12 steps from the start
+    for _ in range(8):
+        cand = torch.stack([r0 + torch.randint(-12, 13, (envs,), device=device, generator=generator),
+                            c0 + torch.randint(-12, 13, (envs,), device=device, generator=generator)], -1)  # fmt: skip
+        d = (cand - s.position).abs().sum(-1)
+        ok = (_at(m, cand) == int(B.GRASS)) & (d >= 6)
+        unset = (s.ladder_down[:, 0] == 0).all(-1)
+        s.ladder_down[:, 0] = torch.where((ok & unset)[:, None], cand, s.ladder_down[:, 0])
+    unset = (s.ladder_down[:, 0] == 0).all(-1)
+    s.ladder_down[:, 0] = torch.where(unset[:, None], s.position + torch.tensor([0, 2], device=device), s.ladder_down[:, 0])
+    e = torch.arange(envs, device=device)
+    m[e, s.ladder_down[:, 0, 0], s.ladder_down[:, 0, 1]] = int(B.GRASS)
+    s.item_map[e, s.ladder_down[:, 0, 0], s.ladder_down[:, 0, 1]] = int(I.LADDER_DOWN)
+    s.map = m
+
+    dungeon, d_items, up, down = _dungeon(envs, generator=generator, device=device)
+    s.floor_map[:, 0], s.floor_items[:, 0] = m, s.item_map
+    s.floor_map[:, 1], s.floor_items[:, 1] = dungeon, d_items
+    s.ladder_up[:, 1], s.ladder_down[:, 1] = up, down
+    s.visited[:, 0] = True
+    s.potion_effect = torch.rand(envs, 6, device=device, generator=generator).argsort(-1)
+
     # a few cows on grass near the start
     for slot in range(C.MAX_PASSIVE_MOBS):
         pos = torch.stack([torch.randint(r0 - 8, r0 + 9, (envs,), device=device, generator=generator),
@@ -100,3 +127,56 @@ def generate(envs: int, *, generator: torch.Generator | None, device: torch.devi
         s.passive.health[:, slot] = C.PASSIVE_HEALTH
     s.light = daylight(s.timestep)
     return s
+
+
+def _at(grid: Tensor, pos: Tensor) -> Tensor:
+    rows, cols = grid.shape[-2:]
+    p0, p1 = pos[:, 0].clamp(0, rows - 1), pos[:, 1].clamp(0, cols - 1)
+    return grid[torch.arange(grid.shape[0], device=grid.device), p0, p1]
+
+
+def _dungeon(envs: int, *, generator: torch.Generator | None, device: torch.device,
+             rooms: int = 8) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+    """Walled floor with ``rooms`` rectangular rooms joined in sequence by L-shaped corridors;
+    chests in about half the rooms, a fountain in one, the ladder up in the first room's centre
+    and the (blocked) ladder down in the last one's."""
+    rows, cols = C.MAP_SIZE
+
+    def ri(lo: int, hi: int) -> Tensor:
+        return torch.randint(lo, hi, (envs, rooms), device=device, generator=generator)
+
+    h, w = ri(4, 9), ri(4, 9)
+    top, left = ri(1, rows - 10), ri(1, cols - 10)
+    rr = torch.arange(rows, device=device).view(1, 1, rows, 1)
+    cc = torch.arange(cols, device=device).view(1, 1, 1, cols)
+    inside = (rr >= top[..., None, None]) & (rr < (top + h)[..., None, None]) & \
+             (cc >= left[..., None, None]) & (cc < (left + w)[..., None, None])  # fmt: skip
+    open_ = inside.any(1)
+    cr, cc_ = top + h // 2, left + w // 2  # room centres
+    for k in range(rooms - 1):
+        a_r, a_c, b_r, b_c = cr[:, k], cc_[:, k], cr[:, k + 1], cc_[:, k + 1]
+        row = rr[0, 0, :, 0]
+        col = cc[0, 0, 0, :]
+        horiz = (row[None, :, None] == a_r[:, None, None]) & \
+                (col[None, None, :] >= torch.minimum(a_c, b_c)[:, None, None]) & \
+                (col[None, None, :] <= torch.maximum(a_c, b_c)[:, None, None])  # fmt: skip
+        vert = (col[None, None, :] == b_c[:, None, None]) & \
+               (row[None, :, None] >= torch.minimum(a_r, b_r)[:, None, None]) & \
+               (row[None, :, None] <= torch.maximum(a_r, b_r)[:, None, None])  # fmt: skip
+        open_ |= horiz | vert
+    m = torch.where(open_, int(B.PATH), int(B.WALL))
+    e = torch.arange(envs, device=device)
+    # chests in rooms 1..rooms-2 with probability 1/2, at the room's top-left interior tile
+    for k in range(1, rooms - 1):
+        put = torch.rand(envs, device=device, generator=generator) < 0.5
+        pr, pc = top[:, k], left[:, k]
+        m[e, pr, pc] = torch.where(put, int(B.CHEST), m[e, pr, pc])
+    m[e, top[:, 1] + h[:, 1] - 1, left[:, 1] + w[:, 1] - 1] = int(B.FOUNTAIN)
+    items = torch.zeros_like(m)
+    up = torch.stack([cr[:, 0], cc_[:, 0]], -1)
+    down = torch.stack([cr[:, -1], cc_[:, -1]], -1)
+    m[e, up[:, 0], up[:, 1]] = int(B.PATH)
+    m[e, down[:, 0], down[:, 1]] = int(B.PATH)
+    items[e, up[:, 0], up[:, 1]] = int(I.LADDER_UP)
+    items[e, down[:, 0], down[:, 1]] = int(I.LADDER_DOWN_BLOCKED)  # the floors below are not built
+    return m, items, up, down

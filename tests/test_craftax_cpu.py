@@ -208,3 +208,51 @@ def test_experiment_chain_and_smoke_loop(tmp_path) -> None:  # noqa: ANN001
     loop.run()
     assert loop.global_step == 3
     assert "eval/craftax_episodes" in loop.last_eval or "eval/total_loss" in loop.last_eval
+
+
+def test_ladders_need_kills_and_the_dungeon_is_dark() -> None:
+    s = _world(2)
+    s.position = s.ladder_down[:, 0].clone()
+    s, _ = _act(s, Act.DESCEND)
+    assert s.level.tolist() == [0, 0]  # the floor is not cleared yet
+    s.kills[:, 0] = C.MONSTERS_KILLED_TO_CLEAR_LEVEL
+    s, reward = _act(s, Act.DESCEND)
+    assert s.level.tolist() == [1, 1] and bool(s.achievements[:, A.ENTER_DUNGEON].all()) and s.xp.tolist() == [1, 1]
+    assert torch.equal(s.position, s.ladder_up[:, 1]) and bool((reward >= 3).all())
+    tiles = observation.render(s)[:, : 9 * 11 * observation.CHANNELS_PER_TILE].view(2, 9, 11, -1)
+    lit = tiles[..., -1]
+    assert int(lit.sum()) == 2 * 7 * 7  # only the 7 x 7 around the player
+    s, _ = _act(s, Act.ASCEND)
+    assert s.level.tolist() == [0, 0] and torch.equal(s.position, s.ladder_down[:, 0])
+    s, _ = _act(s, Act.DESCEND)
+    assert s.xp.tolist() == [1, 1]  # experience only for the first visit
+
+
+def test_chest_bow_arrow_potion_and_level_up() -> None:
+    s = _world(1)
+    s.level[:] = 1
+    _face(s, B.CHEST)
+    s, _ = _act(s, Act.DO)
+    assert bool(s.achievements[0, A.OPEN_CHEST]) and bool(s.achievements[0, A.FIND_BOW]) and int(s.bow) == 1
+    assert int(s.arrows) >= 1
+    r, c = s.position[0].tolist()
+    s.map[0, r, c + 1 : c + 4] = int(B.PATH)
+    s.melee.mask[0, 0] = True
+    s.melee.position[0, 0] = torch.tensor([r, c + 2])
+    s.melee.health[0, 0] = 1.0
+    s.melee.cooldown[0, 0] = 99
+    s.arrows[:] = 3
+    s, _ = _act(s, Act.SHOOT_ARROW)
+    for _ in range(3):
+        if not bool(s.melee.mask[0, 0]):
+            break
+        s.melee.position[0, 0] = torch.tensor([r, c + 2])  # hold the target still
+        s, _ = _act(s, Act.NOOP)
+    assert bool(s.achievements[0, A.FIRE_BOW]) and not bool(s.melee.mask[0, 0])
+    assert bool(s.achievements[0, A.DEFEAT_ORC_SOLIDER]) and int(s.kills[0, 1]) == 1
+    s.potions[0, 2] = 1
+    s, _ = _act(s, Act.DRINK_POTION_BLUE)
+    assert bool(s.achievements[0, A.DRINK_POTION]) and int(s.potions[0, 2]) == 0
+    s.xp[:] = 1
+    s, _ = _act(s, Act.LEVEL_UP_STRENGTH)
+    assert int(s.strength) == 2 and int(s.xp) == 0
