@@ -203,31 +203,35 @@ MAX_RANGED_MOBS: Final = 2
 MAX_GROWING_PLANTS: Final = 10
 MOB_DESPAWN_DISTANCE: Final = 14
 
-LEVELS: Final = 2
-"""Floors built: 0 = overworld, 1 = dungeon (the game has nine)."""
+LEVELS: Final = 9
+"""Floors: overworld, dungeon, gnomish mines, sewers, vault, troll mines, fire realm, ice realm, graveyard."""
 MONSTERS_KILLED_TO_CLEAR_LEVEL: Final = 8
 """Kills on a floor before its ladder down opens."""
-LEVEL_ACHIEVEMENT: Final = (None, Achievement.ENTER_DUNGEON)
-SPECIES: Final = (0, 2)
-"""Creature species per floor (observation channel offset): overworld 0 (cow / zombie / skeleton),
-dungeon 2 (snail / orc soldier / orc mage)."""
-FLOOR_HEALTH: Final = ((3.0, 5.0, 3.0), (4.0, 7.0, 5.0))
-"""Fresh creature health per floor: (passive, melee, ranged)."""
-FLOOR_DAMAGE: Final = ((2.0, 2.0), (3.0, 3.0))
-"""Damage per floor: (melee hit, ranged projectile)."""
-FLOOR_SPAWN: Final = ((0.1, 0.02, 0.05, 0.1), (0.1, 0.06, 0.05, 0.06))
-"""Spawn probability per floor: (passive, melee by day, ranged, melee at night)."""
-KILL_ACHIEVEMENT: Final = ((Achievement.EAT_COW, Achievement.DEFEAT_ZOMBIE, Achievement.DEFEAT_SKELETON),
-                           (Achievement.EAT_SNAIL, Achievement.DEFEAT_ORC_SOLIDER, Achievement.DEFEAT_ORC_MAGE))  # fmt: skip
+LEVEL_ACHIEVEMENT: Final = (None, Achievement.ENTER_DUNGEON, Achievement.ENTER_GNOMISH_MINES, Achievement.ENTER_SEWERS,
+                            Achievement.ENTER_VAULT, Achievement.ENTER_TROLL_MINES, Achievement.ENTER_FIRE_REALM,
+                            Achievement.ENTER_ICE_REALM, Achievement.ENTER_GRAVEYARD)  # fmt: skip
+FLOOR_SPECIES: Final = ((0, 0, 0), (2, 2, 2), (1, 1, 1), (2, 3, 3), (2, 4, 4), (1, 5, 5), (1, 6, 6), (1, 7, 7), (0, 0, 0))
+"""Per floor, the (passive, melee, ranged) species that live there."""
+FLOOR_HEALTH: Final = ((3.0, 5.0, 3.0), (4.0, 7.0, 5.0), (6.0, 9.0, 6.0), (8.0, 11.0, 8.0), (0.0, 12.0, 12.0),
+                       (0.0, 20.0, 4.0), (0.0, 20.0, 14.0), (0.0, 24.0, 16.0), (0.0, 5.0, 3.0))  # fmt: skip
+"""Per floor, fresh creature health (passive, melee, ranged); 0 where the floor has none."""
+SPECIES_DAMAGE: Final = ((2.0, 2.0), (4.0, 4.0), (3.0, 3.0), (5.0, 3.0), (6.0, 5.0), (8.0, 10.0), (8.0, 8.0), (9.0, 9.0))
+"""Per melee / ranged species, (melee hit, projectile) damage: the game's physical, fire and ice
+parts summed (this build models no elemental resistance)."""
+FLOOR_SPAWN: Final = ((0.1, 0.02, 0.05, 0.1),) + ((0.1, 0.06, 0.05, 0.0),) * 3 + ((0.0, 0.06, 0.05, 0.0),) * 5
+"""Per floor, spawn probability for (passive, melee, ranged, melee at night)."""
+PASSIVE_ACHIEVEMENT: Final = (Achievement.EAT_COW, Achievement.EAT_BAT, Achievement.EAT_SNAIL)
+MELEE_ACHIEVEMENT: Final = (Achievement.DEFEAT_ZOMBIE, Achievement.DEFEAT_GNOME_WARRIOR, Achievement.DEFEAT_ORC_SOLIDER,
+                            Achievement.DEFEAT_LIZARD, Achievement.DEFEAT_KNIGHT, Achievement.DEFEAT_TROLL,
+                            Achievement.DEFEAT_PIGMAN, Achievement.DEFEAT_FROST_TROLL)  # fmt: skip
+RANGED_ACHIEVEMENT: Final = (Achievement.DEFEAT_SKELETON, Achievement.DEFEAT_GNOME_ARCHER, Achievement.DEFEAT_ORC_MAGE,
+                             Achievement.DEFEAT_KOBOLD, Achievement.DEFEAT_ARCHER, Achievement.DEFEAT_DEEP_THING,
+                             Achievement.DEFEAT_FIRE_ELEMENTAL, Achievement.DEFEAT_ICE_ELEMENTAL)  # fmt: skip
+LIT_FLOORS: Final = (True, False, False, False, False, False, True, True, True)
+"""Floors lit throughout; on the others the player sees 3 tiles around itself and 4 around a torch."""
 
-# overworld creatures: passive = cow, melee = zombie, ranged = skeleton (tunnels only)
 PASSIVE_HEALTH: Final = 3.0
-MELEE_HEALTH: Final = 5.0
-RANGED_HEALTH: Final = 3.0
-MELEE_DAMAGE: Final = 2.0
-ARROW_DAMAGE: Final = 2.0
-SPAWN_CHANCE: Final = {"passive": 0.1, "melee": 0.02, "ranged": 0.05, "melee_night": 0.1}
-"""Per-step spawn probabilities on the overworld (passive, melee by day / night, ranged in tunnels)."""
+"""Health of the cows placed at world generation."""
 
 _TIERS: Final = {
     3.0: (Achievement.MAKE_DIAMOND_SWORD, Achievement.MAKE_IRON_ARMOUR, Achievement.MAKE_DIAMOND_ARMOUR,
@@ -261,8 +265,9 @@ SOLID: Final = torch.zeros(len(BlockType), dtype=torch.bool)
 SOLID[[int(b) for b in (BlockType.STONE, BlockType.TREE, BlockType.COAL, BlockType.IRON, BlockType.DIAMOND,
                         BlockType.CRAFTING_TABLE, BlockType.FURNACE, BlockType.PLANT, BlockType.RIPE_PLANT,
                         BlockType.WALL, BlockType.WALL_MOSS, BlockType.STALAGMITE, BlockType.SAPPHIRE, BlockType.RUBY,
-                        BlockType.CHEST, BlockType.FOUNTAIN, BlockType.FIRE_TREE)]] = True  # fmt: skip
+                        BlockType.CHEST, BlockType.FOUNTAIN, BlockType.FIRE_TREE, BlockType.ICE_SHRUB,
+                        BlockType.GRAVE, BlockType.GRAVE2, BlockType.GRAVE3)]] = True  # fmt: skip
 """Blocks that stop the player and creatures."""
 WALKABLE: Final = torch.zeros(len(BlockType), dtype=torch.bool)
-WALKABLE[[int(BlockType.GRASS), int(BlockType.SAND), int(BlockType.PATH)]] = True
+WALKABLE[[int(b) for b in (BlockType.GRASS, BlockType.SAND, BlockType.PATH, BlockType.FIRE_GRASS, BlockType.ICE_GRASS)]] = True
 """Blocks a creature (or the player) may step onto (water and lava stop creatures; lava kills the player)."""

@@ -48,25 +48,26 @@ def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
     mobs = torch.zeros(s.num_envs, vr, vc, 5 * 8, device=s.device)
     corner = s.position - torch.tensor([vr // 2, vc // 2], device=s.device)
     e = torch.arange(s.num_envs, device=s.device)
-    species = torch.tensor(C.SPECIES, device=s.device)[s.level]
-    for creatures, plane, typed in ((s.melee, 1, True), (s.passive, 0, True), (s.ranged, 2, True),
-                                    (s.projectiles, 3, True), (s.shots, 4, False)):  # fmt: skip
-        channel = plane * 8 + (species if typed else torch.zeros_like(species))
+    species = torch.tensor(C.FLOOR_SPECIES, device=s.device)[s.level]  # [E, 3] per class
+    for creatures, plane, cls in ((s.melee, 1, 1), (s.passive, 0, 0), (s.ranged, 2, 2),
+                                  (s.projectiles, 3, 2), (s.shots, 4, None)):  # fmt: skip
+        channel = plane * 8 + (species[:, cls] if cls is not None else torch.zeros_like(s.level))
         for slot in range(creatures.mask.shape[1]):
             local = creatures.position[:, slot] - corner
             seen = creatures.mask[:, slot] & (local[:, 0] >= 0) & (local[:, 0] < vr) & (local[:, 1] >= 0) & (local[:, 1] < vc)
             r, c = local[:, 0].clamp(0, vr - 1), local[:, 1].clamp(0, vc - 1)
             mobs[e, r, c, channel] = torch.maximum(mobs[e, r, c, channel], seen.float())
-    # the surface is lit; below it the player sees 3 tiles around itself and 4 around a torch
+    # lit floors are seen whole; on the others the player sees 3 tiles around itself and 4 around a torch
     rr = torch.arange(vr, device=s.device)[:, None] - vr // 2
     cc = torch.arange(vc, device=s.device)[None, :] - vc // 2
     near = (torch.maximum(rr.abs(), cc.abs()) <= 3).expand(s.num_envs, vr, vc)
     torch_light = F.max_pool2d((items == int(C.ItemType.TORCH)).float()[:, None], 9, 1, 4)[:, 0] > 0
-    lit = ((s.level == 0)[:, None, None] | near | torch_light).float()[..., None]
+    lit_floor = torch.tensor(C.LIT_FLOORS, device=s.device)[s.level]
+    lit = (lit_floor[:, None, None] | near | torch_light).float()[..., None]
     tiles = torch.cat([F.one_hot(blocks, len(C.BlockType)).float(), F.one_hot(items, len(C.ItemType)).float(), mobs], -1)
     view_part = torch.cat([tiles * lit, lit], -1).flatten(1)
     z = torch.zeros(s.num_envs, device=s.device)
-    counts = torch.stack([s.wood, s.stone, s.coal, s.iron, s.diamond, z, z, s.sapling, s.torches, s.arrows], -1).float()
+    counts = torch.stack([s.wood, s.stone, s.coal, s.iron, s.diamond, s.sapphire, s.ruby, s.sapling, s.torches, s.arrows], -1).float()
     tools = torch.stack([z, s.pickaxe.float() / 4.0, s.sword.float() / 4.0, z, z, s.bow.float()], -1)
     potions = s.potions.float().sqrt() / 10.0
     meters = torch.stack([s.health, s.food.float(), s.drink.float(), s.energy.float(), z, s.xp.float(),

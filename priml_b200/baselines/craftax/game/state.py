@@ -38,7 +38,7 @@ class Creatures:
                    direction=torch.zeros(envs, slots, 2, dtype=torch.long, device=device))  # fmt: skip
 
 
-_COUNTS = ("wood", "stone", "coal", "iron", "diamond", "sapling", "pickaxe", "sword", "arrows", "torches")
+_COUNTS = ("wood", "stone", "coal", "iron", "diamond", "sapphire", "ruby", "sapling", "pickaxe", "sword", "arrows", "torches")
 
 
 @dataclass(slots=True, kw_only=True)
@@ -61,6 +61,8 @@ class GameState:
     coal: Tensor
     iron: Tensor
     diamond: Tensor
+    sapphire: Tensor
+    ruby: Tensor
     sapling: Tensor
     pickaxe: Tensor  # tool level 0..4 (none, wood, stone, iron, diamond)
     sword: Tensor

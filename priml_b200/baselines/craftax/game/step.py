@@ -141,6 +141,11 @@ def _level_table(s: GameState, table: tuple, column: int) -> Tensor:
     return torch.tensor([row[column] for row in table], device=s.device)[s.level]
 
 
+def _species_damage(s: GameState, cls: int, column: int) -> Tensor:
+    """Damage dealt by the class-``cls`` species of the current floor (0 melee hit, 1 projectile)."""
+    return torch.tensor([C.SPECIES_DAMAGE[row[cls]][column] for row in C.FLOOR_SPECIES], device=s.device)[s.level]
+
+
 def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) -> Tensor:
     """Damage the creature on ``target``; returns where a creature absorbed the blow."""
     absorbed = torch.zeros_like(doing)
@@ -157,7 +162,8 @@ def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) 
             s.hunger = torch.where(died, torch.zeros_like(s.hunger), s.hunger)
         else:
             s.kills[r, s.level] = s.kills[r, s.level] + died.long()
-        ach = torch.tensor([int(row[cls]) for row in C.KILL_ACHIEVEMENT], device=s.device)[s.level]
+        kinds = (C.PASSIVE_ACHIEVEMENT, C.MELEE_ACHIEVEMENT, C.RANGED_ACHIEVEMENT)[cls]
+        ach = torch.tensor([int(kinds[row[cls]]) for row in C.FLOOR_SPECIES], device=s.device)[s.level]
         s.achievements[r, ach] |= died
         absorbed |= hit_any
     return absorbed
@@ -181,6 +187,8 @@ def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> Non
     mine(B.COAL, 1, "coal")
     mine(B.IRON, 2, "iron")
     mine(B.DIAMOND, 3, "diamond")
+    mine(B.SAPPHIRE, 4, "sapphire")
+    mine(B.RUBY, 4, "ruby")
     sapling = doing & (block == int(B.GRASS)) & (torch.rand(s.num_envs, device=s.device, generator=generator) < 0.1)
     s.sapling = torch.clamp(s.sapling + sapling.long(), max=_CAP)
     chest = doing & (block == int(B.CHEST))
@@ -287,7 +295,9 @@ def _change_floor(s: GameState, a: Tensor) -> None:
     first = move & ~s.visited[r, new]
     s.visited[r, new] |= move
     s.xp = s.xp + first.long()
-    _unlock(s, A.ENTER_DUNGEON, move & (new == 1))
+    for level, ach in enumerate(C.LEVEL_ACHIEVEMENT):
+        if ach is not None:
+            _unlock(s, ach, move & (new == level))
 
 
 # ---------------------------------------------------------------- placing
@@ -375,7 +385,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     _try_move(s, s.melee, step, (B.GRASS, B.SAND, B.PATH))
     dist = (s.position[:, None] - s.melee.position).abs().sum(-1)
     attack = s.melee.mask & (dist <= 1) & (s.melee.cooldown <= 0)
-    melee_hit = _level_table(s, C.FLOOR_DAMAGE, 0)
+    melee_hit = _species_damage(s, 1, 0)
     damage = torch.where(s.sleeping, torch.full_like(s.health, 7.0), melee_hit)
     s.health = s.health - attack.sum(-1).float() * damage * _armour_factor(s)
     s.melee.cooldown = torch.where(attack, torch.full_like(s.melee.cooldown, 5), (s.melee.cooldown - 1).clamp(min=0))
@@ -401,7 +411,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     # arrows fly one tile per step: they hurt the player they reach and stop at solid tiles
     proj.position = proj.position + proj.direction * proj.mask[..., None].long()
     hit = proj.mask & (proj.position == s.position[:, None]).all(-1)
-    s.health = s.health - hit.sum(-1).float() * _level_table(s, C.FLOOR_DAMAGE, 1) * _armour_factor(s)
+    s.health = s.health - hit.sum(-1).float() * _species_damage(s, 2, 1) * _armour_factor(s)
     blocked = torch.zeros_like(proj.mask)
     for slot in range(proj.mask.shape[1]):
         b = _tile(s.map, proj.position[:, slot])
@@ -483,6 +493,7 @@ def _survive(s: GameState, a: Tensor) -> None:
 
 _THRESHOLDS = (("wood", 1, A.COLLECT_WOOD), ("stone", 1, A.COLLECT_STONE), ("coal", 1, A.COLLECT_COAL),
                ("iron", 1, A.COLLECT_IRON), ("diamond", 1, A.COLLECT_DIAMOND), ("sapling", 1, A.COLLECT_SAPLING),
+               ("sapphire", 1, A.COLLECT_SAPPHIRE), ("ruby", 1, A.COLLECT_RUBY),
                ("arrows", 1, A.MAKE_ARROW), ("torches", 1, A.MAKE_TORCH), ("pickaxe", 1, A.MAKE_WOOD_PICKAXE),
                ("pickaxe", 2, A.MAKE_STONE_PICKAXE), ("pickaxe", 3, A.MAKE_IRON_PICKAXE),
                ("pickaxe", 4, A.MAKE_DIAMOND_PICKAXE), ("sword", 1, A.MAKE_WOOD_SWORD), ("sword", 2, A.MAKE_STONE_SWORD),

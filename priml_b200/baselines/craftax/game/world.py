@@ -109,10 +109,13 @@ def generate(envs: int, *, generator: torch.Generator | None, device: torch.devi
     s.item_map[e, s.ladder_down[:, 0, 0], s.ladder_down[:, 0, 1]] = int(I.LADDER_DOWN)
     s.map = m
 
-    dungeon, d_items, up, down = _dungeon(envs, generator=generator, device=device)
     s.floor_map[:, 0], s.floor_items[:, 0] = m, s.item_map
-    s.floor_map[:, 1], s.floor_items[:, 1] = dungeon, d_items
-    s.ladder_up[:, 1], s.ladder_down[:, 1] = up, down
+    for level in range(1, C.LEVELS):
+        fm, fi, up, down = _FLOORS[level](envs, generator=generator, device=device)
+        if level == C.LEVELS - 1:  # the deepest floor has no way down
+            fi = torch.where(fi == int(I.LADDER_DOWN), int(I.NONE), fi)
+        s.floor_map[:, level], s.floor_items[:, level] = fm, fi
+        s.ladder_up[:, level], s.ladder_down[:, level] = up, down
     s.visited[:, 0] = True
     s.potion_effect = torch.rand(envs, 6, device=device, generator=generator).argsort(-1)
 
@@ -135,11 +138,12 @@ def _at(grid: Tensor, pos: Tensor) -> Tensor:
     return grid[torch.arange(grid.shape[0], device=grid.device), p0, p1]
 
 
-def _dungeon(envs: int, *, generator: torch.Generator | None, device: torch.device,
-             rooms: int = 8) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+def _dungeon(envs: int, *, generator: torch.Generator | None, device: torch.device, rooms: int = 8,
+             chest_prob: float = 0.5, water: bool = False) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
     """Walled floor with ``rooms`` rectangular rooms joined in sequence by L-shaped corridors;
-    chests in about half the rooms, a fountain in one, the ladder up in the first room's centre
-    and the (blocked) ladder down in the last one's."""
+    chests in rooms with probability ``chest_prob``, a fountain in one, water channels down the
+    corridors' side when ``water``, the ladder up in the first room's centre and the ladder down
+    in the last one's."""
     rows, cols = C.MAP_SIZE
 
     def ri(lo: int, hi: int) -> Tensor:
@@ -165,10 +169,13 @@ def _dungeon(envs: int, *, generator: torch.Generator | None, device: torch.devi
                (row[None, :, None] <= torch.maximum(a_r, b_r)[:, None, None])  # fmt: skip
         open_ |= horiz | vert
     m = torch.where(open_, int(B.PATH), int(B.WALL))
+    if water:  # sewer channels: open tiles beside walls on even rows flood
+        beside = F.max_pool2d((m == int(B.WALL)).float()[:, None], 3, 1, 1)[:, 0] > 0
+        m = torch.where(open_ & ~inside.any(1) & beside & (rr[0, 0] % 2 == 0), int(B.WATER), m)
     e = torch.arange(envs, device=device)
-    # chests in rooms 1..rooms-2 with probability 1/2, at the room's top-left interior tile
+    # chests in rooms 1..rooms-2, at the room's top-left interior tile
     for k in range(1, rooms - 1):
-        put = torch.rand(envs, device=device, generator=generator) < 0.5
+        put = torch.rand(envs, device=device, generator=generator) < chest_prob
         pr, pc = top[:, k], left[:, k]
         m[e, pr, pc] = torch.where(put, int(B.CHEST), m[e, pr, pc])
     m[e, top[:, 1] + h[:, 1] - 1, left[:, 1] + w[:, 1] - 1] = int(B.FOUNTAIN)
@@ -178,5 +185,86 @@ def _dungeon(envs: int, *, generator: torch.Generator | None, device: torch.devi
     m[e, up[:, 0], up[:, 1]] = int(B.PATH)
     m[e, down[:, 0], down[:, 1]] = int(B.PATH)
     items[e, up[:, 0], up[:, 1]] = int(I.LADDER_UP)
-    items[e, down[:, 0], down[:, 1]] = int(I.LADDER_DOWN_BLOCKED)  # the floors below are not built
+    items[e, down[:, 0], down[:, 1]] = int(I.LADDER_DOWN)
     return m, items, up, down
+
+
+def _ladders(envs: int, m: Tensor, *, generator: torch.Generator | None,
+             device: torch.device) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+    """Ladders far apart, joined by a cleared L-shaped path so that the floor can be crossed."""
+    rows, cols = C.MAP_SIZE
+    up = torch.stack([torch.randint(4, rows - 4, (envs,), device=device, generator=generator),
+                      torch.randint(4, cols // 3, (envs,), device=device, generator=generator)], -1)  # fmt: skip
+    down = torch.stack([torch.randint(4, rows - 4, (envs,), device=device, generator=generator),
+                        torch.randint(2 * cols // 3, cols - 4, (envs,), device=device, generator=generator)], -1)  # fmt: skip
+    rr = torch.arange(rows, device=device).view(1, rows, 1)
+    cc = torch.arange(cols, device=device).view(1, 1, cols)
+    lo_c, hi_c = torch.minimum(up[:, 1], down[:, 1]), torch.maximum(up[:, 1], down[:, 1])
+    lo_r, hi_r = torch.minimum(up[:, 0], down[:, 0]), torch.maximum(up[:, 0], down[:, 0])
+    path = ((rr == up[:, 0, None, None]) & (cc >= lo_c[:, None, None]) & (cc <= hi_c[:, None, None])) | \
+           ((cc == down[:, 1, None, None]) & (rr >= lo_r[:, None, None]) & (rr <= hi_r[:, None, None]))  # fmt: skip
+    e = torch.arange(envs, device=device)
+    items = torch.zeros_like(m)
+    items[e, up[:, 0], up[:, 1]] = int(I.LADDER_UP)
+    items[e, down[:, 0], down[:, 1]] = int(I.LADDER_DOWN)
+    return m, path, up, down, items  # type: ignore[return-value]
+
+
+def _cave(envs: int, *, generator: torch.Generator | None, device: torch.device, lava: bool,
+          ores: tuple[float, float, float, float, float]) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+    """Stone with noise-carved tunnels; ore probabilities (coal, iron, diamond, sapphire, ruby)."""
+    rows, cols = C.MAP_SIZE
+    n = value_noise(envs, (rows, cols), generator=generator, device=device, octaves=(6, 12))
+    m = torch.where(n.abs() < 0.18, int(B.PATH), int(B.STONE))
+    u = torch.rand(envs, rows, cols, device=device, generator=generator)
+    rock = m == int(B.STONE)
+    edge = 0.0
+    for block, p in zip((B.COAL, B.IRON, B.DIAMOND, B.SAPPHIRE, B.RUBY), ores, strict=True):
+        m = torch.where(rock & (u >= edge) & (u < edge + p), int(block), m)
+        edge += p
+    if lava:
+        m = torch.where((m == int(B.PATH)) & (n > 0.12) & (u > 0.9), int(B.LAVA), m)
+    m, path, up, down, items = _ladders(envs, m, generator=generator, device=device)
+    m = torch.where(path, int(B.PATH), m)
+    return m, items, up, down
+
+
+def _realm(envs: int, *, generator: torch.Generator | None, device: torch.device, ground: B, hazard: B,
+           flora: B, extra: B | None = None) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+    """Open floor of ``ground`` with ``hazard`` pools, ``flora`` scattered, ``extra`` blocks sparse."""
+    rows, cols = C.MAP_SIZE
+    n = value_noise(envs, (rows, cols), generator=generator, device=device)
+    u = torch.rand(envs, rows, cols, device=device, generator=generator)
+    m = torch.full((envs, rows, cols), int(ground), dtype=torch.long, device=device)
+    m = torch.where(n < -0.3, int(hazard), m)
+    m = torch.where((m == int(ground)) & (u < 0.08), int(flora), m)
+    if extra is not None:
+        m = torch.where((m == int(ground)) & (u > 0.985), int(extra), m)
+    m, path, up, down, items = _ladders(envs, m, generator=generator, device=device)
+    m = torch.where(path, int(ground), m)
+    return m, items, up, down
+
+
+def _graveyard(envs: int, *, generator: torch.Generator | None,
+               device: torch.device) -> tuple[Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+    rows, cols = C.MAP_SIZE
+    u = torch.rand(envs, rows, cols, device=device, generator=generator)
+    m = torch.full((envs, rows, cols), int(B.GRASS), dtype=torch.long, device=device)
+    for block, lo in ((B.GRAVE, 0.0), (B.GRAVE2, 0.02), (B.GRAVE3, 0.04)):
+        m = torch.where((u >= lo) & (u < lo + 0.02), int(block), m)
+    m, path, up, down, items = _ladders(envs, m, generator=generator, device=device)
+    m = torch.where(path, int(B.GRASS), m)
+    return m, items, up, down
+
+
+_FLOORS = {
+    1: _dungeon,
+    2: lambda envs, **kw: _cave(envs, lava=False, ores=(0.06, 0.04, 0.01, 0.008, 0.008), **kw),
+    3: lambda envs, **kw: _dungeon(envs, water=True, **kw),
+    4: lambda envs, **kw: _dungeon(envs, chest_prob=1.0, **kw),
+    5: lambda envs, **kw: _cave(envs, lava=True, ores=(0.04, 0.04, 0.015, 0.01, 0.01), **kw),
+    6: lambda envs, **kw: _realm(envs, ground=B.FIRE_GRASS, hazard=B.LAVA, flora=B.FIRE_TREE, extra=B.RUBY, **kw),
+    7: lambda envs, **kw: _realm(envs, ground=B.ICE_GRASS, hazard=B.WATER, flora=B.ICE_SHRUB, extra=B.SAPPHIRE, **kw),
+    8: _graveyard,
+}
+"""Floor generators below the surface (this build's layouts)."""

@@ -256,3 +256,27 @@ def test_chest_bow_arrow_potion_and_level_up() -> None:
     s.xp[:] = 1
     s, _ = _act(s, Act.LEVEL_UP_STRENGTH)
     assert int(s.strength) == 2 and int(s.xp) == 0
+
+
+def test_nine_floors_entry_achievements_and_gems() -> None:
+    s = _world(1)
+    assert s.floor_map.shape[1] == C.LEVELS == 9
+    assert int((s.floor_items[0, C.LEVELS - 1] == int(C.ItemType.LADDER_DOWN)).sum()) == 0  # the graveyard is last
+    for level in range(C.LEVELS - 1):
+        s.position = s.ladder_down[:, level].clone()
+        s.kills[:, level] = C.MONSTERS_KILLED_TO_CLEAR_LEVEL
+        s, _ = _act(s, Act.DESCEND)
+        assert s.level.tolist() == [level + 1] and bool(s.achievements[0, C.LEVEL_ACHIEVEMENT[level + 1]])
+    assert int(s.xp) == C.LEVELS - 1
+    lit = observation.render(s)[:, : 9 * 11 * observation.CHANNELS_PER_TILE].view(1, 9, 11, -1)[..., -1]
+    assert int(lit.sum()) == 9 * 11  # the graveyard is lit throughout
+    _face(s, B.SAPPHIRE)
+    s.pickaxe[:] = 3
+    s, _ = _act(s, Act.DO)
+    assert int(s.sapphire) == 0  # a diamond pickaxe is needed
+    s.pickaxe[:] = 4
+    s, _ = _act(s, Act.DO)
+    assert int(s.sapphire) == 1 and bool(s.achievements[0, A.COLLECT_SAPPHIRE])
+    # the troll mines' deep things throw harder than the overworld's skeletons
+    s.level[:] = 5
+    assert float(rules._species_damage(s, 2, 1)) > C.SPECIES_DAMAGE[0][1]
