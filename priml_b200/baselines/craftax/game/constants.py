@@ -230,6 +230,13 @@ RANGED_ACHIEVEMENT: Final = (Achievement.DEFEAT_SKELETON, Achievement.DEFEAT_GNO
 LIT_FLOORS: Final = (True, False, False, False, False, False, True, True, True)
 """Floors lit throughout; on the others the player sees 3 tiles around itself and 4 around a torch."""
 
+BOSS_EXTRA_DAMAGE: Final = 0.5
+"""On the graveyard the player takes this much more damage."""
+BOSS_WAVE_STEPS: Final = 7
+"""After each wound the necromancer summons for this many steps before it can be struck again."""
+SPELL_DAMAGE: Final = 6.0
+"""Damage of a fireball or iceball at intelligence 1 (this build's figure)."""
+
 PASSIVE_HEALTH: Final = 3.0
 """Health of the cows placed at world generation."""
 
@@ -266,7 +273,8 @@ SOLID[[int(b) for b in (BlockType.STONE, BlockType.TREE, BlockType.COAL, BlockTy
                         BlockType.CRAFTING_TABLE, BlockType.FURNACE, BlockType.PLANT, BlockType.RIPE_PLANT,
                         BlockType.WALL, BlockType.WALL_MOSS, BlockType.STALAGMITE, BlockType.SAPPHIRE, BlockType.RUBY,
                         BlockType.CHEST, BlockType.FOUNTAIN, BlockType.FIRE_TREE, BlockType.ICE_SHRUB,
-                        BlockType.GRAVE, BlockType.GRAVE2, BlockType.GRAVE3)]] = True  # fmt: skip
+                        BlockType.GRAVE, BlockType.GRAVE2, BlockType.GRAVE3, BlockType.NECROMANCER,
+                        BlockType.ENCHANTMENT_TABLE_FIRE, BlockType.ENCHANTMENT_TABLE_ICE)]] = True  # fmt: skip
 """Blocks that stop the player and creatures."""
 WALKABLE: Final = torch.zeros(len(BlockType), dtype=torch.bool)
 WALKABLE[[int(b) for b in (BlockType.GRASS, BlockType.SAND, BlockType.PATH, BlockType.FIRE_GRASS, BlockType.ICE_GRASS)]] = True

@@ -68,13 +68,17 @@ def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
     view_part = torch.cat([tiles * lit, lit], -1).flatten(1)
     z = torch.zeros(s.num_envs, device=s.device)
     counts = torch.stack([s.wood, s.stone, s.coal, s.iron, s.diamond, s.sapphire, s.ruby, s.sapling, s.torches, s.arrows], -1).float()
-    tools = torch.stack([z, s.pickaxe.float() / 4.0, s.sword.float() / 4.0, z, z, s.bow.float()], -1)
+    tools = torch.stack([s.books.float() / 2.0, s.pickaxe.float() / 4.0, s.sword.float() / 4.0, s.sword_enchant.float(),
+                         s.bow_enchant.float(), s.bow.float()], -1)  # fmt: skip
     potions = s.potions.float().sqrt() / 10.0
-    meters = torch.stack([s.health, s.food.float(), s.drink.float(), s.energy.float(), z, s.xp.float(),
+    meters = torch.stack([s.health, s.food.float(), s.drink.float(), s.energy.float(), s.mana.float(), s.xp.float(),
                           s.dexterity.float(), s.strength.float(), s.intelligence.float()], -1)  # fmt: skip
     facing = F.one_hot((s.direction - 1).clamp(min=0), 4).float()
     cleared = (s.kills[e, s.level] >= C.MONSTERS_KILLED_TO_CLEAR_LEVEL).float()
-    condition = torch.stack([s.light, s.sleeping.float(), z, z, z, s.level.float() / 10.0, cleared, z], -1)
+    last = s.level == C.LEVELS - 1
+    vulnerable = last & ~s.melee.mask.any(-1) & ~s.ranged.mask.any(-1) & (s.boss_wait <= 0)
+    condition = torch.stack([s.light, s.sleeping.float(), s.resting.float(), s.spells[:, 0].float(), s.spells[:, 1].float(),
+                             s.level.float() / 10.0, cleared, vulnerable.float()], -1)  # fmt: skip
     player = torch.cat([counts.sqrt() / 10.0, tools, potions, meters / 10.0, facing, s.armour.float() / 2.0,
-                        torch.zeros(s.num_envs, 4, device=s.device), condition], -1)  # fmt: skip
+                        s.armour_enchant.float(), condition], -1)  # fmt: skip
     return torch.cat([view_part, player], -1)

@@ -94,7 +94,18 @@ class GameState:
     dexterity: Tensor  # [E] attributes 1..5
     strength: Tensor
     intelligence: Tensor
-    shots: Creatures  # the player's arrows in flight
+    shots: Creatures  # the player's arrows and spells in flight (``cooldown`` holds the kind: 0 arrow, 1 fire, 2 ice)
+    mana: Tensor  # [E]
+    mana_regen: Tensor  # [E] float accumulator
+    books: Tensor  # [E]
+    spells: Tensor  # [E, 2] bool fireball, iceball learned
+    sword_enchant: Tensor  # [E] 0 none, 1 fire, 2 ice
+    bow_enchant: Tensor  # [E]
+    armour_enchant: Tensor  # [E, 4]
+    chests_opened: Tensor  # [E, L]
+    resting: Tensor  # [E] bool
+    boss_progress: Tensor  # [E] wounds dealt to the necromancer
+    boss_wait: Tensor  # [E] steps until the necromancer can next be struck
 
     @property
     def num_envs(self) -> int:
@@ -171,5 +182,8 @@ def empty_state(envs: int, device: torch.device) -> GameState:
         dexterity=torch.ones(envs, dtype=torch.long, device=device),
         strength=torch.ones(envs, dtype=torch.long, device=device),
         intelligence=torch.ones(envs, dtype=torch.long, device=device),
-        shots=Creatures.empty(envs, 3, device), **counts,
+        shots=Creatures.empty(envs, 3, device),
+        mana=torch.full((envs,), 9, dtype=torch.long, device=device), mana_regen=z(torch.float32), books=z(),
+        spells=z(torch.bool, 2), sword_enchant=z(), bow_enchant=z(), armour_enchant=z(torch.long, 4),
+        chests_opened=z(torch.long, C.LEVELS), resting=z(torch.bool), boss_progress=z(), boss_wait=z(), **counts,
     )  # fmt: skip

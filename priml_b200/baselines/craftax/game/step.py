@@ -1,18 +1,22 @@
-"""One batched step of the Craftax game, overworld and dungeon (``priml/baselines/craftax/game/step.py``).
+"""One batched step of the Craftax game on any of its nine floors (``priml/baselines/craftax/game/step.py``).
 
 Order of operations per step (every rule is a masked tensor update over all
 workers at once): sleeping workers act NOOP -> ladders (descend needs 8 kills on
 the floor; creatures stay behind) -> crafting -> DO on the facing tile
 (creatures first, then the block: mining, chests, water / fountain, plants) ->
-placing -> potions, attribute level-ups and bow shots -> movement -> creatures
-(move, attack, projectiles) -> the player's arrows -> spawning / despawning ->
-plants -> survival meters -> achievements from the inventory -> reward.
+placing -> potions, attribute level-ups, bow shots, spells, books and
+enchanting -> movement -> creatures (move, attack, projectiles) -> the player's
+arrows and spells -> spawning / despawning -> plants -> survival meters and mana
+-> the necromancer's countdown -> achievements from the inventory -> reward.
 
 The rules are Crafter's and Craftax's published ones for the overworld (tool
 tiers for mining, crafting next to a table (and furnace), cows / zombies /
 skeletons, food / drink / energy / recovery counters, sleeping, saplings that
 ripen). Reward = newly unlocked achievements' rewards + 0.1 x the change in
-health. An episode ends when health reaches 0 or after 100,000 steps.
+health. An episode ends when health reaches 0, after 100,000 steps, or when the
+necromancer on the graveyard has taken one wound per floor below the surface;
+it can be struck only while none of its summons live and it is not summoning
+(7 steps after each wound), and the graveyard hurts the player half again.
 """
 
 from __future__ import annotations
@@ -37,6 +41,10 @@ _DELTA[Act.UP] = torch.tensor([-1, 0])
 _DELTA[Act.DOWN] = torch.tensor([1, 0])
 _SWORD_DAMAGE = torch.tensor([1.0, 2.0, 3.0, 5.0, 8.0])
 _PLANT_RIPE_AGE = 600
+_GROUND = (B.GRASS, B.SAND, B.PATH, B.FIRE_GRASS, B.ICE_GRASS)
+"""Tiles creatures walk on."""
+_FLOOR_GROUND = (B.GRASS, B.PATH, B.PATH, B.PATH, B.PATH, B.PATH, B.FIRE_GRASS, B.ICE_GRASS, B.GRASS)
+"""Per floor, the tile creatures spawn on."""
 _CAP = C.MAX_METER
 
 
@@ -146,6 +154,26 @@ def _species_damage(s: GameState, cls: int, column: int) -> Tensor:
     return torch.tensor([C.SPECIES_DAMAGE[row[cls]][column] for row in C.FLOOR_SPECIES], device=s.device)[s.level]
 
 
+def _player_damage(s: GameState) -> Tensor:
+    """Sword damage: the tier's figure, strength adding a quarter per level above 1; an enchanted sword
+    adds half the tier's figure in its element, intelligence adding a twentieth of that per level."""
+    base = _SWORD_DAMAGE.to(s.device)[s.sword]
+    element = 0.5 * base * (s.sword_enchant > 0).float() * (1.0 + 0.05 * (s.intelligence - 1).float())
+    return base * (1.0 + 0.25 * (s.strength - 1).float()) + element
+
+
+def _boss_vulnerable(s: GameState) -> Tensor:
+    """The necromancer can be struck on the graveyard once its summons are dead and it has stopped summoning."""
+    return (s.level == C.LEVELS - 1) & ~s.melee.mask.any(-1) & ~s.ranged.mask.any(-1) & (s.boss_wait <= 0)
+
+
+def _wound_boss(s: GameState, striking: Tensor) -> None:
+    hit = striking & _boss_vulnerable(s)
+    s.boss_progress = s.boss_progress + hit.long()
+    s.boss_wait = torch.where(hit, torch.full_like(s.boss_wait, C.BOSS_WAVE_STEPS), s.boss_wait)
+    _unlock(s, A.DAMAGE_NECROMANCER, hit)
+
+
 def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) -> Tensor:
     """Damage the creature on ``target``; returns where a creature absorbed the blow."""
     absorbed = torch.zeros_like(doing)
@@ -172,9 +200,9 @@ def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) 
 def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> None:
     doing = a == int(Act.DO)
     target = _facing(s)
-    damage = _SWORD_DAMAGE.to(s.device)[s.sword] * (1.0 + 0.25 * (s.strength - 1).float())
-    doing = doing & ~_hit_creatures(s, target, doing, damage)
+    doing = doing & ~_hit_creatures(s, target, doing, _player_damage(s))
     block = _tile(s.map, target)
+    _wound_boss(s, doing & (block == int(B.NECROMANCER)))
 
     def mine(kind: B, tool: int, item: str) -> None:
         ok = doing & (block == int(kind)) & (s.pickaxe >= tool)
@@ -210,7 +238,8 @@ def _interact(s: GameState, a: Tensor, generator: torch.Generator | None) -> Non
 def _open_chest(s: GameState, opening: Tensor, generator: torch.Generator | None) -> None:
     """Loot (this build's table): 1-4 arrows, and each with probability 1/2: 1-2 torches, a potion
     of a random colour, 1 iron; 1 diamond with probability 1/10. The first chest on a floor below
-    the surface also holds a bow if the player has none."""
+    the surface also holds a bow if the player has none, and the first on the sewers and on the
+    vault a spellbook."""
     dev, n = s.device, s.num_envs
 
     def roll(p: float) -> Tensor:
@@ -225,6 +254,9 @@ def _open_chest(s: GameState, opening: Tensor, generator: torch.Generator | None
     s.diamond = torch.clamp(s.diamond + roll(0.1).long(), max=_CAP)
     bow = opening & (s.bow == 0) & (s.level > 0)
     s.bow = s.bow + bow.long()
+    first_here = opening & (s.chests_opened[_rows(s), s.level] == 0)
+    s.books = s.books + (first_here & ((s.level == 3) | (s.level == 4))).long()  # a spellbook in each
+    s.chests_opened[_rows(s), s.level] += opening.long()
     _unlock(s, A.OPEN_CHEST, opening)
     _unlock(s, A.FIND_BOW, bow)
 
@@ -249,28 +281,78 @@ def _abilities(s: GameState, a: Tensor) -> None:
         up = (a == int(act)) & (s.xp >= 1) & (getattr(s, name) < 5)
         setattr(s, name, getattr(s, name) + up.long())
         s.xp = s.xp - up.long()
-    # a bow shot: an arrow leaves the facing tile and flies one tile per step
-    shoot = (a == int(Act.SHOOT_ARROW)) & (s.bow >= 1) & (s.arrows >= 1) & ~s.shots.mask.all(-1)
+    # a bow shot or a spell leaves the player's tile and flies one tile per step
+    room = ~s.shots.mask.all(-1)
+    shoot = (a == int(Act.SHOOT_ARROW)) & (s.bow >= 1) & (s.arrows >= 1) & room
+    fire = (a == int(Act.CAST_FIREBALL)) & s.spells[:, 0] & (s.mana >= 2) & room
+    ice = (a == int(Act.CAST_ICEBALL)) & s.spells[:, 1] & (s.mana >= 2) & room
+    _launch(s, shoot | fire | ice, fire.int() + 2 * ice.int())
+    s.arrows = s.arrows - shoot.long()
+    s.mana = s.mana - 2 * (fire | ice).long()
+    _unlock(s, A.FIRE_BOW, shoot)
+    _unlock(s, A.CAST_FIREBALL, fire)
+    _unlock(s, A.CAST_ICEBALL, ice)
+    # a book teaches a spell not yet known (fireball first), and is spent either way
+    reading = (a == int(Act.READ_BOOK)) & (s.books >= 1)
+    learn = torch.where(~s.spells[:, 0], 0, torch.where(~s.spells[:, 1], 1, 0))
+    s.spells[r, learn] |= reading
+    s.books = s.books - reading.long()
+    _unlock(s, A.LEARN_FIREBALL, reading & (learn == 0))
+    _unlock(s, A.LEARN_ICEBALL, reading & (learn == 1))
+    _enchant(s, a)
+
+
+def _launch(s: GameState, firing: Tensor, kind: Tensor) -> None:
+    r = _rows(s)
     first = torch.argmax((~s.shots.mask).long(), -1)
     d = _DELTA.to(s.device)[s.direction]
-    pos, dirn, mask = s.shots.position.clone(), s.shots.direction.clone(), s.shots.mask.clone()
-    pos[r, first] = torch.where(shoot[:, None], s.position, pos[r, first])
-    dirn[r, first] = torch.where(shoot[:, None], d, dirn[r, first])
-    mask[r, first] = mask[r, first] | shoot
-    s.shots.position, s.shots.direction, s.shots.mask = pos, dirn, mask
-    s.arrows = s.arrows - shoot.long()
-    _unlock(s, A.FIRE_BOW, shoot)
+    sh = s.shots
+    pos, dirn, mask, kinds = sh.position.clone(), sh.direction.clone(), sh.mask.clone(), sh.cooldown.clone()
+    pos[r, first] = torch.where(firing[:, None], s.position, pos[r, first])
+    dirn[r, first] = torch.where(firing[:, None], d, dirn[r, first])
+    mask[r, first] = mask[r, first] | firing
+    kinds[r, first] = torch.where(firing, kind.to(kinds.dtype), kinds[r, first])
+    sh.position, sh.direction, sh.mask, sh.cooldown = pos, dirn, mask, kinds
+
+
+def _enchant(s: GameState, a: Tensor) -> None:
+    """At an enchantment table, 9 mana and a gem (ruby at a fire table, sapphire at an ice one) bind
+    the table's element to the sword, the bow, or the first armour piece that is bare or holds the
+    other element."""
+    fire_table, ice_table = _near(s, B.ENCHANTMENT_TABLE_FIRE), _near(s, B.ENCHANTMENT_TABLE_ICE)
+    element = torch.where(fire_table, 1, 2)
+    gem = torch.where(fire_table, s.ruby, s.sapphire)
+    ready = (fire_table | ice_table) & (s.mana >= 9) & (gem >= 1)
+    sword = ready & (a == int(Act.ENCHANT_SWORD)) & (s.sword >= 1)
+    bow = ready & (a == int(Act.ENCHANT_BOW)) & (s.bow >= 1)
+    fits = (s.armour > 0) & (s.armour_enchant != element[:, None])
+    armour = ready & (a == int(Act.ENCHANT_ARMOUR)) & fits.any(-1)
+    s.sword_enchant = torch.where(sword, element, s.sword_enchant)
+    s.bow_enchant = torch.where(bow, element, s.bow_enchant)
+    piece = torch.argmax((fits & (s.armour_enchant == 0)).long() * 2 + fits.long(), -1)
+    r = _rows(s)
+    s.armour_enchant[r, piece] = torch.where(armour, element, s.armour_enchant[r, piece])
+    done = sword | bow | armour
+    s.ruby = s.ruby - (done & (element == 1)).long()
+    s.sapphire = s.sapphire - (done & (element == 2)).long()
+    s.mana = s.mana - 9 * done.long()
+    _unlock(s, A.ENCHANT_SWORD, sword)
+    _unlock(s, A.ENCHANT_ARMOUR, armour)
 
 
 def _fly_shots(s: GameState) -> None:
     shots = s.shots
     shots.position = shots.position + shots.direction * shots.mask[..., None].long()
-    damage = torch.full((s.num_envs,), 2.0, device=s.device) * (1.0 + 0.25 * (s.dexterity - 1).float())
+    # arrows: 2, dexterity adding a quarter per level, an enchanted bow half again; spells: intelligence
+    # adding a tenth per level
+    arrow = 2.0 * (1.0 + 0.25 * (s.dexterity - 1).float()) * (1.0 + 0.5 * (s.bow_enchant > 0).float())
+    spell = C.SPELL_DAMAGE * (1.0 + 0.1 * (s.intelligence - 1).float())
     for slot in range(shots.mask.shape[1]):
         live = shots.mask[:, slot]
+        damage = torch.where(shots.cooldown[:, slot] == 0, arrow, spell)
         hit = _hit_creatures(s, shots.position[:, slot], live, damage)
         b = _tile(s.map, shots.position[:, slot])
-        passable = (b == int(B.GRASS)) | (b == int(B.SAND)) | (b == int(B.PATH)) | (b == int(B.WATER)) | (b == int(B.LAVA))
+        passable = torch.stack([b == int(g) for g in (*_GROUND, B.WATER, B.LAVA)]).any(0)
         shots.mask[:, slot] = live & ~hit & passable
 
 
@@ -356,24 +438,35 @@ def _random_step(mobs: Creatures, generator: torch.Generator | None) -> Tensor:
     return _DELTA.to(mobs.mask.device)[choice]
 
 
-def _try_move(s: GameState, mobs: Creatures, step: Tensor, allowed: tuple[B, ...]) -> None:
+def _try_move(s: GameState, mobs: Creatures, step: Tensor, allowed: tuple[B, ...],
+              also: tuple[B, Tensor] | None = None) -> None:  # fmt: skip
+    """Move each creature by ``step`` onto a free ``allowed`` tile (or ``also[0]`` where ``also[1]``)."""
     for slot in range(mobs.mask.shape[1]):
         pos = mobs.position[:, slot]
         target = pos + step[:, slot]
         block = _tile(s.map, target)
         ok = mobs.mask[:, slot] & _in_bounds(target) & ~_occupied(s, target) & ~(target == s.position).all(-1)
-        ok &= torch.stack([block == int(b) for b in allowed]).any(0)
+        fits = torch.stack([block == int(b) for b in allowed]).any(0)
+        if also is not None:
+            fits |= (block == int(also[0])) & also[1]
+        ok &= fits
         mobs.position[:, slot] = torch.where(ok[:, None], target, pos)
 
 
 def _armour_factor(s: GameState) -> Tensor:
-    return 1.0 - 0.1 * (s.armour == 1).sum(-1).float() - 0.2 * (s.armour == 2).sum(-1).float()
+    """Fraction of a blow that lands: iron pieces block a tenth, diamond a fifth, an enchanted piece a
+    twentieth more (its element's fifth of the blow's elemental share, summed into one figure here);
+    the graveyard adds half again."""
+    block = 0.1 * (s.armour == 1).sum(-1).float() + 0.2 * (s.armour == 2).sum(-1).float()
+    block = block + 0.05 * ((s.armour_enchant > 0) & (s.armour > 0)).sum(-1).float()
+    boss = 1.0 + C.BOSS_EXTRA_DAMAGE * (s.level == C.LEVELS - 1).float()
+    return (1.0 - block) * boss
 
 
 def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     dev = s.device
     # cows wander
-    _try_move(s, s.passive, _random_step(s.passive, generator), (B.GRASS, B.SAND, B.PATH))
+    _try_move(s, s.passive, _random_step(s.passive, generator), _GROUND)
     # zombies chase when close, else wander; adjacent ones attack every 5 steps
     offset = s.position[:, None] - s.melee.position
     dist = offset.abs().sum(-1)
@@ -382,7 +475,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
                          torch.stack([torch.zeros_like(offset[..., 1]), offset[..., 1].sign()], -1))  # fmt: skip
     chase = (dist < 8) & (torch.rand(dist.shape, device=dev, generator=generator) < 0.8)
     step = torch.where(chase[..., None], toward, _random_step(s.melee, generator))
-    _try_move(s, s.melee, step, (B.GRASS, B.SAND, B.PATH))
+    _try_move(s, s.melee, step, _GROUND)
     dist = (s.position[:, None] - s.melee.position).abs().sum(-1)
     attack = s.melee.mask & (dist <= 1) & (s.melee.cooldown <= 0)
     melee_hit = _species_damage(s, 1, 0)
@@ -390,7 +483,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     s.health = s.health - attack.sum(-1).float() * damage * _armour_factor(s)
     s.melee.cooldown = torch.where(attack, torch.full_like(s.melee.cooldown, 5), (s.melee.cooldown - 1).clamp(min=0))
     # skeletons keep to the caves and shoot along rows / columns when the player is within 4 tiles
-    _try_move(s, s.ranged, _random_step(s.ranged, generator), (B.PATH,))
+    _try_move(s, s.ranged, _random_step(s.ranged, generator), _GROUND[2:], also=(B.GRASS, s.level > 0))
     offset = s.position[:, None] - s.ranged.position
     aligned = (offset == 0).any(-1) & (offset.abs().sum(-1) <= 4)
     shoot = s.ranged.mask & aligned & (s.ranged.cooldown <= 0)
@@ -415,7 +508,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     blocked = torch.zeros_like(proj.mask)
     for slot in range(proj.mask.shape[1]):
         b = _tile(s.map, proj.position[:, slot])
-        blocked[:, slot] = ~((b == int(B.GRASS)) | (b == int(B.SAND)) | (b == int(B.PATH)) | (b == int(B.WATER)))
+        blocked[:, slot] = ~(torch.stack([b == int(g) for g in (*_GROUND, B.WATER, B.LAVA)]).any(0))
     proj.mask = proj.mask & ~hit & ~blocked
 
 
@@ -425,11 +518,14 @@ def _spawn(s: GameState, generator: torch.Generator | None) -> None:
     night = s.light < 0.5
     surface = s.level == 0
     melee_chance = torch.where(night & surface, _level_table(s, C.FLOOR_SPAWN, 3), _level_table(s, C.FLOOR_SPAWN, 1))
-    grass_or_path = torch.where(surface, int(B.GRASS), int(B.PATH))
+    grass_or_path = torch.tensor([int(b) for b in _FLOOR_GROUND], device=dev)[s.level]
+    ranged_tile = torch.where(surface, int(B.PATH), grass_or_path)  # overworld skeletons keep to tunnels
+    # the graveyard's creatures are the necromancer's summons: they come only while it summons
+    summoning = (s.level != C.LEVELS - 1) | (s.boss_wait > 0)
     for cls, mobs, chance, tile, min_dist in (
         (0, s.passive, _level_table(s, C.FLOOR_SPAWN, 0), grass_or_path, 3),
-        (1, s.melee, melee_chance, grass_or_path, 6),
-        (2, s.ranged, _level_table(s, C.FLOOR_SPAWN, 2), torch.full_like(s.level, int(B.PATH)), 4),
+        (1, s.melee, melee_chance * summoning, grass_or_path, 6),
+        (2, s.ranged, _level_table(s, C.FLOOR_SPAWN, 2) * summoning, ranged_tile, 4),
     ):  # fmt: skip
         far = (mobs.position - s.position[:, None]).abs().max(-1).values > C.MOB_DESPAWN_DISTANCE
         mobs.mask = mobs.mask & ~far
@@ -466,6 +562,11 @@ def _plants(s: GameState) -> None:
 
 # ---------------------------------------------------------------- survival
 def _survive(s: GameState, a: Tensor) -> None:
+    # mana: one point per 20 steps (10 asleep), intelligence adding a quarter per level; cap 6 + 3 x intelligence
+    s.mana_regen = s.mana_regen + torch.where(s.sleeping, 0.1, 0.05) * (1.0 + 0.25 * (s.intelligence - 1).float())
+    s.mana = torch.minimum(torch.where(s.mana_regen >= 1, s.mana + 1, s.mana).clamp(min=0), 6 + 3 * s.intelligence)
+    s.mana_regen = torch.where(s.mana_regen >= 1, s.mana_regen - 1, s.mana_regen)
+    s.resting = a == int(Act.REST)
     start = (a == int(Act.SLEEP)) & (s.energy < _CAP)
     s.sleeping = s.sleeping | start
     slow = torch.where(s.sleeping, 0.5, 1.0)
@@ -480,7 +581,7 @@ def _survive(s: GameState, a: Tensor) -> None:
     s.energy = torch.where(s.fatigue < -10, s.energy + 1, s.energy)
     s.fatigue = torch.where((s.fatigue > 30) | (s.fatigue < -10), torch.zeros_like(s.fatigue), s.fatigue)
     fine = (s.food > 0) & (s.drink > 0) & ((s.energy > 0) | s.sleeping)
-    s.recover = s.recover + torch.where(fine, torch.where(s.sleeping, 2.0, 1.0), torch.where(s.sleeping, -0.5, -1.0))
+    s.recover = s.recover + torch.where(fine, torch.where(s.sleeping | s.resting, 2.0, 1.0), torch.where(s.sleeping, -0.5, -1.0))
     s.health = torch.where(s.recover > 25, s.health + 1, s.health)
     s.health = torch.where(s.recover < -15, s.health - 1, s.health)
     s.recover = torch.where((s.recover > 25) | (s.recover < -15), torch.zeros_like(s.recover), s.recover)
@@ -516,6 +617,8 @@ def step(s: GameState, action: Tensor, *, generator: torch.Generator | None = No
     _spawn(s, generator)
     _plants(s)
     _survive(s, a)
+    s.boss_wait = (s.boss_wait - (s.level == C.LEVELS - 1).long()).clamp(min=0)
+    _unlock(s, A.DEFEAT_NECROMANCER, s.boss_progress >= C.LEVELS - 1)
     for name, n, ach in _THRESHOLDS:
         _unlock(s, ach, getattr(s, name) >= n)
     newly = (s.achievements & ~before).float()
@@ -526,4 +629,5 @@ def step(s: GameState, action: Tensor, *, generator: torch.Generator | None = No
 
 
 def is_done(s: GameState) -> Tensor:
-    return (s.health <= 0) | (s.timestep >= C.MAX_TIMESTEPS)
+    """Death, the time limit, or the necromancer's defeat (after one wound per floor below the surface)."""
+    return (s.health <= 0) | (s.timestep >= C.MAX_TIMESTEPS) | (s.boss_progress >= C.LEVELS - 1)

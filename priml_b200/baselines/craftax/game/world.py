@@ -1,4 +1,4 @@
-"""Overworld generation and the day / night cycle (``priml/baselines/craftax/game/world_gen.py``).
+"""World generation for all nine floors and the day / night cycle (``priml/baselines/craftax/game/world_gen.py``).
 
 Terrain comes from fractal value noise: per world, random lattices at three
 resolutions are upsampled bilinearly and summed (each octave half the weight of
@@ -12,10 +12,15 @@ the last), all batched over worlds. Four fields decide the tiles:
 
 The player starts at the map centre on a cleared 3 x 3 patch of grass; a few
 cows are placed on grass and a ladder down lies on grass 6-12 steps away. The
-dungeon below is this build's own layout: walls with eight rectangular rooms
-joined by L-shaped corridors, chests in about half the rooms, a fountain, the
-ladder up in the first room and the ladder down (blocked: the deeper floors
-are not built) in the last. The day length is 300 steps and
+floors below are this build's own layouts: the dungeon, sewers (water channels)
+and vault (a chest in every room, both enchantment tables) are walls with eight
+rectangular rooms joined by L-shaped corridors, a fountain and the ladders in
+the first and last rooms; the gnomish and troll mines (the latter with lava)
+are stone with noise-carved tunnels and ores including sapphire and ruby; the
+fire and ice realms are open ground with lava / water pools, fire trees / ice
+shrubs and the realm's enchantment table; the graveyard is grass with graves,
+the necromancer and no ladder down. Ladders on cave and open floors are joined
+by a cleared path. The day length is 300 steps and
 ``daylight = 1 - |cos(pi * (t / 300 mod 1 + 0.3))|^3`` (Crafter's cycle: the
 episode starts in the morning).
 """
@@ -116,6 +121,7 @@ def generate(envs: int, *, generator: torch.Generator | None, device: torch.devi
             fi = torch.where(fi == int(I.LADDER_DOWN), int(I.NONE), fi)
         s.floor_map[:, level], s.floor_items[:, level] = fm, fi
         s.ladder_up[:, level], s.ladder_down[:, level] = up, down
+    _furnish(s)
     s.visited[:, 0] = True
     s.potion_effect = torch.rand(envs, 6, device=device, generator=generator).argsort(-1)
 
@@ -255,6 +261,24 @@ def _graveyard(envs: int, *, generator: torch.Generator | None,
     m, path, up, down, items = _ladders(envs, m, generator=generator, device=device)
     m = torch.where(path, int(B.GRASS), m)
     return m, items, up, down
+
+
+def _furnish(s: GameState) -> None:
+    """Enchantment tables beside the ladder up (both in the vault, the fire one in the fire realm,
+    the ice one in the ice realm) and the necromancer in the graveyard's centre column."""
+    e = torch.arange(s.num_envs, device=s.device)
+    for level, tables in ((4, (B.ENCHANTMENT_TABLE_FIRE, B.ENCHANTMENT_TABLE_ICE)), (6, (B.ENCHANTMENT_TABLE_FIRE,)),
+                          (7, (B.ENCHANTMENT_TABLE_ICE,))):  # fmt: skip
+        up = s.ladder_up[:, level]
+        for side, table in zip((-1, 1), tables, strict=False):
+            s.floor_map[e, level, up[:, 0] - 1, up[:, 1] + side] = int(table)
+    last = C.LEVELS - 1
+    rows, cols = C.MAP_SIZE
+    boss_r = torch.where(s.ladder_up[:, last, 0] == rows // 2, rows // 2 - 4, rows // 2)
+    for dr in (-1, 0, 1):
+        for dc in (-1, 0, 1):
+            s.floor_map[e, last, boss_r + dr, cols // 2 + dc] = int(B.GRASS)
+    s.floor_map[e, last, boss_r, cols // 2] = int(B.NECROMANCER)
 
 
 _FLOORS = {

@@ -280,3 +280,57 @@ def test_nine_floors_entry_achievements_and_gems() -> None:
     # the troll mines' deep things throw harder than the overworld's skeletons
     s.level[:] = 5
     assert float(rules._species_damage(s, 2, 1)) > C.SPECIES_DAMAGE[0][1]
+
+
+def test_books_spells_enchanting_and_the_necromancer() -> None:
+    s = _world(1)
+    s.level[:] = 3
+    _face(s, B.CHEST)
+    s, _ = _act(s, Act.DO)
+    assert int(s.books) == 1  # the sewers' first chest holds a spellbook
+    s, _ = _act(s, Act.READ_BOOK)
+    assert bool(s.spells[0, 0]) and bool(s.achievements[0, A.LEARN_FIREBALL]) and int(s.books) == 0
+    r, c = s.position[0].tolist()
+    s.map[0, r, c + 1 : c + 4] = int(B.PATH)
+    s.melee.mask[0, 0] = True
+    s.melee.position[0, 0] = torch.tensor([r, c + 2])
+    s.melee.health[0, 0] = 5.0
+    s.melee.cooldown[0, 0] = 99
+    mana = int(s.mana)
+    s, _ = _act(s, Act.CAST_FIREBALL)
+    assert bool(s.achievements[0, A.CAST_FIREBALL]) and int(s.mana) == mana - 2
+    for _ in range(3):
+        if not bool(s.melee.mask[0, 0]):
+            break
+        s.melee.position[0, 0] = torch.tensor([r, c + 2])
+        s, _ = _act(s, Act.NOOP)
+    assert not bool(s.melee.mask[0, 0])  # 6 spell damage beats 5 health in one hit
+    # enchanting at a fire table spends a ruby and 9 mana
+    _face(s, B.ENCHANTMENT_TABLE_FIRE)
+    s.sword[:], s.ruby[:], s.mana[:] = 1, 1, 9
+    before = float(rules._player_damage(s))
+    s, _ = _act(s, Act.ENCHANT_SWORD)
+    assert int(s.sword_enchant) == 1 and int(s.ruby) == 0 and int(s.mana) <= 1 and bool(s.achievements[0, A.ENCHANT_SWORD])
+    assert float(rules._player_damage(s)) > before
+    s.armour[0] = torch.tensor([1, 0, 0, 0])
+    s.sapphire[:], s.mana[:] = 1, 9
+    _face(s, B.ENCHANTMENT_TABLE_ICE)
+    s, _ = _act(s, Act.ENCHANT_ARMOUR)
+    assert s.armour_enchant[0].tolist() == [2, 0, 0, 0] and bool(s.achievements[0, A.ENCHANT_ARMOUR])
+    # the necromancer: struck only while nothing it summoned lives and it is not summoning
+    s = _world(1)
+    last = C.LEVELS - 1
+    s.map, s.item_map, s.level[:] = s.floor_map[:, last].clone(), s.floor_items[:, last].clone(), last
+    assert int((s.map == int(B.NECROMANCER)).sum()) == 1
+    s.melee.mask[:] = False
+    s.ranged.mask[:] = False
+    _face(s, B.NECROMANCER)
+    s, _ = _act(s, Act.DO)
+    assert int(s.boss_progress) == 1 and bool(s.achievements[0, A.DAMAGE_NECROMANCER]) and int(s.boss_wait) > 0
+    s, _ = _act(s, Act.DO)
+    assert int(s.boss_progress) == 1  # summoning: shielded
+    s.boss_progress[:] = last
+    s, reward = _act(s, Act.NOOP)
+    assert bool(s.achievements[0, A.DEFEAT_NECROMANCER]) and float(reward) >= 8 and bool(rules.is_done(s))
+    obs = observation.render(s)
+    assert obs.shape[-1] == observation.observation_size() and torch.isfinite(obs).all()
