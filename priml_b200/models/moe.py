@@ -150,6 +150,8 @@ class GroupedSwiGLUExperts(nn.Module):
 
     def reset_parameters(self) -> None:
         tpl = self._template[0]
+        if tpl.up_proj.weight.device != self.up_proj.device:  # built on meta, materialized since
+            tpl.to_empty(device=self.up_proj.device)
         with torch.no_grad():
             for e in range(self.num_experts):
                 tpl.reset_parameters()

@@ -68,3 +68,17 @@ def test_moe_module_grouped_equals_loop_dispatch() -> None:
         gate, up = gu.chunk(2)
         want[ti] += weights[ti, j] * ((torch.nn.functional.silu(gate) * up) @ m.experts.down_proj[ei].t())
     torch.testing.assert_close(a, want, rtol=1e-5, atol=1e-5)
+
+
+def test_moe_built_on_meta_materializes_every_expert() -> None:
+    from priml_b200.models.moe import MoE, Router
+    from priml_b200.models.swiglu import SwiGLU
+    from priml_b200.parallel.strategies import materialize_meta
+
+    with torch.device("meta"):
+        m = MoE.Config(channels_in=32, router=Router.Config(num_experts=4, top_k=2),
+                       expert=SwiGLU.Config(channels_hidden=48)).make()  # fmt: skip
+    assert m.experts.up_proj.is_meta
+    m = materialize_meta(m, torch.device("cpu"))  # raises on any tensor left uninitialized
+    assert not m.experts.up_proj.is_meta and float(m.experts.up_proj.std()) > 0
+    assert not torch.equal(m.experts.up_proj[0], m.experts.up_proj[1])  # each expert drawn afresh
