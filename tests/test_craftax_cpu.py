@@ -334,3 +334,15 @@ def test_books_spells_enchanting_and_the_necromancer() -> None:
     assert bool(s.achievements[0, A.DEFEAT_NECROMANCER]) and float(reward) >= 8 and bool(rules.is_done(s))
     obs = observation.render(s)
     assert obs.shape[-1] == observation.observation_size() and torch.isfinite(obs).all()
+
+
+def test_bench_prints_env_steps_per_second(capsys, monkeypatch) -> None:  # noqa: ANN001
+    import json
+    import sys
+
+    from priml_b200.baselines.craftax import bench
+
+    monkeypatch.setattr(sys, "argv", ["bench", "--device", "cpu", "--envs", "8", "--rollout", "2", "--steps", "1"])
+    bench.main()
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["unit"] == "steps/s" and line["value"] > 0
