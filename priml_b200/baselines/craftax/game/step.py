@@ -363,7 +363,7 @@ def _change_floor(s: GameState, a: Tensor) -> None:
     down = (a == int(Act.DESCEND)) & (here == int(I.LADDER_DOWN)) & cleared & (lvl < C.LEVELS - 1)
     up = (a == int(Act.ASCEND)) & (here == int(I.LADDER_UP)) & (lvl > 0)
     move = down | up
-    if not bool(move.any()):
+    if s.device.type == "cpu" and not bool(move.any()):  # on the GPU a host read costs more than the swap
         return
     s.floor_map[r, lvl] = torch.where(move[:, None, None], s.map, s.floor_map[r, lvl])
     s.floor_items[r, lvl] = torch.where(move[:, None, None], s.item_map, s.floor_items[r, lvl])

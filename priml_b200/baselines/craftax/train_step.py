@@ -111,7 +111,7 @@ class _RolloutStep(TrainStep):
         self._done = torch.zeros(n, dtype=torch.bool, device=self.device)
         self._ep_return = torch.zeros(n, device=self.device)
         self._ep_length = torch.zeros(n, dtype=torch.long, device=self.device)
-        self._finished: list[tuple[float, int]] = []
+        self._finished = torch.zeros(3, dtype=torch.float64, device=self.device)  # episodes, return sum, length sum
 
     @property
     def global_step(self) -> int:
@@ -133,22 +133,22 @@ class _RolloutStep(TrainStep):
             g["lr"] = self.config.learning_rate * scale
 
     def _record(self, reward: Tensor, done: Tensor) -> None:
+        """Sums over finished episodes stay on the device (no host read per environment step)."""
         self._ep_return += reward
         self._ep_length += 1
-        if bool(done.any()):
-            self._finished += list(zip(self._ep_return[done].tolist(), self._ep_length[done].tolist(), strict=True))
-            self._ep_return = self._ep_return * ~done
-            self._ep_length = self._ep_length * ~done
+        d = done.to(torch.float64)
+        self._finished += torch.stack([d.sum(), (self._ep_return * d).sum(), (self._ep_length * d).sum()])
+        self._ep_return = self._ep_return * ~done
+        self._ep_length = self._ep_length * ~done
 
     def _episode_metrics(self) -> dict[str, float]:
-        if not self._finished:
+        n, ret_sum, len_sum = self._finished.tolist()
+        self._finished.zero_()
+        if n == 0:
             return {"episodes": 0.0}
-        ret = sum(r for r, _ in self._finished) / len(self._finished)
-        out = {"episodes": float(len(self._finished)), "episode_return": ret,
-               "episode_length": sum(n for _, n in self._finished) / len(self._finished),
-               "normalized_return_pct": ret / C.REWARD_CEILING * 100.0}  # fmt: skip
-        self._finished = []
-        return out
+        ret = ret_sum / n
+        return {"episodes": n, "episode_return": ret, "episode_length": len_sum / n,
+                "normalized_return_pct": ret / C.REWARD_CEILING * 100.0}  # fmt: skip
 
     def _apply(self, loss: Tensor) -> Tensor:
         self.optimizer.zero_grad(set_to_none=True)
