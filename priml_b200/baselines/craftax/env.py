@@ -71,7 +71,8 @@ class CraftaxEnv:
         s, reward = rules.step(self.state, actions.to(self.device), generator=self._generator)
         done = rules.is_done(s)
         unlocked = s.achievements & done[:, None]
-        info = {f"Achievements/{a.name.lower()}": unlocked[:, int(a)].float() * 100.0 for a in C.Achievement}
+        pct = unlocked.float() * 100.0  # one kernel; the entries are column views
+        info = {f"Achievements/{a.name.lower()}": pct[:, int(a)] for a in C.Achievement}
         if bool(done.any()):
             pool = max(1, s.num_envs // self.config.optimistic_reset_ratio)
             want = min(int(done.sum()), pool)
