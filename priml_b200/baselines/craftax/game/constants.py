@@ -279,3 +279,15 @@ SOLID[[int(b) for b in (BlockType.STONE, BlockType.TREE, BlockType.COAL, BlockTy
 WALKABLE: Final = torch.zeros(len(BlockType), dtype=torch.bool)
 WALKABLE[[int(b) for b in (BlockType.GRASS, BlockType.SAND, BlockType.PATH, BlockType.FIRE_GRASS, BlockType.ICE_GRASS)]] = True
 """Blocks a creature (or the player) may step onto (water and lava stop creatures; lava kills the player)."""
+
+
+_CACHE: dict[tuple, torch.Tensor] = {}
+
+
+def device_table(key: object, device: torch.device, build: object) -> torch.Tensor:
+    """A constant table on ``device``, copied there once (a per-step host copy would stall the stream)."""
+    k = (key, device)
+    t = _CACHE.get(k)
+    if t is None:
+        t = _CACHE[k] = torch.as_tensor(build() if callable(build) else build).to(device)
+    return t

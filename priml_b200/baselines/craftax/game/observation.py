@@ -46,9 +46,9 @@ def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
     blocks = _local(s.map, s.position, view, int(C.BlockType.OUT_OF_BOUNDS))
     items = _local(s.item_map, s.position, view, int(C.ItemType.NONE))
     mobs = torch.zeros(s.num_envs, vr, vc, 5 * 8, device=s.device)
-    corner = s.position - torch.tensor([vr // 2, vc // 2], device=s.device)
+    corner = s.position - C.device_table(("half", vr, vc), s.device, [vr // 2, vc // 2])
     e = torch.arange(s.num_envs, device=s.device)
-    species = torch.tensor(C.FLOOR_SPECIES, device=s.device)[s.level]  # [E, 3] per class
+    species = C.device_table("species", s.device, C.FLOOR_SPECIES)[s.level]  # [E, 3] per class
     for creatures, plane, cls in ((s.melee, 1, 1), (s.passive, 0, 0), (s.ranged, 2, 2),
                                   (s.projectiles, 3, 2), (s.shots, 4, None)):  # fmt: skip
         channel = plane * 8 + (species[:, cls] if cls is not None else torch.zeros_like(s.level))
@@ -62,7 +62,7 @@ def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
     cc = torch.arange(vc, device=s.device)[None, :] - vc // 2
     near = (torch.maximum(rr.abs(), cc.abs()) <= 3).expand(s.num_envs, vr, vc)
     torch_light = F.max_pool2d((items == int(C.ItemType.TORCH)).float()[:, None], 9, 1, 4)[:, 0] > 0
-    lit_floor = torch.tensor(C.LIT_FLOORS, device=s.device)[s.level]
+    lit_floor = C.device_table("lit", s.device, C.LIT_FLOORS)[s.level]
     lit = (lit_floor[:, None, None] | near | torch_light).float()[..., None]
     tiles = torch.cat([F.one_hot(blocks, len(C.BlockType)).float(), F.one_hot(items, len(C.ItemType)).float(), mobs], -1)
     view_part = torch.cat([tiles * lit, lit], -1).flatten(1)

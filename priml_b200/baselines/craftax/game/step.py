@@ -57,6 +57,9 @@ def _in_bounds(pos: Tensor) -> Tensor:
     return (pos[..., 0] >= 0) & (pos[..., 0] < rows) & (pos[..., 1] >= 0) & (pos[..., 1] < cols)
 
 
+_const = C.device_table
+
+
 def _clamp(pos: Tensor) -> Tensor:
     rows, cols = C.MAP_SIZE
     return torch.stack([pos[..., 0].clamp(0, rows - 1), pos[..., 1].clamp(0, cols - 1)], -1)
@@ -73,7 +76,7 @@ def _set(grid: Tensor, pos: Tensor, value: Tensor | int, where: Tensor) -> Tenso
     p = _clamp(pos)
     r = torch.arange(grid.shape[0], device=grid.device)
     old = grid[r, p[:, 0], p[:, 1]]
-    new = torch.as_tensor(value, device=grid.device).expand_as(old).to(grid.dtype)
+    new = value.expand_as(old).to(grid.dtype) if isinstance(value, Tensor) else torch.full_like(old, value)
     grid = grid.clone()
     grid[r, p[:, 0], p[:, 1]] = torch.where(where & _in_bounds(pos), new, old)
     return grid
@@ -88,12 +91,15 @@ def _occupied(s: GameState, pos: Tensor) -> Tensor:
 
 
 def _near(s: GameState, block: B, radius: int = 1) -> Tensor:
-    r, c = s.position[:, 0], s.position[:, 1]
-    found = torch.zeros(s.num_envs, dtype=torch.bool, device=s.device)
-    for dr in range(-radius, radius + 1):
-        for dc in range(-radius, radius + 1):
-            found |= _tile(s.map, torch.stack([r + dr, c + dc], -1)) == int(block)
-    return found
+    """``[E]`` true where ``block`` lies in the (2 radius + 1)^2 window around the player (one gather)."""
+    rows, cols = C.MAP_SIZE
+    span = torch.arange(-radius, radius + 1, device=s.device)
+    rr = (s.position[:, 0:1] + span)[:, :, None].expand(-1, -1, span.numel())
+    cc = (s.position[:, 1:2] + span)[:, None, :].expand(-1, span.numel(), -1)
+    inside = (rr >= 0) & (rr < rows) & (cc >= 0) & (cc < cols)
+    e = torch.arange(s.num_envs, device=s.device)[:, None, None]
+    window = s.map[e, rr.clamp(0, rows - 1), cc.clamp(0, cols - 1)]
+    return ((window == int(block)) & inside).flatten(1).any(-1)
 
 
 def _unlock(s: GameState, achievement: A, where: Tensor) -> None:
@@ -101,7 +107,7 @@ def _unlock(s: GameState, achievement: A, where: Tensor) -> None:
 
 
 def _facing(s: GameState) -> Tensor:
-    return s.position + _DELTA.to(s.device)[s.direction]
+    return s.position + _const("delta", s.device, _DELTA)[s.direction]
 
 
 # ---------------------------------------------------------------- crafting
@@ -146,18 +152,19 @@ def _craft(s: GameState, a: Tensor) -> None:
 
 # ---------------------------------------------------------------- DO
 def _level_table(s: GameState, table: tuple, column: int) -> Tensor:
-    return torch.tensor([row[column] for row in table], device=s.device)[s.level]
+    return _const((id(table), column), s.device, lambda: [row[column] for row in table])[s.level]
 
 
 def _species_damage(s: GameState, cls: int, column: int) -> Tensor:
     """Damage dealt by the class-``cls`` species of the current floor (0 melee hit, 1 projectile)."""
-    return torch.tensor([C.SPECIES_DAMAGE[row[cls]][column] for row in C.FLOOR_SPECIES], device=s.device)[s.level]
+    build = lambda: [C.SPECIES_DAMAGE[row[cls]][column] for row in C.FLOOR_SPECIES]  # noqa: E731
+    return _const(("species_damage", cls, column), s.device, build)[s.level]
 
 
 def _player_damage(s: GameState) -> Tensor:
     """Sword damage: the tier's figure, strength adding a quarter per level above 1; an enchanted sword
     adds half the tier's figure in its element, intelligence adding a twentieth of that per level."""
-    base = _SWORD_DAMAGE.to(s.device)[s.sword]
+    base = _const("sword", s.device, _SWORD_DAMAGE)[s.sword]
     element = 0.5 * base * (s.sword_enchant > 0).float() * (1.0 + 0.05 * (s.intelligence - 1).float())
     return base * (1.0 + 0.25 * (s.strength - 1).float()) + element
 
@@ -191,7 +198,7 @@ def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) 
         else:
             s.kills[r, s.level] = s.kills[r, s.level] + died.long()
         kinds = (C.PASSIVE_ACHIEVEMENT, C.MELEE_ACHIEVEMENT, C.RANGED_ACHIEVEMENT)[cls]
-        ach = torch.tensor([int(kinds[row[cls]]) for row in C.FLOOR_SPECIES], device=s.device)[s.level]
+        ach = _const(("kill", cls), s.device, lambda: [int(kinds[row[cls]]) for row in C.FLOOR_SPECIES])[s.level]  # noqa: B023
         s.achievements[r, ach] |= died
         absorbed |= hit_any
     return absorbed
@@ -305,7 +312,7 @@ def _abilities(s: GameState, a: Tensor) -> None:
 def _launch(s: GameState, firing: Tensor, kind: Tensor) -> None:
     r = _rows(s)
     first = torch.argmax((~s.shots.mask).long(), -1)
-    d = _DELTA.to(s.device)[s.direction]
+    d = _const("delta", s.device, _DELTA)[s.direction]
     sh = s.shots
     pos, dirn, mask, kinds = sh.position.clone(), sh.direction.clone(), sh.mask.clone(), sh.cooldown.clone()
     pos[r, first] = torch.where(firing[:, None], s.position, pos[r, first])
@@ -423,7 +430,7 @@ def _place(s: GameState, a: Tensor) -> None:
 def _move(s: GameState, a: Tensor) -> None:
     moving = (a >= int(Act.LEFT)) & (a <= int(Act.DOWN))
     s.direction = torch.where(moving, a, s.direction)
-    target = s.position + _DELTA.to(s.device)[a]
+    target = s.position + _const("delta", s.device, _DELTA)[a]
     block = _tile(s.map, target)
     ok = moving & _in_bounds(target) & ~_occupied(s, target)
     ok &= (block == int(B.GRASS)) | (block == int(B.SAND)) | (block == int(B.PATH)) | (block == int(B.LAVA))
@@ -518,7 +525,7 @@ def _spawn(s: GameState, generator: torch.Generator | None) -> None:
     night = s.light < 0.5
     surface = s.level == 0
     melee_chance = torch.where(night & surface, _level_table(s, C.FLOOR_SPAWN, 3), _level_table(s, C.FLOOR_SPAWN, 1))
-    grass_or_path = torch.tensor([int(b) for b in _FLOOR_GROUND], device=dev)[s.level]
+    grass_or_path = _const("ground", dev, lambda: [int(b) for b in _FLOOR_GROUND])[s.level]
     ranged_tile = torch.where(surface, int(B.PATH), grass_or_path)  # overworld skeletons keep to tunnels
     # the graveyard's creatures are the necromancer's summons: they come only while it summons
     summoning = (s.level != C.LEVELS - 1) | (s.boss_wait > 0)
@@ -622,7 +629,7 @@ def step(s: GameState, action: Tensor, *, generator: torch.Generator | None = No
     for name, n, ach in _THRESHOLDS:
         _unlock(s, ach, getattr(s, name) >= n)
     newly = (s.achievements & ~before).float()
-    reward = (newly * C.ACHIEVEMENT_REWARD.to(s.device)).sum(-1) + 0.1 * (s.health - health_before)
+    reward = (newly * _const("reward", s.device, C.ACHIEVEMENT_REWARD)).sum(-1) + 0.1 * (s.health - health_before)
     s.timestep = s.timestep + 1
     s.light = daylight(s.timestep)
     return s, reward
