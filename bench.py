@@ -63,6 +63,9 @@ def _parse() -> argparse.Namespace:
     ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "tp", "ep", "single"], default="auto",
                     help="auto: fused-collective sharding for N>1, single-GPU for N=1; "
                     "tp: sequence-parallel tensor parallelism on the fused NVLink GEMMs")
+    ap.add_argument("--ref-compile", choices=["auto", "on", "off"], default="auto",
+                    help="reference arm: auto runs the reference's stock torch.compile path and falls back to its "
+                    "eager config (compile=None) only if compilation fails on one GPU")
     ap.add_argument("--out", type=str, default="")
     return ap.parse_args()
 
@@ -84,18 +87,272 @@ def _layout(strategy: str, world: int, tp: int) -> str:
     return f"fsdp{world}"
 
 
-def _reference_unavailable() -> None:
-    print(
-        json.dumps(
-            {
-                "impl": "reference",
-                "unavailable": "pip install of the reference fails offline: its build backend (hatchling) is not in "
-                "the wheelhouse and its git-only dependency configgle cannot be fetched, so the package cannot be "
-                "installed or imported here",
-            }
-        ),
-        flush=True,
+_REF_ROOT = Path(__file__).resolve().parent / "baseline" / "_ref"
+
+
+def _reference_unavailable(why: str) -> None:
+    print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+def _install_configgle_standin() -> None:
+    """Register a pure-Python ``configgle`` for the reference's imports, in this process only.
+
+    The reference's config trees import ``configgle`` (``priml/model/causal_lm.py:38``,
+    ``priml/train/train_step.py``), a git-only dependency that cannot be installed offline.
+    ``priml_b200.config`` implements the same public surface (``Fig``, ``Makeable``, ``Makes``,
+    ``PartialConfig``, ``InlineConfig``, ``MutableNamespace``, ``copy_tree``, ``apply_overrides``,
+    ``resolve_config``) in plain Python and imports no kernel code, so registering it under that
+    name leaves every model, optimizer and strategy of the reference run its own code.
+    """
+    import types
+
+    import priml_b200.config as standin
+
+    root = types.ModuleType("configgle")
+    root.__dict__.update({name: getattr(standin, name) for name in standin.__all__})
+    walk = types.ModuleType("configgle.walk")
+    walk.copy_tree = standin.copy_tree  # type: ignore[attr-defined]
+    launch = types.ModuleType("configgle.launch")
+    launch.resolve_config = standin.resolve_config  # type: ignore[attr-defined]
+    root.walk, root.launch = walk, launch  # type: ignore[attr-defined]
+    sys.modules.update({"configgle": root, "configgle.walk": walk, "configgle.launch": launch})
+
+
+def _reference_model(args: argparse.Namespace) -> tuple[Any, str, Any]:
+    """Config 1 through the reference's own blocks (``priml/model/causal_lm.py:45-176``)."""
+    from functools import partial
+
+    from priml.model.attention import SelfAttention
+    from priml.model.causal_lm import CausalLM
+    from priml.model.init import normal
+    from priml.model.linear import Linear
+    from priml.model.norm import RMSNorm
+    from priml.model.rope import RoPE
+    from priml.model.swiglu import SwiGLU
+    from priml.model.transformer import TransformerBlock
+
+    from priml_b200 import cost
+
+    init = partial(normal, std=0.02)
+    block = TransformerBlock.Config(
+        attn=SelfAttention.Config(heads=32, channels_head=64, num_heads_kv=8, causal=True,
+                                  rope=RoPE.Config(64, base=5e5), init_weight=init),
+        ffn=SwiGLU.Config(channels_hidden=8192, init_weight=init),
+        norm1=RMSNorm.Config(eps=1e-5),
+        norm2=RMSNorm.Config(eps=1e-5),
+    )  # fmt: skip
+    model = CausalLM.Config(
+        32768,
+        channels=2048,
+        num_layers=args.layers,
+        block=block,
+        final_norm=RMSNorm.Config(eps=1e-5),
+        lm_head=Linear.Config(bias=False, shard="vocab", init_weight=init),
     )
+    shape = cost.DenseLMShape(d_model=2048, n_layers=args.layers, n_heads=32, n_kv_heads=8, head_dim=64,
+                              ffn_hidden=8192, vocab=32768)  # fmt: skip
+    name = f"llama-1b dense decoder (d2048 L{args.layers} 32q/8kv h64 swiglu8192 vocab32768 untied)"
+    return model, name, shape
+
+
+def _run_reference(args: argparse.Namespace) -> None:
+    """The unmodified reference (a plain copy under ``baseline/_ref``) on the same workload.
+
+    Stock path: ``priml.train.TrainStep`` (``priml/train/train_step.py:557-625``) with its default
+    ``torch.compile(fullgraph=True)`` and bf16 autocast, ``priml.optimizers.FusedAdamW`` (compiled
+    per-parameter update, ``priml/optimizers/fused_adamw.py:87-93``), the reference's per-token
+    cross-entropy (``priml/baselines/nanochat/train_step.py:43-79``), gradient clipping, and for N > 1
+    ``priml.runtime.MultiProcess`` + ``priml.train.parallelism.FullySharded`` (FSDP2 over NCCL,
+    bf16 params, fp32 reduce; ``priml/train/parallelism.py:146-202``). Nothing of this package's
+    models, kernels or strategies is imported; only the config stand-in above.
+    """
+    if not (_REF_ROOT / "priml" / "__init__.py").exists():
+        _reference_unavailable(f"the reference is not present under {_REF_ROOT.name}")
+        return
+    if args.config != "llama1b":
+        _reference_unavailable(f"the reference arm runs the llama1b workload only, not {args.config}")
+        return
+    sys.path.insert(0, str(_REF_ROOT))
+    _install_configgle_standin()
+
+    import torch
+    import torch.distributed as dist
+    from priml.baselines.nanochat.train_step import TokenCrossEntropy
+    from priml.optimizers.fused_adamw import FusedAdamW as RefFusedAdamW
+    from priml.runtime import MultiProcess as RefMultiProcess
+    from priml.runtime import SingleProcess as RefSingleProcess
+    from priml.train.parallelism import FullySharded as RefFullySharded
+    from priml.train.parallelism import NoParallel as RefNoParallel
+    from priml.train.train_step import TrainStep as RefTrainStep
+
+    from priml_b200 import cost
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    for k, v in _CONFIGS[args.config].items():
+        if getattr(args, k) is None:
+            setattr(args, k, v)
+    runtime = (RefMultiProcess.Config(mesh_topology={"dp": -1}) if world > 1 else RefSingleProcess.Config()).make()
+    runtime.initialize()
+    rank = dist.get_rank() if world > 1 else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(1234 + rank)
+    model_cfg, model_name, shape = _reference_model(args)
+    parallel = (
+        RefFullySharded.Config(mp_param_dtype=torch.bfloat16, mp_reduce_dtype=torch.float32)
+        if world > 1
+        else RefNoParallel.Config(device=dev)
+    )
+
+    def build(compiled: bool) -> Any:
+        kw: dict[str, Any] = {} if compiled else {"compile": None}
+        cfg = RefTrainStep.Config(
+            model=model_cfg,
+            optimizer=RefFusedAdamW.Config(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, compile=compiled),
+            loss=TokenCrossEntropy.Config(),
+            parallelism=parallel,
+            dtype_autocast=torch.bfloat16,
+            gradient_clip_norm=1.0,
+            **kw,
+        )
+        with torch.device(dev):  # construct on the GPU instead of allocating 5 GB of fp32 on the host first
+            return cfg.make()
+
+    vocab = shape.vocab
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    batches = [torch.randint(0, vocab, (args.mbs, args.seq + 1), device=dev, generator=g) for _ in range(4)]
+
+    def run_step(step: Any, i: int) -> None:
+        seq = batches[i % len(batches)]
+        step.train_step(tokens=seq[:, :-1], label=seq[:, 1:])
+
+    compiled = args.ref_compile != "off"
+    note = "stock path: torch.compile(fullgraph=True) model + compiled FusedAdamW update"
+    step = build(compiled)
+    try:
+        for i in range(args.warmup):
+            run_step(step, i)
+        torch.cuda.synchronize()
+    except Exception as exc:  # noqa: BLE001 - a compile failure falls back to the reference's eager config
+        if not compiled or args.ref_compile == "on" or world > 1:
+            raise
+        note = f"eager (compile=None): the compiled stock path raised {type(exc).__name__}: {str(exc)[:160]}"
+        del step
+        torch.cuda.empty_cache()
+        step = build(False)
+        for i in range(args.warmup):
+            run_step(step, i)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _ClockSampler(torch.cuda.current_device()) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            run_step(step, args.warmup + i)
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens_per_step = args.mbs * args.seq * world
+    ms_per_step = ms / args.steps
+    value = tokens_per_step / (ms_per_step / 1e3)
+
+    launches = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            run_step(step, 0)
+            torch.cuda.synchronize()
+        launches = sum(1 for e in prof.events() if e.device_type.name == "CUDA") * args.steps
+    except Exception:  # noqa: BLE001
+        launches = None
+
+    e2e = None
+    if not args.no_e2e:
+        n = args.warmup + args.steps
+        host = [torch.randint(0, vocab, (args.mbs, args.seq + 1)).pin_memory() for _ in range(n)]
+        host_batches = [{"tokens": h[:, :-1].contiguous().pin_memory(), "label": h[:, 1:].contiguous().pin_memory()}
+                        for h in host]  # fmt: skip
+        h2d = sum(t.numel() * t.element_size() for t in host_batches[0].values())
+        for i in range(args.warmup):
+            out = step.train_step(**step.preprocess_batch(host_batches[i]))
+            float(out["loss"].detach().mean())
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            out = step.train_step(**step.preprocess_batch(host_batches[args.warmup + i]))
+            float(out["loss"].detach().mean())  # device -> host read of the step's loss
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([el], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el = float(t.item())
+            dist.barrier()
+        e2e = {
+            "value": round(tokens_per_step * args.steps / el, 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": 4,
+            "ms_per_step": round(el * 1e3 / args.steps, 3),
+        }
+
+    fpt = cost.train_flops_per_token(shape, args.seq)
+    peaks = cost.load_peaks()
+    result = {
+        "impl": "reference",
+        "metric": "train tokens/s per box at 1/2/4/8 B200 (device-timed, max over ranks); MFU",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (uniform random tokens, random-init weights)",
+        "mfu": round(cost.mfu(value, fpt, world, peaks, sustained=True), 4),
+        "mfu_of": f"{peaks.source} sustained bf16 {peaks.bf16_tflops_sustained} TFLOP/s per GPU",
+        "flops_per_token": fpt,
+        "config": {
+            "model": model_name,
+            "global_batch": args.mbs * world,
+            "micro_batch_per_gpu": args.mbs,
+            "seq_len": args.seq,
+            "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+            "strategy": ("reference FullySharded (FSDP2 fully_shard, NCCL, bf16 params, fp32 reduce)" if world > 1
+                         else "reference NoParallel"),  # fmt: skip
+            "reference_path": note,
+            "reference_source": "plain copy of the reference package (pip install fails offline: no hatchling); "
+            "configgle provided by a pure-Python stand-in",
+            "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",
+        },
+        "clocks": clocks.summary(),
+        "gpu_launches": launches,
+        "e2e": e2e,
+    }
+    if rank == 0:
+        line = json.dumps(result)
+        print(line, flush=True)
+        if args.out:
+            Path(args.out).write_text(line + "\n")
+    del step
+    runtime.destroy()
 
 
 class _ClockSampler:
@@ -158,7 +415,7 @@ class _ClockSampler:
 def main() -> None:
     args = _parse()
     if args.impl == "reference":
-        _reference_unavailable()
+        _run_reference(args)
         return
 
     import torch

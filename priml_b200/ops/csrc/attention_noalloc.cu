@@ -25,10 +25,22 @@
 //     the kernels read for visible (unmasked) positions.
 //   * The first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress (that device must be current) and caches it; make
-//     that first call before any stream capture begins.
+//     that first call before any stream capture begins. The cache is keyed by
+//     device ordinal and assumes the device's primary context (the one the
+//     CUDA runtime and torch use); it is not refreshed after cudaDeviceReset,
+//     so a caller that resets a device or drives it from its own driver-API
+//     context must not use this entry point on that device afterwards.
+//   * For D = 64 the regular entry point runs a fused single-kernel backward
+//     that accumulates dQ in an fp32 buffer of B * H * S * D floats; that
+//     buffer is too large for a static array, so this entry point always runs
+//     the two-kernel backward (dK/dV, then dQ), which needs only per-row
+//     scratch.
 //   * Nothing here calls cudaMalloc, cudaFree or any allocating routine.
+#include "attention_noalloc.h"
+
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 
 #include "kernels.h"
@@ -73,23 +85,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 extern "C" {
 
-enum {
-  PB_NOALLOC_OK = 0,
-  PB_NOALLOC_BAD_ARGUMENT = 1,
-  PB_NOALLOC_TOO_LARGE = 2,
-  PB_NOALLOC_CUDA_ERROR = 3,
-};
-
-// Backward of causal / windowed / full flash attention with grouped KV heads.
-//
-// All tensors are contiguous bf16 except lse (fp32):
-//   q, o, dout, dq : [B, S, H, D]      k, v, dk, dv : [B, T, Hkv, D]
-//   lse            : [B, H, S]  (natural log-sum-exp from the forward pass)
-// D must be 64 or 128, H a multiple of Hkv, T >= S for causal masks, and
-// B * H * S <= 524288. `window` < 0 disables the sliding window. The call is
-// asynchronous on `stream`; it returns PB_NOALLOC_OK or an error code (a CUDA
-// launch error returns PB_NOALLOC_CUDA_ERROR). Kernel wait timeouts are
-// recorded in the first int of the scratch array's status word.
+// Contract in attention_noalloc.h. Kernel wait timeouts are recorded in the
+// first int of the scratch array (the status word).
 __attribute__((visibility("default"))) int pb_attn_bwd_noalloc(
     const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse, void* dq,
     void* dk, void* dv, int B, int S, int T, int H, int Hkv, int D, float scale, int causal, int window,
@@ -105,6 +102,9 @@ __attribute__((visibility("default"))) int pb_attn_bwd_noalloc(
     if (!aligned16(p)) return PB_NOALLOC_BAD_ARGUMENT;
   const long long rows = static_cast<long long>(B) * H * S;
   if (rows > kMaxRows) return PB_NOALLOC_TOO_LARGE;
+  // An error left by earlier, unrelated work stays visible to its owner: report
+  // it without clearing it, and launch nothing.
+  if (cudaPeekAtLastError() != cudaSuccess) return PB_NOALLOC_CUDA_ERROR;
 
   float* scratch = nullptr;
   if (scratch_for_current_device(&scratch) != cudaSuccess) return PB_NOALLOC_CUDA_ERROR;
@@ -136,13 +136,15 @@ __attribute__((visibility("default"))) int pb_attn_bwd_noalloc(
   return cudaGetLastError() == cudaSuccess ? PB_NOALLOC_OK : PB_NOALLOC_CUDA_ERROR;
 }
 
-// Reads (synchronously, on the current device) the status word of
-// the most recent pb_attn_bwd_noalloc call: 0 means no kernel wait timed out.
-__attribute__((visibility("default"))) int pb_attn_bwd_noalloc_status(void) {
+// Contract in attention_noalloc.h: the copy is queued on the caller's stream,
+// behind the backward kernels, and the stream is then synchronized, so the
+// read sees this call's status even on a non-blocking stream.
+__attribute__((visibility("default"))) int pb_attn_bwd_noalloc_status(cudaStream_t stream) {
   float* scratch = nullptr;
   if (scratch_for_current_device(&scratch) != cudaSuccess) return -1;
   int host = 0;
-  if (cudaMemcpy(&host, scratch, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (cudaMemcpyAsync(&host, scratch, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return -1;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
   return host;
 }
 

@@ -101,6 +101,33 @@ def test_kvcache_fifo_and_seen() -> None:
     assert c.k[0, 0, :, 0].tolist() == [2.0, 3.0, 4.0, 5.0]
 
 
+def test_kvcache_matches_naive_window_over_many_appends() -> None:
+    """Mixed single- and multi-row appends far past capacity keep the newest rows in time order."""
+    g = torch.Generator().manual_seed(3)
+    for wrapped in (False, True):
+        if wrapped:
+            c = KVCache(torch.zeros(2, 3, 7, 4), torch.zeros(2, 3, 7, 5), length=0)
+        else:
+            c = KVCache.alloc(batch=2, heads=3, max_seq=7, channels_head=4, channels_v_head=5)
+        hist_k, hist_v = [], []
+        for step in range(40):
+            s = int(torch.randint(1, 8, (1,), generator=g))
+            k = torch.randn(2, 3, s, 4, generator=g)
+            v = torch.randn(2, 3, s, 5, generator=g)
+            hist_k.append(k)
+            hist_v.append(v)
+            kv, vv = c.update(k, v)
+            want_k = torch.cat(hist_k, dim=-2)[..., -7:, :]
+            want_v = torch.cat(hist_v, dim=-2)[..., -7:, :]
+            assert torch.equal(kv, want_k) and torch.equal(vv, want_v), step
+            assert c.length == want_k.shape[-2] and c.k.shape[-2] == 7
+            assert torch.equal(c.k[..., : c.length, :], want_k)
+        assert c.seen == sum(t.shape[-2] for t in hist_k)
+        frozen = c.freeze()
+        fk, _ = frozen.update(torch.ones(2, 3, 2, 4), torch.ones(2, 3, 2, 5))
+        assert torch.equal(fk, want_k) and frozen.seen == c.seen
+
+
 def test_generate_greedy_matches_full_forward() -> None:
     torch.manual_seed(0)
     m = tiny_lm().make().eval()
