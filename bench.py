@@ -251,10 +251,12 @@ def _run_reference(args: argparse.Namespace) -> None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        torch.cuda.profiler.start()  # an external profiler run with --profile-from-start off sees the timed steps only
         start.record()
         for i in range(args.steps):
             run_step(step, args.warmup + i)
         end.record()
+        torch.cuda.profiler.stop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -533,10 +535,12 @@ def main() -> None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        torch.cuda.profiler.start()  # an external profiler run with --profile-from-start off sees the timed steps only
         start.record()
         for i in range(args.steps):
             run_step(args.warmup + i)
         end.record()
+        torch.cuda.profiler.stop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()

@@ -17,6 +17,7 @@ reference's compiled model + loss graph.
 
 from __future__ import annotations
 
+import contextlib
 import math
 import time
 from dataclasses import field
@@ -140,17 +141,26 @@ class NanoChatTrainStep(TrainStep):
         super().__init__(config)
         self.config: NanoChatTrainStep.Config = config
         self.accumulate_passes = config.tokens_per_optimizer_step // (config.rows_per_pass * config.model.max_seq_len)
-        self._pending_passes = 0
-        self._pending_worst: Tensor | None = None
-        self.elapsed_sec = 0.0
-        self._steps_this_process = 0
+        self.clock = _BudgetClock(config.budget_warmup_steps, self._synchronize)
+        self.window = _PassWindow(self.accumulate_passes)
+        self.lr_schedule = config.schedule.make()
+        self.knobs = _RecipeKnobs(config)
         for group in self.optimizer.param_groups:
             group.setdefault("initial_weight_decay", group.get("weight_decay", 0.0))
-        self.lr_schedule = config.schedule.make()
+
+    # The budget clock is the recipe's notion of time: schedules anneal over it and the loop's
+    # time limit reads it.
+    @property
+    def elapsed_sec(self) -> float:
+        return self.clock.seconds
+
+    @elapsed_sec.setter
+    def elapsed_sec(self, value: float) -> None:
+        self.clock.seconds = float(value)
 
     @property
     def progress_learning_schedule(self) -> float:
-        return min(self.elapsed_sec / float(self.config.train_budget_sec), 1.0)
+        return min(self.clock.seconds / float(self.config.train_budget_sec), 1.0)
 
     @property
     def global_step(self) -> int:
@@ -160,33 +170,27 @@ class NanoChatTrainStep(TrainStep):
         return self.compute_loss(**batch)["loss"]
 
     def train_step(self, **batch: Any) -> TrainStepOutput:  # type: ignore[override]
-        """Forward + backward of one pass; steps once ``accumulate_passes`` passes are in."""
-        config = self.config
-        if self._pending_passes == 0:
-            self._synchronize()
-        started = time.perf_counter()
-        self.model.train()
-        per_token = self._per_token_loss(batch)
-        loss = per_token.float().mean()
-        (loss / self.accumulate_passes).backward()
-        worst = loss.detach()
-        self._pending_worst = worst if self._pending_worst is None else torch.maximum(worst, self._pending_worst)
-        self._pending_passes += 1
-        metrics: dict[str, Any] = {}
-        if self._pending_passes >= self.accumulate_passes:
-            with self.timer_step:
-                metrics = self._apply_update()
-            self._pending_passes = 0
-            self._steps_this_process += 1
-        if self._steps_this_process > config.budget_warmup_steps:
-            if self._pending_passes == 0:
-                self._synchronize()
-            self.elapsed_sec += time.perf_counter() - started
-        if self._pending_passes == 0:
-            self._assert_not_diverged()
+        """Forward + backward of one pass; the optimizer steps when the window of passes is full."""
+        with self.clock.charge(boundary=self.window.empty):
+            self.model.train()
+            per_token = self._per_token_loss(batch)
+            loss = per_token.float().mean()
+            (loss / self.accumulate_passes).backward()
+            self.window.add(loss.detach())
+            metrics: dict[str, Any] = {}
+            if self.window.full:
+                with self.timer_step:
+                    metrics = self._apply_update()
+                self.clock.count_step()
+                worst = self.window.close()
+            else:
+                worst = None
+        if worst is not None:
+            self._check_loss(worst)
         self.last_loss = loss.detach()
+        stepped = self.window.empty
         return TrainStepOutput({"loss": loss.detach().reshape(1), "model": per_token.detach(), "metrics": metrics,
-                                "num_samples": int(per_token.shape[0]), "stepped": self._pending_passes == 0})  # fmt: skip
+                                "num_samples": int(per_token.shape[0]), "stepped": stepped})  # fmt: skip
 
     def train_loss(self, **batch: Any) -> TrainStepOutput:
         self.model.train()
@@ -208,61 +212,56 @@ class NanoChatTrainStep(TrainStep):
             return self.model(batch["media"])
 
     def on_epoch_end(self) -> None:
-        if self._pending_passes:
+        """A partly filled window at the end of the data is discarded, gradients included."""
+        if not self.window.empty:
             self.model.zero_grad(set_to_none=True)
-            self._pending_passes = 0
-            self._pending_worst = None
+            self.window.reset()
 
     def state_dict(self) -> dict[str, Any]:
         state = super().state_dict()
-        state["elapsed_sec"] = self.elapsed_sec
-        state["local_step"] = self._steps_this_process
+        state["elapsed_sec"] = self.clock.seconds
+        state["local_step"] = self.clock.steps
         return state
 
     def load_state_dict(self, state_dict: dict[str, Any], **kwargs: Any) -> None:
         del kwargs
         if "local_step" not in state_dict:
-            raise ValueError("this checkpoint records no 'local_step'; its budget accounting cannot be restored.")
+            raise ValueError("checkpoint lacks 'local_step': the budget clock of that run cannot be resumed.")
         super().load_state_dict(state_dict)
-        self.elapsed_sec = float(state_dict["elapsed_sec"])
-        self._steps_this_process = int(state_dict["local_step"])
-        self._pending_passes = 0
-        self._pending_worst = None
+        self.clock.seconds = float(state_dict["elapsed_sec"])
+        self.clock.steps = int(state_dict["local_step"])
+        self.window.reset()
 
     def charge_budget(self, seconds: float) -> None:
-        """Add loop-side work (batch fetch and staging) to the budget once warmup is past."""
-        if self._steps_this_process > self.config.budget_warmup_steps:
-            self.elapsed_sec += seconds
+        """Bill loop-side work (fetching and staging a batch) to the budget, once warmup is over."""
+        self.clock.bill(seconds)
 
-    def _assert_not_diverged(self) -> None:
-        if self._pending_worst is None:
-            return
-        worst = float(self._pending_worst)
-        self._pending_worst = None
-        if math.isfinite(worst) and worst <= self.config.divergence_threshold:
+    def _check_loss(self, worst: Tensor) -> None:
+        """One host read per optimizer step: the worst pass loss of the window just closed."""
+        value = float(worst)
+        if math.isfinite(value) and value <= self.config.divergence_threshold:
             return
         self.model.zero_grad(set_to_none=True)
-        self._pending_passes = 0
-        raise RuntimeError(f"training diverged at step {self.global_step}: loss={worst}.")
+        self.window.reset()
+        raise RuntimeError(f"loss {value} crossed the divergence limit at optimizer step {self.global_step}.")
 
     def _apply_update(self) -> dict[str, Any]:
-        config = self.config
         metrics: dict[str, Any] = {}
-        if math.isfinite(config.gradient_clip_norm):
-            metrics["grad_norm"] = nn.utils.clip_grad_norm_(self.model.parameters(), config.gradient_clip_norm).detach()
+        if math.isfinite(self.config.gradient_clip_norm):
+            norm = nn.utils.clip_grad_norm_(self.model.parameters(), self.config.gradient_clip_norm)
+            metrics["grad_norm"] = norm.detach()
         progress = self.progress_learning_schedule
         apply_lr_scale([self.optimizer], float(self.lr_schedule(progress)))
-        share = min(self.global_step / config.momentum_warmup_steps, 1.0)
-        momentum = (1 - share) * config.momentum_start + share * config.momentum_end
+        momentum = self.knobs.momentum(self.global_step)
+        decay_scale = self.knobs.decay_scale(progress)
         for group in self.optimizer.param_groups:
             if "momentum" in group:
                 group["momentum"] = momentum
-            if config.decay_to_zero and "weight_decay" in group:
-                group["weight_decay"] = group["initial_weight_decay"] * (1 - progress)
+            if "weight_decay" in group and decay_scale is not None:
+                group["weight_decay"] = group["initial_weight_decay"] * decay_scale
         self.optimizer.step()
         self.model.zero_grad(set_to_none=True)
-        for name, rate in _learning_rates(self.optimizer).items():
-            metrics[f"lr_{name}"] = rate
+        metrics.update({f"lr_{name}": rate for name, rate in _learning_rates(self.optimizer).items()})
         metrics["progress"] = progress
         metrics["momentum"] = momentum
         return metrics
@@ -270,6 +269,89 @@ class NanoChatTrainStep(TrainStep):
     def _synchronize(self) -> None:
         if self.device.type == "cuda":
             torch.cuda.synchronize()
+
+
+class _BudgetClock:
+    """Seconds of training spent, counted only after ``warmup_steps`` optimizer steps.
+
+    Passes are timed on the host; the device is synchronized only at the edges of a window of
+    passes, so the charge for a window is exact while no single pass waits for the GPU.
+    """
+
+    def __init__(self, warmup_steps: int, synchronize: Any) -> None:
+        self.warmup_steps = warmup_steps
+        self.synchronize = synchronize
+        self.seconds = 0.0
+        self.steps = 0  # optimizer steps taken by this process
+
+    @property
+    def running(self) -> bool:
+        return self.steps > self.warmup_steps
+
+    def count_step(self) -> None:
+        self.steps += 1
+
+    def bill(self, seconds: float) -> None:
+        if self.running:
+            self.seconds += seconds
+
+    @contextlib.contextmanager
+    def charge(self, *, boundary: bool) -> Any:
+        if boundary:
+            self.synchronize()
+        began = time.perf_counter()
+        stepped_before = self.steps
+        yield
+        if self.running:
+            if self.steps != stepped_before:
+                self.synchronize()
+            self.seconds += time.perf_counter() - began
+
+
+class _PassWindow:
+    """The passes of one optimizer step and the largest pass loss among them (kept on the device)."""
+
+    def __init__(self, size: int) -> None:
+        self.size = size
+        self.count = 0
+        self.worst: Tensor | None = None
+
+    @property
+    def empty(self) -> bool:
+        return self.count == 0
+
+    @property
+    def full(self) -> bool:
+        return self.count >= self.size
+
+    def add(self, loss: Tensor) -> None:
+        self.worst = loss if self.worst is None else torch.maximum(self.worst, loss)
+        self.count += 1
+
+    def close(self) -> Tensor | None:
+        worst = self.worst
+        self.reset()
+        return worst
+
+    def reset(self) -> None:
+        self.count = 0
+        self.worst = None
+
+
+class _RecipeKnobs:
+    """Momentum ramp over the first steps and weight-decay anneal over the budget."""
+
+    def __init__(self, config: NanoChatTrainStep.Config) -> None:
+        self.start, self.end = config.momentum_start, config.momentum_end
+        self.ramp_steps = config.momentum_warmup_steps
+        self.anneal_decay = config.decay_to_zero
+
+    def momentum(self, step: int) -> float:
+        ramp = min(step / self.ramp_steps, 1.0)
+        return self.start + (self.end - self.start) * ramp
+
+    def decay_scale(self, progress: float) -> float | None:
+        return max(0.0, 1.0 - progress) if self.anneal_decay else None
 
 
 def _learning_rates(optimizer: Any) -> dict[str, float]:

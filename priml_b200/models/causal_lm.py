@@ -22,7 +22,7 @@ from priml_b200.models.custom_types import ChannelsIn, ChannelsOut, propagate_at
 from priml_b200.models.embedding import Embedding
 from priml_b200.models.linear import Linear
 from priml_b200.models.norm import RMSNorm
-from priml_b200.models.transformer import TransformerBlock
+from priml_b200.models.transformer import TransformerBlock, add_then_norm
 
 __all__ = ["CausalLM"]
 
@@ -111,12 +111,22 @@ class CausalLM(nn.Module):
         return self.lm_head(hidden)
 
     def hidden_states(self, tokens: Tensor) -> Tensor:
-        """``final_norm(blocks(embed(tokens)))``."""
-        x = self.embed(tokens)
+        """``final_norm(blocks(embed(tokens)))``.
+
+        Blocks that can leave their last residual add to the next norm
+        (``supports_deferred_residual``) pass ``(stream, delta)`` along, so every add of the
+        residual stream runs inside the following norm kernel, the final norm's included.
+        """
+        stream, pending = self.embed(tokens), None
         for block in self.blocks:
-            out = block(x)
-            x = out[0] if isinstance(out, tuple) else out
-        return self.final_norm(x)
+            if getattr(block, "supports_deferred_residual", False):
+                stream, pending = block(stream, pending=pending, defer_residual=True)
+                continue
+            if pending is not None:
+                stream, pending = stream + pending, None
+            out = block(stream)
+            stream = out[0] if isinstance(out, tuple) else out
+        return add_then_norm(self.final_norm, stream, pending)[1]
 
     def forward(
         self,

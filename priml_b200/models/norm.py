@@ -54,6 +54,10 @@ class RMSNorm(nn.RMSNorm):
         del args, kwargs
         return ops.rms_norm(input, self.weight, self.eps)
 
+    def add_forward(self, x: Tensor, delta: Tensor | None) -> tuple[Tensor, Tensor]:
+        """``(x + delta, norm(x + delta))`` with the add done inside the norm kernel on CUDA."""
+        return ops.add_rms_norm(x, delta, self.weight, self.eps)
+
 
 class CenteredRMSNorm(nn.Module):
     """RMSNorm scaled by ``1 + weight`` (weight starts at zero), computed in fp32."""
@@ -73,9 +77,11 @@ class CenteredRMSNorm(nn.Module):
 
     def forward(self, input: Tensor, *args: Any, **kwargs: Any) -> Tensor:  # noqa: A002
         del args, kwargs
-        x = input.float()
-        y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps)
-        return ((1.0 + self.weight.float()) * y).type_as(input)
+        # The gain is the zero-initialised offset plus one; the norm kernel accumulates in fp32
+        # (on the host path the input is widened first), and the result keeps the input's dtype.
+        gain = self.weight.float() + 1.0
+        x = input if input.is_cuda else input.float()
+        return ops.rms_norm(x, gain, self.eps).to(input.dtype)
 
 
 class LayerNorm(nn.LayerNorm):
@@ -125,8 +131,10 @@ class BatchNorm(nn.BatchNorm1d):
 
     def forward(self, input: Tensor, *args: Any, **kwargs: Any) -> Tensor:  # noqa: A002
         del args, kwargs
-        shape = input.shape
-        return super().forward(input.reshape(-1, shape[-1])).reshape(shape)
+        # BatchNorm1d takes (N, C) or (N, C, L): present the features-last input channels-first,
+        # merging any extra middle axes into L, and turn the result back.
+        x = input if input.dim() <= 3 else input.flatten(1, -2)
+        return super().forward(x.movedim(-1, 1)).movedim(1, -1).reshape(input.shape)
 
 
 class BatchRenorm(nn.Module):

@@ -20,6 +20,7 @@ from priml_b200.ops._loader import native, native_available
 
 __all__ = [
     "adamw_",
+    "add_rms_norm",
     "attention",
     "cross_entropy",
     "grouped_swiglu_experts",
@@ -76,6 +77,21 @@ def rms_norm(x: Tensor, weight: Tensor | None, eps: float | None) -> Tensor:
 
         return functional.rms_norm(x, weight, eps)
     return reference.rms_norm(x, weight, eps)
+
+
+def add_rms_norm(x: Tensor, d: Tensor | None, weight: Tensor | None, eps: float | None) -> tuple[Tensor, Tensor]:
+    """Residual add fused into RMSNorm: ``h = x + d`` (``x`` when ``d`` is None) and ``rmsnorm(h)``."""
+    fusable = (
+        x.shape[-1] % 8 == 0
+        and x.dtype in (torch.bfloat16, torch.float32)
+        and (d is None or (d.dtype in (torch.bfloat16, torch.float32) and d.shape == x.shape))
+    )
+    if fusable and use_native(x, d) and _compute_dtype(x) in (torch.bfloat16, torch.float32):
+        from priml_b200.ops import functional
+
+        return functional.add_rms_norm(x, d, weight, eps)
+    h = x if d is None else x + d
+    return h, reference.rms_norm(h, weight, eps)
 
 
 def rotary(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor) -> tuple[Tensor, Tensor]:

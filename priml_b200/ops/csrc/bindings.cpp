@@ -239,6 +239,75 @@ std::vector<Tensor> rmsnorm_bwd(const Tensor& dy, const Tensor& x, const c10::op
   return {dx, dw};
 }
 
+// h = x + d (fp32 when either operand is fp32), y = rmsnorm(h); returns {h, y, rstd}.
+std::vector<Tensor> add_rmsnorm_fwd(const Tensor& x, const Tensor& d, const c10::optional<Tensor>& w, double eps,
+                                    bool out_f32) {
+  check_cuda(x, "x");
+  check_cuda(d, "d");
+  PB_CHECK(x.sizes() == d.sizes(), "x and d must have the same shape");
+  PB_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "x must be fp32 or bf16");
+  PB_CHECK(d.scalar_type() == torch::kFloat32 || d.scalar_type() == torch::kBFloat16, "d must be fp32 or bf16");
+  const int C = x.size(-1);
+  PB_CHECK(C % 8 == 0, "channels must be a multiple of 8");
+  const int R = x.numel() / C;
+  auto xc = x.contiguous();
+  auto dc = d.contiguous();
+  const bool h_f32 = x.scalar_type() == torch::kFloat32 || d.scalar_type() == torch::kFloat32;
+  auto h = torch::empty(x.sizes(), x.options().dtype(h_f32 ? torch::kFloat32 : torch::kBFloat16));
+  auto y = torch::empty(x.sizes(), x.options().dtype(out_f32 ? torch::kFloat32 : torch::kBFloat16));
+  auto rstd = torch::empty({R}, x.options().dtype(torch::kFloat32));
+  const float* wp = nullptr;
+  Tensor wc;
+  if (w.has_value() && w->defined()) {
+    wc = w->to(torch::kFloat32).contiguous();
+    wp = wc.data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (R > 0)
+    pb::rmsnorm_fwd(xc.data_ptr(), xc.scalar_type() == torch::kFloat32, wp, y.data_ptr(), out_f32,
+                    rstd.data_ptr<float>(), R, C, static_cast<float>(eps), stream(), dc.data_ptr(),
+                    dc.scalar_type() == torch::kFloat32, h.data_ptr(), h_f32);
+  return {h, y, rstd};
+}
+
+// Gradient of (h, y) = (x + d, rmsnorm(x + d)) given dy and the residual-path gradient dres
+// (optional): returns {dx (dx_f32 selects fp32), dd (dtype code: -1 none, 0 bf16, 1 fp32), dw}.
+std::vector<Tensor> add_rmsnorm_bwd(const Tensor& dy, const Tensor& h, const c10::optional<Tensor>& w,
+                                    const Tensor& rstd, const c10::optional<Tensor>& dres, bool dx_f32,
+                                    int64_t dd_dtype) {
+  check_cuda(h, "h");
+  const int C = h.size(-1);
+  const int R = h.numel() / C;
+  auto dyc = dy.contiguous();
+  PB_CHECK(dyc.sizes() == h.sizes(), "dy must match h");
+  Tensor drc;
+  if (dres.has_value() && dres->defined()) {
+    drc = dres->contiguous();
+    PB_CHECK(drc.sizes() == h.sizes(), "dres must match h");
+    PB_CHECK(drc.scalar_type() == torch::kFloat32 || drc.scalar_type() == torch::kBFloat16, "dres must be fp32/bf16");
+  }
+  auto dx = torch::empty(h.sizes(), h.options().dtype(dx_f32 ? torch::kFloat32 : torch::kBFloat16));
+  Tensor dd;
+  if (dd_dtype >= 0) dd = torch::empty(h.sizes(), h.options().dtype(dd_dtype == 1 ? torch::kFloat32 : torch::kBFloat16));
+  Tensor dw, wc;
+  const float* wp = nullptr;
+  float* dwp = nullptr;
+  if (w.has_value() && w->defined()) {
+    wc = w->to(torch::kFloat32).contiguous();
+    wp = wc.data_ptr<float>();
+    dw = torch::zeros({C}, h.options().dtype(torch::kFloat32));
+    dwp = dw.data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(h.device());
+  if (R > 0)
+    pb::rmsnorm_bwd(dyc.data_ptr(), dyc.scalar_type() == torch::kFloat32, h.data_ptr(),
+                    h.scalar_type() == torch::kFloat32, wp, rstd.data_ptr<float>(), dx.data_ptr(), dx_f32, dwp, R, C,
+                    stream(), drc.defined() ? drc.data_ptr() : nullptr,
+                    drc.defined() && drc.scalar_type() == torch::kFloat32, dd.defined() ? dd.data_ptr() : nullptr,
+                    dd_dtype == 1);
+  return {dx, dd, dw};
+}
+
 // x: [B, S, H, D] bf16 (last dim contiguous, any other strides). cos/sin: fp32 [S, D/2] contiguous.
 Tensor rope(const Tensor& x, const Tensor& cos, const Tensor& sin, double sign) {
   check_cuda(x, "x");
@@ -922,6 +991,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, "tcgen05 GEMM dy @ W_down with the SwiGLU backward in the epilogue");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);
   m.def("rope", &rope);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);

@@ -58,7 +58,18 @@ __device__ __forceinline__ void store8(void* base, bool f32, long long idx, cons
 
 // ------------------------------------------------------------------ RMSNorm
 // One warp per row; C % 8 == 0.
-__global__ void rmsnorm_fwd_kernel(const void* __restrict__ x, bool x_f32, const float* __restrict__ w,
+//
+// Residual form: with an addend d the kernel normalizes h = x + d and, when h
+// is given, stores it (the next residual-stream value) in the same pass, so a
+// pre-norm block needs no separate add kernel. A bf16 h is rounded before the
+// statistics, so y is exactly the normalization of the stored h.
+__device__ __forceinline__ void round_bf16_8(float (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+}
+
+__global__ void rmsnorm_fwd_kernel(const void* __restrict__ x, bool x_f32, const void* __restrict__ d, bool d_f32,
+                                   const float* __restrict__ w, void* __restrict__ h, bool h_f32,
                                    void* __restrict__ y, bool y_f32, float* __restrict__ rstd, int R, int C,
                                    float eps) {
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
@@ -69,6 +80,16 @@ __global__ void rmsnorm_fwd_kernel(const void* __restrict__ x, bool x_f32, const
   for (int c = lane * 8; c < C; c += 256) {
     float v[8];
     load8(x, x_f32, base + c, v);
+    if (d != nullptr) {
+      float a[8];
+      load8(d, d_f32, base + c, a);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += a[j];
+      if (h != nullptr) {
+        if (!h_f32) round_bf16_8(v);
+        store8(h, h_f32, base + c, v);
+      }
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
   }
@@ -77,16 +98,31 @@ __global__ void rmsnorm_fwd_kernel(const void* __restrict__ x, bool x_f32, const
   if (lane == 0 && rstd != nullptr) rstd[row] = r;
   for (int c = lane * 8; c < C; c += 256) {
     float v[8];
-    load8(x, x_f32, base + c, v);
+    if (d != nullptr && h != nullptr) {
+      load8(h, h_f32, base + c, v);  // this thread's own stores from the first pass
+    } else {
+      load8(x, x_f32, base + c, v);
+      if (d != nullptr) {
+        float a[8];
+        load8(d, d_f32, base + c, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += a[j];
+      }
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = v[j] * r * (w != nullptr ? w[c + j] : 1.f);
     store8(y, y_f32, base + c, v);
   }
 }
 
+// dx = dres + rstd * (w*dy - xhat * mean(w*dy*xhat)); dres is the gradient that
+// reached the normalized input along the residual path (optional). dx2, when
+// given, receives the same values in a second dtype: the gradient of the
+// addend d, which shares h's gradient.
 __global__ void rmsnorm_bwd_kernel(const void* __restrict__ dy, bool dy_f32, const void* __restrict__ x, bool x_f32,
-                                   const float* __restrict__ w, const float* __restrict__ rstd, void* __restrict__ dx,
-                                   bool dx_f32, float* __restrict__ dw, int R, int C) {
+                                   const float* __restrict__ w, const float* __restrict__ rstd,
+                                   const void* __restrict__ dres, bool dres_f32, void* __restrict__ dx, bool dx_f32,
+                                   void* __restrict__ dx2, bool dx2_f32, float* __restrict__ dw, int R, int C) {
   extern __shared__ float dw_acc[];  // C floats when dw != nullptr
   if (dw != nullptr) {
     for (int c = threadIdx.x; c < C; c += blockDim.x) dw_acc[c] = 0.f;
@@ -110,14 +146,21 @@ __global__ void rmsnorm_bwd_kernel(const void* __restrict__ dy, bool dy_f32, con
       float g[8], v[8], o[8];
       load8(dy, dy_f32, base + c, g);
       load8(x, x_f32, base + c, v);
+      if (dres != nullptr) {
+        load8(dres, dres_f32, base + c, o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = 0.f;
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float xh = v[j] * r;
         const float wg = g[j] * (w != nullptr ? w[c + j] : 1.f);
-        o[j] = r * (wg - xh * dot);
+        o[j] += r * (wg - xh * dot);
         if (dw != nullptr) atomicAdd(&dw_acc[c + j], g[j] * xh);
       }
       store8(dx, dx_f32, base + c, o);
+      if (dx2 != nullptr) store8(dx2, dx2_f32, base + c, o);
     }
   }
   if (dw != nullptr) {
@@ -354,13 +397,15 @@ int grid_for(long long work, int threads) {
 }  // namespace
 
 void rmsnorm_fwd(const void* x, bool x_f32, const float* w, void* y, bool y_f32, float* rstd, int R, int C, float eps,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const void* d, bool d_f32, void* h, bool h_f32) {
   const int warps = 8;
-  rmsnorm_fwd_kernel<<<(R + warps - 1) / warps, warps * 32, 0, stream>>>(x, x_f32, w, y, y_f32, rstd, R, C, eps);
+  rmsnorm_fwd_kernel<<<(R + warps - 1) / warps, warps * 32, 0, stream>>>(x, x_f32, d, d_f32, w, h, h_f32, y, y_f32,
+                                                                          rstd, R, C, eps);
 }
 
 void rmsnorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* w, const float* rstd, void* dx,
-                 bool dx_f32, float* dw, int R, int C, cudaStream_t stream) {
+                 bool dx_f32, float* dw, int R, int C, cudaStream_t stream, const void* dres, bool dres_f32, void* dx2,
+                 bool dx2_f32) {
   const int warps = 8;
   int blocks = (R + warps - 1) / warps;
   const size_t smem = dw != nullptr ? static_cast<size_t>(C) * sizeof(float) : 0;
@@ -370,7 +415,8 @@ void rmsnorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const f
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   }
-  rmsnorm_bwd_kernel<<<blocks, warps * 32, smem, stream>>>(dy, dy_f32, x, x_f32, w, rstd, dx, dx_f32, dw, R, C);
+  rmsnorm_bwd_kernel<<<blocks, warps * 32, smem, stream>>>(dy, dy_f32, x, x_f32, w, rstd, dres, dres_f32, dx, dx_f32,
+                                                            dx2, dx2_f32, dw, R, C);
 }
 
 void rope_apply(const void* x, long long sb, long long ss, long long sh, void* y, int B, int S, int H, int D,

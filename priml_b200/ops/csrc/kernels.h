@@ -50,10 +50,15 @@ void mx_gemm(const void* A, const void* sfa, const void* B, const void* sfb, voi
              int epi, int* status, cudaStream_t stream);
 
 // RMSNorm over the last dim C of R rows. x: bf16 or fp32 (x_f32 selects), y: bf16 or fp32.
+// Residual form: with an addend d the normalized value is h = x + d, stored to h when given.
 void rmsnorm_fwd(const void* x, bool x_f32, const float* w, void* y, bool y_f32, float* rstd, int R, int C, float eps,
-                 cudaStream_t stream);
+                 cudaStream_t stream, const void* d = nullptr, bool d_f32 = false, void* h = nullptr,
+                 bool h_f32 = false);
+// dx = dres (optional residual-path gradient) + the normalization's gradient; dx2 (optional)
+// receives the same values in a second dtype.
 void rmsnorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* w, const float* rstd, void* dx,
-                 bool dx_f32, float* dw, int R, int C, cudaStream_t stream);
+                 bool dx_f32, float* dw, int R, int C, cudaStream_t stream, const void* dres = nullptr,
+                 bool dres_f32 = false, void* dx2 = nullptr, bool dx2_f32 = false);
 
 // Half-split RoPE on [B, S, H, D] views (last dim contiguous); cos/sin fp32 [S, D/2].
 // sign = +1 forward rotation, -1 inverse (backward).

@@ -20,6 +20,7 @@ from priml_b200.ops._loader import native
 
 __all__ = [
     "GradSink",
+    "add_rms_norm",
     "attention",
     "attention_supported",
     "bf16_shadow",
@@ -318,6 +319,52 @@ def rms_norm(x: Tensor, weight: Tensor | None, eps: float | None) -> Tensor:
         return F.rms_norm(x, (x.shape[-1],), weight, eps)
     out_f32 = x.dtype == torch.float32 and not torch.is_autocast_enabled("cuda")
     return _RMSNorm.apply(x, weight, _eps(eps, x), out_f32)
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    """``(h, y) = (x + d, rmsnorm(x + d))`` in one kernel; ``d`` may be ``None`` (then ``h`` is ``x``).
+
+    The backward merges the two gradients that reach ``h`` -- along the residual stream and
+    through the norm -- in the norm's backward kernel, and writes ``d``'s copy of that gradient
+    in ``d``'s dtype, so neither the add nor its gradient costs a separate elementwise pass.
+    """
+
+    @staticmethod
+    def forward(ctx, x: Tensor, d: Tensor | None, weight: Tensor | None, eps: float, out_f32: bool):  # type: ignore[override]
+        ctx.set_materialize_grads(False)
+        if d is None:
+            h = x.contiguous()
+            y, rstd = native().rmsnorm_fwd(h, weight, eps, out_f32)
+        else:
+            h, y, rstd = native().add_rmsnorm_fwd(x, d, weight, eps, out_f32)
+        ctx.save_for_backward(h, weight, rstd)
+        ctx.x_dtype = x.dtype
+        ctx.d_dtype = None if d is None else d.dtype
+        return h, y
+
+    @staticmethod
+    def backward(ctx, dh: Tensor | None, dy: Tensor | None):  # type: ignore[override]
+        h, weight, rstd = ctx.saved_tensors
+        if dy is None:
+            if dh is None:
+                return None, None, None, None, None
+            dd = None if ctx.d_dtype is None else dh.to(ctx.d_dtype)
+            return dh.to(ctx.x_dtype), dd, None, None, None
+        dd_code = -1 if ctx.d_dtype is None else (1 if ctx.d_dtype == torch.float32 else 0)
+        dx, dd, dw = native().add_rmsnorm_bwd(dy, h, weight, rstd, dh, ctx.x_dtype == torch.float32, dd_code)
+        sink = grad_sink(weight) if weight is not None and dw is not None else None
+        if sink is not None:
+            sink.deliver(weight, dw)
+            dw = None
+        elif weight is not None and dw is not None and dw.dtype != weight.dtype:
+            dw = dw.to(weight.dtype)
+        return dx, (dd if ctx.d_dtype is not None else None), (dw if weight is not None else None), None, None
+
+
+def add_rms_norm(x: Tensor, d: Tensor | None, weight: Tensor | None, eps: float | None) -> tuple[Tensor, Tensor]:
+    """Residual add fused into RMSNorm: returns ``(x + d, rmsnorm(x + d))`` (``d=None``: ``(x, rmsnorm(x))``)."""
+    out_f32 = x.dtype == torch.float32 and not torch.is_autocast_enabled("cuda")
+    return _AddRMSNorm.apply(x, d, weight, _eps(eps, x), out_f32)
 
 
 class _Rotary(torch.autograd.Function):

@@ -112,6 +112,58 @@ def test_rmsnorm_fwd_bwd() -> None:
         assert _rel_err(w.grad, wr.grad) < 1e-3
 
 
+@pytest.mark.parametrize("x_dtype,d_dtype", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                             (torch.float32, torch.float32), (torch.float32, None)])
+@pytest.mark.parametrize("affine", [False, True])
+def test_add_rmsnorm_matches_fp32(x_dtype, d_dtype, affine) -> None:  # noqa: ANN001
+    """h = x + d and rmsnorm(h) in one kernel; the backward merges the residual gradient dh with
+    the norm's and writes d's gradient in d's dtype."""
+    from priml_b200.ops import functional as fn
+
+    torch.manual_seed(5)
+    x = torch.randn(300, 2048, device="cuda", dtype=x_dtype, requires_grad=True)
+    d = None if d_dtype is None else torch.randn(300, 2048, device="cuda", dtype=d_dtype, requires_grad=True)
+    w = torch.randn(2048, device="cuda", requires_grad=True) if affine else None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        h, y = fn.add_rms_norm(x, d, w, 1e-5)
+    gh, gy = torch.randn_like(h), torch.randn_like(y)
+    torch.autograd.backward([h, y], [gh, gy])
+
+    xr = x.detach().float().requires_grad_()
+    dr = None if d is None else d.detach().float().requires_grad_()
+    wr = None if w is None else w.detach().requires_grad_()
+    hr = xr if dr is None else xr + dr
+    if h.dtype == torch.bfloat16:
+        hr = hr.bfloat16().float()  # the kernel normalizes the stored (rounded) sum
+    yr = F.rms_norm(hr, (2048,), wr, 1e-5)
+    torch.autograd.backward([hr, yr], [gh.float(), gy.float()])
+    assert h.dtype == (torch.float32 if torch.float32 in (x_dtype, d_dtype) else torch.bfloat16)
+    assert _rel_err(h, hr) < 1e-2
+    assert _rel_err(y, yr) < 1e-2
+    assert x.grad.dtype == x_dtype and _rel_err(x.grad, xr.grad) < 2e-2
+    if d is not None:
+        assert d.grad.dtype == d_dtype and _rel_err(d.grad, dr.grad) < 2e-2
+    if w is not None:
+        assert _rel_err(w.grad, wr.grad) < 1e-2
+
+
+def test_deferred_residual_blocks_match_plain_blocks() -> None:
+    """A CausalLM whose blocks pass (stream, delta) pairs equals one that adds after every block."""
+    from priml_b200.models.presets import dense_lm
+
+    torch.manual_seed(0)
+    model = dense_lm(vocab=512, d_model=256, n_layers=3, n_heads=4, n_kv_heads=2, head_dim=64, ffn_hidden=512,
+                     rope_theta=1e4).make().cuda()  # fmt: skip
+    tokens = torch.randint(0, 512, (2, 128), device="cuda")
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        fused = model.hidden_states(tokens)
+        x = model.embed(tokens)
+        for block in model.blocks:
+            x = block(x)
+        plain = model.final_norm(x)
+    assert _rel_err(fused, plain) < 1e-2
+
+
 def test_rope_matches_reference() -> None:
     from priml_b200.ops import functional as fn
     from priml_b200.ops import reference
