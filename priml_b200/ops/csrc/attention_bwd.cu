@@ -1,7 +1,7 @@
 // Flash-attention backward for sm_100a (layouts as in attention_fwd.cu).
 //
 // Two variants. With an fp32 dQ scratch and D = 64: the delta kernel, one fused
-// dK/dV/dQ kernel (attn_bwd_fused_kernel, below) and a dQ conversion kernel.
+// dK/dV/dQ kernel (attention_bwd_d64.cu) and a dQ conversion kernel.
 // Otherwise three kernels, no atomics:
 //   delta : delta = rowsum(dO * O)
 //   dkdv  : one CTA per (b, kv head, 128-key tile) loops over every query head
@@ -552,383 +552,6 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 
-// ============================================================================ fused dK dV dQ (D = 64)
-// One CTA per (b, kv head, 128-key tile) loops over every (query head, 64-query
-// tile) step of its GQA group:
-//   * K and V rows are copied into TMEM once and serve as the A operands of
-//     S^T = K Q^T and dP^T = V dO^T (two TMEM buffer pairs, one step ahead);
-//   * eight softmax warps in two ping-pong groups of four turn S^T / dP^T into
-//     P^T / dS^T (bf16, back into TMEM) and also store dS^T in shared memory
-//     (128B-swizzled, queries contiguous);
-//   * the MMA warp issues dV += P^T dO, dK += dS^T Q (A from TMEM) and
-//     dQ^T = K^T dS^T (M = 128: rows 0-63 read V as filler, rows 64-127 read K;
-//     N = 64 queries; K = 128 keys);
-//   * two epilogue warps (TMEM lanes 64-127 = d) move each dQ^T tile through
-//     shared memory and bulk-reduce-add it (fp32, performed in L2) into
-//     dq_acc [B, H, S, D]; a last kernel scales and converts dq_acc to bf16.
-// exp() runs once per score and the backward needs five GEMMs instead of the
-// seven of the two-kernel variant.
-struct FusedSmem {
-  static constexpr int kStages = 3;
-  static constexpr int kKVBytes = kChunkBytes;   // [128 keys][64 d]
-  static constexpr int kQBytes = kLChunk;        // [64 q][64 d]
-  static constexpr int kDSBytes = 128 * 128;     // [128 keys][64 q] bf16
-  static constexpr int kDQBytes = 64 * 32 * 4;   // [64 q][32 d] fp32 (one warp's half)
-  static constexpr int kBytes = 2 * kKVBytes + kStages * 2 * kQBytes + 2 * kDSBytes + 4 * kDQBytes +
-                                kStages * 2 * kLT * 4 + 1024 + 256;
-};
-
-__global__ void __launch_bounds__(384, 1)
-    attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                          const __grid_constant__ CUtensorMap tmDQ, const AttnParams p) {
-  constexpr int D = 64;
-  using SM = FusedSmem;
-  constexpr int NS = SM::kStages;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sV = smem;                    // V first: the dQ^T A operand reads [V | K] as its two M halves
-  uint8_t* sK = sV + SM::kKVBytes;
-  uint8_t* sQ = sK + SM::kKVBytes;       // [NS]
-  uint8_t* sDO = sQ + NS * SM::kQBytes;  // [NS]
-  uint8_t* sDS = sDO + NS * SM::kQBytes;  // [2]
-  float* sDQ = reinterpret_cast<float*>(sDS + 2 * SM::kDSBytes);  // [2 warps][2 buffers]
-  float* sVec = sDQ + 4 * (SM::kDQBytes / 4);                     // [NS][lse 64 | delta 64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sVec + NS * 2 * kLT);
-  uint64_t* kv_full = bars;
-  uint64_t* in_full = kv_full + 1;     // [NS]
-  uint64_t* in_empty = in_full + NS;   // [NS]
-  uint64_t* s_full = in_empty + NS;    // [2]
-  uint64_t* p_ready = s_full + 2;      // [2]
-  uint64_t* dq_full = p_ready + 2;
-  uint64_t* dq_empty = dq_full + 1;
-  uint64_t* kv_tmem = dq_empty + 1;    // K and V copied into TMEM
-  uint64_t* mm_done = kv_tmem + 1;
-  uint64_t* acc_final = mm_done + 1;
-  uint64_t* drain = acc_final + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int bhk = blockIdx.x % (p.B * p.Hkv);
-  const int kt = blockIdx.x / (p.B * p.Hkv);  // key tile 0 (seen by the most queries) first
-  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
-  const int g = p.H / p.Hkv;
-  const int k0 = kt * kTile;
-  const int off = p.T - p.S;
-  int qlo = 0, qhi = p.S - 1;
-  if (p.causal) qlo = max(0, k0 - off);
-  if (p.window >= 0) qhi = min(qhi, k0 + kTile - 1 + p.window - off);
-  const int qt_lo = qlo / kLT;
-  const int qt_hi = qhi < qlo ? qt_lo - 1 : qhi / kLT;
-  const int nq = qt_hi >= qt_lo ? qt_hi - qt_lo + 1 : 0;
-  const int n_steps = nq * g;  // (query head, 64-query tile) pairs
-  const bool bulk_vec = (p.vec_s & 3) == 0;
-
-  const int warp = warp_id(), lane = lane_id();
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&in_full[s], 1);
-      mbar_init(&in_empty[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_ready[s], 4);
-    }
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 2);
-    mbar_init(kv_tmem, 8);
-    mbar_init(mm_done, 1);
-    mbar_init(acc_final, 1);
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // cols: S^T [0,64) [64,128); dP^T [128,192) [192,256); dV [256,320); dK [320,384); dQ^T [384,448);
-  // K [448,480) and V [480,512) as bf16 pairs: the A operands of S^T = K Q^T and dP^T = V dO^T stay in
-  // TMEM for the whole CTA, so those MMAs read only Q / dO from shared memory.
-  const uint32_t tdV = tmem + 256;
-  const uint32_t tdK = tmem + 320;
-  const uint32_t tdQ = tmem + 384;
-  const uint32_t tK = tmem + 448;
-  const uint32_t tV = tmem + 480;
-
-  if (warp == 0 && lane == 0) {
-    bool ok = true;
-    mbar_arrive_expect_tx(kv_full, 2 * SM::kKVBytes);
-    load_tile(sK, &tmK, kv_full, hk * D, k0, b, D);
-    load_tile(sV, &tmV, kv_full, hk * D, k0, b, D);
-    for (int i = 0; i < n_steps && ok; ++i) {
-      const int st = i % NS;
-      const uint32_t ph = static_cast<uint32_t>((i / NS) & 1);
-      const int h = hk * g + i / nq;
-      const int q0 = (qt_lo + i % nq) * kLT;
-      if (!mbar_wait(&in_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
-      float* vec = sVec + st * 2 * kLT;
-      const long long row = (static_cast<long long>(b) * p.H + h) * p.vec_s + q0;
-      if (bulk_vec) {
-        mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes + 2 * kLT * 4);
-        bulk_load(vec, p.nlse2 + row, kLT * 4, &in_full[st]);
-        bulk_load(vec + kLT, p.delta + row, kLT * 4, &in_full[st]);
-      } else {
-        for (int r = 0; r < kLT; ++r) {
-          const bool in = q0 + r < p.S;
-          vec[r] = in ? p.nlse2[row + r] : 0.f;
-          vec[kLT + r] = in ? p.delta[row + r] : 0.f;
-        }
-        mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes);
-      }
-      load_tile(sQ + st * SM::kQBytes, &tmQ, &in_full[st], h * D, q0, b, D, kLChunk);
-      load_tile(sDO + st * SM::kQBytes, &tmDO, &in_full[st], h * D, q0, b, D, kLChunk);
-    }
-    if (!ok) mbar_wait(kv_full, 0, p.status, kTimeoutDrain, nullptr);
-  } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc_ss = make_idesc_bf16(128, kLT, false, false);  // [128 keys x 64 q]
-    constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, false, true);   // [128 keys x D]
-    constexpr uint32_t idesc_dq = make_idesc_bf16(128, kLT, true, true);   // [128 (V|K) x 64 q]
-    bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag) &&
-              mbar_wait(kv_tmem, 0, p.status, kTimeoutMma, abort_flag);
-    tc_fence_after();
-    const uint32_t v_base = smem_u32(sV);
-    auto issue_scores = [&](int i) -> bool {
-      const int st = i % NS;
-      if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutMma, abort_flag)) return false;
-      tc_fence_after();
-      const uint32_t q_base = smem_u32(sQ + st * SM::kQBytes);
-      const uint32_t do_base = smem_u32(sDO + st * SM::kQBytes);
-      const uint32_t tS = tmem + (i & 1) * kLT;
-      const uint32_t tP = tmem + 128 + (i & 1) * kLT;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        umma_f16_tmem_a(tS, tK + kk * 8, kmajor_desc(q_base, kk, kLChunk), idesc_ss, kk > 0);
-        umma_f16_tmem_a(tP, tV + kk * 8, kmajor_desc(do_base, kk, kLChunk), idesc_ss, kk > 0);
-      }
-      umma_commit(&s_full[i & 1]);
-      return true;
-    };
-    if (ok && n_steps > 0) ok = issue_scores(0);
-    for (int i = 0; i < n_steps && ok; ++i) {
-      if (i + 1 < n_steps && !(ok = issue_scores(i + 1))) break;
-      if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const int st = i % NS;
-      const uint32_t q_base = smem_u32(sQ + st * SM::kQBytes);
-      const uint32_t do_base = smem_u32(sDO + st * SM::kQBytes);
-      const uint32_t tS = tmem + (i & 1) * kLT;
-      const uint32_t tP = tmem + 128 + (i & 1) * kLT;
-      // dQ^T was last read by the epilogue warps at step i-1.
-      if (!mbar_wait(dq_empty, (i & 1) ^ 1u, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t ds_base = smem_u32(sDS + (i & 1) * SM::kDSBytes);
-      const uint32_t tQ = tdQ;
-      // dV, dK and the first half of dQ^T interleaved (three independent accumulators), then
-      // the rest of dQ^T.
-#pragma unroll
-      for (int kk = 0; kk < kLT / 16; ++kk) {
-        umma_f16_tmem_a(tdV, tS + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(do_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
-        umma_f16_tmem_a(tdK, tP + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(q_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
-        umma_f16(tQ, make_sw128_desc(v_base + kk * 2048, SM::kKVBytes, 1024),
-                   make_sw128_desc(ds_base + kk * 2048, SM::kDSBytes, 1024), idesc_dq, kk > 0);
-      }
-#pragma unroll
-      for (int kk = kLT / 16; kk < kTile / 16; ++kk)
-        umma_f16(tQ, make_sw128_desc(v_base + kk * 2048, SM::kKVBytes, 1024),
-                 make_sw128_desc(ds_base + kk * 2048, SM::kDSBytes, 1024), idesc_dq, true);
-      umma_commit(dq_full);
-      umma_commit(&in_empty[st]);
-      umma_commit(mm_done);
-      // Buffer pair i&1 (TMEM S/dP and shared dS^T) is rewritten at step i+2.
-      if (!mbar_wait(mm_done, i & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
-    }
-    umma_commit(acc_final);
-    umma_commit(drain);
-    mbar_wait(drain, 0, p.status, kTimeoutDrain, nullptr);
-  } else if (warp == 2 || warp == 3) {
-    // dQ epilogue: TMEM lane quarter 2 / 3 holds d = 0..31 / 32..63 of dQ^T.
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const int d0 = (warp - 2) * 32;
-    float* stage = sDQ + (warp - 2) * 2 * (SM::kDQBytes / 4);
-    for (int i = 0; i < n_steps; ++i) {
-      const int h = hk * g + i / nq;
-      const int q0 = (qt_lo + i % nq) * kLT;
-      if (!mbar_wait_warp(dq_full, i & 1, p.status, kTimeoutEpilogue, abort_flag)) break;
-      tc_fence_after();
-      uint32_t v0[32], v1[32];
-      tmem_ld_32x32b_x32(tdQ + lane_off, v0);
-      tmem_ld_32x32b_x32(tdQ + lane_off + 32, v1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(dq_empty);
-        bulk_wait_read_1();  // the reduce issued two steps ago no longer reads this staging buffer
-      }
-      __syncwarp();
-      float* buf = stage + (i & 1) * (SM::kDQBytes / 4);  // [64 q][32 d]
-#pragma unroll
-      for (int q = 0; q < 32; ++q) buf[q * 32 + lane] = __uint_as_float(v0[q]);
-#pragma unroll
-      for (int q = 0; q < 32; ++q) buf[(q + 32) * 32 + lane] = __uint_as_float(v1[q]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_reduce_add_2d(&tmDQ, buf, d0, static_cast<int>((static_cast<long long>(b) * p.H + h) * p.S + q0));
-        tma_store_commit();
-      }
-    }
-    if (lane == 0) tma_store_wait_all();
-  } else if (warp >= 4) {
-    // 8 softmax warps in two groups of four (one warp per TMEM lane quarter):
-    // group g takes the steps i with i % 2 == g (TMEM / dS^T buffer g), so one
-    // group computes while the other waits on TMEM or barriers. Each warp covers
-    // 32 key rows x 64 queries in two 32-column halves.
-    const int quarter = warp & 3;
-    const int grp = (warp - 4) >> 2;
-    const int kr = quarter * 32 + lane;  // key row
-    const int key = k0 + kr;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const float sl2 = p.scale_log2;
-    bool ok = mbar_wait_warp(kv_full, 0, p.status, kTimeoutEpilogue, abort_flag);
-    {
-      // Row kr of K (group 0) or V (group 1): eight swizzled 16-byte chunks -> 32 TMEM columns.
-      const uint8_t* src = (grp == 0 ? sK : sV) + kr * 128;
-      uint32_t w[32];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 x = *reinterpret_cast<const uint4*>(src + ((c ^ (kr & 7)) << 4));
-        w[4 * c] = x.x;
-        w[4 * c + 1] = x.y;
-        w[4 * c + 2] = x.z;
-        w[4 * c + 3] = x.w;
-      }
-      tmem_st_32x32b_x32((grp == 0 ? tK : tV) + lane_off, w);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(kv_tmem);
-    }
-    for (int i = grp; i < n_steps && ok; i += 2) {
-      const int st = i % NS;
-      const int q0 = (qt_lo + i % nq) * kLT;
-      if (!mbar_wait_warp(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      if (!mbar_wait_warp(&s_full[grp], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t tS = tmem + lane_off + grp * kLT;
-      const uint32_t tP = tS + 128;
-      uint8_t* row = sDS + grp * SM::kDSBytes + kr * 128;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        const int c0 = half * 32;
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tS + c0, sv);
-        tmem_ld_32x32b_x32(tP + c0, dv);
-        const float4* nl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kLT + c0);
-        const float4* dl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kLT + kLT + c0);
-        float nl[32], dl[32];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float4 a = nl4[t], d = dl4[t];
-          nl[4 * t] = a.x;
-          nl[4 * t + 1] = a.y;
-          nl[4 * t + 2] = a.z;
-          nl[4 * t + 3] = a.w;
-          dl[4 * t] = d.x;
-          dl[4 * t + 1] = d.y;
-          dl[4 * t + 2] = d.z;
-          dl[4 * t + 3] = d.w;
-        }
-        tmem_wait_ld();
-        const bool need_mask = (p.causal && k0 + kTile - 1 > off + q0 + c0) || (k0 + kTile > p.T) ||
-                               (q0 + c0 + 32 > p.S) || (p.window >= 0 && k0 < off + q0 + c0 + 31 - p.window);
-        uint32_t pk[16], dk[16];
-        if (!need_mask) {
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * t]), sl2, nl[2 * t]));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * t + 1]), sl2, nl[2 * t + 1]));
-            pk[t] = pack_bf16x2(p0, p1);
-            dk[t] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * t]) - dl[2 * t]),
-                                p1 * (__uint_as_float(dv[2 * t + 1]) - dl[2 * t + 1]));
-          }
-        } else {
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            float pr[2], ds[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int qi = 2 * t + e;
-              const bool vis = visible(p, q0 + c0 + qi, key);
-              const float pv = vis ? fast_exp2(fmaf(__uint_as_float(sv[qi]), sl2, nl[qi])) : 0.f;
-              pr[e] = pv;
-              ds[e] = vis ? pv * (__uint_as_float(dv[qi]) - dl[qi]) : 0.f;
-            }
-            pk[t] = pack_bf16x2(pr[0], pr[1]);
-            dk[t] = pack_bf16x2(ds[0], ds[1]);
-          }
-        }
-        tmem_st_32x32b_x16(tS + c0, pk);  // inside this half's own S columns
-        tmem_st_32x32b_x16(tP + c0, dk);
-        // dS^T row `kr`, queries [c0, c0 + 32): four 16-byte chunks of the 128B-swizzled row.
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int chunk = (c0 >> 3) + t;
-          *reinterpret_cast<uint4*>(row + ((chunk ^ (kr & 7)) << 4)) =
-              make_uint4(dk[4 * t], dk[4 * t + 1], dk[4 * t + 2], dk[4 * t + 3]);
-        }
-      }
-      fence_proxy_async_smem();
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[grp]);
-    }
-    const int half = grp;  // epilogue: group g writes d columns [32 g, 32 g + 32)
-    if (ok && n_steps > 0) ok = mbar_wait_warp(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
-    tc_fence_after();
-    // TMEM loads are warp-collective: every lane executes them; only stores are predicated.
-    const bool row_ok = key < p.T;
-    const long long row_off = b * p.dk_sb + static_cast<long long>(row_ok ? key : 0) * p.dk_ss + hk * p.dk_sh;
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      __nv_bfloat16* dst = (which == 0 ? static_cast<__nv_bfloat16*>(p.dv) : static_cast<__nv_bfloat16*>(p.dk)) + row_off;
-      const uint32_t src = (which == 0 ? tdV : tdK) + lane_off;
-      const float f = which == 0 ? 1.f : p.scale;
-      const int c = half * 32;
-      uint32_t v[32];
-      if (ok && n_steps > 0) {
-        tmem_ld_32x32b_x32(src + c, v);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int t = 0; t < 32; ++t) v[t] = 0u;
-      }
-      if (row_ok) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) pk[t] = pack_bf16x2(__uint_as_float(v[2 * t]) * f, __uint_as_float(v[2 * t + 1]) * f);
-        uint4* o4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) o4[t] = make_uint4(pk[4 * t], pk[4 * t + 1], pk[4 * t + 2], pk[4 * t + 3]);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) {
-    __syncwarp();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // dq[b, s, h, :] = bf16(scale * dq_acc[b, h, s, :]), 8 elements per thread.
 __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int B, int S,
                                        int H, int D, long long dq_sb, long long dq_ss, float scale) {
@@ -992,7 +615,7 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   const bool fused = D == 64 && dq_acc != nullptr;
   {
     const long long rows = static_cast<long long>(p.B) * p.S * p.H;
-    // The fused kernel reads delta and -lse * log2(e) in 64-row bulk copies, so their rows are
+    // The fused kernel reads delta and -lse * log2(e) in 128-row bulk copies, so their rows are
     // padded to a multiple of 4 floats (16 bytes); delta holds 2 * (B * H * vec_s + 128) floats,
     // zeroed when padding rows exist so that the padded queries read finite values.
     p.vec_s = fused ? (p.S + 3) / 4 * 4 : p.S;
@@ -1017,9 +640,8 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
     const long long n_acc = static_cast<long long>(p.B) * p.H * p.S * D;
     cudaMemsetAsync(dq_acc, 0, n_acc * sizeof(float), stream);
     CUtensorMap mdq;
-    make_tmap_2d_f32(&mdq, dq_acc, D, static_cast<long long>(p.B) * p.H * p.S, D, 32, kLT);
-    set_smem(attn_bwd_fused_kernel, FusedSmem::kBytes);
-    attn_bwd_fused_kernel<<<grid_kv, 384, FusedSmem::kBytes, stream>>>(mq64, mk128, mv128, mdo64, mdq, p);
+    make_tmap_2d_f32_sw64(&mdq, dq_acc, D, static_cast<long long>(p.B) * p.H * p.S, D, 16, 32);
+    attn_bwd_d64_launch(mq128, mk128, mv128, mdo128, mdq, p, grid_kv, stream);
     const long long n8 = n_acc / 8;
     const int blocks = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));
     attn_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc, static_cast<__nv_bfloat16*>(p.dq), p.B, p.S, p.H, D,

@@ -104,6 +104,11 @@ inline void set_smem(K kern, int bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Fused backward for head dim 64 (attention_bwd_d64.cu): Q / dO / K / V maps with 128-row
+// boxes, dQ accumulator map [B*H*S, 64] fp32 with 16 x 32 boxes and 64-byte swizzle.
+void attn_bwd_d64_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                         const CUtensorMap& mdq, const AttnParams& p, int grid, cudaStream_t stream);
+
 
 }  // namespace attn
 }  // namespace pb
