@@ -640,7 +640,7 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
     const long long n_acc = static_cast<long long>(p.B) * p.H * p.S * D;
     cudaMemsetAsync(dq_acc, 0, n_acc * sizeof(float), stream);
     CUtensorMap mdq;
-    make_tmap_2d_f32_sw64(&mdq, dq_acc, D, static_cast<long long>(p.B) * p.H * p.S, D, 16, 32);
+    make_tmap_2d_f32_sw128(&mdq, dq_acc, D, static_cast<long long>(p.B) * p.H * p.S, D, 32, 32);
     attn_bwd_d64_launch(mq128, mk128, mv128, mdo128, mdq, p, grid_kv, stream);
     const long long n8 = n_acc / 8;
     const int blocks = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));

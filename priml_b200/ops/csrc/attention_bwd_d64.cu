@@ -21,10 +21,13 @@
 //
 // TMEM columns: S^T [0,128) dP^T [128,256) dV [256,320) dK [320,384)
 //               dQ [384,448) K [448,480) V [480,512) (K, V as bf16 pairs).
-// Warps: 0 TMA producer, 1 MMA issuer, 2-17 softmax. Softmax warp w covers TMEM
-// lane quarter (w & 3) -- 32 keys -- and query quarter (w - 2) >> 2 -- 32 queries
-// -- of a step; sixteen warps keep enough work in flight to hide the latency of
-// the TMEM loads, the exponentials and the shared-memory stores.
+// Warps: 0 TMA producer, 1 MMA issuer, 2-17 softmax, 18-21 dQ flush.
+//   Softmax warp w covers TMEM lane quarter (w & 3) -- 32 keys -- and query quarter
+//   (w - 2) >> 2 -- 32 queries -- of a step: sixteen warps keep enough work in flight
+//   to hide the latency of the TMEM loads, the exponentials and the shared-memory
+//   stores; the score arithmetic runs on packed fp32 pairs (f32x2).
+//   dQ warp w moves the 32 query rows of lane quarter (w & 3) out of TMEM, so that
+//   work never sits on the softmax warps' path.
 #include "attention_common.cuh"
 
 namespace pb {
@@ -34,13 +37,14 @@ namespace {
 using namespace attn;
 
 constexpr int kSoftmaxWarps = 16;
-constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
+constexpr int kDqWarps = 4;
+constexpr int kThreads = 32 * (2 + kSoftmaxWarps + kDqWarps);
 
 struct BwdD64Smem {
   static constexpr int kStages = 3;
   static constexpr int kTileBytes = kChunkBytes;           // [128 rows][64 bf16], 128B-swizzled
   static constexpr int kPairBytes = 2 * kChunkBytes;       // [128 keys][128 queries] as two 64-query chunks
-  static constexpr int kDQWarpBytes = 32 * 64;             // [32 queries][16 fp32], 64B-swizzled
+  static constexpr int kDQWarpBytes = 2 * 32 * 128;        // [32 queries][64 fp32] as two 128B-swizzled boxes
   static constexpr int kVecBytes = 2 * kTile * 4;          // -lse*log2e and delta of 128 queries
   static constexpr int kOffK = 0;
   static constexpr int kOffQ = kOffK + kTileBytes;
@@ -48,20 +52,10 @@ struct BwdD64Smem {
   static constexpr int kOffPT = kOffDO + kStages * kTileBytes;  // also stages V before it moves to TMEM
   static constexpr int kOffDST = kOffPT + kPairBytes;
   static constexpr int kOffDQ = kOffDST + kPairBytes;
-  static constexpr int kOffVec = kOffDQ + kSoftmaxWarps * kDQWarpBytes;
+  static constexpr int kOffVec = kOffDQ + kDqWarps * kDQWarpBytes;
   static constexpr int kOffBars = kOffVec + kStages * kVecBytes;
   static constexpr int kBytes = kOffBars + 256 + 1024;
 };
-
-// P^T and dS^T of 32 key rows x 32 queries (4 packed columns per 16-byte piece) into the
-// 128B-swizzled [128 keys][64 queries] chunk that holds them.
-__device__ __forceinline__ void store_pair_rows(uint8_t* chunk_base, int kr, int piece0, const uint32_t (&v)[16]) {
-  uint8_t* row = chunk_base + kr * 128;
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    *reinterpret_cast<uint4*>(row + (((piece0 + j) ^ (kr & 7)) << 4)) =
-        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_d64_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -124,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(ds_ready, kSoftmaxWarps);
     mbar_init(ds_free, 1);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, kSoftmaxWarps);
+    mbar_init(dq_free, kDqWarps);
     mbar_init(acc_final, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -228,15 +222,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     umma_commit(acc_final);
     umma_commit(drain);
     mbar_wait(drain, 0, p.status, kTimeoutDrain, nullptr);
+  } else if (warp >= 2 + kSoftmaxWarps) {
+    // ------------------------------------------------------------------ dQ flush
+    // Query rows 32 quarter .. of dQ_j, all 64 columns: TMEM -> two 128B-swizzled staging boxes
+    // [32 rows][32 fp32] -> bulk tensor reduce-add (fp32, in L2) into dq_acc.
+    const int quarter = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t* stage = sDQ + (warp - 2 - kSoftmaxWarps) * SM::kDQWarpBytes;
+    int h = hk * g, qt = qt_lo;  // (query head, query tile) of step j, advanced without divisions
+    bool ok = true;
+    for (int j = 0; j < n_steps && ok; ++j) {
+      if (!mbar_wait_warp(dq_full, j & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) tma_store_wait_read();  // the previous reduces no longer read the staging rows
+      __syncwarp();
+#pragma unroll
+      for (int box = 0; box < 2; ++box) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tdQ + lane_off + 32 * box, v);
+        tmem_wait_ld();
+        if (box == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dq_free);
+        }
+        uint8_t* row = stage + box * (32 * 128) + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(row + ((c ^ (lane & 7)) << 4)) =
+              make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int y = static_cast<int>((static_cast<long long>(b) * p.H + h) * p.S + qt * kTile + quarter * 32);
+        tma_reduce_add_2d(&tmDQ, stage, 0, y);
+        tma_reduce_add_2d(&tmDQ, stage + 32 * 128, 32, y);
+        tma_store_commit();
+      }
+      if (++qt > qt_hi) {
+        qt = qt_lo;
+        ++h;
+      }
+    }
+    if (lane == 0) tma_store_wait_all();
   } else if (warp >= 2) {
-    // ------------------------------------------------------------------ softmax, dQ, final epilogue
-    const int quarter = warp & 3;          // TMEM lanes: keys (S^T, dP^T, dK, dV) or queries (dQ)
-    const int part = (warp - 2) >> 2;      // 32-query slice of a step; 16-column slice of dQ
+    // ------------------------------------------------------------------ softmax, final epilogue
+    const int quarter = warp & 3;          // TMEM lanes: keys of S^T, dP^T, dK, dV
+    const int part = (warp - 2) >> 2;      // 32-query slice of a step
     const int kr = quarter * 32 + lane;    // key row of this thread
     const int key = k0 + kr;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const float sl2 = p.scale_log2;
-    uint8_t* dq_stage = sDQ + (warp - 2) * SM::kDQWarpBytes;
+    const uint64_t sl2x2 = f2_pack(p.scale_log2, p.scale_log2);
     bool ok = mbar_wait_warp(kv_full, 0, p.status, kTimeoutEpilogue, abort_flag);
     if (ok && part < 2) {
       // Key row kr of K (part 0) or V (part 1) into TMEM: eight swizzled 16-byte chunks -> 32 columns.
@@ -257,108 +294,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(kv_tmem);
 
-    // dQ of step j, columns [16 part, 16 part + 16) of query rows 32 quarter ..: TMEM ->
-    // 64B-swizzled staging -> L2 reduce-add.
-    auto flush_dq = [&](int j) -> bool {
-      if (!mbar_wait_warp(dq_full, j & 1, p.status, kTimeoutEpilogue, abort_flag)) return false;
-      tc_fence_after();
-      uint32_t v[16];
-      tmem_ld_32x32b_x16(tdQ + lane_off + part * 16, v);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(dq_free);
-        tma_store_wait_read();  // the previous reduce no longer reads the staging rows
-      }
-      __syncwarp();
-      uint8_t* row = dq_stage + lane * 64;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
-            make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        const int h = hk * g + j / nq;
-        const int q0 = (qt_lo + j % nq) * kTile;
-        tma_reduce_add_2d(&tmDQ, dq_stage, part * 16,
-                          static_cast<int>((static_cast<long long>(b) * p.H + h) * p.S + q0 + quarter * 32));
-        tma_store_commit();
-      }
-      return true;
-    };
-
-    uint8_t* pt_chunk = sPT + (part >> 1) * kChunkBytes;
-    uint8_t* dst_chunk = sDST + (part >> 1) * kChunkBytes;
-    const int piece0 = (part & 1) * 4;
+    uint8_t* prow = sPT + (part >> 1) * kChunkBytes + kr * 128;
+    uint8_t* drow = sDST + (part >> 1) * kChunkBytes + kr * 128;
+    const int piece0 = (part & 1) * 4;  // this warp's four 16-byte pieces of the 128-byte row
+    int qt = qt_lo;                     // query tile of step i, advanced without divisions
     for (int i = 0; i < n_steps && ok; ++i) {
       const int st = i % NS;
-      const int q0 = (qt_lo + i % nq) * kTile;
+      const int qa = qt * kTile + part * 32;  // first query of this warp's 32 columns
+      if (++qt > qt_hi) qt = qt_lo;
       if (!mbar_wait_warp(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       if (!mbar_wait_warp(s_full, i & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sv[32], dv[32];
-      tmem_ld_32x32b_x32(tS + lane_off + part * 32, sv);
-      tmem_ld_32x32b_x32(tP + lane_off + part * 32, dv);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(st_free);  // the MMA warp may now write the next step's scores
-
-      const float4* nl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kTile + part * 32);
-      const float4* dl4 = reinterpret_cast<const float4*>(sVec + st * 2 * kTile + kTile + part * 32);
-      const int qa = q0 + part * 32;  // first query of these 32 columns
+      const ulonglong2* nl2 = reinterpret_cast<const ulonglong2*>(sVec + st * 2 * kTile + part * 32);
+      const ulonglong2* dl2 = reinterpret_cast<const ulonglong2*>(sVec + st * 2 * kTile + kTile + part * 32);
       const bool need_mask = (p.causal && k0 + kTile - 1 > off + qa) || (k0 + kTile > p.T) || (qa + 32 > p.S) ||
                              (p.window >= 0 && k0 < off + qa + 31 - p.window);
       uint32_t pk[16], dk[16];
-      if (!need_mask) {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float4 nl = nl4[t], dl = dl4[t];
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[4 * t]), sl2, nl.x));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[4 * t + 1]), sl2, nl.y));
-          const float p2 = fast_exp2(fmaf(__uint_as_float(sv[4 * t + 2]), sl2, nl.z));
-          const float p3 = fast_exp2(fmaf(__uint_as_float(sv[4 * t + 3]), sl2, nl.w));
-          pk[2 * t] = pack_bf16x2(p0, p1);
-          pk[2 * t + 1] = pack_bf16x2(p2, p3);
-          dk[2 * t] = pack_bf16x2(p0 * (__uint_as_float(dv[4 * t]) - dl.x), p1 * (__uint_as_float(dv[4 * t + 1]) - dl.y));
-          dk[2 * t + 1] =
-              pack_bf16x2(p2 * (__uint_as_float(dv[4 * t + 2]) - dl.z), p3 * (__uint_as_float(dv[4 * t + 3]) - dl.w));
+      for (int pass = 0; pass < 2; ++pass) {  // two 16-column passes keep the register footprint small
+        uint32_t sv[16], dv[16];
+        tmem_ld_32x32b_x16(tS + lane_off + part * 32 + pass * 16, sv);
+        tmem_ld_32x32b_x16(tP + lane_off + part * 32 + pass * 16, dv);
+        tmem_wait_ld();
+        if (pass == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(st_free);  // the MMA warp may now write the next step's scores
         }
-      } else {
-        // Diagonal, ragged or windowed tile: invisible entries become exact zeros (they may
-        // read padding rows of the per-query vectors).
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float4 nl = nl4[t], dl = dl4[t];
-          const float nls[4] = {nl.x, nl.y, nl.z, nl.w};
-          const float dls[4] = {dl.x, dl.y, dl.z, dl.w};
-          float pr[4], ds[4];
+        for (int t = 0; t < 4; ++t) {
+          const ulonglong2 nl = nl2[pass * 4 + t], dl = dl2[pass * 4 + t];
+          const uint64_t nls[2] = {nl.x, nl.y}, dls[2] = {dl.x, dl.y};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const bool vis = visible(p, qa + 4 * t + e, key);
-            const float pv = fast_exp2(fmaf(__uint_as_float(sv[4 * t + e]), sl2, nls[e]));
-            pr[e] = vis ? pv : 0.f;
-            ds[e] = vis ? pv * (__uint_as_float(dv[4 * t + e]) - dls[e]) : 0.f;
+          for (int e = 0; e < 2; ++e) {
+            const int col = 4 * t + 2 * e;           // within this pass
+            const int qc = pass * 16 + col;          // within the warp's 32 queries
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[col]), __uint_as_float(sv[col + 1])), sl2x2, nls[e]), x0, x1);
+            const uint64_t pr = f2_pack(fast_exp2(x0), fast_exp2(x1));
+            const uint64_t d2 = f2_pack(__uint_as_float(dv[col]), __uint_as_float(dv[col + 1]));
+            float p0, p1, g0, g1;
+            f2_unpack(pr, p0, p1);
+            f2_unpack(f2_mul(pr, f2_sub(d2, dls[e])), g0, g1);
+            if (need_mask) {
+              // diagonal, ragged or windowed tile: invisible entries are exact zeros (they may
+              // read padding rows of the per-query vectors)
+              const bool v0 = visible(p, qa + qc, key), v1 = visible(p, qa + qc + 1, key);
+              p0 = v0 ? p0 : 0.f;
+              g0 = v0 ? g0 : 0.f;
+              p1 = v1 ? p1 : 0.f;
+              g1 = v1 ? g1 : 0.f;
+            }
+            pk[qc >> 1] = pack_bf16x2(p0, p1);
+            dk[qc >> 1] = pack_bf16x2(g0, g1);
           }
-          pk[2 * t] = pack_bf16x2(pr[0], pr[1]);
-          pk[2 * t + 1] = pack_bf16x2(pr[2], pr[3]);
-          dk[2 * t] = pack_bf16x2(ds[0], ds[1]);
-          dk[2 * t + 1] = pack_bf16x2(ds[2], ds[3]);
         }
       }
       // B(i-1) has finished reading the previous P^T / dS^T.
       if (i > 0 && !mbar_wait_warp(ds_free, (i - 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      store_pair_rows(pt_chunk, kr, piece0, pk);
-      store_pair_rows(dst_chunk, kr, piece0, dk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int pos = ((piece0 + j) ^ (kr & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + pos) = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        *reinterpret_cast<uint4*>(drow + pos) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
-      if (i > 0 && !(ok = flush_dq(i - 1))) break;
     }
-    if (ok && n_steps > 0) ok = flush_dq(n_steps - 1);
-    if (lane == 0) tma_store_wait_all();
 
     // dV (parts 0, 1) and dK scaled by the softmax scale (parts 2, 3): TMEM lanes = keys.
     if (ok && n_steps > 0) ok = mbar_wait_warp(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);

@@ -93,6 +93,45 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return true;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is incomplete
+// (it returns as soon as the phase completes): waiting warps stop issuing instructions.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait like mbar_wait, for waits that are usually long (a role waiting for another
+// role's whole phase of work): the thread sleeps between polls instead of spinning.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                volatile int* abort, uint32_t hint_ns = 20000) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait_hint(bar, parity, hint_ns)) {
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      record_error(status, code);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                     volatile int* abort) {
+  const bool ok = mbar_wait_sleep(bar, parity, status, code, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // The same wait for a whole warp that next issues warp-collective (.sync.aligned) instructions
 // such as tcgen05.ld / tcgen05.st: the lanes can disagree after a timeout (one lane's wait
 // expires just as another's completes), so the warp goes on only if every lane saw the phase,

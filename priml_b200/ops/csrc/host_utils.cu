@@ -99,13 +99,6 @@ void make_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, long long inner,
             CU_TENSOR_MAP_SWIZZLE_128B, "2d f32 sw128");
 }
 
-void make_tmap_2d_f32_sw64(CUtensorMap* map, const void* base, long long inner, long long outer,
-                           long long row_stride, int box_inner, int box_outer) {
-  if (box_inner * 4 != 64) throw std::runtime_error("64-byte swizzle needs a 64-byte box row");
-  encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, inner, outer, row_stride, box_inner, box_outer,
-            CU_TENSOR_MAP_SWIZZLE_64B, "2d f32 sw64");
-}
-
 void make_tmap_2d_u8(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
                      int box_inner, int box_outer) {
   ensure_context();

@@ -21,8 +21,6 @@ void make_tmap_2d_bf16_sw64(CUtensorMap* map, const void* base, long long inner,
                             long long row_stride, int box_inner, int box_outer);
 void make_tmap_2d_f32_sw128(CUtensorMap* map, const void* base, long long inner, long long outer,
                             long long row_stride, int box_inner, int box_outer);
-void make_tmap_2d_f32_sw64(CUtensorMap* map, const void* base, long long inner, long long outer,
-                            long long row_stride, int box_inner, int box_outer);
 // 3-D bf16 tensor map (inner, mid, outer) with element strides for mid/outer.
 // 2-D fp32 map without swizzle (bulk reduce targets).
 void make_tmap_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
