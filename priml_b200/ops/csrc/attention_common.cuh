@@ -129,6 +129,10 @@ inline void set_smem(K kern, int bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Forward with two query tiles per CTA (attention_fwd3.cu): Q / K / V maps with 128-row boxes.
+void attn_fwd3_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p,
+                      int D, cudaStream_t stream);
+
 // Fused backward for head dim 64 (attention_bwd_d64.cu): Q / dO / K / V maps with 128-row
 // boxes, dQ accumulator map [B*H*S, 64] fp32 with 32 x 32 boxes and 128-byte swizzle.
 void attn_bwd_d64_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,

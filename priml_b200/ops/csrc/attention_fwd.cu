@@ -311,6 +311,13 @@ void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.status = status;
   CUtensorMap mq, mk, mv;
   make_bshd_map(&mq, q, H, D, kTile);
+  if (trace == nullptr) {
+    const int kt = D == 64 ? kKT : kTile;  // keys per tile of the two-tile kernel
+    make_bshd_map(&mk, k, Hkv, D, kt);
+    make_bshd_map(&mv, v, Hkv, D, kt);
+    attn_fwd3_launch(mq, mk, mv, p, D, stream);
+    return;
+  }
   make_bshd_map(&mk, k, Hkv, D, kKT);
   make_bshd_map(&mv, v, Hkv, D, kKT);
   const int grid = ((p.S + kTile - 1) / kTile) * p.B * p.H;
