@@ -87,35 +87,8 @@ def _layout(strategy: str, world: int, tp: int) -> str:
     return f"fsdp{world}"
 
 
-_REF_ROOT = Path(__file__).resolve().parent / "baseline" / "_ref"
-
-
 def _reference_unavailable(why: str) -> None:
     print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
-
-
-def _install_configgle_standin() -> None:
-    """Register a pure-Python ``configgle`` for the reference's imports, in this process only.
-
-    The reference's config trees import ``configgle`` (``priml/model/causal_lm.py:38``,
-    ``priml/train/train_step.py``), a git-only dependency that cannot be installed offline.
-    ``priml_b200.config`` implements the same public surface (``Fig``, ``Makeable``, ``Makes``,
-    ``PartialConfig``, ``InlineConfig``, ``MutableNamespace``, ``copy_tree``, ``apply_overrides``,
-    ``resolve_config``) in plain Python and imports no kernel code, so registering it under that
-    name leaves every model, optimizer and strategy of the reference run its own code.
-    """
-    import types
-
-    import priml_b200.config as standin
-
-    root = types.ModuleType("configgle")
-    root.__dict__.update({name: getattr(standin, name) for name in standin.__all__})
-    walk = types.ModuleType("configgle.walk")
-    walk.copy_tree = standin.copy_tree  # type: ignore[attr-defined]
-    launch = types.ModuleType("configgle.launch")
-    launch.resolve_config = standin.resolve_config  # type: ignore[attr-defined]
-    root.walk, root.launch = walk, launch  # type: ignore[attr-defined]
-    sys.modules.update({"configgle": root, "configgle.walk": walk, "configgle.launch": launch})
 
 
 def _reference_model(args: argparse.Namespace) -> tuple[Any, str, Any]:
@@ -164,16 +137,18 @@ def _run_reference(args: argparse.Namespace) -> None:
     cross-entropy (``priml/baselines/nanochat/train_step.py:43-79``), gradient clipping, and for N > 1
     ``priml.runtime.MultiProcess`` + ``priml.train.parallelism.FullySharded`` (FSDP2 over NCCL,
     bf16 params, fp32 reduce; ``priml/train/parallelism.py:146-202``). Nothing of this package's
-    models, kernels or strategies is imported; only the config stand-in above.
+    models, kernels or strategies is imported; only the config stand-in of
+    ``priml_b200.testing.reference``.
     """
-    if not (_REF_ROOT / "priml" / "__init__.py").exists():
-        _reference_unavailable(f"the reference is not present under {_REF_ROOT.name}")
+    from priml_b200.testing.reference import load_reference, reference_available
+
+    if not reference_available():
+        _reference_unavailable("the reference package is not present under baseline/_ref")
         return
     if args.config != "llama1b":
         _reference_unavailable(f"the reference arm runs the llama1b workload only, not {args.config}")
         return
-    sys.path.insert(0, str(_REF_ROOT))
-    _install_configgle_standin()
+    load_reference()  # the reference's own code, with a pure-Python configgle stand-in
 
     import torch
     import torch.distributed as dist

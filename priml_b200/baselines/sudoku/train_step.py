@@ -91,7 +91,9 @@ class SudokuTrainStep(TrainStep):
                 self.act.seq_len = self.model.total_seq_len
                 self.act.hidden_size = self.model.hidden_size
             if self.use_ema:
-                self.ema = EMA.Config(decay=self.ema_decay, warmup_steps=self.ema_warmup_steps)
+                # a name-keyed param-dict shadow, seeded from the live weights when averaging starts
+                self.ema = EMA.Config(decay=self.ema_decay, update_after_step=self.ema_warmup_steps,
+                                      shadow_kind="param_dict", warmup_seed=True, track_buffers=False)  # fmt: skip
             else:
                 self.ema = NoEMA.Config()
             return super().finalize()
@@ -126,7 +128,7 @@ class SudokuTrainStep(TrainStep):
 
     @property
     def ema_shadow(self) -> dict[str, Tensor] | None:
-        return self.ema.shadow if isinstance(self.ema, EMA) else None
+        return self.ema.shadow_params if isinstance(self.ema, EMA) else None
 
     # ------------------------------------------------------------------ train
     def train_step(self, **batch: Any) -> TrainStepOutput:

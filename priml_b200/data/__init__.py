@@ -9,6 +9,7 @@ from typing import Any, Protocol
 import torch
 from torch import Tensor
 
+from priml_b200.timer import CheckpointableStepTimer
 from priml_b200.config import Fig
 
 __all__ = ["DatasetProtocol", "DummyDataset", "SyntheticTokens"]
@@ -22,17 +23,6 @@ class DatasetProtocol(Protocol):
     def state_dict(self) -> dict[str, Any]: ...
 
     def load_state_dict(self, state_dict: dict[str, Any]) -> None: ...
-
-
-class _EpochCounter:
-    def __init__(self) -> None:
-        self.epoch = 0
-
-    def state_dict(self) -> dict[str, Any]:
-        return {"epoch": self.epoch}
-
-    def load_state_dict(self, s: dict[str, Any]) -> None:
-        self.epoch = int(s.get("epoch", 0))
 
 
 class DummyDataset:
@@ -52,7 +42,7 @@ class DummyDataset:
         g = torch.Generator().manual_seed(config.seed)
         self.media = torch.randn((config.num_samples, *config.input_shape), generator=g)
         self.label = torch.randint(0, config.num_classes, (config.num_samples,), generator=g)
-        self.timer_epoch = _EpochCounter()
+        self.timer_epoch = CheckpointableStepTimer()
 
     def _batches(self) -> Iterator[dict[str, Tensor]]:
         b = self.config.batch_size
@@ -70,7 +60,8 @@ class DummyDataset:
         return {"timer_epoch": self.timer_epoch.state_dict()}
 
     def load_state_dict(self, s: dict[str, Any]) -> None:
-        self.timer_epoch.load_state_dict(s.get("timer_epoch", {}))
+        if "timer_epoch" in s:
+            self.timer_epoch.load_state_dict(s["timer_epoch"])
 
 
 class SyntheticTokens:
@@ -89,7 +80,7 @@ class SyntheticTokens:
 
     def __init__(self, config: Config) -> None:
         self.config = config
-        self.timer_epoch = _EpochCounter()
+        self.timer_epoch = CheckpointableStepTimer()
         self._step = 0
 
     def _make(self, index: int) -> dict[str, Tensor]:
@@ -106,7 +97,6 @@ class SyntheticTokens:
             for _ in range(self.config.steps_per_epoch):
                 yield self._make(self._step)
                 self._step += 1
-            self.timer_epoch.epoch += 1
             return
 
     def eval_dataloader(self) -> Iterator[dict[str, Tensor]]:
@@ -118,5 +108,6 @@ class SyntheticTokens:
 
     def load_state_dict(self, s: dict[str, Any]) -> None:
         self._step = int(s.get("step", 0))
-        self.timer_epoch.load_state_dict(s.get("timer_epoch", {}))
+        if "timer_epoch" in s:
+            self.timer_epoch.load_state_dict(s["timer_epoch"])
 from priml_b200.data import augmentation_gpu, environment  # noqa: E402, F401

@@ -40,5 +40,8 @@ class CheckpointableStepTimer:
         return {"global_count": self.global_count, "global_sec": self.global_sec}
 
     def load_state_dict(self, state: dict[str, Any]) -> None:
+        """Restore the checkpointed totals; this process's own counts start again at zero."""
         self.global_count = int(state.get("global_count", 0))
         self.global_sec = float(state.get("global_sec", 0.0))
+        self.local_count = 0
+        self.local_sec = 0.0

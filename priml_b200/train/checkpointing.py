@@ -104,7 +104,7 @@ class SyncLocalStateDictStorer:
             dcp.load(into, checkpoint_id=str(path))
             return into
         dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
-        state = torch.load(path, map_location=dev, weights_only=False)
+        state = torch.load(path, map_location=dev, weights_only=True)
         if "rng" in state:
             state["rng"] = _to_cpu(state["rng"])
         return state

@@ -146,8 +146,6 @@ class TrainLoop:
             "dataset": self.dataset.state_dict() if hasattr(self.dataset, "state_dict") else {},
             "metrics": {k: m.state_dict() for k, m in self.metrics.items() if hasattr(m, "state_dict")},
             "rng": get_rng_state(),
-            "global_step": self.global_step,
-            "epoch": self.epoch,
         }
 
     def load_state_dict(self, s: dict[str, Any]) -> None:
@@ -159,8 +157,11 @@ class TrainLoop:
                 m.load_state_dict(s["metrics"][k])
         if self.config.restore_rng_state and "rng" in s:
             set_rng_state(s["rng"])
-        self.global_step = int(s.get("global_step", self.step.timer_step.global_count))
-        self.epoch = int(s.get("epoch", 0))
+        # Progress is not stored twice: optimizer steps ride the step's timer and completed
+        # passes the dataset's epoch timer, as in the reference's checkpoints.
+        self.global_step = int(getattr(self.step, "global_step", self.step.timer_step.global_count))
+        epochs = getattr(self.dataset, "timer_epoch", None)
+        self.epoch = int(epochs.global_count) if epochs is not None else 0
 
     # ------------------------------------------------------------------ helpers
     def _time_limit_reached(self) -> bool:
@@ -269,6 +270,10 @@ class TrainLoop:
                 self._on_batch_ready(time.perf_counter() - fetch_t0)
             except StopIteration:
                 self.epoch += 1
+                passes = getattr(self.dataset, "timer_epoch", None)
+                if passes is not None:  # the dataset checkpoints its pass count
+                    passes.global_count += 1
+                    passes.local_count += 1
                 self.step.on_epoch_end()
                 if c.eval_every_epoch and self.metrics:
                     self.eval()

@@ -22,8 +22,7 @@ from __future__ import annotations
 
 import contextlib
 import math
-import time
-from collections.abc import Callable
+from collections.abc import Callable, Mapping
 from dataclasses import field
 from typing import Any, Literal
 
@@ -31,6 +30,8 @@ import torch
 import torch.distributed as dist
 from torch import Tensor, nn
 
+from priml_b200.timer import CheckpointableStepTimer
+from priml_b200.train.ema import NoEMA
 from priml_b200.config import Fig, PartialConfig
 from priml_b200.loss import SimpleLoss, TokenCrossEntropy
 from priml_b200.math.schedules import constant
@@ -54,39 +55,6 @@ class _NoQuant:
         return model
 
 
-class _StepTimer:
-    """Global / local count and seconds (``priml/timer.py:24-105`` state keys)."""
-
-    def __init__(self) -> None:
-        self.global_count = 0
-        self.global_sec = 0.0
-        self.local_count = 0
-        self.local_sec = 0.0
-        self._t0: float | None = None
-
-    def __enter__(self) -> _StepTimer:
-        if self._t0 is not None:
-            raise RuntimeError("timer is not re-entrant")
-        self._t0 = time.perf_counter()
-        return self
-
-    def __exit__(self, *exc: Any) -> None:
-        assert self._t0 is not None
-        dt = time.perf_counter() - self._t0
-        self._t0 = None
-        self.global_count += 1
-        self.local_count += 1
-        self.global_sec += dt
-        self.local_sec += dt
-
-    def state_dict(self) -> dict[str, Any]:
-        return {"global_count": self.global_count, "global_sec": self.global_sec}
-
-    def load_state_dict(self, s: dict[str, Any]) -> None:
-        self.global_count = int(s.get("global_count", 0))
-        self.global_sec = float(s.get("global_sec", 0.0))
-
-
 class TrainStep:
     class Config(Fig["TrainStep"], kw_only=False):
         model: Any = field(default_factory=Identity.Config)
@@ -105,7 +73,7 @@ class TrainStep:
         model_quantization: Any = field(default_factory=_NoQuant.Config)
         activation_memoization: Any = None
         compile: Any = None
-        ema: Any = None
+        ema: Any = field(default_factory=lambda: NoEMA.Config())
         gradient_clip_norm: float = math.inf
         device_init: Literal["meta", "eager"] = "eager"
         dtype_autocast: torch.dtype | None = None
@@ -113,7 +81,6 @@ class TrainStep:
 
     def __init__(self, config: Config) -> None:
         from priml_b200.parallel.strategies import NoParallel
-        from priml_b200.train.ema import NoEMA
 
         self.config = config
         ctx = torch.device("meta") if config.device_init == "meta" else contextlib.nullcontext()
@@ -134,14 +101,14 @@ class TrainStep:
         for g in self.optimizer.param_groups:
             g.setdefault("initial_lr", g["lr"])
         self.schedule: Callable[[float], float] = config.learning_rate_scheduler.make()
-        self.ema = config.ema.make()(model) if config.ema is not None else NoEMA()
+        self.ema = config.ema.make() if config.ema is not None else NoEMA()
         self.loss_fn = config.loss.make()
         self._compiled: Callable[..., Any] | None = None
         self.accumulation_steps = 0
         self.accumulated_samples = 0
-        self.timer_forward = _StepTimer()
-        self.timer_eval = _StepTimer()
-        self.timer_step = _StepTimer()
+        self.timer_forward = CheckpointableStepTimer()
+        self.timer_eval = CheckpointableStepTimer()
+        self.timer_step = CheckpointableStepTimer()
         self.epoch = 0.0
         self.epoch_timer: Any = None
         self.last_loss: Tensor | None = None
@@ -351,12 +318,31 @@ class TrainStep:
             "accumulated_samples": self.accumulated_samples,
         }
 
-    def load_state_dict(self, s: dict[str, Any]) -> None:
-        self.model.load_state_dict(s["model"])
-        self.optimizer.load_state_dict(s["optimizer"])
-        self.timer_forward.load_state_dict(s.get("timer_forward", {}))
-        self.timer_eval.load_state_dict(s.get("timer_eval", {}))
-        self.timer_step.load_state_dict(s.get("timer_step", {}))
-        self.ema.load_state_dict(s.get("ema", {}))
-        self.accumulation_steps = int(s.get("accumulation_steps", 0))
-        self.accumulated_samples = int(s.get("accumulated_samples", 0))
+    def load_state_dict(
+        self,
+        state_dict: dict[str, Any],
+        *,
+        strict: bool = True,
+        load_optimizer: bool = True,
+        remap: Callable[[Mapping[str, Any]], Mapping[str, Any]] | None = None,
+    ) -> None:
+        """Resume from a checkpoint (``priml/train/train_step.py:704-752`` semantics).
+
+        ``remap`` rewrites the saved model keys first; ``strict`` requires an exact key match;
+        ``load_optimizer=False`` keeps the fresh optimizer and EMA (fine-tuning a changed
+        model). Timers absent from the checkpoint stay at zero. A pending gradient
+        accumulation is not resumable, so the accumulation counters restart at zero.
+        """
+        model_state = state_dict["model"]
+        if remap is not None:
+            model_state = remap(model_state)
+        self.model.load_state_dict(model_state, strict=strict)
+        for name in ("timer_forward", "timer_eval", "timer_step"):
+            if name in state_dict:
+                getattr(self, name).load_state_dict(state_dict[name])
+        self.accumulation_steps = 0
+        self.accumulated_samples = 0
+        if load_optimizer:
+            self.optimizer.load_state_dict(state_dict["optimizer"])
+            if "ema" in state_dict:
+                self.ema.load_state_dict(state_dict["ema"])

@@ -170,11 +170,46 @@ def test_corrupt_latest_checkpoint_falls_back(tmp_path) -> None:  # noqa: ANN001
 
 
 def test_ema_param_dict_tracks_weights() -> None:
+    """The reference's update rule: the shadow is taken at the first call, averaged from then on."""
     m = torch.nn.Linear(3, 3)
-    ema = EMA.Config(decay=0.5).make()(m)
+    ema = EMA.Config(decay=0.5, shadow_kind="param_dict").make()
+    ema(m)  # shadow = current weights (averaging them with themselves)
+    start = m.weight.detach().clone()
     with torch.no_grad():
         m.weight.add_(1.0)
     ema(m)
     with ema.apply_to(m):
         inside = m.weight.detach().clone()
-    assert not torch.equal(inside, m.weight.detach())
+    torch.testing.assert_close(inside, start + 0.5)
+    torch.testing.assert_close(m.weight.detach(), start + 1.0)  # live weights come back
+    state = ema.state_dict()
+    assert set(state) == {"shadow_params", "shadow_buffers", "global_step", "local_step"}
+    assert state["global_step"] == 2 and state["local_step"] == 2
+
+
+def test_ema_warmup_seed_and_karras_schedule() -> None:
+    from priml_b200.train.ema import karras_decay
+
+    m = torch.nn.Linear(2, 2)
+    ema = EMA.Config(decay=0.999, update_after_step=2, warmup_seed=True, decay_schedule=karras_decay).make()
+    for i in range(2):
+        with torch.no_grad():
+            m.weight.fill_(float(i))
+        ema(m)  # warmup calls only count
+    assert ema.local_step == 0 and ema.global_step == 2
+    with torch.no_grad():
+        m.weight.fill_(10.0)
+    ema(m)  # boundary: seeded from the live weights
+    with torch.no_grad():
+        m.weight.fill_(20.0)
+    ema(m)  # first average: decay min(0.999, 2 / 11)
+    d = 2 / 11
+    with ema.apply_to(m):
+        torch.testing.assert_close(m.weight.detach(), torch.full((2, 2), d * 10.0 + (1 - d) * 20.0))
+    # module shadows checkpoint as a state dict and load before the first call
+    mod = EMA.Config(decay=0.9).make()
+    mod(m)
+    fresh = EMA.Config(decay=0.9).make()
+    fresh.load_state_dict(mod.state_dict())
+    fresh(m)
+    assert fresh.global_step == 2 and fresh.shadow_model is not None
