@@ -102,10 +102,8 @@ class KimiK2(CausalLM):
                 kv_lora_rank=self.kv_lora_rank,
                 rope=RoPE.Config(self.channels_qk_rope_head, base=self.rope_theta, yarn=self.yarn, hf_inv_freq=True),
             )
-            if self.yarn is not None:
-                m = 0.1 * __import__("math").log(self.yarn.factor) * self.yarn.mscale_all_dim + 1.0
-                qk = self.channels_qk_nope_head + self.channels_qk_rope_head
-                attn.softmax_scale = qk**-0.5 * m * m if self.yarn.mscale_all_dim else None
+            # YaRN's attention-scale correction lives in the rotation tables (RoPE with ``yarn``
+            # scales cos / sin), as in the reference; the softmax scale stays qk_head_dim ** -0.5.
             blocks = []
             for i in range(self.num_hidden_layers):
                 if i < self.first_k_dense_replace or self.n_routed_experts == 0:

@@ -187,3 +187,69 @@ def test_sparse_sign_sgd_sums_row_gradients_across_ranks() -> None:
     assert t[0].tolist() == [-0.5, 0.5] and t[1].tolist() == [0.5, 0.5]
     assert t[4].tolist() == [0.5, -0.5]  # sign of (1 - 3, 2 - 1)
     assert t[[2, 3, 5]].abs().sum() == 0
+
+
+def _strategy_losses(rank: int, world: int, steps: int, kind: str) -> list[float]:
+    from priml_b200.parallel.strategies import HybridSharded, RecursiveFullySharded
+
+    torch.manual_seed(0)
+    if kind == "hsdp":
+        parallel = HybridSharded.Config(device="cpu", replicate_dim="dp", shard_dim="tp")
+    else:
+        parallel = RecursiveFullySharded.Config(device="cpu", block_types=["TransformerBlock", "SwiGLU"])
+    step = _tiny_step_cfg(parallel).make()
+    losses = []
+    for seq in _batches(steps, world):
+        local = seq.chunk(world)[rank]
+        out = step.train_step(tokens=local[:, :-1], targets=local[:, 1:])
+        t = out["loss"].detach().float().mean()
+        torch.distributed.all_reduce(t)
+        losses.append(float(t) / world)
+    return losses
+
+
+@pytest.mark.parametrize("kind,world,mesh", [("hsdp", 4, {"dp": 2, "tp": 2}), ("recursive", 2, {"dp": 2})])
+def test_hybrid_and_recursive_sharding_match_single_process(kind: str, world: int, mesh: dict) -> None:
+    """HSDP (replicate over dp, shard over tp) and per-module FSDP track the one-process run."""
+    steps = 4
+    ranks = run_ranks(_strategy_losses, world, steps, kind, mesh_shape=mesh)
+    ref = _single_losses(steps, world)
+    for r in ranks:
+        for a, b in zip(r, ref, strict=True):
+            assert abs(a - b) < 1e-4 * max(1.0, abs(b))
+
+
+def _async_roundtrip(rank: int, world: int, path: str) -> float:
+    from priml_b200.parallel.strategies import FullySharded
+    from priml_b200.train.checkpointing import AsyncLocalStateDictStorer, Checkpointer
+
+    torch.manual_seed(0)
+    step = _tiny_step_cfg(FullySharded.Config(device="cpu")).make()
+    seq = _batches(1, world)[0].chunk(world)[rank]
+    step.train_step(tokens=seq[:, :-1], targets=seq[:, 1:])
+
+    class _Holder:
+        def state_dict(self) -> dict:
+            return {"step": step.state_dict()}
+
+        def load_state_dict(self, s: dict) -> None:
+            step.load_state_dict(s["step"])
+
+    ck = Checkpointer.Config(working_dir=path, save_every=1, allow_checkpoint_overwrite=True,
+                             storer=AsyncLocalStateDictStorer.Config()).make()  # fmt: skip
+    ck.save(_Holder(), 1)
+    ck.flush()  # the background write is joined at an all-rank point
+    before = [p.full_tensor().clone() for p in step.model.parameters()]
+    with torch.no_grad():
+        for p in step.model.parameters():
+            p.zero_()
+    resumed = ck.load(_Holder(), guard=False)
+    after = [p.full_tensor() for p in step.model.parameters()]
+    assert resumed == 1
+    return max(float((a - b).abs().max()) for a, b in zip(after, before, strict=True))
+
+
+def test_async_storer_roundtrip_world2() -> None:
+    with tempfile.TemporaryDirectory() as d:
+        diffs = run_ranks(_async_roundtrip, 2, d, mesh_shape={"dp": 2})
+    assert max(diffs) == 0.0
