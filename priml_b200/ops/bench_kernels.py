@@ -210,15 +210,18 @@ def main() -> None:
         return
     rows = bench_gemms(args.tokens) if not args.attn_only else []
     if not args.gemm_only:
-        rows += bench_attention()
+        rows += bench_attention()  # Llama-1B: 32 q / 8 kv heads x 64
+        rows += bench_attention(b=1, s=8192, h=32, hkv=8, d=128)  # Llama-3-8B: 32 / 8 heads x 128
+        rows += bench_attention(b=2, s=4096, h=16, hkv=16, d=192, dv=128)  # MLA: 16 heads, 128+64 / 128
     for r in rows:
         print(json.dumps(r))
     if args.json:
         Path(args.json).write_text(json.dumps(rows, indent=1))
 
 
-def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int = 64) -> list[dict]:
+def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int = 64, dv: int | None = None) -> list[dict]:
     """Causal GQA attention fwd / fwd+bwd: ours vs torch SDPA (cuDNN / flash)."""
+    dv = d if dv is None else dv
     import math as _m
 
     import torch.nn.functional as F
@@ -227,10 +230,10 @@ def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int
 
     q = torch.randn(b, s, h, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     k = torch.randn(b, s, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    v = torch.randn(b, s, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    do = torch.randn(b, s, h, d, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(b, s, hkv, dv, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    do = torch.randn(b, s, h, dv, device="cuda", dtype=torch.bfloat16)
     sc = 1 / _m.sqrt(d)
-    flops_f = 4.0 * b * h * s * s * d / 2
+    flops_f = 2.0 * b * h * s * s * (d + dv) / 2
     rows = []
 
     def ours_f():
@@ -244,7 +247,7 @@ def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int
         with torch.no_grad():
             t_f = time_fn(f)
         t_fb = time_fn(lambda f=f: torch.autograd.backward(f(), do if name == "ours" else do.transpose(1, 2)))
-        rows.append({"case": f"attn.{name}", "B": b, "S": s, "H": h, "Hkv": hkv, "D": d, "fwd_ms": round(t_f, 3),
+        rows.append({"case": f"attn.{name}", "B": b, "S": s, "H": h, "Hkv": hkv, "D": d, "Dv": dv, "fwd_ms": round(t_f, 3),
                      "fwd_tflops": round(flops_f / t_f / 1e9, 1), "fwdbwd_ms": round(t_fb, 3),
                      "bwd_tflops": round(2.5 * flops_f / (t_fb - t_f) / 1e9, 1)})  # fmt: skip
     return rows
