@@ -29,7 +29,7 @@ constexpr int kLChunk = kLT * 128;  // one [64 rows][64 d] swizzled chunk = 8 KB
 // ============================================================================ delta
 __global__ void attn_delta_kernel(const AttnParams p) {
   // D / 8 threads per (b, q, h) row, one 16-byte load of O and dO each: delta = sum_d dO * O.
-  const int tpr = p.D / 8;
+  const int tpr = p.Dv / 8;  // delta = rowsum(dO * O) over the value width
   const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long row = t / tpr;
   const int part = static_cast<int>(t % tpr);
@@ -63,28 +63,35 @@ __global__ void attn_delta_kernel(const AttnParams p) {
 }
 
 // ============================================================================ dK dV
-template <int D>
+// D: query / key head dim, DV: value head dim. When dK and dV together are too wide for two
+// score buffers in TMEM (MLA: 192 + 128), the S^T / dP^T buffers are single (NB = 1) and the
+// next step's scores wait until this step's dV / dK MMAs have read P^T / dS^T.
+template <int D, int DV>
 struct KVSmem {
   static constexpr int kStages = 3;
-  static constexpr int kKBytes = (D / 64) * kChunkBytes;  // [128 keys][D]
-  static constexpr int kQBytes = (D / 64) * kLChunk;      // [64 q][D]
-  static constexpr int kBytes = 2 * kKBytes + kStages * (2 * kQBytes + 2 * kLT * 4) + 1024 + 256;
+  static constexpr int NB = 256 + D + DV <= 512 ? 2 : 1;  // score buffers
+  static constexpr int kKBytes = (D / 64) * kChunkBytes;   // [128 keys][D]
+  static constexpr int kVBytes = (DV / 64) * kChunkBytes;  // [128 keys][DV]
+  static constexpr int kQBytes = (D / 64) * kLChunk;       // [64 q][D]
+  static constexpr int kDOBytes = (DV / 64) * kLChunk;     // [64 q][DV]
+  static constexpr int kBytes = kKBytes + kVBytes + kStages * (kQBytes + kDOBytes + 2 * kLT * 4) + 1024 + 256;
 };
 
-template <int D>
+template <int D, int DV>
 __global__ void __launch_bounds__(320, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                      const AttnParams p) {
-  using SM = KVSmem<D>;
+  using SM = KVSmem<D, DV>;
   constexpr int NS = SM::kStages;
+  constexpr int NB = SM::NB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + SM::kKBytes;
-  uint8_t* sQ = sV + SM::kKBytes;        // [NS]
+  uint8_t* sQ = sV + SM::kVBytes;        // [NS]
   uint8_t* sDO = sQ + NS * SM::kQBytes;  // [NS]
-  float* sVec = reinterpret_cast<float*>(sDO + NS * SM::kQBytes);  // [NS][lse 64 | delta 64]
+  float* sVec = reinterpret_cast<float*>(sDO + NS * SM::kDOBytes);  // [NS][lse 64 | delta 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sVec + NS * 2 * kLT);
   uint64_t* kv_full = bars;
   uint64_t* in_full = kv_full + 1;    // [NS]
@@ -137,15 +144,16 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // cols: S^T buffers [0,64) [64,128); dP^T buffers [128,192) [192,256); dV [256, 256+D); dK [256+D, 256+2D)
-  const uint32_t tdV = tmem + 256;
-  const uint32_t tdK = tmem + 256 + D;
+  // cols: S^T buffers [0, 64 NB); dP^T buffers [64 NB, 128 NB); dV [128 NB, 128 NB + DV); dK after dV
+  const uint32_t tPT = tmem + 64 * NB;  // dP^T buffers
+  const uint32_t tdV = tmem + 128 * NB;
+  const uint32_t tdK = tdV + DV;
 
   if (warp == 0 && lane == 0) {
     bool ok = true;
-    mbar_arrive_expect_tx(kv_full, 2 * SM::kKBytes);
+    mbar_arrive_expect_tx(kv_full, SM::kKBytes + SM::kVBytes);
     load_tile(sK, &tmK, kv_full, hk * D, k0, b, D);
-    load_tile(sV, &tmV, kv_full, hk * D, k0, b, D);
+    load_tile(sV, &tmV, kv_full, hk * DV, k0, b, DV);
     for (int i = 0; i < n_steps && ok; ++i) {
       const int st = i % NS;
       const uint32_t ph = static_cast<uint32_t>((i / NS) & 1);
@@ -157,7 +165,7 @@ __global__ void __launch_bounds__(320, 1)
       if (bulk_vec) {
         // 256-byte bulk copies; lse / delta carry 128 floats of tail padding and
         // entries past S belong to masked queries.
-        mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes + 2 * kLT * 4);
+        mbar_arrive_expect_tx(&in_full[st], SM::kQBytes + SM::kDOBytes + 2 * kLT * 4);
         bulk_load(vec, p.lse + row, kLT * 4, &in_full[st]);
         bulk_load(vec + kLT, p.delta + row, kLT * 4, &in_full[st]);
       } else {
@@ -166,15 +174,16 @@ __global__ void __launch_bounds__(320, 1)
           vec[r] = in ? p.lse[row + r] : 0.f;
           vec[kLT + r] = in ? p.delta[row + r] : 0.f;
         }
-        mbar_arrive_expect_tx(&in_full[st], 2 * SM::kQBytes);
+        mbar_arrive_expect_tx(&in_full[st], SM::kQBytes + SM::kDOBytes);
       }
       load_tile(sQ + st * SM::kQBytes, &tmQ, &in_full[st], h * D, q0, b, D, kLChunk);
-      load_tile(sDO + st * SM::kQBytes, &tmDO, &in_full[st], h * D, q0, b, D, kLChunk);
+      load_tile(sDO + st * SM::kDOBytes, &tmDO, &in_full[st], h * DV, q0, b, DV, kLChunk);
     }
     if (!ok) mbar_wait(kv_full, 0, p.status, kTimeoutDrain, nullptr);
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc_ss = make_idesc_bf16(128, kLT, false, false);  // [128 keys x 64 q]
-    constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, false, true);   // [128 keys x D]
+    constexpr uint32_t idesc_dv = make_idesc_bf16(128, DV, false, true);   // [128 keys x DV]
+    constexpr uint32_t idesc_dk = make_idesc_bf16(128, D, false, true);    // [128 keys x D]
     bool ok = mbar_wait(kv_full, 0, p.status, kTimeoutMma, abort_flag);
     tc_fence_after();
     const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
@@ -183,38 +192,39 @@ __global__ void __launch_bounds__(320, 1)
       if (!mbar_wait(&in_full[st], (i / NS) & 1, p.status, kTimeoutMma, abort_flag)) return false;
       tc_fence_after();
       const uint32_t q_base = smem_u32(sQ + st * SM::kQBytes);
-      const uint32_t do_base = smem_u32(sDO + st * SM::kQBytes);
-      const uint32_t tS = tmem + (i & 1) * kLT;
-      const uint32_t tP = tmem + 128 + (i & 1) * kLT;
+      const uint32_t do_base = smem_u32(sDO + st * SM::kDOBytes);
+      const uint32_t tS = tmem + (i % NB) * kLT;
+      const uint32_t tP = tPT + (i % NB) * kLT;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk)
         umma_f16(tS, kmajor_desc(k_base, kk), kmajor_desc(q_base, kk, kLChunk), idesc_ss, kk > 0);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
+      for (int kk = 0; kk < DV / 16; ++kk)
         umma_f16(tP, kmajor_desc(v_base, kk), kmajor_desc(do_base, kk, kLChunk), idesc_ss, kk > 0);
-      umma_commit(&s_full[i & 1]);
+      umma_commit(&s_full[i % NB]);
       return true;
     };
     if (ok && n_steps > 0) ok = issue_scores(0);
     for (int i = 0; i < n_steps && ok; ++i) {
-      if (i + 1 < n_steps && !(ok = issue_scores(i + 1))) break;
-      if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
+      if (NB == 2 && i + 1 < n_steps && !(ok = issue_scores(i + 1))) break;
+      if (!mbar_wait(&p_ready[i % NB], (i / NB) & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const int st = i % NS;
       const uint32_t q_base = smem_u32(sQ + st * SM::kQBytes);
-      const uint32_t do_base = smem_u32(sDO + st * SM::kQBytes);
-      const uint32_t tS = tmem + (i & 1) * kLT;
-      const uint32_t tP = tmem + 128 + (i & 1) * kLT;
+      const uint32_t do_base = smem_u32(sDO + st * SM::kDOBytes);
+      const uint32_t tS = tmem + (i % NB) * kLT;
+      const uint32_t tP = tPT + (i % NB) * kLT;
 #pragma unroll
       for (int kk = 0; kk < kLT / 16; ++kk)
-        umma_f16_tmem_a(tdV, tS + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(do_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
+        umma_f16_tmem_a(tdV, tS + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(do_base, kk, kLChunk), idesc_dv, (i | kk) != 0);
 #pragma unroll
       for (int kk = 0; kk < kLT / 16; ++kk)
-        umma_f16_tmem_a(tdK, tP + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(q_base, kk, kLChunk), idesc_acc, (i | kk) != 0);
+        umma_f16_tmem_a(tdK, tP + (kk >> 1) * 32 + (kk & 1) * 8, mnmajor_desc(q_base, kk, kLChunk), idesc_dk, (i | kk) != 0);
       umma_commit(&in_empty[st]);
       umma_commit(mm_done);
-      // Buffer pair i&1 is rewritten by scores i+2 (next iteration): wait for these reads.
+      // The buffer of step i is rewritten by the scores of step i + NB: wait for these reads.
       if (!mbar_wait(mm_done, i & 1, p.status, kTimeoutMma, abort_flag)) { ok = false; break; }
+      if (NB == 1 && i + 1 < n_steps && !(ok = issue_scores(i + 1))) break;
     }
     umma_commit(acc_final);
     umma_commit(drain);
@@ -235,10 +245,10 @@ __global__ void __launch_bounds__(320, 1)
       const int q0 = (qt_lo + i % nq) * kLT;
       // Acquire the lse / delta vectors (bulk copies or the producer's plain stores).
       if (!mbar_wait_warp(&in_full[st], (i / NS) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
-      if (!mbar_wait_warp(&s_full[i & 1], (i >> 1) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[i % NB], (i / NB) & 1, p.status, kTimeoutEpilogue, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t tS = tmem + lane_off + (i & 1) * kLT;
-      const uint32_t tP = tmem + lane_off + 128 + (i & 1) * kLT;
+      const uint32_t tS = tmem + lane_off + (i % NB) * kLT;
+      const uint32_t tP = tPT + lane_off + (i % NB) * kLT;
       uint32_t sv[32], dv[32];
       tmem_ld_32x32b_x32(tS + c0, sv);
       tmem_ld_32x32b_x32(tP + c0, dv);
@@ -292,21 +302,25 @@ __global__ void __launch_bounds__(320, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[i & 1]);
+      if (lane == 0) mbar_arrive(&p_ready[i % NB]);
     }
     if (ok && n_steps > 0) ok = mbar_wait_warp(acc_final, 0, p.status, kTimeoutEpilogue, abort_flag);
     tc_fence_after();
     // TMEM loads are warp-collective: every lane executes them; only stores are predicated.
     const bool row_ok = key < p.T;
-    const long long row_off = b * p.dk_sb + static_cast<long long>(row_ok ? key : 0) * p.dk_ss + hk * p.dk_sh;
+    const long long krow = row_ok ? key : 0;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
-      __nv_bfloat16* dst = (which == 0 ? static_cast<__nv_bfloat16*>(p.dv) : static_cast<__nv_bfloat16*>(p.dk)) + row_off;
+      __nv_bfloat16* dst = which == 0
+                               ? static_cast<__nv_bfloat16*>(p.dv) + b * p.dv_sb + krow * p.dv_ss + hk * p.dv_sh
+                               : static_cast<__nv_bfloat16*>(p.dk) + b * p.dk_sb + krow * p.dk_ss + hk * p.dk_sh;
       const uint32_t src = (which == 0 ? tdV : tdK) + lane_off;
       const float f = which == 0 ? 1.f : p.scale;
+      const int width = which == 0 ? DV : D;
 #pragma unroll
-      for (int cc = 0; cc < D / 64; ++cc) {
-        const int c = half * (D / 2) + cc * 32;
+      for (int cc = 0; cc < (D > DV ? D : DV) / 64; ++cc) {
+        if (cc >= width / 64) break;
+        const int c = half * (width / 2) + cc * 32;
         uint32_t v[32];
         if (ok && n_steps > 0) {
           tmem_ld_32x32b_x32(src + c, v);
@@ -336,28 +350,30 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ============================================================================ dQ
-template <int D>
+template <int D, int DV>
 struct QSmem {
   static constexpr int kStages = 3;
-  static constexpr int kQBytes = (D / 64) * kChunkBytes;  // [128 q][D]
-  static constexpr int kKBytes = (D / 64) * kLChunk;      // [64 keys][D]
-  static constexpr int kBytes = 2 * kQBytes + kStages * 2 * kKBytes + 1024 + 256;
+  static constexpr int kQBytes = (D / 64) * kChunkBytes;    // [128 q][D]
+  static constexpr int kDOBytes = (DV / 64) * kChunkBytes;  // [128 q][DV]
+  static constexpr int kKBytes = (D / 64) * kLChunk;        // [64 keys][D]
+  static constexpr int kVBytes = (DV / 64) * kLChunk;       // [64 keys][DV]
+  static constexpr int kBytes = kQBytes + kDOBytes + kStages * (kKBytes + kVBytes) + 1024 + 256;
 };
 
-template <int D>
+template <int D, int DV>
 __global__ void __launch_bounds__(320, 1)
     attn_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                    const AttnParams p) {
-  using SM = QSmem<D>;
+  using SM = QSmem<D, DV>;
   constexpr int NS = SM::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sDO = sQ + SM::kQBytes;
-  uint8_t* sK = sDO + SM::kQBytes;      // [NS]
+  uint8_t* sK = sDO + SM::kDOBytes;     // [NS]
   uint8_t* sV = sK + NS * SM::kKBytes;  // [NS]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * SM::kKBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * SM::kVBytes);
   uint64_t* qd_full = bars;
   uint64_t* kv_full = qd_full + 1;    // [NS]
   uint64_t* kv_empty = kv_full + NS;  // [NS]
@@ -411,16 +427,16 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0 && lane == 0) {
     bool ok = true;
-    mbar_arrive_expect_tx(qd_full, 2 * SM::kQBytes);
+    mbar_arrive_expect_tx(qd_full, SM::kQBytes + SM::kDOBytes);
     load_tile(sQ, &tmQ, qd_full, h * D, q0, b, D);
-    load_tile(sDO, &tmDO, qd_full, h * D, q0, b, D);
+    load_tile(sDO, &tmDO, qd_full, h * DV, q0, b, DV);
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int st = j % NS;
       const int k0 = (kt_lo + j) * kLT;
       if (!mbar_wait(&kv_empty[st], ((j / NS) & 1) ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
-      mbar_arrive_expect_tx(&kv_full[st], 2 * SM::kKBytes);
+      mbar_arrive_expect_tx(&kv_full[st], SM::kKBytes + SM::kVBytes);
       load_tile(sK + st * SM::kKBytes, &tmK, &kv_full[st], hk * D, k0, b, D, kLChunk);
-      load_tile(sV + st * SM::kKBytes, &tmV, &kv_full[st], hk * D, k0, b, D, kLChunk);
+      load_tile(sV + st * SM::kVBytes, &tmV, &kv_full[st], hk * DV, k0, b, DV, kLChunk);
     }
     if (!ok) mbar_wait(qd_full, 0, p.status, kTimeoutDrain, nullptr);
   } else if (warp == 1 && lane == 0) {
@@ -434,14 +450,14 @@ __global__ void __launch_bounds__(320, 1)
       if (!mbar_wait(&kv_full[st], (j / NS) & 1, p.status, kTimeoutMma, abort_flag)) return false;
       tc_fence_after();
       const uint32_t k_base = smem_u32(sK + st * SM::kKBytes);
-      const uint32_t v_base = smem_u32(sV + st * SM::kKBytes);
+      const uint32_t v_base = smem_u32(sV + st * SM::kVBytes);
       const uint32_t tS = tmem + (j & 1) * kLT;
       const uint32_t tP = tmem + 128 + (j & 1) * kLT;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk)
         umma_f16(tS, kmajor_desc(q_base, kk), kmajor_desc(k_base, kk, kLChunk), idesc_ss, kk > 0);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
+      for (int kk = 0; kk < DV / 16; ++kk)
         umma_f16(tP, kmajor_desc(do_base, kk), kmajor_desc(v_base, kk, kLChunk), idesc_ss, kk > 0);
       umma_commit(&s_full[j & 1]);
       return true;
@@ -580,7 +596,8 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloa
 void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o,
               const AttnTensor& dout, const float* lse, float* delta, const AttnTensor& dq, const AttnTensor& dk,
               const AttnTensor& dv, int H, int Hkv, int D, float scale, bool causal, int window, int* status,
-              cudaStream_t stream, float* dq_acc) {
+              cudaStream_t stream, float* dq_acc, int Dv) {
+  if (Dv <= 0) Dv = D;
   AttnParams p{};
   p.B = q.batch;
   p.S = q.seq;
@@ -588,6 +605,7 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.H = H;
   p.Hkv = Hkv;
   p.D = D;
+  p.Dv = Dv;
   p.scale = scale;
   p.scale_log2 = scale * kLog2e;
   p.causal = causal;
@@ -595,13 +613,13 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.o = o.ptr;
   p.o_sb = o.s_batch;
   p.o_ss = o.s_seq;
-  p.o_sh = D;
+  p.o_sh = Dv;
   p.lse = const_cast<float*>(lse);
   p.delta = delta;
   p.dout = dout.ptr;
   p.do_sb = dout.s_batch;
   p.do_ss = dout.s_seq;
-  p.do_sh = D;
+  p.do_sh = Dv;
   p.dq = dq.ptr;
   p.dq_sb = dq.s_batch;
   p.dq_ss = dq.s_seq;
@@ -611,8 +629,11 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.dk_sb = dk.s_batch;
   p.dk_ss = dk.s_seq;
   p.dk_sh = D;
+  p.dv_sb = dv.s_batch;
+  p.dv_ss = dv.s_seq;
+  p.dv_sh = Dv;
   p.status = status;
-  const bool fused = D == 64 && dq_acc != nullptr;
+  const bool fused = D == 64 && Dv == 64 && dq_acc != nullptr;
   {
     const long long rows = static_cast<long long>(p.B) * p.S * p.H;
     // The fused kernel reads delta and -lse * log2(e) in 128-row bulk copies, so their rows are
@@ -622,18 +643,18 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
     const long long n_vec = static_cast<long long>(p.B) * p.H * p.vec_s;
     p.nlse2 = fused ? delta + n_vec + 128 : nullptr;
     if (fused && p.vec_s != p.S) cudaMemsetAsync(delta, 0, 2 * (n_vec + 128) * sizeof(float), stream);
-    const long long threads = rows * (D / 8);
+    const long long threads = rows * (Dv / 8);
     attn_delta_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p);
   }
   CUtensorMap mq128, mdo128, mq64, mdo64, mk128, mv128, mk64, mv64;
   make_bshd_map(&mq128, q, H, D, kTile);
-  make_bshd_map(&mdo128, dout, H, D, kTile);
+  make_bshd_map(&mdo128, dout, H, Dv, kTile);
   make_bshd_map(&mq64, q, H, D, kLT);
-  make_bshd_map(&mdo64, dout, H, D, kLT);
+  make_bshd_map(&mdo64, dout, H, Dv, kLT);
   make_bshd_map(&mk128, k, Hkv, D, kTile);
-  make_bshd_map(&mv128, v, Hkv, D, kTile);
+  make_bshd_map(&mv128, v, Hkv, Dv, kTile);
   make_bshd_map(&mk64, k, Hkv, D, kLT);
-  make_bshd_map(&mv64, v, Hkv, D, kLT);
+  make_bshd_map(&mv64, v, Hkv, Dv, kLT);
   const int grid_kv = ((p.T + kTile - 1) / kTile) * p.B * p.Hkv;
   const int grid_q = ((p.S + kTile - 1) / kTile) * p.B * p.H;
   if (fused) {
@@ -648,16 +669,18 @@ void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
                                                        p.dq_sb, p.dq_ss, scale);
     return;
   }
-  if (D == 64) {
-    set_smem(attn_dkdv_kernel<64>, KVSmem<64>::kBytes);
-    set_smem(attn_dq_kernel<64>, QSmem<64>::kBytes);
-    attn_dkdv_kernel<64><<<grid_kv, 320, KVSmem<64>::kBytes, stream>>>(mq64, mk128, mv128, mdo64, p);
-    attn_dq_kernel<64><<<grid_q, 320, QSmem<64>::kBytes, stream>>>(mq128, mk64, mv64, mdo128, p);
-  } else {
-    set_smem(attn_dkdv_kernel<128>, KVSmem<128>::kBytes);
-    set_smem(attn_dq_kernel<128>, QSmem<128>::kBytes);
-    attn_dkdv_kernel<128><<<grid_kv, 320, KVSmem<128>::kBytes, stream>>>(mq64, mk128, mv128, mdo64, p);
-    attn_dq_kernel<128><<<grid_q, 320, QSmem<128>::kBytes, stream>>>(mq128, mk64, mv64, mdo128, p);
+  auto run = [&](auto dkdv, int kv_bytes, auto dqk, int q_bytes) {
+    set_smem(dkdv, kv_bytes);
+    set_smem(dqk, q_bytes);
+    dkdv<<<grid_kv, 320, kv_bytes, stream>>>(mq64, mk128, mv128, mdo64, p);
+    dqk<<<grid_q, 320, q_bytes, stream>>>(mq128, mk64, mv64, mdo128, p);
+  };
+  if (D == 64 && Dv == 64) {
+    run(attn_dkdv_kernel<64, 64>, KVSmem<64, 64>::kBytes, attn_dq_kernel<64, 64>, QSmem<64, 64>::kBytes);
+  } else if (D == 128 && Dv == 128) {
+    run(attn_dkdv_kernel<128, 128>, KVSmem<128, 128>::kBytes, attn_dq_kernel<128, 128>, QSmem<128, 128>::kBytes);
+  } else {  // multi-head latent attention: 128 + 64 rotary query / key channels, 128 value channels
+    run(attn_dkdv_kernel<192, 128>, KVSmem<192, 128>::kBytes, attn_dq_kernel<192, 128>, QSmem<192, 128>::kBytes);
   }
 }
 

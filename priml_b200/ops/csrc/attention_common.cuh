@@ -45,7 +45,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 struct AttnParams {
-  int B, S, T, H, Hkv, D;
+  int B, S, T, H, Hkv, D;  // D: query / key head dim
+  int Dv;                   // value head dim (== D except for MLA's 192 / 128)
   float scale_log2;  // softmax scale * log2(e)
   float scale;
   int causal;
@@ -64,6 +65,7 @@ struct AttnParams {
   void* dk;  // [B, T, Hkv, D] bf16 out
   void* dv;
   long long dk_sb, dk_ss, dk_sh;
+  long long dv_sb, dv_ss, dv_sh;
   int* status;
   int* trace;  // optional progress record, 8 ints per CTA (stage, SM, producer / MMA / softmax tile), for diagnosis
 };

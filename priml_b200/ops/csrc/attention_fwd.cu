@@ -290,7 +290,9 @@ __global__ void __launch_bounds__(192, 2)
 }  // namespace
 
 void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, float* lse, int H,
-              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream, int* trace) {
+              int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream, int* trace,
+              int Dv) {
+  if (Dv <= 0) Dv = D;
   AttnParams p{};
   p.trace = trace;
   p.B = q.batch;
@@ -299,6 +301,7 @@ void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.H = H;
   p.Hkv = Hkv;
   p.D = D;
+  p.Dv = Dv;
   p.scale = scale;
   p.scale_log2 = scale * kLog2e;
   p.causal = causal;
@@ -306,15 +309,15 @@ void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, con
   p.o = o.ptr;
   p.o_sb = o.s_batch;
   p.o_ss = o.s_seq;
-  p.o_sh = D;
+  p.o_sh = Dv;
   p.lse = lse;
   p.status = status;
   CUtensorMap mq, mk, mv;
   make_bshd_map(&mq, q, H, D, kTile);
-  if (trace == nullptr) {
-    const int kt = D == 64 ? kKT : kTile;  // keys per tile of the two-tile kernel
+  if (trace == nullptr || Dv != D) {
+    const int kt = D == 128 ? kTile : kKT;  // keys per tile of the two-tile kernel
     make_bshd_map(&mk, k, Hkv, D, kt);
-    make_bshd_map(&mv, v, Hkv, D, kt);
+    make_bshd_map(&mv, v, Hkv, Dv, kt);
     attn_fwd3_launch(mq, mk, mv, p, D, stream);
     return;
   }

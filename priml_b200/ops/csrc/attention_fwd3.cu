@@ -1,4 +1,5 @@
-// Flash-attention forward for sm_100a, two query tiles per CTA (head dim 64 or 128).
+// Flash-attention forward for sm_100a, two query tiles per CTA. Query / key head dim D and value
+// head dim DV: (64, 64), (128, 128), and (192, 128) for multi-head latent attention.
 //
 // Layouts as in attention_fwd.cu: q/o [B, S, H, D], k/v [B, T, Hkv, D] (token and
 // batch strides free, heads x D contiguous), lse [B, H, S] fp32 natural log.
@@ -20,7 +21,7 @@
 //              PV_t(j) has read it. The running max moves (and O is rescaled) only
 //              when it grows by more than 2^8; the epilogue divides by the row sum
 //              and writes bf16 O and the natural-log LSE.
-// TMEM: S_0 [0,KT) S_1 [KT,2KT) O_0 [2KT, 2KT + D) O_1 [2KT + D, 2KT + 2D), KT keys per tile.
+// TMEM: S_0 [0,KT) S_1 [KT,2KT) O_0 [2KT, 2KT + DV) O_1 [2KT + DV, 2KT + 2DV), KT keys per tile.
 #include "attention_common.cuh"
 
 namespace pb {
@@ -29,27 +30,28 @@ namespace {
 
 using namespace attn;
 
-template <int D>
+template <int D, int DV>
 struct Fwd3Cfg {
-  static constexpr int KT = D == 64 ? 64 : 128;               // keys per tile
+  static constexpr int KT = D == 128 ? 128 : 64;              // keys per tile
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
-  static constexpr int kTmemCols = D == 64 ? 256 : 512;
-  static constexpr int kStages = D == 64 ? 4 : 2;
+  static constexpr int kTmemCols = 2 * KT + 2 * DV <= 256 ? 256 : 512;
+  static constexpr int kStages = D == 64 ? 4 : (D == 128 ? 2 : 3);
   static constexpr int kQBytes = (D / 64) * kChunkBytes;      // [128 rows][D] in 64-column chunks
   static constexpr int kKVChunk = KT * 128;                   // [KT rows][64 columns] swizzled chunk
-  static constexpr int kKVBytes = (D / 64) * kKVChunk;
+  static constexpr int kKBytes = (D / 64) * kKVChunk;
+  static constexpr int kVBytes = (DV / 64) * kKVChunk;
   static constexpr int kOffQ = 0;                             // two query tiles
   static constexpr int kOffK = 2 * kQBytes;
-  static constexpr int kOffV = kOffK + kStages * kKVBytes;
-  static constexpr int kOffBars = kOffV + kStages * kKVBytes;
+  static constexpr int kOffV = kOffK + kStages * kKBytes;
+  static constexpr int kOffBars = kOffV + kStages * kVBytes;
   static constexpr int kBytes = kOffBars + 256 + 1024;
 };
 
-template <int D>
-__global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
+template <int D, int DV>
+__global__ void __launch_bounds__(320, Fwd3Cfg<D, DV>::kCtasPerSm)
     attn_fwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using SM = Fwd3Cfg<D>;
+  using SM = Fwd3Cfg<D, DV>;
   constexpr int NS = SM::kStages;
   constexpr int KT = SM::KT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -135,17 +137,17 @@ __global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
       const uint32_t ph = static_cast<uint32_t>((j / NS) & 1);
       const int k0 = (j_lo + j) * KT;
       if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
-      mbar_arrive_expect_tx(&k_full[st], SM::kKVBytes);
-      load_tile(sK + st * SM::kKVBytes, &tmK, &k_full[st], hk * D, k0, b, D, SM::kKVChunk);
+      mbar_arrive_expect_tx(&k_full[st], SM::kKBytes);
+      load_tile(sK + st * SM::kKBytes, &tmK, &k_full[st], hk * D, k0, b, D, SM::kKVChunk);
       if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kTimeoutProducer, abort_flag)) { ok = false; break; }
-      mbar_arrive_expect_tx(&v_full[st], SM::kKVBytes);
-      load_tile(sV + st * SM::kKVBytes, &tmV, &v_full[st], hk * D, k0, b, D, SM::kKVChunk);
+      mbar_arrive_expect_tx(&v_full[st], SM::kVBytes);
+      load_tile(sV + st * SM::kVBytes, &tmV, &v_full[st], hk * DV, k0, b, DV, SM::kKVChunk);
     }
     if (!ok) mbar_wait(q_full, 0, p.status, kTimeoutDrain, nullptr);
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_s = make_idesc_bf16(128, KT, false, false);     // [128 q x KT keys]
-    constexpr uint32_t idesc_o = make_idesc_bf16(128, D, false, true);       // [128 q x D]
+    constexpr uint32_t idesc_o = make_idesc_bf16(128, DV, false, true);      // [128 q x DV]
     bool ok = mbar_wait(q_full, 0, p.status, kTimeoutMma, abort_flag);
     tc_fence_after();
     int done0 = 0, done1 = 0;  // key tiles already accumulated into O_0 / O_1
@@ -159,7 +161,7 @@ __global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
       tc_fence_after();
       if (active(t, j)) {
         const uint32_t q_base = smem_u32(sQ + t * SM::kQBytes);
-        const uint32_t k_base = smem_u32(sK + st * SM::kKVBytes);
+        const uint32_t k_base = smem_u32(sK + st * SM::kKBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_f16(tmem + t * KT, kmajor_desc(q_base, kk), kmajor_desc(k_base, kk, SM::kKVChunk), idesc_s, kk > 0);
@@ -174,10 +176,10 @@ __global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
       const int st = j % NS;
       if (!mbar_wait(&v_full[st], (j / NS) & 1, p.status, kTimeoutMma, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t v_base = smem_u32(sV + st * SM::kKVBytes);
+      const uint32_t v_base = smem_u32(sV + st * SM::kVBytes);
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk)
-        umma_f16_tmem_a(tmem + 2 * KT + t * D, tmem + t * KT + kk * 8, mnmajor_desc(v_base, kk, SM::kKVChunk), idesc_o,
+        umma_f16_tmem_a(tmem + 2 * KT + t * DV, tmem + t * KT + kk * 8, mnmajor_desc(v_base, kk, SM::kKVChunk), idesc_o,
                         (done | kk) != 0);
       ++done;
       return true;
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
     const int q = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + t * KT + lane_off;
-    const uint32_t tO = tmem + 2 * KT + t * D + lane_off;
+    const uint32_t tO = tmem + 2 * KT + t * DV + lane_off;
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
     const int my_lo = t == 0 ? lo[0] : lo[1], my_hi = t == 0 ? hi[0] : hi[1];
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
         const float f = scale_o ? fast_exp2(m - mxs) : 1.f;
         l *= f;
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
+        for (int c = 0; c < DV / 16; ++c) {
           uint32_t o[16];
           tmem_ld_32x32b_x16(tO + c * 16, o);
           tmem_wait_ld();
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(320, Fwd3Cfg<D>::kCtasPerSm)
     __nv_bfloat16* orow =
         static_cast<__nv_bfloat16*>(p.o) + b * p.o_sb + static_cast<long long>(row_ok ? q : 0) * p.o_ss + h * p.o_sh;
 #pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = 0; c < DV / 32; ++c) {
       uint32_t o[32];
       if (ok && has) {
         tmem_ld_32x32b_x32(tO + c * 32, o);
@@ -334,12 +336,16 @@ void attn_fwd3_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtens
                       int D, cudaStream_t stream) {
   const int num_q = (p.S + kTile - 1) / kTile;
   const int grid = ((num_q + 1) / 2) * p.B * p.H;
-  if (D == 64) {
-    set_smem(attn_fwd3_kernel<64>, Fwd3Cfg<64>::kBytes);
-    attn_fwd3_kernel<64><<<grid, 320, Fwd3Cfg<64>::kBytes, stream>>>(mq, mk, mv, p);
+  auto run = [&](auto kern, int bytes) {
+    set_smem(kern, bytes);
+    kern<<<grid, 320, bytes, stream>>>(mq, mk, mv, p);
+  };
+  if (D == 64 && p.Dv == 64) {
+    run(attn_fwd3_kernel<64, 64>, Fwd3Cfg<64, 64>::kBytes);
+  } else if (D == 128 && p.Dv == 128) {
+    run(attn_fwd3_kernel<128, 128>, Fwd3Cfg<128, 128>::kBytes);
   } else {
-    set_smem(attn_fwd3_kernel<128>, Fwd3Cfg<128>::kBytes);
-    attn_fwd3_kernel<128><<<grid, 320, Fwd3Cfg<128>::kBytes, stream>>>(mq, mk, mv, p);
+    run(attn_fwd3_kernel<192, 128>, Fwd3Cfg<192, 128>::kBytes);
   }
 }
 

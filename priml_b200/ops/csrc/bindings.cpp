@@ -468,45 +468,50 @@ pb::AttnTensor attn_view(const Tensor& t, const char* name) {
 // (o [B,S,H,D] bf16, lse [B,H,S] fp32)
 std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, double scale, bool causal,
                              int64_t window, const c10::optional<Tensor>& trace) {
-  const int D = q.size(3), H = q.size(2), Hkv = k.size(2);
-  PB_CHECK(D == 64 || D == 128, "head dim must be 64 or 128");
-  PB_CHECK(v.size(3) == D && k.size(3) == D && H % Hkv == 0 && v.size(2) == Hkv, "q/k/v shapes");
+  const int D = q.size(3), Dv = v.size(3), H = q.size(2), Hkv = k.size(2);
+  PB_CHECK((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128),
+           "head dims (query/key, value) must be (64, 64), (128, 128) or (192, 128)");
+  PB_CHECK(k.size(3) == D && H % Hkv == 0 && v.size(2) == Hkv, "q/k/v shapes");
+  PB_CHECK(D != 192 || !trace.has_value(), "the progress trace covers head dims 64 and 128 only");
   PB_CHECK(k.size(0) == q.size(0) && v.size(1) == k.size(1), "batch / key lengths");
   const c10::cuda::CUDAGuard guard(q.device());
-  auto o = torch::empty({q.size(0), q.size(1), H, D}, q.options());
+  auto o = torch::empty({q.size(0), q.size(1), H, Dv}, q.options());
   // 128 floats of tail padding: the backward reads lse rows in 512-byte bulk copies.
   const long long n_lse = q.size(0) * H * q.size(1);
   auto lse = torch::empty({n_lse + 128}, q.options().dtype(torch::kFloat32)).narrow(0, 0, n_lse).view({q.size(0), H, q.size(1)});
   if (q.numel() == 0) return {o, lse};
   pb::attn_fwd(attn_view(q, "q"), attn_view(k, "k"), attn_view(v, "v"), attn_view(o, "o"), lse.data_ptr<float>(), H, Hkv,
                D, static_cast<float>(scale), causal, static_cast<int>(window), status_ptr(), stream(),
-               trace.has_value() ? trace->data_ptr<int>() : nullptr);
+               trace.has_value() ? trace->data_ptr<int>() : nullptr, Dv);
   return {o, lse};
 }
 
 // (dq, dk, dv) in the layouts of q / k / v (contiguous).
 std::vector<Tensor> attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& dout,
                              const Tensor& lse, double scale, bool causal, int64_t window) {
-  const int D = q.size(3), H = q.size(2), Hkv = k.size(2);
+  const int D = q.size(3), Dv = v.size(3), H = q.size(2), Hkv = k.size(2);
+  PB_CHECK((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128),
+           "head dims (query/key, value) must be (64, 64), (128, 128) or (192, 128)");
   const c10::cuda::CUDAGuard guard(q.device());
   auto dq = torch::empty({q.size(0), q.size(1), H, D}, q.options());
   auto dk = torch::empty({k.size(0), k.size(1), Hkv, D}, k.options());
-  auto dv = torch::empty({v.size(0), v.size(1), Hkv, D}, v.options());
+  auto dv = torch::empty({v.size(0), v.size(1), Hkv, Dv}, v.options());
   const long long n_rows = q.size(0) * H * q.size(1);
   // delta rows + 128 floats of padding; the fused D = 64 path pads each (b, h) row of delta to a
   // multiple of 4 floats and keeps -lse*log2(e) after it in the same layout.
   const long long n_vec = q.size(0) * H * ((q.size(1) + 3) / 4 * 4);
-  auto delta = torch::empty({D == 64 ? 2 * (n_vec + 128) : n_rows + 128}, q.options().dtype(torch::kFloat32));
+  const bool fused = D == 64 && Dv == 64;
+  auto delta = torch::empty({fused ? 2 * (n_vec + 128) : n_rows + 128}, q.options().dtype(torch::kFloat32));
   PB_CHECK(lse.is_contiguous() && lse.numel() == n_rows, "lse must be the forward's [B, H, S] output");
-  auto doc = dout.stride(3) == 1 && dout.stride(2) == D ? dout : dout.contiguous();
+  auto doc = dout.stride(3) == 1 && dout.stride(2) == Dv ? dout : dout.contiguous();
   if (q.numel() == 0) return {dq, dk, dv};
   // D = 64 runs the fused dK/dV/dQ kernel, which bulk-reduces dQ into fp32 scratch.
   Tensor dq_acc;
-  if (D == 64) dq_acc = torch::empty({n_rows * D}, q.options().dtype(torch::kFloat32));
+  if (fused) dq_acc = torch::empty({n_rows * D}, q.options().dtype(torch::kFloat32));
   pb::attn_bwd(attn_view(q, "q"), attn_view(k, "k"), attn_view(v, "v"), attn_view(o, "o"), attn_view(doc, "dout"),
                lse.data_ptr<float>(), delta.data_ptr<float>(), attn_view(dq, "dq"), attn_view(dk, "dk"),
                attn_view(dv, "dv"), H, Hkv, D, static_cast<float>(scale), causal, static_cast<int>(window),
-               status_ptr(), stream(), dq_acc.defined() ? dq_acc.data_ptr<float>() : nullptr);
+               status_ptr(), stream(), dq_acc.defined() ? dq_acc.data_ptr<float>() : nullptr, Dv);
   return {dq, dk, dv};
 }
 

@@ -105,16 +105,18 @@ struct AttnTensor {
   long long s_batch;
   long long s_seq;
 };
+// D: query / key head dim; Dv: value head dim (0: same as D). Supported pairs: (64, 64),
+// (128, 128) and (192, 128) (multi-head latent attention).
 void attn_fwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, float* lse, int H,
               int Hkv, int D, float scale, bool causal, int window, int* status, cudaStream_t stream,
-              int* trace = nullptr);
-// dq_acc: optional fp32 scratch of B*H*S*D floats; with it (and D == 64) the
+              int* trace = nullptr, int Dv = 0);
+// dq_acc: optional fp32 scratch of B*H*S*D floats; with it (and D == Dv == 64) the
 // backward runs as one fused kernel that bulk-reduces dQ partials into it, and
 // `delta` must then hold 2 * (B*H*S + 128) floats.
 void attn_bwd(const AttnTensor& q, const AttnTensor& k, const AttnTensor& v, const AttnTensor& o,
               const AttnTensor& dout, const float* lse, float* delta, const AttnTensor& dq, const AttnTensor& dk,
               const AttnTensor& dv, int H, int Hkv, int D, float scale, bool causal, int window, int* status,
-              cudaStream_t stream, float* dq_acc = nullptr);
+              cudaStream_t stream, float* dq_acc = nullptr, int Dv = 0);
 
 // fp32 -> bf16 cast of n elements.
 void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);

@@ -1,8 +1,9 @@
 """Flash attention entry point for ``[B, S, H, D]`` tensors with grouped KV heads.
 
-Runs the hand-written tcgen05 kernels of ``csrc/attention.cu`` when the shape
-is supported (head dims 64 / 128, bf16). Shapes outside that set go through
-``torch.nn.functional.scaled_dot_product_attention``.
+Runs the hand-written tcgen05 kernels (``csrc/attention_*.cu``) for bf16 inputs
+with (query/key, value) head dims (64, 64), (128, 128) or (192, 128) -- the last is
+multi-head latent attention's 128 + 64 rotary channels with 128 value channels.
+Other head dims go through ``torch.nn.functional.scaled_dot_product_attention``.
 """
 
 from __future__ import annotations
@@ -27,8 +28,7 @@ def kernel_supports(q: Tensor, k: Tensor, v: Tensor, window: int | None) -> bool
         q.dtype == torch.bfloat16
         and k.dtype == torch.bfloat16
         and v.dtype == torch.bfloat16
-        and d == dv
-        and d in (64, 128)
+        and (d, dv) in ((64, 64), (128, 128), (192, 128))
         and q.shape[-2] % k.shape[-2] == 0
     )
 

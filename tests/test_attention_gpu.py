@@ -96,3 +96,56 @@ def test_flash_attention_rows_rescale_independently(D: int, window) -> None:  # 
     assert _err(o, ref) < 2e-2
     assert _err(dq, rq) < 5e-2 and _err(dk, rk) < 5e-2 and _err(dv, rv) < 5e-2
     assert int(native().read_status(True)) == 0
+
+
+MLA_CASES = [
+    # B, S, T, H, Hkv, causal, window -- query/key head dim 192 (128 + 64 rotary), value head dim 128
+    (1, 256, 256, 4, 4, True, None),
+    (2, 300, 300, 2, 2, True, None),
+    (1, 256, 256, 2, 2, False, None),
+    (1, 128, 384, 2, 2, True, None),
+    (1, 384, 384, 2, 1, True, 100),
+]
+
+
+@pytest.mark.parametrize("B,S,T,H,Hkv,causal,window", MLA_CASES)
+def test_latent_attention_head_dims_fwd_bwd(B, S, T, H, Hkv, causal, window) -> None:  # noqa: ANN001
+    """Multi-head latent attention shapes: q / k 192 wide, v 128 wide, against the fp32 oracle."""
+    from priml_b200.ops import native
+    from priml_b200.ops.attention_fn import FlashAttnFn
+
+    torch.manual_seed(2)
+    q = torch.randn(B, S, H, 192, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, T, Hkv, 192, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, T, Hkv, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    scale = 1.0 / math.sqrt(192)
+    o = FlashAttnFn.apply(q, k, v, causal, scale, -1 if window is None else window)
+    assert o.shape == (B, S, H, 128)
+    do = torch.randn_like(o)
+    o.backward(do)
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    orf = _ref(qr, kr, vr, causal, scale, window)
+    orf.backward(do.float())
+    torch.cuda.synchronize()
+    assert native().read_status(True) == 0
+    assert _err(o, orf) < 2e-2
+    assert _err(q.grad, qr.grad) < 3e-2
+    assert _err(k.grad, kr.grad) < 3e-2
+    assert _err(v.grad, vr.grad) < 3e-2
+
+
+def test_mla_module_training_path_uses_the_kernel() -> None:
+    """The MLA block's expanded training attention matches the absorbed oracle path."""
+    from priml_b200.models.mla import MultiHeadLatentAttention
+    from priml_b200.models.rope import RoPE
+
+    torch.manual_seed(0)
+    mla = MultiHeadLatentAttention.Config(channels_in=256, heads=4, kv_lora_rank=64, channels_qk_nope_head=128,
+                                          channels_qk_rope_head=64, channels_v_head=128,
+                                          rope=RoPE.Config(64, base=1e4)).make().cuda().train()  # fmt: skip
+    x = torch.randn(2, 256, 256, device="cuda")
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        fast, _ = mla(x)
+        mla.eval()
+        slow, _ = mla(x)  # the absorbed path (einsums), not the kernel
+    assert _err(fast, slow) < 3e-2
