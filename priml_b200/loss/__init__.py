@@ -23,6 +23,8 @@ from priml_b200.config import Fig
 __all__ = [
     "AdversarialLoss",
     "DiffusionLoss",
+    "LPIPS",
+    "LPIPSLoss",
     "LossOutput",
     "SimpleLoss",
     "TokenCrossEntropy",
@@ -150,3 +152,6 @@ def clipped_policy_loss(logp_new: Tensor, logp_old: Tensor, advantage: Tensor, c
 
 
 _ = math
+
+
+from priml_b200.loss.lpips import LPIPS, LPIPSLoss  # noqa: E402

@@ -13,6 +13,8 @@ from priml_b200.train.activation import (
     DefaultActivationStorage,
     Float8ActivationStorage,
     LayerActivationCheckpointing,
+    QuantizedActivationStorage,
+    QuantizedModuleActivationStorage,
     SelectiveActivationCheckpointing,
 )
 from priml_b200.train.checkpointing import AsyncLocalStateDictStorer, Checkpointer, SyncLocalStateDictStorer
@@ -46,6 +48,8 @@ __all__ = [
     "FullySharded",
     "HybridSharded",
     "LayerActivationCheckpointing",
+    "QuantizedActivationStorage",
+    "QuantizedModuleActivationStorage",
     "NoEMA",
     "NoParallel",
     "NoTracker",

@@ -17,6 +17,8 @@ def pytest_configure(config: pytest.Config) -> None:
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200 / sm_100a)")
     config.addinivalue_line("markers", "multigpu: needs two or more CUDA devices")
     config.addinivalue_line("markers", "slow: long-running test")
+    for name in ("cuda", "performance", "integration"):  # selector marks that resource markers imply
+        config.addinivalue_line("markers", f"{name}: implied by a resource marker")
 
 
 def pytest_collection_modifyitems(config: pytest.Config, items: list[pytest.Item]) -> None:
