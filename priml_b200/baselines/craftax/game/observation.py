@@ -20,7 +20,7 @@ from torch.nn import functional as F
 from priml_b200.baselines.craftax.game import constants as C
 from priml_b200.baselines.craftax.game.state import GameState
 
-__all__ = ["CHANNELS_PER_TILE", "observation_size", "render"]
+__all__ = ["CHANNELS_PER_TILE", "local_view", "observation_size", "render", "visible_tiles"]
 
 CHANNELS_PER_TILE = len(C.BlockType) + len(C.ItemType) + 5 * 8 + 1
 
@@ -41,10 +41,27 @@ def _local(grid: Tensor, pos: Tensor, view: tuple[int, int], outside: int) -> Te
     return padded[e[:, None, None], rr[:, :, None], cc[:, None, :]]
 
 
-def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
-    vr, vc = view
+def local_view(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> tuple[Tensor, Tensor]:
+    """``(blocks, items)`` of the ``view`` window centred on the player (``[E, rows, cols]``)."""
     blocks = _local(s.map, s.position, view, int(C.BlockType.OUT_OF_BOUNDS))
     items = _local(s.item_map, s.position, view, int(C.ItemType.NONE))
+    return blocks, items
+
+
+def visible_tiles(s: GameState, items: Tensor, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
+    """``[E, rows, cols]`` bool: lit floors are seen whole; elsewhere 3 tiles around the player, 4 around a torch."""
+    vr, vc = view
+    rr = torch.arange(vr, device=s.device)[:, None] - vr // 2
+    cc = torch.arange(vc, device=s.device)[None, :] - vc // 2
+    near = (torch.maximum(rr.abs(), cc.abs()) <= 3).expand(s.num_envs, vr, vc)
+    torch_light = F.max_pool2d((items == int(C.ItemType.TORCH)).float()[:, None], 9, 1, 4)[:, 0] > 0
+    lit_floor = C.device_table("lit", s.device, C.LIT_FLOORS)[s.level]
+    return lit_floor[:, None, None] | near | torch_light
+
+
+def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
+    vr, vc = view
+    blocks, items = local_view(s, view)
     mobs = torch.zeros(s.num_envs, vr, vc, 5 * 8, device=s.device)
     corner = s.position - C.device_table(("half", vr, vc), s.device, [vr // 2, vc // 2])
     e = torch.arange(s.num_envs, device=s.device)
@@ -57,13 +74,7 @@ def render(s: GameState, view: tuple[int, int] = C.OBS_DIM) -> Tensor:
             seen = creatures.mask[:, slot] & (local[:, 0] >= 0) & (local[:, 0] < vr) & (local[:, 1] >= 0) & (local[:, 1] < vc)
             r, c = local[:, 0].clamp(0, vr - 1), local[:, 1].clamp(0, vc - 1)
             mobs[e, r, c, channel] = torch.maximum(mobs[e, r, c, channel], seen.float())
-    # lit floors are seen whole; on the others the player sees 3 tiles around itself and 4 around a torch
-    rr = torch.arange(vr, device=s.device)[:, None] - vr // 2
-    cc = torch.arange(vc, device=s.device)[None, :] - vc // 2
-    near = (torch.maximum(rr.abs(), cc.abs()) <= 3).expand(s.num_envs, vr, vc)
-    torch_light = F.max_pool2d((items == int(C.ItemType.TORCH)).float()[:, None], 9, 1, 4)[:, 0] > 0
-    lit_floor = C.device_table("lit", s.device, C.LIT_FLOORS)[s.level]
-    lit = (lit_floor[:, None, None] | near | torch_light).float()[..., None]
+    lit = visible_tiles(s, items, view).float()[..., None]
     tiles = torch.cat([F.one_hot(blocks, len(C.BlockType)).float(), F.one_hot(items, len(C.ItemType)).float(), mobs], -1)
     view_part = torch.cat([tiles * lit, lit], -1).flatten(1)
     z = torch.zeros(s.num_envs, device=s.device)

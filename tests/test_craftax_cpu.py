@@ -346,3 +346,53 @@ def test_bench_prints_env_steps_per_second(capsys, monkeypatch) -> None:  # noqa
     bench.main()
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["unit"] == "steps/s" and line["value"] > 0
+
+
+def test_pixel_renderer_layers_and_shading(tmp_path) -> None:  # noqa: ANN001
+    """Frames are the 9 x 11 view in tiles of P pixels; sprites from a folder replace the stand-ins;
+    sleep halves the brightness, night fades toward blue, unseen tiles are black."""
+    from torchvision.io import write_png
+
+    from priml_b200.baselines.craftax.game import constants as C
+    from priml_b200.baselines.craftax.game import world
+    from priml_b200.baselines.craftax.game.pixels import PixelRenderer
+
+    s = world.generate(3, generator=torch.Generator().manual_seed(0), device=torch.device("cpu"))
+    red = torch.zeros(3, 8, 8, dtype=torch.uint8)
+    red[0] = 255
+    write_png(red, str(tmp_path / "grass.png"))
+    r = PixelRenderer(block_pixels=8, sprite_dir=tmp_path)
+    assert r.found == ["grass.png"]
+    frame = r.render(s)
+    assert frame.shape == (3, 9 * 8, 11 * 8, 3) and frame.dtype == torch.uint8
+    assert torch.equal(frame, r.render(s))  # deterministic
+
+    from priml_b200.baselines.craftax.game.observation import local_view
+
+    blocks, _ = local_view(s)
+    grass = (blocks[0] == int(C.BlockType.GRASS)).nonzero()
+    assert len(grass) > 0
+    for row, col in grass.tolist()[:5]:
+        if (row, col) == (4, 5):
+            continue  # the player stands here
+        tile = frame[0, row * 8 : row * 8 + 8, col * 8 : col * 8 + 8]
+        # daylight may dim the frame a little, but grass stays red-dominated
+        assert (tile[..., 0].float() > tile[..., 1].float() + 50).all()
+
+    s.sleeping[1] = True
+    s.light[2] = 0.0
+    dimmed = r.render(s)
+    away = torch.ones(9 * 8, 11 * 8, dtype=torch.bool)
+    away[4 * 8 : 5 * 8, 5 * 8 : 6 * 8] = False  # the player's own tile shows the sleeping sprite
+    assert (dimmed[1].float() <= frame[1].float() * 0.5 + 1)[away].all()
+    night = torch.tensor([0, 16, 64], dtype=torch.float32)
+    assert ((dimmed[2].float() - night).abs() <= 1).all()  # fully dark surface is the night colour
+
+    # a player in a dark cave sees only the tiles near it
+    s.level[0] = 1
+    s.map[0] = s.floor_map[0, 1]
+    s.item_map[0] = torch.zeros_like(s.item_map[0])
+    cave = r.render(s)
+    assert cave[0, :8, :8].max() == 0  # the corner tile is 4+ tiles away: unseen
+    PixelRenderer.write_png(cave[0], tmp_path / "frame.png")
+    assert (tmp_path / "frame.png").stat().st_size > 0
