@@ -84,6 +84,9 @@ def _layout(strategy: str, world: int, tp: int) -> str:
         return f"dp{world // tp}xtp{tp}-sp" if world // tp > 1 else f"tp{world}-sp"
     if strategy == "ep":
         return f"ep{world}"
+    if strategy == "fused":
+        # ZeRO-2-like: optimizer state and fp32 master sharded, bf16 weights resident on every rank
+        return f"dp{world}-zero2"
     return f"fsdp{world}"
 
 

@@ -22,6 +22,7 @@ from priml_b200.config import Fig
 
 __all__ = [
     "AdversarialLoss",
+    "ClippedPolicyLoss",
     "DiffusionLoss",
     "LPIPS",
     "LPIPSLoss",
@@ -104,21 +105,6 @@ class WeightedSum:
         return out
 
 
-class DiffusionLoss:
-    """MSE between the model output and a diffusion target (``noise``, ``x0`` or ``v``)."""
-
-    class Config(Fig["DiffusionLoss"]):
-        target: str = "noise"
-        target_key: str = "target"
-
-    def __init__(self, config: Config) -> None:
-        self.target_key = config.target_key
-
-    def __call__(self, prediction: Tensor, **batch: Any) -> LossOutput:
-        err = (prediction.float() - batch[self.target_key].float()).square()
-        return {"loss": err.reshape(err.shape[0], -1).mean(-1)}
-
-
 class AdversarialLoss:
     """Generator loss of a GAN step (``priml/loss/gan.py:19-90``), per sample:
     ``adversarial_weight * BCE(D(G(z)), 1) + content_weight * mean |G(z) - real|``."""
@@ -140,18 +126,9 @@ class AdversarialLoss:
         return {"loss": self.adversarial_weight * adversarial + self.content_weight * content}
 
 
-def categorical_entropy(logits: Tensor, dim: int = -1) -> Tensor:
-    logp = F.log_softmax(logits.float(), dim=dim)
-    return -(logp.exp() * logp).sum(dim)
-
-
-def clipped_policy_loss(logp_new: Tensor, logp_old: Tensor, advantage: Tensor, clip: float = 0.2) -> Tensor:
-    """PPO clipped surrogate (negated, unreduced)."""
-    ratio = torch.exp(logp_new - logp_old)
-    return -torch.minimum(ratio * advantage, ratio.clamp(1 - clip, 1 + clip) * advantage)
-
-
 _ = math
 
 
+from priml_b200.loss.diffusion import DiffusionLoss  # noqa: E402
 from priml_b200.loss.lpips import LPIPS, LPIPSLoss  # noqa: E402
+from priml_b200.loss.policy_gradient import ClippedPolicyLoss, categorical_entropy, clipped_policy_loss  # noqa: E402
