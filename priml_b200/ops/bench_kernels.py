@@ -200,7 +200,12 @@ def main() -> None:
     ap.add_argument("--gemm-only", action="store_true")
     ap.add_argument("--profile", type=str, default="")
     ap.add_argument("--mx", action="store_true", help="MXFP8 GEMMs and quantizers only")
+    ap.add_argument("--decode", action="store_true", help="decode attention kernel and graph-replayed decode steps")
     args = ap.parse_args()
+    if args.decode:
+        for r in bench_decode():
+            print(json.dumps(r))
+        return
     if args.profile:
         profile_case(args.profile)
         return
@@ -253,6 +258,53 @@ def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int
     return rows
 
 
+def bench_decode() -> list[dict]:
+    """Decode attention (ours vs SDPA over the same cache) and Llama-1B decode steps (graph vs eager)."""
+    import torch.nn.functional as F
+
+    from priml_b200 import ops
+
+    _, hbm = _peaks()
+    rows = []
+    for b, h, hkv, t, d in ((1, 32, 8, 4096, 64), (16, 32, 8, 4096, 64), (64, 32, 8, 4096, 64), (16, 32, 8, 8192, 128)):
+        q = torch.randn(b, h, d, device="cuda", dtype=torch.bfloat16)
+        k = torch.randn(b, hkv, t, d, device="cuda", dtype=torch.bfloat16)
+        v = torch.randn(b, hkv, t, d, device="cuda", dtype=torch.bfloat16)
+        lengths = torch.full((b,), t, device="cuda", dtype=torch.int32)
+        nbytes = 2 * k.numel() * 2
+        t_ours = time_fn(lambda: ops.decode_attention(q, k, v, lengths), iters=20)
+        t_sdpa = time_fn(lambda: F.scaled_dot_product_attention(q[:, :, None], k, v, enable_gqa=True), iters=20)
+        rows.append({"case": "decode_attn", "B": b, "H": h, "Hkv": hkv, "T": t, "D": d, "ours_us": round(1e3 * t_ours, 1),
+                     "sdpa_us": round(1e3 * t_sdpa, 1), "ours_gbs": round(nbytes / t_ours / 1e6, 1),
+                     "ours_frac_hbm": round(nbytes / t_ours / 1e6 / hbm, 3)})  # fmt: skip
+
+    from priml_b200.inference import Decoder
+    from priml_b200.models.presets import llama_1b
+
+    torch.manual_seed(0)
+    model = llama_1b().make().cuda().to(torch.bfloat16).eval()
+    for batch, ctx in ((1, 1024), (64, 1024)):
+        for graph in (True, False):
+            dec = Decoder(model, batch=batch, max_seq=ctx + 64, cuda_graph=graph)
+            dec.prefill(torch.randint(0, 32768, (batch, ctx), device="cuda"))
+            tok = torch.zeros(batch, dtype=torch.long, device="cuda")
+            for _ in range(3):
+                dec.step(tok)
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = 32
+            s.record()
+            for _ in range(n):
+                dec.step(tok)
+            e.record()
+            torch.cuda.synchronize()
+            ms = s.elapsed_time(e) / n
+            rows.append({"case": "llama1b_decode_step", "batch": batch, "context": ctx, "cuda_graph": graph,
+                         "ms_per_step": round(ms, 3), "tokens_per_s": round(batch * 1e3 / ms, 1)})  # fmt: skip
+            del dec
+    return rows
+
+
 def profile_case(name: str) -> None:
     """Run one small instance of a kernel a few times (for an external profiler)."""
     from priml_b200.ops import native
@@ -281,6 +333,57 @@ def profile_case(name: str) -> None:
         dgu = torch.empty(16384, 3072, device="cuda", dtype=torch.bfloat16)
         for _ in range(3):
             n.gemm_swiglu_bwd(dy, wd, gu, dgu)
+    elif name == "memory":
+        # the memory-bound kernels of a training / decode step, each twice, on inputs larger than L2
+        from priml_b200 import ops
+        from priml_b200.models.rope import RoPE
+        from priml_b200.ops import functional as fn
+
+        x = torch.randn(65536, 2048, device="cuda", dtype=torch.bfloat16, requires_grad=True)  # 256 MiB
+        d = torch.randn_like(x, requires_grad=True)
+        w = torch.ones(2048, device="cuda", requires_grad=True)
+        for _ in range(2):
+            h, y = ops.add_rms_norm(x, d, w, 1e-5)
+            torch.autograd.backward((h, y), (torch.ones_like(h), torch.ones_like(y)))
+        del x, d, h, y
+        q = torch.randn(16, 4096, 32, 64, device="cuda", dtype=torch.bfloat16)  # 256 MiB
+        k = torch.randn(16, 4096, 8, 64, device="cuda", dtype=torch.bfloat16)
+        cos, sin = RoPE.Config(64, base=5e5).make().table(4096, torch.device("cuda"))
+        for _ in range(2):
+            ops.rotary(q, k, cos, sin)
+        del q, k
+        logits = torch.randn(16384, 32768, device="cuda", dtype=torch.bfloat16, requires_grad=True)  # 1 GiB
+        t = torch.randint(0, 32768, (16384,), device="cuda")
+        for _ in range(2):
+            ops.cross_entropy(logits, t).sum().backward()
+        del logits
+        xm = torch.randn(16384, 8192, device="cuda", dtype=torch.bfloat16)
+        for _ in range(2):
+            n.mx_quantize(xm, False)
+        del xm
+        qd = torch.randn(64, 32, 64, device="cuda", dtype=torch.bfloat16)
+        kc = torch.randn(64, 8, 4096, 64, device="cuda", dtype=torch.bfloat16)  # 2 x 256 MiB
+        vc = torch.randn_like(kc)
+        lengths = torch.full((64,), 4096, device="cuda", dtype=torch.int32)
+        for _ in range(2):
+            ops.decode_attention(qd, kc, vc, lengths)
+        del kc, vc
+        e, rows, c, hid = 8, 16384, 2048, 1024
+        xs = torch.randn(rows, c, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        up = (torch.randn(e, 2 * hid, c, device="cuda") * c**-0.5).requires_grad_()
+        down = (torch.randn(e, c, hid, device="cuda") * hid**-0.5).requires_grad_()
+        offsets = torch.arange(0, rows + 1, rows // e, device="cuda", dtype=torch.int32)
+        for _ in range(2):
+            fn.grouped_swiglu_mlp(xs, up, down, offsets).sum().backward()
+        del xs, up, down
+        from priml_b200.optimizers import FusedAdamW
+
+        params = [torch.nn.Parameter(torch.randn(4096, 4096, device="cuda")) for _ in range(4)]  # 64 M params
+        for p in params:
+            p.grad = torch.randn_like(p)
+        opt = FusedAdamW(params, lr=1e-3)
+        for _ in range(2):
+            opt.step()
     elif name in ("attn_fwd", "attn_bwd"):
         q = torch.randn(1, 4096, 32, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         k = torch.randn(1, 4096, 8, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
