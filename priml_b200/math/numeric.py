@@ -76,6 +76,10 @@ def matrix_signum_via_newtonschulz(
     dtype = x.dtype
     y = x.bfloat16()
     y = y / y.norm(dim=(-2, -1), keepdim=True).clamp(min=eps)
+    if y.is_cuda:
+        from priml_b200.ops.orthogonalize import newton_schulz_steps
+
+        return newton_schulz_steps(y, [(a, b, c)] * steps).to(dtype)
     tall = y.shape[-2] > y.shape[-1]
     if tall:
         y = y.transpose(-2, -1)
@@ -92,6 +96,10 @@ def polar_express(x: Tensor, steps: int = 5, coefficients=POLAR_EXPRESS_COEFFICI
     """Polar-Express orthogonalization in bf16 (norm scaled by 1.02 for safety)."""
     y = x.bfloat16()
     y = y / (y.norm(dim=(-2, -1), keepdim=True) * 1.02 + 1e-6)
+    if y.is_cuda:
+        from priml_b200.ops.orthogonalize import newton_schulz_steps
+
+        return newton_schulz_steps(y, coefficients[:steps])
     tall = y.size(-2) > y.size(-1)
     for a, b, c in coefficients[:steps]:
         if tall:

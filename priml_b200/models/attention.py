@@ -350,6 +350,13 @@ class SelfAttention(nn.Module):
                 cos, sin = self.rope(positions)
             q, k = RoPE.rotate(q, k, cos, sin)
 
+        attend = getattr(cache, "attend", None)
+        if attend is not None:
+            # a cache that attends itself (static buffers with device-side lengths)
+            out = attend(q, k, v, window=self.window).flatten(-2)
+            if self.norm_out is not None:
+                out = self.norm_out(out)
+            return self.proj_out(out), cache
         if cache is not None:
             kc, vc = cache.update(k.movedim(-3, -2), v.movedim(-3, -2))
             k, v = kc.movedim(-2, -3), vc.movedim(-2, -3)

@@ -23,6 +23,7 @@ __all__ = [
     "add_rms_norm",
     "attention",
     "cross_entropy",
+    "decode_attention",
     "grouped_swiglu_experts",
     "grouped_swiglu_mlp",
     "linear",
@@ -153,7 +154,55 @@ def swiglu(gate_up: Tensor) -> Tensor:
     return reference.swiglu(gate_up)
 
 
+def decode_attention(
+    q: Tensor,
+    k_cache: Tensor,
+    v_cache: Tensor,
+    lengths: Tensor,
+    *,
+    scale: float | None = None,
+    window: int | None = None,
+) -> Tensor:
+    """One query token per sequence against a KV cache with per-sequence lengths.
+
+    ``q`` is ``[B, H, D]``; the caches are ``[B, Hkv, T, D]`` whose first
+    ``lengths[b]`` rows are visible to sequence ``b`` (the query's own key
+    included); query head ``h`` reads KV head ``h // (H / Hkv)``. ``window``
+    hides keys more than ``window`` positions behind the query. The lengths stay
+    on the device, so a decode step that calls this needs no host sync and can be
+    captured in a CUDA graph. Returns ``[B, H, D]``.
+    """
+    if scale is None:
+        scale = q.shape[-1] ** -0.5
+    if (
+        use_native(q)
+        and q.dtype == torch.bfloat16
+        and k_cache.dtype == torch.bfloat16
+        and q.shape[-1] in (64, 128)
+        and v_cache.shape[-1] == q.shape[-1]
+    ):
+        return native().decode_attn(
+            q.contiguous(), k_cache, v_cache, lengths.to(torch.int32).contiguous(), float(scale),
+            -1 if window is None else int(window),
+        )  # fmt: skip
+    return reference.decode_attention(q, k_cache, v_cache, lengths, scale=float(scale), window=window)
+
+
 def cross_entropy(logits: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None) -> Tensor:
+    """Unreduced token CE in fp32 of ``[..., V]`` logits, optionally soft-capped by ``softcap * tanh(x / softcap)``.
+
+    bf16 CUDA logits with ``V % 8 == 0`` run the CE kernels (one read of the row for the
+    log-sum-exp, one read and one write for the gradient).
+    """
+    if (
+        use_native(logits)
+        and logits.dtype == torch.bfloat16
+        and logits.shape[-1] % 8 == 0
+        and (softcap is None or softcap > 0)
+    ):
+        from priml_b200.ops import functional
+
+        return functional.cross_entropy(logits, targets, ignore_index=ignore_index, softcap=softcap)
     return reference.cross_entropy(logits, targets, ignore_index=ignore_index, softcap=softcap)
 
 
@@ -165,8 +214,12 @@ def linear_cross_entropy(
     ignore_index: int = -100,
     softcap: float | None = None,
 ) -> Tensor:
-    """Unreduced CE of ``hidden @ weight.T`` without materializing the logits
-    (chunked over tokens on CUDA; fp32 log-sum-exp)."""
+    """Unreduced CE of ``hidden @ weight.T`` in fp32, optionally soft-capped.
+
+    On CUDA the bf16 logits are written once by the GEMM; the CE kernels read them
+    for the log-sum-exp (with the cap applied on the fly) and overwrite them with
+    d(logits) in the backward, so no fp32 or capped copy of the logits exists.
+    """
     if use_native(hidden) and _compute_dtype(hidden) == torch.bfloat16:
         from priml_b200.ops import functional
 

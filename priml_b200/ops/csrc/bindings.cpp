@@ -72,6 +72,29 @@ void gemm(const Tensor& A, const Tensor& B, Tensor& C, bool a_mn, bool b_mn, int
                 K, static_cast<int>(epi), nullptr, 0, status_ptr(), stream());
 }
 
+// C = alpha * (A @ B^T) + beta * X in bf16, with X [M, N] bf16 in C's row stride (epilogue 5; 2-CTA
+// tiles, so M and N of at least 256). C must not overlap A or B: other tiles still read them.
+void gemm_axpby(const Tensor& A, const Tensor& B, const Tensor& X, Tensor& C, bool a_mn, bool b_mn, double alpha,
+                double beta) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(X, "X");
+  check_cuda(C, "C");
+  PB_CHECK(A.scalar_type() == torch::kBFloat16 && B.scalar_type() == torch::kBFloat16 &&
+               X.scalar_type() == torch::kBFloat16 && C.scalar_type() == torch::kBFloat16,
+           "bf16 tensors");
+  const int M = a_mn ? A.size(1) : A.size(0);
+  const int K = a_mn ? A.size(0) : A.size(1);
+  const int N = b_mn ? B.size(1) : B.size(0);
+  PB_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "contraction sizes differ");
+  PB_CHECK(C.size(0) == M && C.size(1) == N && X.sizes() == C.sizes(), "C and X must be [M, N]");
+  PB_CHECK(row_stride(X) == row_stride(C), "X and C must share a row stride");
+  PB_CHECK(M >= 256 && N >= 256 && N % 8 == 0 && K > 0, "the scaled-add GEMM needs M, N >= 256, N % 8 == 0, K > 0");
+  const c10::cuda::CUDAGuard guard(A.device());
+  pb::gemm_bf16(A.data_ptr(), row_stride(A), a_mn, B.data_ptr(), row_stride(B), b_mn, C.data_ptr(), row_stride(C), M, N,
+                K, 5, X.data_ptr(), 0, status_ptr(), stream(), static_cast<float>(alpha), static_cast<float>(beta));
+}
+
 // h = silu(x @ Wg^T) * (x @ Wu^T) with W = [Wg; Wu] ([2H, K]); also writes the bf16 pre-activation gu [M, 2H].
 void gemm_swiglu(const Tensor& X, const Tensor& W, Tensor& H, Tensor& GU) {
   check_cuda(X, "X");
@@ -345,7 +368,7 @@ Tensor swiglu_bwd(const Tensor& gu, const Tensor& dh) {
   return dgu;
 }
 
-std::vector<Tensor> ce_fwd(const Tensor& logits, const Tensor& targets, int64_t ignore_index) {
+std::vector<Tensor> ce_fwd(const Tensor& logits, const Tensor& targets, int64_t ignore_index, double softcap) {
   PB_CHECK(logits.dim() == 2 && logits.scalar_type() == torch::kBFloat16 && logits.stride(1) == 1, "logits [R, V] bf16");
   const long long R = logits.size(0);
   const int V = logits.size(1);
@@ -355,13 +378,13 @@ std::vector<Tensor> ce_fwd(const Tensor& logits, const Tensor& targets, int64_t 
   PB_CHECK(logits.stride(0) % 8 == 0, "logits row stride must be a multiple of 8");
   if (R > 0)
     pb::ce_fwd(logits.data_ptr(), logits.stride(0), t.data_ptr<int64_t>(), loss.data_ptr<float>(), lse.data_ptr<float>(),
-               R, V, ignore_index, stream());
+               R, V, ignore_index, static_cast<float>(softcap), stream());
   return {loss, lse};
 }
 
 // Writes d(logits) into `out` (may alias logits).
 void ce_bwd(const Tensor& logits, const Tensor& targets, const Tensor& lse, const Tensor& g, Tensor& out,
-            int64_t ignore_index) {
+            int64_t ignore_index, double softcap) {
   const long long R = logits.size(0);
   const int V = logits.size(1);
   auto t = targets.to(torch::kInt64).contiguous();
@@ -370,7 +393,7 @@ void ce_bwd(const Tensor& logits, const Tensor& targets, const Tensor& lse, cons
   PB_CHECK(out.stride(0) == logits.stride(0), "out must share the logits layout");
   if (R > 0)
     pb::ce_bwd(logits.data_ptr(), logits.stride(0), t.data_ptr<int64_t>(), lse.data_ptr<float>(), gf.data_ptr<float>(),
-               g_stride, out.data_ptr(), R, V, ignore_index, stream());
+               g_stride, out.data_ptr(), R, V, ignore_index, static_cast<float>(softcap), stream());
 }
 
 // Multi-tensor optimizer plan: device-resident tensor table + chunk map, built once per parameter set.
@@ -484,6 +507,59 @@ std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, 
                D, static_cast<float>(scale), causal, static_cast<int>(window), status_ptr(), stream(),
                trace.has_value() ? trace->data_ptr<int>() : nullptr, Dv);
   return {o, lse};
+}
+
+// Decode attention: q [B, H, D] over caches [B, Hkv, T, D] (rows contiguous) with
+// int32 lengths [B] on the device; returns [B, H, D].
+Tensor decode_attn(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lengths, double scale,
+                   int64_t window) {
+  PB_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.is_contiguous(),
+           "q must be contiguous CUDA bf16 [B, H, D]");
+  const int B = q.size(0), H = q.size(1), D = q.size(2);
+  PB_CHECK(D == 64 || D == 128, "decode attention covers head dims 64 and 128");
+  for (const Tensor* t : {&k, &v}) {
+    PB_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 4, "caches must be CUDA bf16 [B, Hkv, T, D]");
+    PB_CHECK(t->size(0) == B && t->size(3) == D && t->stride(3) == 1 && t->stride(2) == D,
+             "cache rows must be contiguous with the query's head dim");
+    PB_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0 && t->stride(0) % 8 == 0 && t->stride(1) % 8 == 0,
+             "cache base and strides must be 16-byte aligned");
+  }
+  PB_CHECK(k.sizes() == v.sizes(), "k and v caches differ in shape");
+  const int Hkv = k.size(1), T = k.size(2);
+  PB_CHECK(Hkv > 0 && H % Hkv == 0, "query heads must be a multiple of the KV heads");
+  PB_CHECK(lengths.is_cuda() && lengths.scalar_type() == torch::kInt32 && lengths.numel() == B && lengths.is_contiguous(),
+           "lengths must be contiguous int32 [B] on the device");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty_like(q);
+  if (q.numel() == 0) return out;
+  const int group = H / Hkv;
+  const int splits = pb::decode_attn_splits(B, H, group, T, pb::device_sm_count());
+  Tensor part_acc, part_ml;
+  if (splits > 1) {
+    part_acc = torch::empty({static_cast<long long>(B) * H * splits * D}, q.options().dtype(torch::kFloat32));
+    part_ml = torch::empty({static_cast<long long>(B) * H * splits * 2}, q.options().dtype(torch::kFloat32));
+  }
+  pb::DecodeAttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = static_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = static_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.k_sb = k.stride(0);
+  p.k_sh = k.stride(1);
+  p.v_sb = v.stride(0);
+  p.v_sh = v.stride(1);
+  p.lengths = lengths.data_ptr<int>();
+  p.out = static_cast<__nv_bfloat16*>(out.data_ptr());
+  p.part_acc = splits > 1 ? part_acc.data_ptr<float>() : nullptr;
+  p.part_ml = splits > 1 ? part_ml.data_ptr<float>() : nullptr;
+  p.H = H;
+  p.group = group;
+  p.T = T;
+  p.splits = splits;
+  p.chunk = (T + splits - 1) / splits;
+  p.window = static_cast<int>(window);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  pb::decode_attn(p, B, D, stream());
+  return out;
 }
 
 // (dq, dk, dv) in the layouts of q / k / v (contiguous).
@@ -993,6 +1069,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM: C (op)= A B^T", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epi"));
   m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 GEMM with fused SwiGLU epilogue");
+  m.def("gemm_axpby", &gemm_axpby, "tcgen05 GEMM C = alpha * A B^T + beta * X (bf16)", py::arg("A"), py::arg("B"),
+        py::arg("X"), py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("alpha"), py::arg("beta"));
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, "tcgen05 GEMM dy @ W_down with the SwiGLU backward in the epilogue");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
@@ -1001,8 +1079,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope", &rope);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
-  m.def("ce_fwd", &ce_fwd);
-  m.def("ce_bwd", &ce_bwd);
+  m.def("ce_fwd", &ce_fwd, "token CE over bf16 logits -> (loss, lse); softcap > 0 caps the logits first",
+        py::arg("logits"), py::arg("targets"), py::arg("ignore_index"), py::arg("softcap") = 0.0);
+  m.def("ce_bwd", &ce_bwd, "d(logits) of ce_fwd, written into out (may alias logits)", py::arg("logits"),
+        py::arg("targets"), py::arg("lse"), py::arg("g"), py::arg("out"), py::arg("ignore_index"),
+        py::arg("softcap") = 0.0);
+  m.def("decode_attn", &decode_attn, "one-token decode attention over a KV cache with device lengths",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("lengths"), py::arg("scale"), py::arg("window") = -1);
   m.def("attn_fwd", &attn_fwd, "flash attention forward (tcgen05); trace: optional int32 [8 * CTAs] progress record",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("causal"), py::arg("window"),
         py::arg("trace") = py::none());

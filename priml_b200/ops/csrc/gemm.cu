@@ -258,7 +258,7 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   // per epilogue warp: streams x (32 rows x 32 columns)
   static constexpr int kChunkBytes = (EPI == 1 || EPI == 2) ? 4096 : 2048;
-  static constexpr int kStreams = EPI == 3 ? 3 : (EPI == 4 ? 2 : 1);
+  static constexpr int kStreams = EPI == 3 ? 3 : (EPI == 4 ? 2 : 1);  // epilogue 5 reuses its one buffer
   static constexpr int kStgPerWarp = TOUT ? kStreams * kChunkBytes : 0;
   static constexpr int kSmemBytes = kStages * kStageBytes + kPairEpiWarps * kStgPerWarp + 1024 + 256;
   static_assert(kSmemBytes <= 232448, "pair GEMM shared memory exceeds the per-CTA limit");
@@ -419,6 +419,60 @@ __device__ __forceinline__ void epilogue_swiglu_bwd_tile(const GemmParams& p, ui
     if (lane == 0) {
       tma_store_2d(tmDG, stg, col, row0);
       tma_store_2d(tmDU, stg + 2048, col, row0);
+      tma_store_commit();
+    }
+  }
+}
+
+// Scaled-add epilogue: the matching 32 x 32 chunk of aux is fetched one chunk ahead with
+// coalesced 16-byte loads (lane l: rows l / 4 + 8 j, column group l % 4), handed to the lane
+// that owns each row through the warp's staging buffer, combined with the accumulator row,
+// and the bf16 result leaves through the same buffer as a bulk tensor store.
+__device__ __forceinline__ void axpby_prefetch(const GemmParams& p, int row0, int col, int lane, uint4 (&x)[4]) {
+  const __nv_bfloat16* aux = static_cast<const __nv_bfloat16*>(p.aux);
+  const int cc = col + (lane & 3) * 8;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = row0 + (lane >> 2) + 8 * j;
+    x[j] = (r < p.M && cc < p.N) ? __ldg(reinterpret_cast<const uint4*>(aux + static_cast<long long>(r) * p.ldc + cc))
+                                 : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+__device__ __forceinline__ void epilogue_axpby_tile(const GemmParams& p, uint32_t t_base, int row0, int nb, int c_lo,
+                                                    int c_hi, uint8_t* stg, int lane, uint4 (&x)[4],
+                                                    const CUtensorMap* tmC) {
+  constexpr int TN = 256;
+#pragma unroll 1
+  for (int c = c_lo; c < c_hi; c += 32) {
+    const int col = nb * TN + c;
+    if (lane == 0) tma_store_wait_read();  // the previous chunk's store has read the buffer
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = (lane >> 2) + 8 * j;
+      *reinterpret_cast<uint4*>(stg + r * 64 + swz_chunk<4>(r, lane & 3) * 16) = x[j];
+    }
+    __syncwarp();
+    uint32_t xw[16];
+    load_row<4>(stg, lane, xw);
+    __syncwarp();
+    if (c + 32 < c_hi) axpby_prefetch(p, row0, col + 32, lane, x);
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(t_base + c, v);
+    tmem_wait_ld();
+    uint32_t out[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[j]));
+      out[j] = pack_bf16x2(fmaf(p.alpha, __uint_as_float(v[2 * j]), p.beta * a.x),
+                           fmaf(p.alpha, __uint_as_float(v[2 * j + 1]), p.beta * a.y));
+    }
+    stage_row<4>(stg, lane, out);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, stg, col, row0);
       tma_store_commit();
     }
   }
@@ -626,11 +680,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
       [[maybe_unused]] uint4 pre_g[4], pre_u[4];
       if constexpr (TOUT && EPI == 4) swiglu_bwd_prefetch(p, row0, nb * TN + c_lo, lane, pre_g, pre_u);
+      if constexpr (TOUT && EPI == 5) axpby_prefetch(p, row0, nb * TN + c_lo, lane, pre_g);
       if (!mbar_wait_warp(&tfull[b], acc_phase, p.status, kTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + b * TN;
       if constexpr (TOUT && EPI == 4) {
         epilogue_swiglu_bwd_tile(p, t_row, row0, nb, c_lo, c_hi, my_stg, lane, pre_g, pre_u, &tmC, &tmG);
+      } else if constexpr (TOUT && EPI == 5) {
+        epilogue_axpby_tile(p, t_row, row0, nb, c_lo, c_hi, my_stg, lane, pre_g, &tmC);
       } else if constexpr (TOUT) {
         epilogue_tma_tile<EPI>(t_row, row0, nb, c_lo, c_hi, my_stg, lane, &tmC, &tmG, &tmU);
       } else {
@@ -725,6 +782,11 @@ bool make_out_maps(int epi, void* C, long long ldc, int M, int N, const void* au
     make_tmap_2d_bf16_sw64(tu, gu + H, H, M, 2 * H, 32, 32);
     return true;
   }
+  if (epi == 5) {
+    if ((ldc * 2) % 16 != 0 || N % 8 != 0 || !aligned(aux)) return false;
+    make_tmap_2d_bf16_sw64(tc, C, N, M, ldc, 32, 32);
+    return true;
+  }
   if (epi == 4) {
     // C = dgu [M, 2H]: dgate and dup views; aux = gu read with 16-byte loads
     const long long H = swiglu_h;
@@ -744,6 +806,17 @@ bool tma_store_enabled() {
     return e == nullptr || e[0] != '0';
   }();
   return on;
+}
+
+// Epilogue 5 exists only as the 2-CTA kernel with bulk tensor stores.
+template <bool A_MN, bool B_MN>
+void launch_pair_axpby(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, int num_sms, cudaStream_t stream) {
+  CUtensorMap tc{}, tg{}, tu{};
+  p.splits = 1;
+  if (!make_out_maps(5, p.C, p.ldc, p.M, p.N, p.aux, 0, &tc, &tg, &tu)) {
+    throw std::invalid_argument("gemm epilogue 5 needs 16-byte aligned C / aux rows and N % 8 == 0");
+  }
+  launch_pair_k<A_MN, B_MN, 5, true>(ta, tb, tc, tg, tu, p, num_sms, stream);
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -783,10 +856,12 @@ static bool pair_gemm_enabled() {
 // lda / ldb are the row strides (elements) of A and B as stored.
 void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
                long long ldc, int M, int N, int K, int epi, const void* aux, int swiglu_h, int* status,
-               cudaStream_t stream) {
+               cudaStream_t stream, float alpha, float beta) {
   const int num_sms = device_sm_count();
   CUtensorMap ta, tb;
   GemmParams p{M, N, K, C, ldc, aux, status, swiglu_h};
+  p.alpha = alpha;
+  p.beta = beta;
   // 2-CTA 256 x 256 tiles once the problem has enough of them; 1-CTA 128 x 256 otherwise.
   const bool pair = M >= 256 && N >= 256 && pair_gemm_enabled();
   // A tile: 128 (M) x 64 (K) per CTA in both kernels.
@@ -821,6 +896,19 @@ void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long
     make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, BK);
   } else {
     make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, pair ? 128 : BN);
+  }
+  if (epi == 5) {
+    if (!pair) throw std::invalid_argument("gemm epilogue 5 needs M >= 256 and N >= 256 (2-CTA tiles)");
+    if (a_mn && b_mn) {
+      launch_pair_axpby<true, true>(ta, tb, p, num_sms, stream);
+    } else if (a_mn) {
+      launch_pair_axpby<true, false>(ta, tb, p, num_sms, stream);
+    } else if (b_mn) {
+      launch_pair_axpby<false, true>(ta, tb, p, num_sms, stream);
+    } else {
+      launch_pair_axpby<false, false>(ta, tb, p, num_sms, stream);
+    }
+    return;
   }
 #define PB_DISPATCH(AM, BMJ)                                                                  \
   if (pair) {                                                                                 \

@@ -30,6 +30,8 @@ struct GemmParams {
   int* status;
   int num_n_half;        // fused SwiGLU: H (gate/up split point in B rows)
   int splits = 1;        // split-K factor (pair kernel, fp32 reduce-add epilogue only)
+  float alpha = 1.f;     // epilogue 5: C = alpha * acc + beta * aux (aux bf16 with row stride ldc)
+  float beta = 0.f;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {

@@ -30,10 +30,11 @@ void make_tmap_2d_u8(CUtensorMap* map, const void* base, long long inner, long l
 void make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long inner, long long mid, long long outer,
                        long long mid_stride, long long outer_stride, int box_inner, int box_mid, bool swizzle128);
 
-// GEMM: C[M,N] (op)= sum_k A(m,k) B(n,k). epi: 0 bf16, 1 fp32, 2 fp32 +=, 3 fused SwiGLU.
+// GEMM: C[M,N] (op)= sum_k A(m,k) B(n,k). epi: 0 bf16, 1 fp32, 2 fp32 +=, 3 fused SwiGLU,
+// 4 SwiGLU backward, 5 bf16 C = alpha * acc + beta * aux (aux: bf16 rows of stride ldc).
 void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
                long long ldc, int M, int N, int K, int epi, const void* aux, int swiglu_h, int* status,
-               cudaStream_t stream);
+               cudaStream_t stream, float alpha = 1.f, float beta = 0.f);
 
 // Grouped expert GEMM over 128-row-aligned expert segments (device offsets [experts + 1]).
 // mode 0: C[r] = A[r] @ B_e^T (B stacked per expert, b_rows rows each; epi 0, 1, 3, 4);
@@ -71,10 +72,13 @@ void swiglu_bwd(const void* gu, const void* dh, void* dgu, long long R, int H, c
 
 // Cross-entropy over bf16 logits [R, V] (row stride ld): loss[R] (fp32), lse[R];
 // ignore_index rows get loss 0. Backward writes d(logits) = (softmax - onehot) * g[r] in bf16.
+// Row-wise token cross-entropy over bf16 logits with an fp32 log-sum-exp. softcap > 0 applies
+// z = softcap * tanh(x / softcap) to every logit first (and its derivative in the backward).
 void ce_fwd(const void* logits, long long ld, const int64_t* targets, float* loss, float* lse, long long R, int V,
-            long long ignore_index, cudaStream_t stream);
+            long long ignore_index, float softcap, cudaStream_t stream);
 void ce_bwd(const void* logits, long long ld, const int64_t* targets, const float* lse, const float* g,
-            long long g_stride, void* dlogits, long long R, int V, long long ignore_index, cudaStream_t stream);
+            long long g_stride, void* dlogits, long long R, int V, long long ignore_index, float softcap,
+            cudaStream_t stream);
 
 // Multi-tensor AdamW. Tensor descriptors live in device memory (see AdamTensor).
 struct AdamTensor {
@@ -240,5 +244,23 @@ void tp_gemm_rs(const TpGemmParams& p, const void* A, long long lda, const void*
                 long long ldo, int grid, int reduce_grid, unsigned long long done_target, cudaStream_t stream);
 void tp_wait(const void* signal_local, int word, unsigned long long target, long long timeout_ns, int* status,
              cudaStream_t stream);
+
+// Decode attention (decode_attention.cu): one query token per sequence over a KV
+// cache with per-sequence device lengths. Element strides; cache rows contiguous.
+struct DecodeAttnParams {
+  const __nv_bfloat16* q;  // [B, H, D]
+  const __nv_bfloat16* k;  // [B, Hkv, T, D]
+  const __nv_bfloat16* v;
+  long long k_sb, k_sh, v_sb, v_sh;
+  const int* lengths;      // [B] keys visible to the query, its own included
+  __nv_bfloat16* out;      // [B, H, D]
+  float* part_acc;         // [B, H, splits, D] (splits > 1)
+  float* part_ml;          // [B, H, splits, 2]
+  int H, group, T, splits, chunk, window;
+  float scale_log2;        // softmax scale * log2(e)
+};
+int decode_attn_heads_per_cta(int group);
+int decode_attn_splits(int B, int H, int group, int T, int sm_count);
+void decode_attn(const DecodeAttnParams& p, int B, int D, cudaStream_t stream);
 
 }  // namespace pb

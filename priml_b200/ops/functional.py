@@ -425,16 +425,25 @@ def attention(q: Tensor, k: Tensor, v: Tensor, *, causal: bool, scale: float | N
 
 # --------------------------------------------------------------------------- loss
 class _LinearCE(torch.autograd.Function):
+    """CE of ``hidden @ weight.T``: one bf16 logits buffer, fp32 log-sum-exp, d(logits) written in place.
+
+    ``softcap`` > 0 bounds each logit by ``softcap * tanh(x / softcap)`` inside the
+    CE kernels (``priml/model/softcap.py:89-94`` followed by the loss of
+    ``priml/baselines/nanochat/train_step.py:43-79``), so the capped logits are
+    never stored.
+    """
+
     @staticmethod
-    def forward(ctx, h: Tensor, weight: Tensor, targets: Tensor, ignore_index: int) -> Tensor:  # type: ignore[override]
+    def forward(ctx, h: Tensor, weight: Tensor, targets: Tensor, ignore_index: int, softcap: float) -> Tensor:  # type: ignore[override]
         h2 = _as_bf16_2d(h)
         w16 = bf16_shadow(weight)
         logits = gemm(h2, w16)
         t = targets.reshape(-1)
-        loss, lse = native().ce_fwd(logits, t, ignore_index)
+        loss, lse = native().ce_fwd(logits, t, ignore_index, softcap)
         ctx.save_for_backward(h2, w16, logits, t, lse)
         ctx.weight = weight if grad_sink(weight) is not None else None
         ctx.ignore_index = ignore_index
+        ctx.softcap = softcap
         ctx.h_shape = h.shape
         ctx.h_dtype = h.dtype
         ctx.w_dtype = weight.dtype
@@ -446,7 +455,8 @@ class _LinearCE(torch.autograd.Function):
         gf = g.reshape(-1).float()
         if gf.stride(0) == 0:
             gf = gf[:1]
-        native().ce_bwd(logits, t, lse, gf.contiguous(), logits, ctx.ignore_index)  # in place: logits -> dlogits
+        # in place: logits -> dlogits
+        native().ce_bwd(logits, t, lse, gf.contiguous(), logits, ctx.ignore_index, ctx.softcap)
         dh = dw = None
         if ctx.needs_input_grad[0]:
             dh = gemm(logits, w16, b_mn=True).view(ctx.h_shape)
@@ -454,17 +464,46 @@ class _LinearCE(torch.autograd.Function):
                 dh = dh.to(ctx.h_dtype)
         if ctx.needs_input_grad[1]:
             dw = wgrad(ctx.weight if ctx.weight is not None else w16, logits, h2, ctx.w_dtype)
-        return dh, dw, None, None
+        return dh, dw, None, None, None
 
 
 def linear_cross_entropy(
     hidden: Tensor, weight: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None
 ) -> Tensor:
-    if softcap is not None or weight.shape[0] % 8 != 0 or hidden.shape[-1] % 8 != 0:
+    if weight.shape[0] % 8 != 0 or hidden.shape[-1] % 8 != 0 or (softcap is not None and not softcap > 0):
         from priml_b200.ops import reference
 
         return reference.linear_cross_entropy(hidden, weight, targets, ignore_index=ignore_index, softcap=softcap)
-    return _LinearCE.apply(hidden, weight, targets, ignore_index)
+    return _LinearCE.apply(hidden, weight, targets, ignore_index, float(softcap or 0.0))
+
+
+class _CE(torch.autograd.Function):
+    """Token CE over given bf16 logits (optionally soft-capped); d(logits) comes back in bf16."""
+
+    @staticmethod
+    def forward(ctx, logits: Tensor, targets: Tensor, ignore_index: int, softcap: float) -> Tensor:  # type: ignore[override]
+        l2 = logits.reshape(-1, logits.shape[-1])
+        if l2.stride(-1) != 1 or l2.stride(0) % 8 != 0:
+            l2 = l2.contiguous()
+        t = targets.reshape(-1)
+        loss, lse = native().ce_fwd(l2, t, ignore_index, softcap)
+        ctx.save_for_backward(l2, t, lse)
+        ctx.ignore_index, ctx.softcap, ctx.shape = ignore_index, softcap, logits.shape
+        return loss.view(targets.shape)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):  # type: ignore[override]
+        l2, t, lse = ctx.saved_tensors
+        gf = g.reshape(-1).float()
+        if gf.stride(0) == 0:
+            gf = gf[:1]
+        d = torch.empty_like(l2)
+        native().ce_bwd(l2, t, lse, gf.contiguous(), d, ctx.ignore_index, ctx.softcap)
+        return d.view(ctx.shape), None, None, None
+
+
+def cross_entropy(logits: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None) -> Tensor:
+    return _CE.apply(logits, targets, ignore_index, float(softcap or 0.0))
 
 
 # --------------------------------------------------------------------------- MoE

@@ -78,6 +78,25 @@ def swiglu(gate_up: Tensor) -> Tensor:
     return F.silu(gate) * up
 
 
+def decode_attention(
+    q: Tensor, k_cache: Tensor, v_cache: Tensor, lengths: Tensor, *, scale: float, window: int | None = None
+) -> Tensor:
+    """fp32 oracle of the decode kernel: ``[B, H, D]`` queries over ``[B, Hkv, T, D]`` caches."""
+    b, h, _ = q.shape
+    hkv, t = k_cache.shape[1], k_cache.shape[2]
+    kf = k_cache.float().repeat_interleave(h // hkv, dim=1)
+    vf = v_cache.float().repeat_interleave(h // hkv, dim=1)
+    s = torch.einsum("bhd,bhtd->bht", q.float(), kf) * scale
+    pos = torch.arange(t, device=q.device)
+    n = lengths.to(device=q.device, dtype=torch.long).clamp(0, t)[:, None]
+    ok = pos[None, :] < n
+    if window is not None:
+        ok &= pos[None, :] >= n - 1 - window
+    s = s.masked_fill(~ok[:, None, :], float("-inf"))
+    p = torch.nan_to_num(s.softmax(dim=-1), nan=0.0)  # an empty row gives zeros
+    return torch.einsum("bht,bhtd->bhd", p, vf).to(q.dtype)
+
+
 def cross_entropy(logits: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None) -> Tensor:
     """Unreduced token cross-entropy computed in fp32."""
     lf = logits.float()

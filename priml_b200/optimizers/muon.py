@@ -22,7 +22,7 @@ from torch.nn import Parameter
 from torch.optim import Optimizer
 
 from priml_b200.config import Fig
-from priml_b200.math.numeric import POLAR_EXPRESS_COEFFICIENTS, matrix_signum_via_newtonschulz
+from priml_b200.math.numeric import POLAR_EXPRESS_COEFFICIENTS, matrix_signum_via_newtonschulz, polar_express
 
 __all__ = [
     "Muon",
@@ -151,16 +151,7 @@ def _normuon_update(
     (norm preserving), cautious decoupled decay -- all on stacked ``[N, R, C]``."""
     mbuf.lerp_(grads, 1 - momentum)
     upd = grads.lerp_(mbuf, momentum)
-    x = upd.bfloat16()
-    x = x / (x.norm(dim=(-2, -1), keepdim=True) * 1.02 + 1e-6)
-    if x.size(-2) > x.size(-1):
-        for a, b, c in coefficients[:ns_steps]:
-            gram = x.mT @ x
-            x = a * x + x @ (b * gram + c * (gram @ gram))
-    else:
-        for a, b, c in coefficients[:ns_steps]:
-            gram = x @ x.mT
-            x = a * x + (b * gram + c * (gram @ gram)) @ x
+    x = polar_express(upd, steps=ns_steps, coefficients=coefficients)
     energy = x.float().square().mean(dim=reduce_dim, keepdim=True)
     width = x.size(reduce_dim)
     before = (energy.sum(dim=(-2, -1), keepdim=True) * width).sqrt()

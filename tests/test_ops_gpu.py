@@ -210,6 +210,42 @@ def test_swiglu_and_ce() -> None:
     assert _rel_err(w.grad, wr.grad) < 3e-2
 
 
+@pytest.mark.parametrize("cap", [None, 15.0, 4.0])
+@pytest.mark.parametrize("v", [1000, 8200])
+def test_softcapped_cross_entropy_matches_fp32(cap, v: int) -> None:  # noqa: ANN001
+    """Logit-level and fused-linear CE, capped and uncapped, against fp32 torch on the same bf16 logits."""
+    from priml_b200 import ops
+
+    torch.manual_seed(11)
+    logits = (torch.randn(257, v, device="cuda") * 6).to(torch.bfloat16).requires_grad_()
+    t = torch.randint(0, v, (257,), device="cuda")
+    t[3] = -100
+    loss = ops.cross_entropy(logits, t, softcap=cap)
+    (loss * torch.linspace(0.5, 1.5, 257, device="cuda")).sum().backward()
+    lf = logits.detach().float().requires_grad_()
+    z = cap * torch.tanh(lf / cap) if cap is not None else lf
+    lr = F.cross_entropy(z, t, reduction="none")
+    (lr * torch.linspace(0.5, 1.5, 257, device="cuda")).sum().backward()
+    assert float((loss - lr).abs().max()) < 2e-3 * (1 + float(lr.abs().max()))
+    assert loss[3] == 0 and logits.grad[3].abs().max() == 0
+    assert _rel_err(logits.grad, lf.grad) < 1e-2
+
+    hid = torch.randn(300, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(v, 256, device="cuda") / 4).requires_grad_()
+    tt = torch.randint(0, v, (300,), device="cuda")
+    loss = ops.linear_cross_entropy(hid, w, tt, softcap=cap)
+    loss.mean().backward()
+    hr = hid.detach().float().requires_grad_()
+    wr = w.detach().to(torch.bfloat16).float().requires_grad_()
+    zl = (hr @ wr.T).to(torch.bfloat16).float()
+    zl = cap * torch.tanh(zl / cap) if cap is not None else zl
+    lr = F.cross_entropy(zl, tt, reduction="none")
+    lr.mean().backward()
+    assert _rel_err(loss, lr) < 1e-2
+    assert _rel_err(hid.grad, hr.grad) < 3e-2
+    assert _rel_err(w.grad, wr.grad) < 3e-2
+
+
 def test_adamw_plan_matches_reference() -> None:
     from priml_b200.ops import reference
 
@@ -313,3 +349,37 @@ def test_grouped_swiglu_experts_fwd_bwd(t: int, k: int, e: int, c: int, h: int) 
     assert _rel_err(ddown, rdown) < 3e-2
     assert float(dup[e - 1].abs().max()) == 0.0 and float(ddown[e - 1].abs().max()) == 0.0
     assert int(native().read_status(True)) == 0
+
+
+@pytest.mark.parametrize("a_mn,b_mn", LAYOUTS)
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (304, 520, 200), (1024, 2048, 512), (768, 3072, 768)])
+def test_gemm_scaled_add_epilogue(a_mn: bool, b_mn: bool, m: int, n: int, k: int) -> None:
+    """C = alpha * A @ B^T + beta * X against fp32 torch on the same bf16 operands."""
+    torch.manual_seed(m + n + k)
+    a = torch.randn(k, m, device="cuda").to(torch.bfloat16) if a_mn else torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    b = torch.randn(k, n, device="cuda").to(torch.bfloat16) if b_mn else torch.randn(n, k, device="cuda").to(torch.bfloat16)
+    x = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+    c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _native().gemm_axpby(a, b, x, c, a_mn, b_mn, -0.75, 1.5)
+    af = a.float().T if a_mn else a.float()
+    bf = b.float() if b_mn else b.float().T
+    ref = -0.75 * (af @ bf) + 1.5 * x.float()
+    assert _rel_err(c, ref) < 1e-2
+
+
+@pytest.mark.parametrize("shape", [(4, 768, 3072), (2, 2048, 512), (1, 1024, 1024), (3, 300, 200)])
+def test_newton_schulz_chain_matches_fp32(shape: tuple[int, ...]) -> None:
+    """The tcgen05 Polar-Express chain (wide, tall, square, and a shape the torch path takes)
+    against the same polynomial in fp32; its output is near-orthogonal."""
+    from priml_b200.math.numeric import POLAR_EXPRESS_COEFFICIENTS
+    from priml_b200.ops.orthogonalize import newton_schulz_reference, newton_schulz_steps
+
+    torch.manual_seed(sum(shape))
+    x = torch.randn(*shape, device="cuda")
+    y = (x / (x.norm(dim=(-2, -1), keepdim=True) * 1.02 + 1e-6)).to(torch.bfloat16)
+    out = newton_schulz_steps(y, POLAR_EXPRESS_COEFFICIENTS)
+    ref = newton_schulz_reference(y.float(), POLAR_EXPRESS_COEFFICIENTS)
+    assert out.shape == y.shape and out.dtype == torch.bfloat16
+    assert _rel_err(out, ref) < 6e-2
+    sv = torch.linalg.svdvals(out.float())
+    assert float(sv.max()) < 1.3 and float(sv.median()) > 0.7
