@@ -60,8 +60,10 @@ def _parse() -> argparse.Namespace:
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default: the config's)")
     ap.add_argument("--layers", type=int, default=None, help="decoder layers (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--strategy", choices=["auto", "fused", "fsdp2", "tp", "ep", "single"], default="auto",
-                    help="auto: fused-collective sharding for N>1, single-GPU for N=1; "
+    ap.add_argument("--strategy", choices=["auto", "fused", "fused-shard", "fsdp2", "tp", "ep", "single"],
+                    default="auto",
+                    help="auto: fused-collective sharding for N>1, single-GPU for N=1; fused-shard: the same with "
+                    "1/N of the bf16 weights per rank, each block gathered a block ahead of use; "
                     "tp: sequence-parallel tensor parallelism on the fused NVLink GEMMs")
     ap.add_argument("--ref-compile", choices=["auto", "on", "off"], default="auto",
                     help="reference arm: auto runs the reference's stock torch.compile path and falls back to its "
@@ -87,7 +89,20 @@ def _layout(strategy: str, world: int, tp: int) -> str:
     if strategy == "fused":
         # ZeRO-2-like: optimizer state and fp32 master sharded, bf16 weights resident on every rank
         return f"dp{world}-zero2"
+    if strategy == "fused-shard":
+        return f"fsdp{world}"
     return f"fsdp{world}"
+
+
+def _memory_note(step: Any, dev: Any) -> dict[str, Any]:
+    """Peak caching-allocator memory, and the bf16 weight bytes per parameter a sharded strategy keeps."""
+    import torch
+
+    note: dict[str, Any] = {"peak_torch_alloc_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 2)}
+    st = getattr(getattr(step, "parallelism", None), "state", None)
+    if st is not None and hasattr(st, "weight_bytes"):
+        note["bf16_weight_bytes_per_param"] = round(st.weight_bytes() / st.total, 3)
+    return note
 
 
 def _reference_unavailable(why: str) -> None:
@@ -466,6 +481,7 @@ def main() -> None:
     vocab = shape.vocab
     parallel = {
         "fused": lambda: FusedFullySharded.Config(),
+        "fused-shard": lambda: FusedFullySharded.Config(shard_params=True),
         "fsdp2": lambda: FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True),
         "tp": lambda: FusedSequenceParallel.Config(),
         "ep": lambda: ExpertParallel.Config(),
@@ -607,6 +623,9 @@ def main() -> None:
             "strategy": {
                 "fused": "sharded fp32 master + Adam state, resident bf16 weights; reduce-scatter, clip, AdamW and "
                 "weight all-gather in hand-written NVLink peer-memory kernels",
+                "fused-shard": "sharded fp32 master, Adam state AND bf16 weights; each block's weights gathered by "
+                "peer copy-engine copies a block ahead of its forward and backward into two rotating windows; "
+                "reduce-scatter, clip and AdamW in hand-written NVLink peer-memory kernels",
                 "fsdp2": "torch FSDP2 fully_shard over NCCL (bf16 params, fp32 reduce)",
                 "tp": "sequence-parallel tensor parallelism: all-gather GEMM and GEMM reduce-scatter fused over "
                 "NVLink peer memory; replicated grads averaged once per step",
@@ -615,6 +634,7 @@ def main() -> None:
                 "single": "one GPU, fused AdamW",
             }[strategy],
             "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",
+            "memory": _memory_note(step, dev),
         },
         "clocks": clocks.summary(),
         "gpu_launches": launches,

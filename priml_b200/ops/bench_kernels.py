@@ -201,7 +201,12 @@ def main() -> None:
     ap.add_argument("--profile", type=str, default="")
     ap.add_argument("--mx", action="store_true", help="MXFP8 GEMMs and quantizers only")
     ap.add_argument("--decode", action="store_true", help="decode attention kernel and graph-replayed decode steps")
+    ap.add_argument("--ns", action="store_true", help="Newton-Schulz / Polar-Express chains vs the torch path")
     args = ap.parse_args()
+    if args.ns:
+        for r in bench_newton_schulz():
+            print(json.dumps(r))
+        return
     if args.decode:
         for r in bench_decode():
             print(json.dumps(r))
@@ -255,6 +260,28 @@ def bench_attention(b: int = 4, s: int = 4096, h: int = 32, hkv: int = 8, d: int
         rows.append({"case": f"attn.{name}", "B": b, "S": s, "H": h, "Hkv": hkv, "D": d, "Dv": dv, "fwd_ms": round(t_f, 3),
                      "fwd_tflops": round(flops_f / t_f / 1e9, 1), "fwdbwd_ms": round(t_fb, 3),
                      "bwd_tflops": round(2.5 * flops_f / (t_fb - t_f) / 1e9, 1)})  # fmt: skip
+    return rows
+
+
+def bench_newton_schulz() -> list[dict]:
+    """Five Polar-Express steps on stacks of momentum matrices: tcgen05 chain vs torch bf16 matmuls (cuBLAS)."""
+    from priml_b200.math.numeric import POLAR_EXPRESS_COEFFICIENTS
+    from priml_b200.ops.orthogonalize import newton_schulz_reference, newton_schulz_steps
+
+    peak, _ = _peaks()
+    rows = []
+    # Llama-1B (16 layers): q/o 2048 x 2048, SwiGLU up 16384 x 2048, down 2048 x 8192; nanochat d20: 1280 x 1280, 1280 x 5120
+    for b, m, n in ((16, 2048, 2048), (16, 16384, 2048), (16, 2048, 8192), (20, 1280, 1280), (20, 1280, 5120)):
+        x = torch.randn(b, m, n, device="cuda")
+        y = (x / (x.norm(dim=(-2, -1), keepdim=True) * 1.02 + 1e-6)).to(torch.bfloat16)
+        del x
+        lo, hi = min(m, n), max(m, n)
+        flops = 5 * b * (4.0 * lo * lo * hi + 2.0 * lo**3)
+        t_ours = time_fn(lambda: newton_schulz_steps(y, POLAR_EXPRESS_COEFFICIENTS), iters=5)
+        t_torch = time_fn(lambda: newton_schulz_reference(y, POLAR_EXPRESS_COEFFICIENTS), iters=5)
+        rows.append({"case": "polar_express_5", "batch": b, "m": m, "n": n, "ours_ms": round(t_ours, 3),
+                     "torch_ms": round(t_torch, 3), "ours_tflops": round(flops / t_ours / 1e9, 1),
+                     "ours_frac_of_bf16_peak": round(flops / t_ours / 1e9 / peak, 3)})  # fmt: skip
     return rows
 
 
@@ -348,7 +375,7 @@ def profile_case(name: str) -> None:
         del x, d, h, y
         q = torch.randn(16, 4096, 32, 64, device="cuda", dtype=torch.bfloat16)  # 256 MiB
         k = torch.randn(16, 4096, 8, 64, device="cuda", dtype=torch.bfloat16)
-        cos, sin = RoPE.Config(64, base=5e5).make().table(4096, torch.device("cuda"))
+        cos, sin = RoPE.Config(64, base=5e5).make().to("cuda").table(4096, torch.device("cuda"))
         for _ in range(2):
             ops.rotary(q, k, cos, sin)
         del q, k

@@ -25,6 +25,12 @@ void check_cuda(const Tensor& t, const char* name) {
   PB_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
 }
 
+// A side input (weights, tables, targets) as `dtype` on `ref`'s device: a kernel is never handed a
+// host pointer or another GPU's memory because a caller built a small tensor elsewhere.
+Tensor aux(const Tensor& t, const Tensor& ref, torch::ScalarType dtype) {
+  return t.to(ref.device(), dtype).contiguous();
+}
+
 // Per-device error status word (int32) that kernels write on a timed-out wait.
 Tensor& status_tensor() {
   static std::mutex mu;
@@ -231,7 +237,7 @@ std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const c10::optional<Tensor>& w,
   const float* wp = nullptr;
   Tensor wc;
   if (w.has_value() && w->defined()) {
-    wc = w->to(torch::kFloat32).contiguous();
+    wc = aux(*w, x, torch::kFloat32);
     wp = wc.data_ptr<float>();
   }
   if (R > 0)
@@ -250,7 +256,7 @@ std::vector<Tensor> rmsnorm_bwd(const Tensor& dy, const Tensor& x, const c10::op
   const float* wp = nullptr;
   float* dwp = nullptr;
   if (w.has_value() && w->defined()) {
-    wc = w->to(torch::kFloat32).contiguous();
+    wc = aux(*w, x, torch::kFloat32);
     wp = wc.data_ptr<float>();
     dw = torch::zeros({C}, x.options().dtype(torch::kFloat32));
     dwp = dw.data_ptr<float>();
@@ -282,7 +288,7 @@ std::vector<Tensor> add_rmsnorm_fwd(const Tensor& x, const Tensor& d, const c10:
   const float* wp = nullptr;
   Tensor wc;
   if (w.has_value() && w->defined()) {
-    wc = w->to(torch::kFloat32).contiguous();
+    wc = aux(*w, x, torch::kFloat32);
     wp = wc.data_ptr<float>();
   }
   const c10::cuda::CUDAGuard guard(x.device());
@@ -316,7 +322,7 @@ std::vector<Tensor> add_rmsnorm_bwd(const Tensor& dy, const Tensor& h, const c10
   const float* wp = nullptr;
   float* dwp = nullptr;
   if (w.has_value() && w->defined()) {
-    wc = w->to(torch::kFloat32).contiguous();
+    wc = aux(*w, h, torch::kFloat32);
     wp = wc.data_ptr<float>();
     dw = torch::zeros({C}, h.options().dtype(torch::kFloat32));
     dwp = dw.data_ptr<float>();
@@ -339,8 +345,8 @@ Tensor rope(const Tensor& x, const Tensor& cos, const Tensor& sin, double sign) 
   PB_CHECK(D % 4 == 0, "head dim must be a multiple of 4");
   PB_CHECK(cos.numel() == static_cast<long long>(S) * D / 2, "cos must hold S * D/2 values");
   auto y = torch::empty({B, S, H, D}, x.options());
-  auto c = cos.to(torch::kFloat32).contiguous();
-  auto s = sin.to(torch::kFloat32).contiguous();
+  auto c = aux(cos, x, torch::kFloat32);
+  auto s = aux(sin, x, torch::kFloat32);
   if (x.numel() > 0)
     pb::rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), y.data_ptr(), B, S, H, D, c.data_ptr<float>(),
                    s.data_ptr<float>(), static_cast<float>(sign), stream());
@@ -372,7 +378,7 @@ std::vector<Tensor> ce_fwd(const Tensor& logits, const Tensor& targets, int64_t 
   PB_CHECK(logits.dim() == 2 && logits.scalar_type() == torch::kBFloat16 && logits.stride(1) == 1, "logits [R, V] bf16");
   const long long R = logits.size(0);
   const int V = logits.size(1);
-  auto t = targets.to(torch::kInt64).contiguous();
+  auto t = aux(targets, logits, torch::kInt64);
   auto loss = torch::empty({R}, logits.options().dtype(torch::kFloat32));
   auto lse = torch::empty({R}, logits.options().dtype(torch::kFloat32));
   PB_CHECK(logits.stride(0) % 8 == 0, "logits row stride must be a multiple of 8");
@@ -387,8 +393,8 @@ void ce_bwd(const Tensor& logits, const Tensor& targets, const Tensor& lse, cons
             int64_t ignore_index, double softcap) {
   const long long R = logits.size(0);
   const int V = logits.size(1);
-  auto t = targets.to(torch::kInt64).contiguous();
-  auto gf = g.to(torch::kFloat32).contiguous();
+  auto t = aux(targets, logits, torch::kInt64);
+  auto gf = aux(g, logits, torch::kFloat32);
   const long long g_stride = gf.numel() == 1 ? 0 : 1;
   PB_CHECK(out.stride(0) == logits.stride(0), "out must share the logits layout");
   if (R > 0)
@@ -681,7 +687,8 @@ class PeerGroup {
 
   // segs: int64 [n, 3] = (local_off, gathered_off, group); hyper: 7 lists of per-group floats.
   void adamw_scatter(const Tensor& segs, Tensor& master, Tensor& m1, Tensor& m2, const Tensor& grad,
-                     c10::optional<Tensor> clip, const std::vector<std::vector<double>>& hyper, int64_t blocks) {
+                     c10::optional<Tensor> clip, const std::vector<std::vector<double>>& hyper, int64_t blocks,
+                     bool local_only) {
     PB_CHECK(opened_ok_, "open() the peer group first");
     PB_CHECK(segs.is_cuda() && segs.scalar_type() == torch::kInt64 && segs.dim() == 2 && segs.size(1) == 3, "segments");
     PB_CHECK(hyper.size() == 7, "hyper = [lr, beta1, beta2, eps, wd, bias1, bias2]");
@@ -696,7 +703,19 @@ class PeerGroup {
     }
     pb::adamw_scatter(table_, world_, reinterpret_cast<const pb::ShardSegment*>(segs.data_ptr()), segs.size(0), n,
                       master.data_ptr<float>(), m1.data_ptr<float>(), m2.data_ptr<float>(), grad.data_ptr<float>(),
-                      clip.has_value() ? clip->data_ptr<float>() : nullptr, hp, blocks, stream());
+                      clip.has_value() ? clip->data_ptr<float>() : nullptr, hp, blocks, stream(),
+                      local_only ? static_cast<int>(rank_) : -1);
+  }
+
+  // Sharded weights: dst (bf16, world * count elements) = every rank's param[src_off, src_off + count)
+  // in rank order, copied on the current stream by the copy engines.
+  void gather_shards(int64_t src_off, int64_t count, Tensor& dst) {
+    PB_CHECK(opened_ok_, "open() the peer group first");
+    PB_CHECK(dst.is_cuda() && dst.scalar_type() == torch::kBFloat16 && dst.is_contiguous() &&
+                 dst.numel() == world_ * count,
+             "dst must be contiguous bf16 of world * count elements");
+    PB_CHECK(src_off >= 0 && src_off + count <= param_.numel(), "shard range outside the param buffer");
+    pb::gather_shards(table_, static_cast<int>(world_), src_off, count, dst.data_ptr(), stream());
   }
 
   void barrier(int64_t target, double timeout_s) {
@@ -1102,7 +1121,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("signal", &PeerGroup::signal)
       .def("reduce_scatter", &PeerGroup::reduce_scatter)
       .def("norm_exchange", &PeerGroup::norm_exchange)
-      .def("adamw_scatter", &PeerGroup::adamw_scatter)
+      .def("adamw_scatter", &PeerGroup::adamw_scatter, py::arg("segs"), py::arg("master"), py::arg("m1"), py::arg("m2"),
+           py::arg("grad"), py::arg("clip"), py::arg("hyper"), py::arg("blocks"), py::arg("local_only") = false)
+      .def("gather_shards", &PeerGroup::gather_shards, py::arg("src_off"), py::arg("count"), py::arg("dst"))
       .def("barrier", &PeerGroup::barrier);
   m.def("status_tensor", &status_tensor_py);
   py::class_<EpGroup>(m, "EpGroup")

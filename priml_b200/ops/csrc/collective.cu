@@ -21,6 +21,15 @@
 //                          weight copy (P2P stores) -- the parameter all-gather
 //                          happens inside the optimizer kernel.
 //   peer_barrier_kernel    waits until every peer's scatter has landed here.
+//   gather_shards          (sharded-weights mode) copies one bucket's bf16
+//                          weight shards from every rank into a local window
+//                          with one peer cudaMemcpyAsync per rank, i.e. on the
+//                          copy engines, so the gather of the next block runs
+//                          beside the current block's kernels without taking SMs.
+//
+// In the sharded-weights mode each rank keeps only its own bf16 shard; the
+// optimizer kernel then stores the new weights into that shard alone
+// (`local_only`), and the forward / backward gather each block ahead of use.
 //
 // Synchronization uses a small signal array per rank (also IPC-mapped):
 // monotone epoch flags written with st.release.sys and read with
@@ -196,7 +205,8 @@ __global__ void __launch_bounds__(256) norm_exchange_kernel(PeerTable t, int ran
   clip_out[0] = (good && max_norm > 0.f) ? fminf(1.f, max_norm / (norm + 1e-6f)) : (good ? 1.f : 0.f);
 }
 
-__global__ void __launch_bounds__(256) adamw_scatter_kernel(PeerTable t, int world, const ShardSegment* __restrict__ segs,
+__global__ void __launch_bounds__(256) adamw_scatter_kernel(PeerTable t, int world, int local_rank,
+                                                             const ShardSegment* __restrict__ segs,
                                                              int nseg, long long n_local, float* __restrict__ master,
                                                              float* __restrict__ m1, float* __restrict__ m2,
                                                              const float* __restrict__ grad,
@@ -248,9 +258,13 @@ __global__ void __launch_bounds__(256) adamw_scatter_kernel(PeerTable t, int wor
     reinterpret_cast<float4*>(m2 + e)[1] = *reinterpret_cast<float4*>(vv + 4);
     const long long dst = seg.gathered_off + (e - seg.local_off);
     const uint4 val = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    if (local_rank >= 0) {  // sharded weights: this rank's shard only
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(t.param[local_rank]) + dst)[0] = val;
+    } else {
 #pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q)
-      if (q < world) reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(t.param[q]) + dst)[0] = val;
+      for (int q = 0; q < kMaxRanks; ++q)
+        if (q < world) reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(t.param[q]) + dst)[0] = val;
+    }
   }
   // Publish: this CTA's stores are visible system-wide, then count it on every peer.
   __threadfence_system();
@@ -338,10 +352,20 @@ void norm_exchange(const PeerTable& t, int rank, int world, const float* partial
 
 void adamw_scatter(const PeerTable& t, int world, const ShardSegment* segs, int nseg, long long n_local, float* master,
                    float* m1, float* m2, const float* grad, const float* clip, const AdamHyper& hp, int blocks,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int local_rank) {
   if ((n_local & 7) != 0) throw std::invalid_argument("adamw_scatter: local shard must be a multiple of 8");
-  adamw_scatter_kernel<<<blocks, 256, 0, stream>>>(t, world, segs, nseg, n_local, master, m1, m2, grad, clip, hp);
+  adamw_scatter_kernel<<<blocks, 256, 0, stream>>>(t, world, local_rank, segs, nseg, n_local, master, m1, m2, grad,
+                                                   clip, hp);
   check(cudaGetLastError(), "adamw_scatter launch");
+}
+
+void gather_shards(const PeerTable& t, int world, long long src_off, long long count, void* dst, cudaStream_t stream) {
+  for (int r = 0; r < world; ++r) {
+    const auto* src = reinterpret_cast<const __nv_bfloat16*>(t.param[r]) + src_off;
+    auto* out = static_cast<__nv_bfloat16*>(dst) + static_cast<long long>(r) * count;
+    check(cudaMemcpyAsync(out, src, static_cast<size_t>(count) * 2, cudaMemcpyDeviceToDevice, stream),
+          "gather_shards copy");
+  }
 }
 
 void peer_barrier(const unsigned long long* done, unsigned long long target, long long timeout_ns, int* status,

@@ -173,9 +173,12 @@ void rs_bucket(const PeerTable& t, int rank, int world, int bucket, long long bu
 void norm_exchange(const PeerTable& t, int rank, int world, const float* partial, int n_partial,
                    unsigned long long epoch, float max_norm, float* norm_out, float* clip_out, long long timeout_ns,
                    int* status, cudaStream_t stream);
+// local_rank >= 0: store the new bf16 weights into that rank's buffer only (sharded weights).
 void adamw_scatter(const PeerTable& t, int world, const ShardSegment* segs, int nseg, long long n_local, float* master,
                    float* m1, float* m2, const float* grad, const float* clip, const AdamHyper& hp, int blocks,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int local_rank = -1);
+// dst[r * count .. (r + 1) * count) = rank r's param buffer [src_off, src_off + count), r < world (bf16).
+void gather_shards(const PeerTable& t, int world, long long src_off, long long count, void* dst, cudaStream_t stream);
 void peer_barrier(const unsigned long long* done, unsigned long long target, long long timeout_ns, int* status,
                   cudaStream_t stream);
 

@@ -89,10 +89,15 @@ class _Bucket:
     numel: int = 0
     shard: int = 0
     local: int = 0
+    block: int | None = None  # transformer block this bucket holds (sharded weights: rotating window)
+    window: Tensor | None = None  # sharded weights: where the gathered bf16 bucket lives
+    slot: int | None = None  # rotating window index, or None for a window of its own
+    valid: bool = False  # own window: holds this step's weights
+    ready: Any = None  # event after which the window holds them
 
 
-def _bucket_units(model: nn.Module, params: list[nn.Parameter]) -> list[list[nn.Parameter]]:
-    """Parameter groups in the order the backward pass finishes them."""
+def _bucket_units(model: nn.Module, params: list[nn.Parameter]) -> list[tuple[list[nn.Parameter], int | None]]:
+    """Parameter groups in the order the backward pass finishes them, each with its block index (or None)."""
     pos = {id(p): i for i, p in enumerate(params)}
     blocks = getattr(model, "blocks", None)
     if isinstance(blocks, nn.ModuleList) and len(blocks) > 0:
@@ -105,17 +110,17 @@ def _bucket_units(model: nn.Module, params: list[nn.Parameter]) -> list[list[nn.
         first = min((pos[id(p)] for ps in per_block for p in ps), default=0)
         pre = [p for p in params if id(p) not in seen and pos[id(p)] < first]
         post = [p for p in params if id(p) not in seen and pos[id(p)] > first]
-        units = [post, *per_block[::-1], pre]
+        units = [(post, None), *[(ps, i) for i, ps in reversed(list(enumerate(per_block)))], (pre, None)]
     else:
         seen = set()
-        units = []
+        plain = []
         for child in model.children():
             ps = [p for p in dict.fromkeys(child.parameters()) if id(p) in pos and id(p) not in seen]
             seen.update(id(p) for p in ps)
-            units.append(ps)
-        units.append([p for p in params if id(p) not in seen])
-        units = units[::-1]
-    return [u for u in units if u]
+            plain.append(ps)
+        plain.append([p for p in params if id(p) not in seen])
+        units = [(u, None) for u in plain[::-1]]
+    return [(u, blk) for u, blk in units if u]
 
 
 class ShardedState:
@@ -140,8 +145,8 @@ class ShardedState:
         self.buckets: list[_Bucket] = []
         self.entries: list[_Entry] = []
         cursor = local = 0
-        for bi, unit in enumerate(units):
-            b = _Bucket(index=bi, offset=cursor)
+        for bi, (unit, block) in enumerate(units):
+            b = _Bucket(index=bi, offset=cursor, block=block)
             for p in unit:
                 cursor = _round_up(cursor, _ALIGN)
                 e = _Entry(param=p, offset=cursor, numel=p.numel(), shape=p.shape, bucket=bi)
@@ -157,9 +162,12 @@ class ShardedState:
         self.total = cursor
         self.local_total = local
 
-        # Buffers: bf16 weights + fp32 gradients (peer-mapped on CUDA), fp32 shards.
+        # Buffers: bf16 weights (all of them, or this rank's shard) + fp32 gradients (peer-mapped on
+        # CUDA), fp32 shards.
+        self.shard_params = bool(config.shard_params)
+        weight_elems = self.local_total if self.shard_params else self.total
         if self.native:
-            self.peers = ops.native().PeerGroup(self.rank, self.world, self.total, self.total)
+            self.peers = ops.native().PeerGroup(self.rank, self.world, weight_elems, self.total)
             handles = self.peers.handles()
             all_handles: list[Any] = [None] * self.world
             if self.dist:
@@ -170,18 +178,25 @@ class ShardedState:
             self.param_buf: Tensor = self.peers.param()
             self.grad_buf: Tensor = self.peers.grad()
             self.comm_stream = torch.cuda.Stream(device=device)
+            self.gather_stream = torch.cuda.Stream(device=device) if self.shard_params else None
         else:
             self.peers = None
-            self.param_buf = torch.zeros(self.total, dtype=torch.bfloat16, device=device)
+            self.param_buf = torch.zeros(weight_elems, dtype=torch.bfloat16, device=device)
             self.grad_buf = torch.zeros(self.total, dtype=torch.float32, device=device)
             self.comm_stream = None
+            self.gather_stream = None
         flat = torch.zeros(self.total, dtype=torch.float32, device=device)
         with torch.no_grad():
             for e in self.entries:
                 flat[e.offset : e.offset + e.numel].copy_(e.param.detach().reshape(-1))
             if self.dist and self.world > 1:
                 dist.broadcast(flat, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
-            self.param_buf.copy_(flat)
+            if self.shard_params:
+                for b in self.buckets:
+                    lo = b.offset + self.rank * b.shard
+                    self.param_buf[b.local : b.local + b.shard].copy_(flat[lo : lo + b.shard])
+            else:
+                self.param_buf.copy_(flat)
         self.master = torch.empty(self.local_total, dtype=torch.float32, device=device)
         for b in self.buckets:
             lo = b.offset + self.rank * b.shard
@@ -195,11 +210,19 @@ class ShardedState:
         self.norm = torch.zeros(1, dtype=torch.float32, device=device)
         self.clip = torch.ones(1, dtype=torch.float32, device=device)
 
-        # Replace every parameter by a bf16 view of the resident weight buffer.
+        # Replace every parameter by a bf16 view of the resident weight buffer (sharded weights: of
+        # its bucket's window).
+        self._make_windows()
         self.sinks: list[GradSink] = []
         mapping: dict[int, nn.Parameter] = {}
         for idx, e in enumerate(self.entries):
-            newp = nn.Parameter(self.param_buf[e.offset : e.offset + e.numel].view(e.shape))
+            if self.shard_params:
+                b = self.buckets[e.bucket]
+                assert b.window is not None
+                view = b.window[e.offset - b.offset : e.offset - b.offset + e.numel]
+            else:
+                view = self.param_buf[e.offset : e.offset + e.numel]
+            newp = nn.Parameter(view.view(e.shape))
             sink = GradSink(self.grad_buf[e.offset : e.offset + e.numel].view(e.shape))
             newp._pb_grad_sink = sink  # type: ignore[attr-defined]
             newp.register_post_accumulate_grad_hook(self._make_hook(idx, sink))
@@ -212,6 +235,9 @@ class ShardedState:
                     mod._parameters[name] = mapping[id(p)]  # noqa: SLF001
         self._param_index = {id(e.param): i for i, e in enumerate(self.entries)}
 
+        if self.shard_params:
+            self._install_gather_hooks(model)
+
         # Per-backward bookkeeping.
         self.sync = True
         self.epoch = 1
@@ -219,6 +245,128 @@ class ShardedState:
         self._armed = False
         self._reset_backward()
         self.reduced = False
+
+    # ------------------------------------------------------------------ sharded weights
+    def _make_windows(self) -> None:
+        """Sharded weights: two rotating windows for the transformer blocks, one window per other bucket."""
+        if not self.shard_params:
+            return
+        blocks = [b for b in self.buckets if b.block is not None]
+        self.window_holds: list[int | None] = [None, None]
+        if blocks:
+            size = max(b.numel for b in blocks)
+            self.slots = [torch.zeros(size, dtype=torch.bfloat16, device=self.device) for _ in range(2)]
+        for b in self.buckets:
+            if b.block is not None:
+                b.slot = b.block % 2
+                b.window = self.slots[b.slot][: b.numel]
+            else:
+                b.window = torch.zeros(b.numel, dtype=torch.bfloat16, device=self.device)
+        self.block_buckets = {b.block: b for b in blocks}
+
+    def _gather(self, b: _Bucket) -> None:
+        """Fill ``b``'s window with every rank's shard (copy engines, gather stream; gloo: all-gather)."""
+        assert b.window is not None
+        shard = self.param_buf[b.local : b.local + b.shard]
+        if self.native:
+            here = torch.cuda.Event()
+            here.record()  # everything issued so far, the last reader of this window included
+            self.gather_stream.wait_event(here)
+            with torch.cuda.stream(self.gather_stream):
+                self.peers.gather_shards(b.local, b.shard, b.window)
+                done = torch.cuda.Event()
+                done.record()
+            b.ready = done
+        else:
+            if self.dist and self.world > 1:
+                dist.all_gather(list(b.window.chunk(self.world)), shard.contiguous(), group=self.group)
+            else:
+                b.window.copy_(shard)
+            b.ready = None
+        if b.slot is not None:
+            self.window_holds[b.slot] = b.index
+        else:
+            b.valid = True
+
+    def _present(self, b: _Bucket) -> bool:
+        return self.window_holds[b.slot] == b.index if b.slot is not None else b.valid
+
+    def _ensure(self, b: _Bucket | None, *, wait: bool = True) -> None:
+        if b is None:
+            return
+        if not self._present(b):
+            self._gather(b)
+        if wait and b.ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(b.ready)
+
+    def _prefetch_own_windows(self) -> None:
+        for b in self.buckets:
+            if b.slot is None and not b.valid:
+                self._gather(b)
+
+    def _install_gather_hooks(self, model: nn.Module) -> None:
+        """Gather each block one block ahead of use, forward (i + 1) and backward (i - 1)."""
+        owners: dict[int, list[nn.Module]] = {}
+        for mod in model.modules():
+            for p in mod._parameters.values():  # noqa: SLF001
+                idx = self._param_index.get(id(p)) if p is not None else None
+                if idx is not None and self.buckets[self.entries[idx].bucket].slot is None:
+                    owners.setdefault(self.entries[idx].bucket, []).append(mod)
+        def own(b: _Bucket) -> Callable[..., None]:
+            def hook(*_args: Any) -> None:  # returns None: the module's inputs stay as they are
+                self._prefetch_own_windows()
+                self._ensure(b)
+
+            return hook
+
+        for bi, mods in owners.items():
+            for mod in dict.fromkeys(mods):
+                mod.register_forward_pre_hook(own(self.buckets[bi]))
+        blocks = getattr(model, "blocks", None)
+        if not self.block_buckets or not isinstance(blocks, nn.ModuleList):
+            return
+        last = len(blocks) - 1
+        post = [b for b in self.buckets if b.slot is None]
+
+        def fwd(i: int) -> Callable[..., None]:
+            def hook(*_args: Any) -> None:
+                self._prefetch_own_windows()
+                self._ensure(self.block_buckets.get(i))
+                if i + 1 in self.block_buckets:
+                    self._ensure(self.block_buckets[i + 1], wait=False)
+                if i == last:  # layers after the blocks may read their weights without a module call
+                    for b in post:
+                        self._ensure(b)
+
+            return hook
+
+        def bwd(i: int) -> Callable[..., None]:
+            def hook(*_args: Any) -> None:
+                self._ensure(self.block_buckets.get(i))
+                if i - 1 in self.block_buckets:
+                    self._ensure(self.block_buckets[i - 1], wait=False)
+
+            return hook
+
+        for i, blk in enumerate(blocks):
+            blk.register_forward_pre_hook(fwd(i))
+            blk.register_full_backward_pre_hook(bwd(i))
+
+    def weights_changed(self) -> None:
+        """After an optimizer step: every gathered window is stale."""
+        if not self.shard_params:
+            return
+        self.window_holds = [None, None]
+        for b in self.buckets:
+            b.valid = False
+
+    def weight_bytes(self) -> int:
+        """bf16 weight storage on this rank (shard + windows, or the resident copy)."""
+        n = self.param_buf.numel()
+        if self.shard_params:
+            n += sum(t.numel() for t in getattr(self, "slots", []))
+            n += sum(b.window.numel() for b in self.buckets if b.slot is None and b.window is not None)
+        return 2 * n
 
     # ------------------------------------------------------------------ backward
     def _reset_backward(self) -> None:
@@ -347,6 +495,8 @@ class ShardedAdamW(Optimizer):
             group_of.setdefault(i, 0)
         self._group_of = group_of
         self._segments = state.segments(group_of)
+        if state.shard_params:  # new weights go to this rank's shard: destination = local offset
+            self._segments[:, 1] = self._segments[:, 0]
         self._group_index = self._element_groups() if not state.native else None
         self.step_count = 0
         self.grad_scale: Tensor | None = None
@@ -407,7 +557,8 @@ class ShardedAdamW(Optimizer):
             st.peers.norm_exchange(st.partial.view(-1), st.epoch, self._max_norm if clipping else 0.0, st.norm,
                                    st.clip, st.config.timeout_s)  # fmt: skip
             st.peers.adamw_scatter(self._segments, st.master, st.exp_avg, st.exp_avg_sq, st.grad_shard,
-                                   st.clip if clipping else None, hyper, self._scatter_blocks)  # fmt: skip
+                                   st.clip if clipping else None, hyper, self._scatter_blocks,
+                                   st.shard_params)  # fmt: skip
             st.done_target += st.world * self._scatter_blocks
             st.peers.barrier(st.done_target, st.config.timeout_s)
             self._status_host.copy_(ops.native().status_tensor(), non_blocking=True)
@@ -415,6 +566,7 @@ class ShardedAdamW(Optimizer):
             self._status_event.record()
         else:
             self._reference_step(hyper, clipping)
+        st.weights_changed()
         st.epoch += 1
         st.reduced = False
         return loss
@@ -437,7 +589,10 @@ class ShardedAdamW(Optimizer):
         st.exp_avg_sq.lerp_(g * g, 1 - b2)
         p -= st.exp_avg / ((st.exp_avg_sq / bias2).sqrt() + eps) * (lr / bias1)
         st.master.copy_(p)
-        st.param_buf.copy_(st.gather_full(st.master))
+        if st.shard_params:
+            st.param_buf.copy_(st.master)  # the shard; the forward gathers it
+        else:
+            st.param_buf.copy_(st.gather_full(st.master))
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         del set_to_none
@@ -513,6 +668,10 @@ def _install_state_dict_hooks(model: nn.Module, state: ShardedState) -> None:
             if key in sd:
                 full[e.offset : e.offset + e.numel].copy_(sd[key].reshape(-1).to(full.device, torch.float32))
         state.scatter_full(full, state.master)
+        if state.shard_params:  # the bf16 shards follow the loaded masters; windows re-gather
+            with torch.no_grad():
+                state.param_buf.copy_(state.master)
+            state.weights_changed()
 
     model.register_state_dict_post_hook(save_hook)
     model.register_load_state_dict_pre_hook(load_hook)
@@ -531,6 +690,10 @@ class FusedFullySharded:
         """CTAs of the optimizer + all-gather kernel; 0 = two per SM."""
         timeout_s: float = 60.0
         """Bound on every cross-rank wait inside the kernels."""
+        shard_params: bool = False
+        """Keep only this rank's 1/R of the bf16 weights. Each transformer block is gathered into
+        one of two rotating windows a block ahead of its forward and of its backward (copy engines,
+        side stream); other parameters get a window each, gathered once per step."""
 
     def __init__(self, config: Config | None = None) -> None:
         self.config = config or FusedFullySharded.Config()

@@ -7,6 +7,7 @@ hooks, shard segments and checkpoint hooks as the CUDA kernels use.
 
 from __future__ import annotations
 
+import pytest
 import torch
 
 from priml_b200.testing import run_ranks
@@ -32,11 +33,11 @@ def _batches(n: int) -> list[torch.Tensor]:
     return [torch.randint(0, 512, (8, 65), generator=g) for _ in range(n)]
 
 
-def _sharded(rank: int, world: int, steps: int, accumulate: int = 1) -> dict:
+def _sharded(rank: int, world: int, steps: int, accumulate: int = 1, shard_params: bool = False) -> dict:
     from priml_b200.parallel.fused_fsdp import FusedFullySharded
 
     torch.manual_seed(0)
-    cfg = _cfg(FusedFullySharded.Config(device="cpu"))
+    cfg = _cfg(FusedFullySharded.Config(device="cpu", shard_params=shard_params))
     cfg.accumulate_grad_batches = accumulate
     step = cfg.make()
     losses, norms = [], []
@@ -58,6 +59,8 @@ def _sharded(rank: int, world: int, steps: int, accumulate: int = 1) -> dict:
         "keys": sorted(sd),
         "opt_keys": sorted(osd["state"][0]),
         "weights": {k: v.clone() for k, v in sd.items()},
+        "shard_elems": step.parallelism.state.param_buf.numel(),
+        "total_elems": step.parallelism.state.total,
     }
 
 
@@ -98,8 +101,11 @@ def test_sharded_gradient_accumulation_matches_full_batch() -> None:
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), (acc[0]["norms"], full[0]["norms"])
 
 
-def _resume(rank: int, world: int) -> list[float]:
+def _resume(rank: int, world: int, shard_params: bool = False) -> list[float]:
     from priml_b200.parallel.fused_fsdp import FusedFullySharded
+
+    def strategy():  # noqa: ANN202
+        return FusedFullySharded.Config(device="cpu", shard_params=shard_params)
 
     batches = _batches(4)
 
@@ -112,21 +118,36 @@ def _resume(rank: int, world: int) -> list[float]:
         return out
 
     torch.manual_seed(0)
-    a = _cfg(FusedFullySharded.Config(device="cpu")).make()
+    a = _cfg(strategy()).make()
     straight = run(a, batches)
     torch.manual_seed(0)
-    b = _cfg(FusedFullySharded.Config(device="cpu")).make()
+    b = _cfg(strategy()).make()
     run(b, batches[:2])
     sd = {"model": b.model.state_dict(), "optimizer": b.optimizer.state_dict()}
     torch.manual_seed(123)
-    c = _cfg(FusedFullySharded.Config(device="cpu")).make()
+    c = _cfg(strategy()).make()
     c.model.load_state_dict(sd["model"])
     c.optimizer.load_state_dict(sd["optimizer"])
     resumed = run(c, batches[2:])
     return [straight[2] - resumed[0], straight[3] - resumed[1]]
 
 
-def test_sharded_checkpoint_roundtrip_resumes_exactly() -> None:
-    diffs = run_ranks(_resume, 2, mesh_shape={"dp": 2})
+@pytest.mark.parametrize("shard_params", [False, True])
+def test_sharded_checkpoint_roundtrip_resumes_exactly(shard_params: bool) -> None:
+    diffs = run_ranks(_resume, 2, shard_params, mesh_shape={"dp": 2})
     for d in diffs:
         assert all(abs(x) < 1e-6 for x in d), diffs
+
+
+@pytest.mark.parametrize("accumulate", [1, 2])
+def test_sharded_weights_match_resident_weights(accumulate: int) -> None:
+    """Each rank keeping 1/R of the bf16 weights and gathering blocks into rotating windows
+    computes exactly what resident weights compute."""
+    resident = run_ranks(_sharded, 2, 4, accumulate, False, mesh_shape={"dp": 2})
+    sharded = run_ranks(_sharded, 2, 4, accumulate, True, mesh_shape={"dp": 2})
+    for r in range(2):
+        assert sharded[r]["losses"] == resident[r]["losses"]
+        assert sharded[r]["norms"] == resident[r]["norms"]
+        for k, v in resident[r]["weights"].items():
+            assert torch.equal(sharded[r]["weights"][k], v), k
+        assert sharded[r]["shard_elems"] * 2 == sharded[r]["total_elems"]

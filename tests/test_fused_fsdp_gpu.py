@@ -113,7 +113,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
+def _rank_main(rank: int, world: int, port: int, q, shard_params: bool = False) -> None:  # noqa: ANN001
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))  # fmt: skip
     torch.cuda.set_device(rank)
@@ -124,7 +124,7 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
     try:
         from priml_b200.parallel.fused_fsdp import FusedFullySharded
 
-        q.put((rank, _losses(FusedFullySharded.Config(timeout_s=30.0), world, rank)))
+        q.put((rank, _losses(FusedFullySharded.Config(timeout_s=30.0, shard_params=shard_params), world, rank)))
     except Exception as exc:  # noqa: BLE001
         q.put((rank, repr(exc)))
     finally:
@@ -151,3 +151,35 @@ def test_fused_sharded_two_gpus_matches_one() -> None:
     assert res[0] == res[1]
     for a, b in zip(res[0], one, strict=True):
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), (res[0], one)
+
+
+def _run_two(shard_params: bool) -> dict:
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, shard_params)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_weights_two_gpus_match_resident_weights() -> None:
+    """1/R bf16 weights per rank, blocks gathered by the copy engines a block ahead: the same losses,
+    bit for bit, as resident weights (the same bf16 values reach the same kernels)."""
+    resident = _run_two(False)
+    sharded = _run_two(True)
+    assert isinstance(sharded[0], list), sharded
+    assert sharded[0] == sharded[1]
+    assert sharded[0] == resident[0], (sharded[0], resident[0])
+
+
+def test_sharded_weights_single_gpu_matches_resident() -> None:
+    from priml_b200.parallel.fused_fsdp import FusedFullySharded
+
+    assert _losses(FusedFullySharded.Config(shard_params=True)) == _losses(FusedFullySharded.Config())
