@@ -101,6 +101,35 @@ void gemm_axpby(const Tensor& A, const Tensor& B, const Tensor& X, Tensor& C, bo
                 K, 5, X.data_ptr(), 0, status_ptr(), stream(), static_cast<float>(alpha), static_cast<float>(beta));
 }
 
+// Batched products over contiguous 3-D stacks: C[b] = alpha * A[b] @ B[b]^T (+ beta * X[b]), in one
+// persistent launch (A [b, M, K] or [b, K, M] with a_mn; B [b, N, K] or [b, K, N] with b_mn; C, X [b, M, N]).
+void gemm_batched(const Tensor& A, const Tensor& B, Tensor& C, bool a_mn, bool b_mn, const c10::optional<Tensor>& X,
+                  double alpha, double beta) {
+  for (const Tensor* t : {&A, &B, static_cast<const Tensor*>(&C)}) {
+    check_cuda(*t, "operand");
+    PB_CHECK(t->dim() == 3 && t->is_contiguous() && t->scalar_type() == torch::kBFloat16,
+             "batched GEMM operands must be contiguous bf16 [batch, rows, cols]");
+  }
+  const int batch = A.size(0);
+  const int M = a_mn ? A.size(2) : A.size(1);
+  const int K = a_mn ? A.size(1) : A.size(2);
+  const int N = b_mn ? B.size(2) : B.size(1);
+  PB_CHECK(B.size(0) == batch && C.size(0) == batch, "batch sizes differ");
+  PB_CHECK((b_mn ? B.size(1) : B.size(2)) == K, "contraction sizes differ");
+  PB_CHECK(C.size(1) == M && C.size(2) == N, "C has the wrong shape");
+  PB_CHECK(X.has_value() || alpha == 1.0, "alpha scales the product only together with X");
+  const void* aux = nullptr;
+  if (X.has_value()) {
+    PB_CHECK(X->sizes() == C.sizes() && X->is_contiguous() && X->scalar_type() == torch::kBFloat16, "X like C");
+    aux = X->data_ptr();
+  }
+  if (batch == 0 || M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(A.device());
+  pb::gemm_bf16_batched(A.data_ptr(), A.size(2), a_mn, B.data_ptr(), B.size(2), b_mn, C.data_ptr(), N, M, N, K, batch,
+                        aux != nullptr ? 5 : 0, aux, status_ptr(), stream(), static_cast<float>(alpha),
+                        static_cast<float>(beta));
+}
+
 // h = silu(x @ Wg^T) * (x @ Wu^T) with W = [Wg; Wu] ([2H, K]); also writes the bf16 pre-activation gu [M, 2H].
 void gemm_swiglu(const Tensor& X, const Tensor& W, Tensor& H, Tensor& GU) {
   check_cuda(X, "X");
@@ -1088,6 +1117,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM: C (op)= A B^T", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epi"));
   m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 GEMM with fused SwiGLU epilogue");
+  m.def("gemm_batched", &gemm_batched, "batched tcgen05 GEMM C[b] = alpha * A[b] B[b]^T (+ beta * X[b])",
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("X") = py::none(),
+        py::arg("alpha") = 1.0, py::arg("beta") = 0.0);
   m.def("gemm_axpby", &gemm_axpby, "tcgen05 GEMM C = alpha * A B^T + beta * X (bf16)", py::arg("A"), py::arg("B"),
         py::arg("X"), py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("alpha"), py::arg("beta"));
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, "tcgen05 GEMM dy @ W_down with the SwiGLU backward in the epilogue");

@@ -434,7 +434,8 @@ __device__ __forceinline__ void axpby_prefetch(const GemmParams& p, int row0, in
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int r = row0 + (lane >> 2) + 8 * j;
-    x[j] = (r < p.M && cc < p.N) ? __ldg(reinterpret_cast<const uint4*>(aux + static_cast<long long>(r) * p.ldc + cc))
+    x[j] = (r < p.M * p.batch && cc < p.N)
+               ? __ldg(reinterpret_cast<const uint4*>(aux + static_cast<long long>(r) * p.ldc + cc))
                                  : make_uint4(0u, 0u, 0u, 0u);
   }
 }
@@ -513,7 +514,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   // Work unit u = (tile u / splits, K slice u % splits); slices accumulate through the
   // fp32 reduce-add epilogue, so a few output tiles with a long K still fill every SM.
   const int splits = p.splits;
-  const int num_units = num_tiles * splits;
+  // Batched launches stack the products along the outer axis of every operand: product b owns rows
+  // [b M, (b + 1) M) of A (K-major) and C, [b N, ...) of B (K-major), [b K, ...) of an MN-major operand.
+  const int num_units = num_tiles * splits * p.batch;
   const auto k_range = [&](int u, int& lo, int& hi) {
     const int ks = u % splits;
     lo = ks * num_kb / splits;
@@ -560,10 +563,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     bool ok = true;
     for (int u = pair; u < num_units && ok; u += num_pairs) {
       int mb, nb, kb_lo, kb_hi;
-      tile_coords(u / splits, num_m, num_n, mb, nb);
+      tile_coords((u / splits) % num_tiles, num_m, num_n, mb, nb);
       k_range(u, kb_lo, kb_hi);
-      const int m0 = mb * TM + 128 * static_cast<int>(rank);
-      const int n0 = nb * TN + 128 * static_cast<int>(rank);
+      const int bi = u / (splits * num_tiles);
+      const int m0 = mb * TM + 128 * static_cast<int>(rank) + (A_MN ? 0 : bi * p.M);
+      const int n0 = nb * TN + 128 * static_cast<int>(rank) + (B_MN ? 0 : bi * p.N);
+      const int kofs_a = A_MN ? bi * p.K : 0, kofs_b = B_MN ? bi * p.K : 0;
       for (int kb = kb_lo; kb < kb_hi; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutProducer, abort_flag)) {
           ok = false;
@@ -575,8 +580,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         uint8_t* b_dst = smB + stage * Cfg::kBBytes;
         const int k0 = kb * BK;
         if constexpr (A_MN) {
-          tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
-          tma_load_2d_pair(a_dst + BK * 128, &tmA, bar, m0 + 64, k0);
+          tma_load_2d_pair(a_dst, &tmA, bar, m0, k0 + kofs_a);
+          tma_load_2d_pair(a_dst + BK * 128, &tmA, bar, m0 + 64, k0 + kofs_a);
         } else {
           tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
         }
@@ -585,8 +590,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           const int h0 = nb * (TN / 2);
           tma_load_2d_pair(b_dst, &tmB, bar, k0, leader ? h0 : p.num_n_half + h0);
         } else if constexpr (B_MN) {
-          tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
-          tma_load_2d_pair(b_dst + BK * 128, &tmB, bar, n0 + 64, k0);
+          tma_load_2d_pair(b_dst, &tmB, bar, n0, k0 + kofs_b);
+          tma_load_2d_pair(b_dst + BK * 128, &tmB, bar, n0 + 64, k0 + kofs_b);
         } else {
           tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
         }
@@ -674,10 +679,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     int local = 0;
     for (int u = pair; u < num_units; u += num_pairs, ++local) {
       int mb, nb;
-      tile_coords(u / splits, num_m, num_n, mb, nb);
+      tile_coords((u / splits) % num_tiles, num_m, num_n, mb, nb);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
+      const int row0 = (u / (splits * num_tiles)) * p.M + mb * TM + 128 * static_cast<int>(rank) + wq * 32;
       [[maybe_unused]] uint4 pre_g[4], pre_u[4];
       if constexpr (TOUT && EPI == 4) swiglu_bwd_prefetch(p, row0, nb * TN + c_lo, lane, pre_g, pre_u);
       if constexpr (TOUT && EPI == 5) axpby_prefetch(p, row0, nb * TN + c_lo, lane, pre_g);
@@ -723,7 +728,7 @@ void launch_pair_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     configured = true;
   }
-  const int units = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.splits;
+  const int units = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.splits * p.batch;
   const int pairs = units < num_sms / 2 ? units : num_sms / 2;
   kern<<<2 * pairs, kPairThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, tg, tu, p);
 }
@@ -934,6 +939,53 @@ void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long
     PB_DISPATCH(true, true)
   }
 #undef PB_DISPATCH
+}
+
+// Batched entry: `batch` independent products C_b = A_b B_b^T (epilogues 0 and 5), each operand a
+// stack of equal matrices along its outer axis (row strides lda / ldb / ldc within and across them).
+// One persistent launch covers every product's tiles. Needs M, N multiples of 256 and K of 64, so
+// that no tile reaches into the next product.
+void gemm_bf16_batched(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
+                       long long ldc, int M, int N, int K, int batch, int epi, const void* aux, int* status,
+                       cudaStream_t stream, float alpha, float beta) {
+  if (M % 256 != 0 || N % 256 != 0 || K % 64 != 0 || batch < 1 || (epi != 0 && epi != 5))
+    throw std::invalid_argument("batched GEMM needs M, N % 256 == 0, K % 64 == 0 and epilogue 0 or 5");
+  const int num_sms = device_sm_count();
+  CUtensorMap ta, tb, tc{}, tg{}, tu{};
+  GemmParams p{M, N, K, C, ldc, aux, status, 0};
+  p.alpha = alpha;
+  p.beta = beta;
+  p.batch = batch;
+  const long long rows_a = static_cast<long long>(a_mn ? K : M) * batch;
+  const long long rows_b = static_cast<long long>(b_mn ? K : N) * batch;
+  if (a_mn) {
+    make_tmap_2d_bf16(&ta, A, M, rows_a, lda, 64, BK);
+  } else {
+    make_tmap_2d_bf16(&ta, A, K, rows_a, lda, 64, BM);
+  }
+  if (b_mn) {
+    make_tmap_2d_bf16(&tb, B, N, rows_b, ldb, 64, BK);
+  } else {
+    make_tmap_2d_bf16(&tb, B, K, rows_b, ldb, 64, 128);
+  }
+  if (!make_out_maps(epi, C, ldc, static_cast<int>(static_cast<long long>(M) * batch), N, aux, 0, &tc, &tg, &tu))
+    throw std::invalid_argument("batched GEMM needs 16-byte aligned C rows (and aux rows)");
+#define PB_BATCHED(AM, BMJ)                                                                    \
+  if (epi == 5) {                                                                              \
+    launch_pair_k<AM, BMJ, 5, true>(ta, tb, tc, tg, tu, p, num_sms, stream);                   \
+  } else {                                                                                     \
+    launch_pair_k<AM, BMJ, 0, true>(ta, tb, tc, tg, tu, p, num_sms, stream);                   \
+  }
+  if (!a_mn && !b_mn) {
+    PB_BATCHED(false, false)
+  } else if (!a_mn && b_mn) {
+    PB_BATCHED(false, true)
+  } else if (a_mn && !b_mn) {
+    PB_BATCHED(true, false)
+  } else {
+    PB_BATCHED(true, true)
+  }
+#undef PB_BATCHED
 }
 
 }  // namespace pb

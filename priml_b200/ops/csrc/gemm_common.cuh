@@ -32,6 +32,7 @@ struct GemmParams {
   int splits = 1;        // split-K factor (pair kernel, fp32 reduce-add epilogue only)
   float alpha = 1.f;     // epilogue 5: C = alpha * acc + beta * aux (aux bf16 with row stride ldc)
   float beta = 0.f;
+  int batch = 1;         // pair kernel: independent products stacked along the outer (row) axis of every operand
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {

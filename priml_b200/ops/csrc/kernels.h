@@ -35,6 +35,11 @@ void make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long inner, long
 void gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
                long long ldc, int M, int N, int K, int epi, const void* aux, int swiglu_h, int* status,
                cudaStream_t stream, float alpha = 1.f, float beta = 0.f);
+// `batch` products in one persistent launch, operands stacked along their outer axis (epi 0 or 5;
+// M, N multiples of 256, K of 64).
+void gemm_bf16_batched(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C,
+                       long long ldc, int M, int N, int K, int batch, int epi, const void* aux, int* status,
+                       cudaStream_t stream, float alpha = 1.f, float beta = 0.f);
 
 // Grouped expert GEMM over 128-row-aligned expert segments (device offsets [experts + 1]).
 // mode 0: C[r] = A[r] @ B_e^T (B stacked per expert, b_rows rows each; epi 0, 1, 3, 4);

@@ -16,9 +16,10 @@ transpose (``A`` is symmetric, so it is its own K-major ``B`` operand). The
 iterate ping-pongs between two buffers because every tile of the next GEMM
 still reads the previous one.
 
-A stack of small matrices leaves most SMs idle in one GEMM (a 768 x 768 Gram
-matrix is 9 pair tiles); the stack is then spread over a few CUDA streams so
-the chains of different matrices run side by side.
+A stack of matrices runs as one batched launch per GEMM when both sides are
+multiples of 256 (the 2-CTA tile): the tiles of every matrix share one
+persistent grid, so a stack of small matrices fills the GPU. Other shapes run
+one chain per matrix, spread over a few CUDA streams.
 
 Shapes the 2-CTA tiles cannot take (a side under 256, or not a multiple of 8) and
 CPU tensors run the same polynomial in torch.
@@ -45,6 +46,12 @@ def newton_schulz_reference(y: Tensor, coefficients: Sequence[tuple[float, float
             gram = y @ y.mT
             y = a * y + (b * gram + c * (gram @ gram)) @ y
     return y
+
+
+def native_module():  # noqa: ANN201
+    from priml_b200.ops._loader import native
+
+    return native()
 
 
 def _native_ok(y: Tensor) -> bool:
@@ -78,6 +85,23 @@ def _chain(y: Tensor, coefficients: Sequence[tuple[float, float, float]]) -> Ten
     return cur
 
 
+def _chain_batched(y: Tensor, coefficients: Sequence[tuple[float, float, float]]) -> Tensor:
+    """Steps on a contiguous ``[B, m, n]`` stack (m, n multiples of 256): every GEMM is one launch for the stack."""
+    from priml_b200.ops._loader import native
+
+    nat = native()
+    b, m, _ = y.shape
+    gram = torch.empty(b, m, m, device=y.device, dtype=torch.bfloat16)
+    poly = torch.empty_like(gram)
+    cur, nxt = y, torch.empty_like(y)
+    for a, bb, c in coefficients:
+        nat.gemm_batched(cur, cur, gram, False, False)  # A = Y Y^T
+        nat.gemm_batched(gram, gram, poly, False, False, gram, float(c), float(bb))  # B = c A A + b A
+        nat.gemm_batched(poly, cur, nxt, False, True, cur, 1.0, float(a))  # Y' = B Y + a Y
+        cur, nxt = nxt, cur
+    return cur
+
+
 def newton_schulz_steps(y: Tensor, coefficients: Sequence[tuple[float, float, float]]) -> Tensor:
     """Apply the ``(a, b, c)`` steps to each matrix of an already normalised ``[..., m, n]`` tensor.
 
@@ -93,6 +117,11 @@ def newton_schulz_steps(y: Tensor, coefficients: Sequence[tuple[float, float, fl
     wide = mats.transpose(-2, -1).contiguous() if tall else mats.clone()  # the chain overwrites its input
     out = torch.empty_like(wide)
     m, n = wide.shape[-2:]
+    if m % 256 == 0 and n % 256 == 0 and hasattr(native_module(), "gemm_batched"):
+        out = _chain_batched(wide, coefficients)
+        if tall:
+            out = out.transpose(-2, -1)
+        return out.reshape(shape)
     pair_tiles = ((m + 255) // 256) * ((n + 255) // 256)
     sms = torch.cuda.get_device_properties(y.device).multi_processor_count
     lanes = max(1, min(len(wide), 8, (sms // 2) // max(1, pair_tiles)))

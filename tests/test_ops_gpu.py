@@ -367,7 +367,30 @@ def test_gemm_scaled_add_epilogue(a_mn: bool, b_mn: bool, m: int, n: int, k: int
     assert _rel_err(c, ref) < 1e-2
 
 
-@pytest.mark.parametrize("shape", [(4, 768, 3072), (2, 2048, 512), (1, 1024, 1024), (3, 300, 200)])
+@pytest.mark.parametrize("a_mn,b_mn", LAYOUTS)
+@pytest.mark.parametrize("scaled", [False, True])
+def test_gemm_batched_matches_fp32(a_mn: bool, b_mn: bool, scaled: bool) -> None:
+    """One launch over a stack of products, plain and scaled-add epilogues."""
+    torch.manual_seed(int(a_mn) + 2 * int(b_mn) + 4 * int(scaled))
+    bsz, m, n, k = 3, 512, 256, 192
+    a = torch.randn(bsz, k, m, device="cuda").to(torch.bfloat16) if a_mn else torch.randn(bsz, m, k, device="cuda").to(torch.bfloat16)
+    b = torch.randn(bsz, k, n, device="cuda").to(torch.bfloat16) if b_mn else torch.randn(bsz, n, k, device="cuda").to(torch.bfloat16)
+    x = torch.randn(bsz, m, n, device="cuda").to(torch.bfloat16)
+    c = torch.empty(bsz, m, n, device="cuda", dtype=torch.bfloat16)
+    if scaled:
+        _native().gemm_batched(a, b, c, a_mn, b_mn, x, 0.5, -2.0)
+    else:
+        _native().gemm_batched(a, b, c, a_mn, b_mn)
+    af = a.float().transpose(1, 2) if a_mn else a.float()
+    bf = b.float() if b_mn else b.float().transpose(1, 2)
+    ref = af @ bf
+    if scaled:
+        ref = 0.5 * ref - 2.0 * x.float()
+    for i in range(bsz):
+        assert _rel_err(c[i], ref[i]) < 1e-2, i
+
+
+@pytest.mark.parametrize("shape", [(4, 768, 3072), (2, 2048, 512), (1, 1024, 1024), (3, 392, 520), (3, 300, 200)])
 def test_newton_schulz_chain_matches_fp32(shape: tuple[int, ...]) -> None:
     """The tcgen05 Polar-Express chain (wide, tall, square, and a shape the torch path takes)
     against the same polynomial in fp32; its output is near-orthogonal."""
