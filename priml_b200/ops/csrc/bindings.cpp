@@ -593,6 +593,7 @@ Tensor decode_attn(const Tensor& q, const Tensor& k, const Tensor& v, const Tens
   p.chunk = (T + splits - 1) / splits;
   p.window = static_cast<int>(window);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.status = status_ptr();
   pb::decode_attn(p, B, D, stream());
   return out;
 }

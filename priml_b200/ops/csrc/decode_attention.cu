@@ -3,26 +3,30 @@
 //
 // Decoding reads every cached key and value once per token and does a handful of
 // FLOPs per byte, so the kernel is built for HBM bandwidth, not the tensor
-// cores: 16-byte row loads, several keys in flight per lane, and a split over
-// the key axis so that even one sequence with a few KV heads spreads over all
-// SMs. Lengths are read on the device, which keeps a whole decode step free of
-// host synchronisation and capturable in one CUDA graph.
+// cores. The rows of one (sequence, KV head) are contiguous in the cache, so a
+// producer thread streams them in 64-row chunks with bulk copies into a ring of
+// shared-memory stages (mbarrier completion) and four consumer warps read them
+// from there: each CTA keeps several chunks of K and V in flight without spending
+// registers on them. A split over the key axis spreads even one sequence with a
+// few KV heads over all SMs. Lengths are read on the device, which keeps a whole
+// decode step free of host synchronisation and capturable in one CUDA graph.
 //
 // Layout: q [B, H, D]; caches [B, Hkv, T, D] with contiguous rows (any batch and
 // head strides); lengths int32 [B] = keys visible to the query (its own key
 // included, already written). Query head h reads KV head h / (H / Hkv).
 // A window w >= 0 hides keys older than position len - 1 - w.
 //
-// Per CTA: GT query heads of one KV head over one key split. A key row is spread
-// over D/8 lanes (8 channels each); a warp covers 32/(D/8) rows per load. Each
-// lane group scores a batch of rows (4, or 2 at eight heads per CTA) before one
-// running-max update, so the exp and rescale work is shared by the batch. Partial (max, sum, acc) per split go to a
-// workspace that the combine kernel merges; with one split the kernel writes the
-// output directly.
+// Per CTA: GT query heads of one KV head over one key split. In a consumer warp a
+// key row is spread over D/8 lanes (8 channels each) and 32/(D/8) rows are scored
+// per instruction; a lane group scores 4 rows before one running-max update, so
+// the exp and rescale work is shared by the batch. Partial (max, sum, acc) per
+// split go to a workspace that the combine kernel merges; with one split the
+// kernel writes the output directly.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace pb {
@@ -49,148 +53,200 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 // exp2 of a difference whose larger side may be -inf (an empty partial): 0 then.
 __device__ __forceinline__ float exp2_or_zero(float x, float m) { return m == -INFINITY ? 0.f : exp2f(x - m); }
 
+template <int D>
+struct DecCfg {
+  static constexpr int kRows = 64;                       // keys per pipeline chunk
+  static constexpr int kStages = D == 64 ? 4 : 3;
+  static constexpr int kChunkBytes = kRows * D * 2;      // one chunk of K (or V): contiguous cache rows
+  static constexpr int kSmem = kStages * 2 * kChunkBytes + 2 * kStages * 8 + 16;
+};
+
+// Warps 0..3 consume (16 keys of every 64-key chunk each); warp 4's lane 0 streams the chunks of K
+// and V into a ring of shared-memory stages with bulk copies (the rows of one (sequence, KV head)
+// are contiguous), so each CTA keeps up to kStages chunks in flight without holding them in
+// registers. Every wait is bounded; a wait that runs out records kTimeoutProducer and the CTA
+// stops early (its partial then only covers the chunks it finished).
 template <int D, int GT>
-__global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(DecodeAttnParams p) {
-  constexpr int LPK = D / 8;       // lanes per key row
-  constexpr int GPW = 32 / LPK;    // key rows per warp load
-  constexpr int NG = kDecWarps * GPW;
-  constexpr int kBatch = GT >= 8 ? 2 : 4;  // rows per lane between max updates (register bound at 8 heads)
+__global__ void __launch_bounds__(kDecThreads + 32) decode_attn_kernel(DecodeAttnParams p) {
+  using Cfg = DecCfg<D>;
+  constexpr int LPK = D / 8;     // lanes per key row
+  constexpr int GPW = 32 / LPK;  // key rows per warp instruction
+  constexpr int kWarpRows = Cfg::kRows / kDecWarps;
+  constexpr int kBatch = GT >= 8 ? 2 : 4;  // rows per lane group between running-max updates
+  constexpr int kRounds = kWarpRows / (GPW * kBatch);
+  static_assert(kWarpRows % (GPW * kBatch) == 0, "rows per warp must split into batches");
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ks = smem;
+  uint8_t* vs = smem + S * Cfg::kChunkBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * S * Cfg::kChunkBytes);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  __shared__ float red[kDecWarps][GT][D + 2];  // per consumer warp: channels, then (max, sum)
+
   const int split = blockIdx.x;
-  const int head0 = blockIdx.y * GT;  // first query head of this CTA
+  const int head0 = blockIdx.y * GT;
   const int b = blockIdx.z;
   const int hk = head0 / p.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane % LPK;
-  const int grp = warp * GPW + lane / LPK;
 
   const int len = min(max(p.lengths[b], 0), p.T);
   int lo = split * p.chunk;
   const int hi = min(lo + p.chunk, len);
   if (p.window >= 0) lo = max(lo, len - 1 - p.window);
+  const int nchunks = hi > lo ? (hi - lo + Cfg::kRows - 1) / Cfg::kRows : 0;
 
-  float qf[GT][8];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    const uint4 raw =
-        *reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * p.H + head0 + h) * D + sub * 8);
-    unpack8(raw, qf[h]);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) qf[h][c] *= p.scale_log2;
-  }
-  float m[GT], l[GT], acc[GT][8];
-#pragma unroll
-  for (int h = 0; h < GT; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[h][c] = 0.f;
-  }
-
-  const __nv_bfloat16* kb = p.k + b * p.k_sb + hk * p.k_sh + sub * 8;
-  const __nv_bfloat16* vb = p.v + b * p.v_sb + hk * p.v_sh + sub * 8;
-  // The loop bound is the same for every lane: the row shuffles below name the whole warp, so
-  // no lane may leave the loop while others still run it (a lane group whose rows are all past
-  // `hi` scores -inf and adds nothing).
-  for (int base = lo; base < hi; base += NG * kBatch) {
-    const int j0 = base + grp;
-    uint4 kr[kBatch], vr[kBatch];
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const int j = j0 + i * NG;
-      if (j < hi) {
-        kr[i] = __ldg(reinterpret_cast<const uint4*>(kb + static_cast<long long>(j) * D));
-        vr[i] = __ldg(reinterpret_cast<const uint4*>(vb + static_cast<long long>(j) * D));
-      } else {
-        kr[i] = make_uint4(0, 0, 0, 0);
-        vr[i] = make_uint4(0, 0, 0, 0);
-      }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kDecWarps);
     }
-    float s[kBatch][GT];
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kDecWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const __nv_bfloat16* kb = p.k + b * p.k_sb + hk * p.k_sh;
+      const __nv_bfloat16* vb = p.v + b * p.v_sb + hk * p.v_sh;
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % S;
+        if (c >= S && !mbar_wait(&empty[st], ((c / S) - 1) & 1, p.status, kTimeoutProducer, abort_flag)) break;
+        const int base = lo + c * Cfg::kRows;
+        const uint32_t bytes = static_cast<uint32_t>(min(Cfg::kRows, hi - base)) * D * 2;
+        mbar_arrive_expect_tx(&full[st], 2 * bytes);
+        bulk_load(ks + st * Cfg::kChunkBytes, kb + static_cast<long long>(base) * D, bytes, &full[st]);
+        bulk_load(vs + st * Cfg::kChunkBytes, vb + static_cast<long long>(base) * D, bytes, &full[st]);
+        issued = c + 1;
+      }
+      // No copy may still be landing in shared memory when the CTA exits: wait (bounded) for the
+      // last chunk issued on every stage. In a normal run the consumers already saw them all.
+      for (int c = max(0, issued - S); c < issued; ++c) mbar_wait(&full[c % S], (c / S) & 1, p.status, kTimeoutDrain, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int sub = lane % LPK;
+    const int grp = lane / LPK;
+    float qf[GT][8];
 #pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      float kf[8];
-      unpack8(kr[i], kf);
+    for (int h = 0; h < GT; ++h) {
+      const uint4 raw =
+          *reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * p.H + head0 + h) * D + sub * 8);
+      unpack8(raw, qf[h]);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) qf[h][c] *= p.scale_log2;
+    }
+    float m[GT], l[GT], acc[GT][8];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+      m[h] = -INFINITY;
+      l[h] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[h][c] = 0.f;
+    }
+    for (int c = 0; c < nchunks; ++c) {
+      const int st = c % S;
+      if (!mbar_wait_warp(&full[st], (c / S) & 1, p.status, kTimeoutProducer, abort_flag)) break;
+      const int valid = min(Cfg::kRows, hi - (lo + c * Cfg::kRows));  // rows of this chunk (all lanes agree)
+      const uint8_t* kc = ks + st * Cfg::kChunkBytes;
+      const uint8_t* vc = vs + st * Cfg::kChunkBytes;
+#pragma unroll
+      for (int rd = 0; rd < kRounds; ++rd) {
+        float sc[kBatch][GT];
+        int rows[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          rows[i] = warp * kWarpRows + (rd * kBatch + i) * GPW + grp;
+          const uint4 kr = *reinterpret_cast<const uint4*>(kc + rows[i] * (D * 2) + sub * 16);
+          float kf[8];
+          unpack8(kr, kf);
+#pragma unroll
+          for (int h = 0; h < GT; ++h) {
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = fmaf(qf[h][e], kf[e], d);
+            sc[i][h] = d;
+          }
+        }
+#pragma unroll
+        for (int off = LPK / 2; off > 0; off >>= 1) {
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i)
+#pragma unroll
+            for (int h = 0; h < GT; ++h) sc[i][h] += __shfl_xor_sync(0xffffffffu, sc[i][h], off);
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (rows[i] >= valid) {
+#pragma unroll
+            for (int h = 0; h < GT; ++h) sc[i][h] = -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < GT; ++h) {
+          float mx = sc[0][h];
+#pragma unroll
+          for (int i = 1; i < kBatch; ++i) mx = fmaxf(mx, sc[i][h]);
+          const float mn = fmaxf(m[h], mx);  // -inf while this lane group has seen no valid row
+          const float corr = exp2_or_zero(m[h], mn);
+          l[h] *= corr;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[h][e] *= corr;
+          m[h] = mn;
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          float vf[8];
+          unpack8(*reinterpret_cast<const uint4*>(vc + rows[i] * (D * 2) + sub * 16), vf);
+#pragma unroll
+          for (int h = 0; h < GT; ++h) {
+            const float pr = exp2_or_zero(sc[i][h], m[h]);  // 0 for a row past the end (-inf)
+            l[h] += pr;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[h][e] = fmaf(pr, vf[e], acc[h][e]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+
+    // Merge the key groups of a warp (lanes with the same channel slice).
+#pragma unroll
+    for (int off = LPK; off < 32; off <<= 1) {
 #pragma unroll
       for (int h = 0; h < GT; ++h) {
-        float d = 0.f;
+        const float m2 = __shfl_xor_sync(0xffffffffu, m[h], off);
+        const float l2 = __shfl_xor_sync(0xffffffffu, l[h], off);
+        const float mn = fmaxf(m[h], m2);
+        const float c1 = exp2_or_zero(m[h], mn), c2 = exp2_or_zero(m2, mn);
+        l[h] = l[h] * c1 + l2 * c2;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) d = fmaf(qf[h][c], kf[c], d);
-        s[i][h] = d;
+        for (int e = 0; e < 8; ++e) {
+          const float a2 = __shfl_xor_sync(0xffffffffu, acc[h][e], off);
+          acc[h][e] = acc[h][e] * c1 + a2 * c2;
+        }
+        m[h] = mn;
       }
     }
-#pragma unroll
-    for (int off = LPK / 2; off > 0; off >>= 1) {
-#pragma unroll
-      for (int i = 0; i < kBatch; ++i)
-#pragma unroll
-        for (int h = 0; h < GT; ++h) s[i][h] += __shfl_xor_sync(0xffffffffu, s[i][h], off);
-    }
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      if (j0 + i * NG >= hi) {
-#pragma unroll
-        for (int h = 0; h < GT; ++h) s[i][h] = -INFINITY;
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      float mx = s[0][h];
-#pragma unroll
-      for (int i = 1; i < kBatch; ++i) mx = fmaxf(mx, s[i][h]);
-      const float mn = fmaxf(m[h], mx);  // -inf while this lane group has seen no valid row
-      const float corr = exp2_or_zero(m[h], mn);
-      l[h] *= corr;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[h][c] *= corr;
-      m[h] = mn;
-    }
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      float vf[8];
-      unpack8(vr[i], vf);
+    if (lane < LPK) {
 #pragma unroll
       for (int h = 0; h < GT; ++h) {
-        const float pr = exp2_or_zero(s[i][h], m[h]);  // 0 for an invalid row (-inf)
-        l[h] += pr;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) acc[h][c] = fmaf(pr, vf[c], acc[h][c]);
-      }
-    }
-  }
-
-  // Merge the key groups of a warp (lanes with the same channel slice).
-#pragma unroll
-  for (int off = LPK; off < 32; off <<= 1) {
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m[h], off);
-      const float l2 = __shfl_xor_sync(0xffffffffu, l[h], off);
-      const float mn = fmaxf(m[h], m2);
-      const float c1 = exp2_or_zero(m[h], mn), c2 = exp2_or_zero(m2, mn);
-      l[h] = l[h] * c1 + l2 * c2;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float a2 = __shfl_xor_sync(0xffffffffu, acc[h][c], off);
-        acc[h][c] = acc[h][c] * c1 + a2 * c2;
-      }
-      m[h] = mn;
-    }
-  }
-
-  // Merge the warps through shared memory: [warp][head][D channels + (max, sum)].
-  __shared__ float red[kDecWarps][GT][D + 2];
-  if (lane < LPK) {
-#pragma unroll
-    for (int h = 0; h < GT; ++h) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) red[warp][h][sub * 8 + c] = acc[h][c];
-      if (sub == 0) {
-        red[warp][h][D] = m[h];
-        red[warp][h][D + 1] = l[h];
+        for (int e = 0; e < 8; ++e) red[warp][h][sub * 8 + e] = acc[h][e];
+        if (sub == 0) {
+          red[warp][h][D] = m[h];
+          red[warp][h][D + 1] = l[h];
+        }
       }
     }
   }
   __syncthreads();
+
+  // Merge the four consumer warps: thread t owns 8 channels of one head.
   const int t = threadIdx.x;
   if (t >= GT * LPK) return;
   const int h = t / LPK, sl = t % LPK;
@@ -203,7 +259,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(DecodeAttnPara
     const float c = exp2_or_zero(red[w][h][D], M);
     L += red[w][h][D + 1] * c;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] += red[w][h][sl * 8 + k] * c;
+    for (int e = 0; e < 8; ++e) o[e] += red[w][h][sl * 8 + e] * c;
   }
   const long long row = static_cast<long long>(b) * p.H + head0 + h;
   if (p.splits == 1) {
@@ -264,7 +320,12 @@ __global__ void decode_combine_kernel(DecodeAttnParams p, int rows) {
 template <int D, int GT>
 void launch_decode(const DecodeAttnParams& p, int B, cudaStream_t stream) {
   const dim3 grid(p.splits, p.H / GT, B);
-  decode_attn_kernel<D, GT><<<grid, kDecThreads, 0, stream>>>(p);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(decode_attn_kernel<D, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecCfg<D>::kSmem);
+    configured = true;
+  }
+  decode_attn_kernel<D, GT><<<grid, kDecThreads + 32, DecCfg<D>::kSmem, stream>>>(p);
   if (p.splits > 1) {
     const int rows = B * p.H;
     decode_combine_kernel<D><<<(rows + 3) / 4, 128, 0, stream>>>(p, rows);

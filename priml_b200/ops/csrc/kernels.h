@@ -266,6 +266,7 @@ struct DecodeAttnParams {
   float* part_ml;          // [B, H, splits, 2]
   int H, group, T, splits, chunk, window;
   float scale_log2;        // softmax scale * log2(e)
+  int* status;             // error word for a wait that runs out
 };
 int decode_attn_heads_per_cta(int group);
 int decode_attn_splits(int B, int H, int group, int T, int sm_count);

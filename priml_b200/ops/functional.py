@@ -73,10 +73,21 @@ def attach_shadow(param: Tensor) -> Tensor:
 
 
 def mark_shadow_fresh(param: Tensor) -> None:
-    """Declare the cached shadow current after a kernel rewrote it in place."""
+    """Declare the cached shadow current after a kernel rewrote it in place.
+
+    Caches derived from the old values (quantized MXFP8 copies) are dropped: the
+    kernel bypassed the version counter their keys check.
+    """
     cached = getattr(param, "_pb_shadow", None)
     if cached is not None:
         param._pb_shadow = (param._version, cached[1])  # noqa: SLF001
+    forget_quantized(param)
+
+
+def forget_quantized(param: Tensor) -> None:
+    """Drop the quantized copies cached on a weight whose values a kernel rewrote in place."""
+    if "_pb_mx" in getattr(param, "__dict__", {}):
+        del param.__dict__["_pb_mx"]
 
 
 class GradSink:

@@ -148,6 +148,9 @@ class FusedAdamW(Optimizer):
         for p, s in zip(params, shadows, strict=True):
             if s is not None:
                 fn.mark_shadow_fresh(_local(p))
+            else:
+                fn.forget_quantized(_local(p))
+            fn.forget_quantized(p)
         return True
 
     @torch.no_grad()

@@ -287,6 +287,16 @@ class ShardedState:
             self.window_holds[b.slot] = b.index
         else:
             b.valid = True
+        self._forget_derived(b.entries)
+
+    @staticmethod
+    def _forget_derived(entries: Iterable[_Entry]) -> None:
+        """Drop per-parameter caches derived from the weight values (quantized MXFP8 copies): the
+        kernels that rewrite the bf16 weights bypass the version counters those caches check."""
+        for e in entries:
+            for attr in ("_pb_mx", "_pb_shadow"):
+                if attr in e.param.__dict__:
+                    del e.param.__dict__[attr]
 
     def _present(self, b: _Bucket) -> bool:
         return self.window_holds[b.slot] == b.index if b.slot is not None else b.valid
@@ -353,7 +363,8 @@ class ShardedState:
             blk.register_full_backward_pre_hook(bwd(i))
 
     def weights_changed(self) -> None:
-        """After an optimizer step: every gathered window is stale."""
+        """After an optimizer step: every gathered window (and every cache derived from a weight) is stale."""
+        self._forget_derived(self.entries)
         if not self.shard_params:
             return
         self.window_holds = [None, None]

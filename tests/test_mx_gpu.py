@@ -85,3 +85,24 @@ def test_mx_linear_matches_reference_path(wgrad_hp: bool) -> None:
     assert rel(y.detach(), yr.detach()) < 1e-2
     assert rel(dx, rx) < 1e-2
     assert rel(dw, rw) < 1e-2
+
+
+def test_mx_weight_copies_follow_optimizer_steps() -> None:
+    """The fused AdamW kernel rewrites the weights in place; the cached MXFP8 weight copies must
+    not outlive that: after a step the quantized forward equals a fresh quantization of the new
+    weights."""
+    from priml_b200.ops.mx import _MXLinearRef, mx_linear
+    from priml_b200.optimizers import FusedAdamW
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    w = torch.nn.Parameter(torch.randn(256, 128, device="cuda", generator=g) / 128**0.5)
+    x = torch.randn(64, 128, device="cuda", generator=g).to(torch.bfloat16)
+    opt = FusedAdamW([w], lr=0.05)
+    for _ in range(3):
+        y = mx_linear(x, w)
+        y.float().square().mean().backward()
+        opt.step()
+        opt.zero_grad()
+    fresh = _MXLinearRef.apply(x.float(), w.detach().to(torch.bfloat16).float(), False)
+    y = mx_linear(x, w).detach().float()
+    assert float((y - fresh).abs().max() / fresh.abs().max()) < 1e-2
