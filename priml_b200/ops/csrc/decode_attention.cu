@@ -199,8 +199,12 @@ __global__ void __launch_bounds__(kDecThreads + 32) decode_attn_kernel(DecodeAtt
         }
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
+          // rows past the end of a partial chunk hold whatever the stage held before (possibly NaN
+          // bit patterns): their weight is 0, and so must their values be
           float vf[8];
-          unpack8(*reinterpret_cast<const uint4*>(vc + rows[i] * (D * 2) + sub * 16), vf);
+          unpack8(rows[i] < valid ? *reinterpret_cast<const uint4*>(vc + rows[i] * (D * 2) + sub * 16)
+                                  : make_uint4(0u, 0u, 0u, 0u),
+                  vf);
 #pragma unroll
           for (int h = 0; h < GT; ++h) {
             const float pr = exp2_or_zero(sc[i][h], m[h]);  // 0 for a row past the end (-inf)

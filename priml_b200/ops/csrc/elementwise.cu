@@ -123,13 +123,16 @@ __global__ void rmsnorm_bwd_kernel(const void* __restrict__ dy, bool dy_f32, con
                                    const float* __restrict__ w, const float* __restrict__ rstd,
                                    const void* __restrict__ dres, bool dres_f32, void* __restrict__ dx, bool dx_f32,
                                    void* __restrict__ dx2, bool dx2_f32, float* __restrict__ dw, int R, int C) {
-  extern __shared__ float dw_acc[];  // C floats when dw != nullptr
-  if (dw != nullptr) {
-    for (int c = threadIdx.x; c < C; c += blockDim.x) dw_acc[c] = 0.f;
-    __syncthreads();
-  }
+  // dw: every warp sums its rows' dy * xhat into its own C-float slice of shared memory (each lane
+  // owns fixed columns, so the adds need no atomics); the slices are summed once at the end.
+  extern __shared__ float dw_acc[];  // warps * C floats when dw != nullptr
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
+  float* my_dw = dw_acc + (threadIdx.x >> 5) * C;
+  if (dw != nullptr) {
+    for (int c = threadIdx.x; c < warps * C; c += blockDim.x) dw_acc[c] = 0.f;
+    __syncthreads();
+  }
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < R; row += gridDim.x * warps) {
     const long long base = static_cast<long long>(row) * C;
     const float r = rstd[row];
@@ -157,7 +160,7 @@ __global__ void rmsnorm_bwd_kernel(const void* __restrict__ dy, bool dy_f32, con
         const float xh = v[j] * r;
         const float wg = g[j] * (w != nullptr ? w[c + j] : 1.f);
         o[j] += r * (wg - xh * dot);
-        if (dw != nullptr) atomicAdd(&dw_acc[c + j], g[j] * xh);
+        if (dw != nullptr) my_dw[c + j] += g[j] * xh;
       }
       store8(dx, dx_f32, base + c, o);
       if (dx2 != nullptr) store8(dx2, dx2_f32, base + c, o);
@@ -165,7 +168,11 @@ __global__ void rmsnorm_bwd_kernel(const void* __restrict__ dy, bool dy_f32, con
   }
   if (dw != nullptr) {
     __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x) atomicAdd(&dw[c], dw_acc[c]);
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float sum = 0.f;
+      for (int q = 0; q < warps; ++q) sum += dw_acc[q * C + c];
+      atomicAdd(&dw[c], sum);
+    }
   }
 }
 
@@ -439,11 +446,17 @@ void rmsnorm_fwd(const void* x, bool x_f32, const float* w, void* y, bool y_f32,
 void rmsnorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* w, const float* rstd, void* dx,
                  bool dx_f32, float* dw, int R, int C, cudaStream_t stream, const void* dres, bool dres_f32, void* dx2,
                  bool dx2_f32) {
-  const int warps = 8;
-  int blocks = (R + warps - 1) / warps;
-  const size_t smem = dw != nullptr ? static_cast<size_t>(C) * sizeof(float) : 0;
+  // With dw, each warp keeps a C-float slice in shared memory: at most 96 KB per block.
+  int warps = 8;
   if (dw != nullptr) {
-    const int cap = device_sm_count() * 4;
+    const int fit = static_cast<int>((96 * 1024) / (static_cast<size_t>(C) * sizeof(float)));
+    warps = fit < 1 ? 1 : (fit < 8 ? fit : 8);
+  }
+  int blocks = (R + warps - 1) / warps;
+  const size_t smem = dw != nullptr ? static_cast<size_t>(warps) * C * sizeof(float) : 0;
+  if (dw != nullptr) {
+    const int per_sm = static_cast<int>((200 * 1024) / smem);  // resident blocks the shared slices allow
+    const int cap = device_sm_count() * (per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm));
     blocks = blocks < cap ? blocks : cap;
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
