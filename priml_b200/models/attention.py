@@ -36,12 +36,16 @@ __all__ = [
 ]
 
 
+_WINDOW_SHARE = {"S": 2, "L": 1}  # a short layer sees half the context, a long layer all of it
+
+
 def layer_window(*, depth: int, max_seq_len: int, pattern: str) -> int:
     """Window of layer ``depth`` from a cycled ``S`` (half) / ``L`` (full) pattern."""
-    pattern = pattern.upper()
-    if not pattern or set(pattern) - set("SL"):
-        raise ValueError(f"pattern must hold only S and L; got {pattern!r}.")
-    return max_seq_len if pattern[depth % len(pattern)] == "L" else max_seq_len // 2
+    letters = pattern.upper()
+    unknown = sorted(set(letters) - set(_WINDOW_SHARE))
+    if not letters or unknown:
+        raise ValueError(f"window pattern {pattern!r} needs one or more letters from 'S' / 'L' (found {unknown}).")
+    return max_seq_len // _WINDOW_SHARE[letters[depth % len(letters)]]
 
 
 def window_sizes(*, num_layers: int, max_seq_len: int, pattern: str) -> list[int]:

@@ -36,10 +36,12 @@ from priml_b200.models.rope import RoPE
 __all__ = ["MultiHeadLatentAttention"]
 
 
-def _fill_unset(cfg: Any, name: str, value: Any) -> None:
-    default = type(cfg).__dataclass_fields__[name].default
-    if getattr(cfg, name) == default:
-        setattr(cfg, name, value)
+def _inherit(cfg: Any, **values: Any) -> None:
+    """Give a projection's config the attention's settings wherever it still has its class default."""
+    fields = type(cfg).__dataclass_fields__
+    for name, value in values.items():
+        if getattr(cfg, name) == fields[name].default:
+            setattr(cfg, name, value)
 
 
 class MultiHeadLatentAttention(nn.Module):
@@ -98,15 +100,13 @@ class MultiHeadLatentAttention(nn.Module):
                 slots.append((self.proj_q_a, self.channels_in, self.q_lora_rank))
                 slots.append((self.proj_q_b, self.q_lora_rank, qk_out))
             for slot, c_in, c_out in slots:
-                if isinstance(slot, ChannelsIn) and slot.channels_in == -1:
-                    slot.channels_in = c_in
-                if isinstance(slot, ChannelsOut) and slot.channels_out == -1:
-                    slot.channels_out = c_out
+                widths = {"channels_in": c_in, "channels_out": c_out}
+                for attr, proto in (("channels_in", ChannelsIn), ("channels_out", ChannelsOut)):
+                    if isinstance(slot, proto) and getattr(slot, attr) == -1:
+                        setattr(slot, attr, widths[attr])
                 if isinstance(slot, Linear.Config):
-                    _fill_unset(slot, "bias", self.bias)
-                    _fill_unset(slot, "init_weight", self.init_weight)
-                    if slot.depth == -1:
-                        slot.depth = self.depth
+                    _inherit(slot, bias=self.bias, init_weight=self.init_weight)
+                    slot.depth = self.depth if slot.depth == -1 else slot.depth
             return super().finalize()
 
     def __init__(self, config: Config) -> None:

@@ -176,15 +176,16 @@ class RoPE(nn.Module):
         return self
 
     def _build_inv_freqs(self, device: torch.device) -> None:
-        self._inv_freqs = [torch.empty(0, device=device) for _ in self.channels_head]
-        for i, (b, c) in enumerate(zip(self.base, self.channels_head, strict=True)):
-            if c == 0:
-                continue
-            self._validate_c(c)
-            inv = self._make_inv_freqs(b, c, hf=self._hf_inv_freq, device=device)
+        def axis(base: float, width: int) -> Tensor:
+            if width == 0:  # an axis without rotary channels
+                return torch.empty(0, device=device)
+            self._validate_c(width)
+            freqs = self._make_inv_freqs(base, width, hf=self._hf_inv_freq, device=device)
             if self._yarn is not None:
-                inv, self._mscale = _yarn_apply(inv, b, c, self._yarn)
-            self._inv_freqs[i] = inv.unsqueeze(-2)
+                freqs, self._mscale = _yarn_apply(freqs, base, width, self._yarn)
+            return freqs.unsqueeze(-2)
+
+        self._inv_freqs = [axis(b, c) for b, c in zip(self.base, self.channels_head, strict=True)]
 
     @classmethod
     def _make_inv_freqs(cls, b: float, c: int, *, hf: bool = False, device: torch.device | None = None) -> Tensor:
@@ -195,17 +196,13 @@ class RoPE(nn.Module):
 
     @classmethod
     def _validate_c(cls, c: int) -> None:
-        if c < 2:
-            raise ValueError(f"Dim {c} must be at least 2.")
-        if c % 2:
-            raise ValueError(f"Dim {c} must be even.")
+        if c < 2 or c % 2:
+            raise ValueError(f"a rotary axis needs an even number (at least 2) of channels; got {c}.")
 
     @classmethod
     def _split_dim(cls, total: int, naxes: int) -> list[int]:
-        if total % 2:
-            raise ValueError(f"Total dim={total} must be even.")
-        if total < 2 * naxes:
-            raise ValueError(f"Cannot split dim={total} across {naxes} axes.")
+        if total % 2 or total < 2 * naxes:
+            raise ValueError(f"{total} rotary channels cannot be shared as channel pairs by {naxes} axes.")
         per = total // naxes // 2 * 2
         dims = [per] * naxes
         for i in range((total - per * naxes) // 2):

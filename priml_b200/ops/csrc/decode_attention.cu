@@ -285,40 +285,56 @@ __global__ void __launch_bounds__(kDecThreads + 32) decode_attn_kernel(DecodeAtt
   }
 }
 
-// One warp per (sequence, head): merge the splits' partials into the output row.
+// One warp per (sequence, head) merges the splits' partials. The lanes split the work two ways:
+// LPK lanes cover the D channels (8 each) and 32 / LPK lane groups take every (32 / LPK)-th
+// split, so the split loop is short and its loads independent; the groups then combine
+// their (max, sum, acc) with shuffles.
 template <int D>
 __global__ void decode_combine_kernel(DecodeAttnParams p, int rows) {
   constexpr int LPK = D / 8;
+  constexpr int G = 32 / LPK;  // split groups per warp
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= rows || lane >= LPK) return;
+  if (row >= rows) return;  // whole warps leave together
+  const int sl = lane % LPK, grp = lane / LPK;
   const float* ml = p.part_ml + static_cast<long long>(row) * p.splits * 2;
   float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, ml[2 * s]);
+  for (int s = grp; s < p.splits; s += G) M = fmaxf(M, ml[2 * s]);
   float L = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < p.splits; ++s) {
+  for (int s = grp; s < p.splits; s += G) {
     const float c = exp2_or_zero(ml[2 * s], M);
-    if (c == 0.f) continue;
     L += ml[2 * s + 1] * c;
-    const float4* pa = reinterpret_cast<const float4*>(p.part_acc + (static_cast<long long>(row) * p.splits + s) * D +
-                                                       lane * 8);
+    const float4* pa =
+        reinterpret_cast<const float4*>(p.part_acc + (static_cast<long long>(row) * p.splits + s) * D + sl * 8);
     const float4 a = pa[0], bb = pa[1];
-    o[0] += a.x * c;
-    o[1] += a.y * c;
-    o[2] += a.z * c;
-    o[3] += a.w * c;
-    o[4] += bb.x * c;
-    o[5] += bb.y * c;
-    o[6] += bb.z * c;
-    o[7] += bb.w * c;
+    o[0] = fmaf(a.x, c, o[0]);
+    o[1] = fmaf(a.y, c, o[1]);
+    o[2] = fmaf(a.z, c, o[2]);
+    o[3] = fmaf(a.w, c, o[3]);
+    o[4] = fmaf(bb.x, c, o[4]);
+    o[5] = fmaf(bb.y, c, o[5]);
+    o[6] = fmaf(bb.z, c, o[6]);
+    o[7] = fmaf(bb.w, c, o[7]);
   }
+#pragma unroll
+  for (int off = LPK; off < 32; off <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, M, off);
+    const float l2 = __shfl_xor_sync(0xffffffffu, L, off);
+    const float mn = fmaxf(M, m2);
+    const float c1 = exp2_or_zero(M, mn), c2 = exp2_or_zero(m2, mn);
+    L = L * c1 + l2 * c2;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = o[e] * c1 + __shfl_xor_sync(0xffffffffu, o[e], off) * c2;
+    M = mn;
+  }
+  if (grp != 0) return;
   const float inv = L > 0.f ? 1.f / L : 0.f;
   uint4 raw;
   raw.x = pack2(o[0] * inv, o[1] * inv);
   raw.y = pack2(o[2] * inv, o[3] * inv);
   raw.z = pack2(o[4] * inv, o[5] * inv);
   raw.w = pack2(o[6] * inv, o[7] * inv);
-  *reinterpret_cast<uint4*>(p.out + static_cast<long long>(row) * D + lane * 8) = raw;
+  *reinterpret_cast<uint4*>(p.out + static_cast<long long>(row) * D + sl * 8) = raw;
 }
 
 template <int D, int GT>
@@ -357,8 +373,8 @@ int decode_attn_heads_per_cta(int group) {
 
 int decode_attn_splits(int B, int H, int group, int T, int sm_count) {
   const int ctas = B * (H / decode_attn_heads_per_cta(group));
-  const int want = (4 * sm_count + ctas - 1) / ctas;  // about four CTAs per SM
-  const int most = (T + 63) / 64;                      // at least 64 keys per split
+  const int want = (2 * sm_count + ctas - 1) / ctas;  // about two CTAs per SM
+  const int most = (T + 255) / 256;                    // at least four 64-key chunks per split (a full ring)
   return want < 1 ? 1 : (want < most ? want : (most < 1 ? 1 : most));
 }
 
