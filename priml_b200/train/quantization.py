@@ -16,9 +16,11 @@ Conversion swaps each selected ``nn.Linear`` (default filter: bias-free, both
 dimensions multiples of 32) to a subclass whose forward runs
 :func:`priml_b200.ops.mx.mx_linear`; parameters and state-dict keys are
 unchanged, so checkpoints move freely between quantized and bf16 models.
-``enable_fsdp_float8_all_gather`` is accepted; the fused sharded strategy keeps
-weights resident and all-gathers only the optimizer's bf16 output, so no
-per-step weight all-gather exists to shrink.
+``enable_fsdp_float8_all_gather`` is accepted and has no effect: with resident
+weights the fused sharded strategy all-gathers only the optimizer's bf16 output,
+and with sharded weights (``shard_params``) its per-block bf16 gather runs on the
+copy engines a block ahead, off the critical path, so fp8 bytes would not shorten
+the step.
 """
 
 from __future__ import annotations

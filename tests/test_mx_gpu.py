@@ -106,3 +106,17 @@ def test_mx_weight_copies_follow_optimizer_steps() -> None:
     fresh = _MXLinearRef.apply(x.float(), w.detach().to(torch.bfloat16).float(), False)
     y = mx_linear(x, w).detach().float()
     assert float((y - fresh).abs().max() / fresh.abs().max()) < 1e-2
+
+
+def test_mxfp8_loss_curve_tracks_bf16() -> None:
+    """The first 40 steps of the same run with MXFP8 linear layers stay on the bf16 curve."""
+    from priml_b200.train.precision_curve import run_curve
+
+    kw = {"layers": 2, "steps": 40, "seq": 256, "batch": 4, "d_model": 512, "heads": 8, "kv_heads": 4,
+          "head_dim": 64, "ffn": 1536, "vocab": 4096, "lr": 2e-3}  # fmt: skip
+    bf16 = run_curve(mxfp8=False, **kw)
+    mx = run_curve(mxfp8=True, **kw)
+    assert bf16[-1] < bf16[0] - 2.0 and mx[-1] < mx[0] - 2.0  # both learn
+    gaps = [abs(a - b) for a, b in zip(bf16, mx, strict=True)]
+    assert max(gaps[:5]) < 0.05, gaps[:5]
+    assert sum(gaps[-10:]) / 10 < 0.15, (bf16[-10:], mx[-10:])
