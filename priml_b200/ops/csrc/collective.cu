@@ -100,14 +100,15 @@ __device__ __forceinline__ float lerp_t(float a, float b, float w) {
 }
 
 // W = world size (compile-time, so the peer loads are fully unrolled); each
-// thread keeps U float4 chunks x W peers (8 to 16) independent 16-byte loads
-// in flight, enough to cover NVLink latency with a few dozen CTAs.
+// thread keeps U float4 chunks x W peers (16) independent 16-byte loads in flight:
+// 48 CTAs then hold about 3 MB of reads in flight, the bandwidth-delay product of
+// a peer link at ~1-2 us round trip.
 template <int W>
 __global__ void __launch_bounds__(256, 2) rs_bucket_kernel(PeerTable t, int rank, int bucket, long long bucket_off,
                                                          long long shard, float* __restrict__ out,
                                                          float* __restrict__ partial, unsigned long long epoch,
                                                          float scale, long long timeout_ns, int* status) {
-  constexpr int U = W <= 2 ? 8 / W : (W >= 16 ? 1 : 16 / W);
+  constexpr int U = W >= 16 ? 1 : 16 / W;
   __shared__ int ok;
   __shared__ float red[32];
   if (threadIdx.x == 0) {
