@@ -207,10 +207,19 @@ class _Linear(torch.autograd.Function):
         return dx, dw, db
 
 
+_GEMV_ROWS = 16
+"""At most this many rows without autograd (decode steps) take a library GEMV: a 2-CTA tcgen05
+tile is 256 rows tall, so a handful of rows leaves most of every tile idle and a layer's few
+output tiles cover only a few SMs, while the product is a plain memory-bound matrix-vector read."""
+
+
 def linear(x: Tensor, weight: Tensor, bias: Tensor | None = None) -> Tensor:
     if x.shape[-1] % 8 != 0 or weight.shape[0] % 8 != 0:
         w = weight.to(torch.bfloat16)
         return F.linear(x.to(torch.bfloat16), w, None if bias is None else bias.to(torch.bfloat16))
+    if not torch.is_grad_enabled() and x.numel() // x.shape[-1] <= _GEMV_ROWS:
+        w16 = bf16_shadow(weight)
+        return F.linear(x.to(torch.bfloat16), w16, None if bias is None else bias.to(torch.bfloat16))
     return _Linear.apply(x, weight, bias)
 
 
@@ -247,6 +256,8 @@ class _LinearSwiGLU(torch.autograd.Function):
 
 
 def linear_swiglu(x: Tensor, weight: Tensor) -> Tensor:
+    if not torch.is_grad_enabled() and x.numel() // x.shape[-1] <= _GEMV_ROWS:
+        return swiglu(linear(x, weight))
     return _LinearSwiGLU.apply(x, weight)
 
 
@@ -292,6 +303,8 @@ class _SwiGLUMLP(torch.autograd.Function):
 
 
 def swiglu_mlp(x: Tensor, w_up: Tensor, w_down: Tensor) -> Tensor:
+    if not torch.is_grad_enabled() and x.numel() // x.shape[-1] <= _GEMV_ROWS:
+        return linear(swiglu(linear(x, w_up)), w_down)
     return _SwiGLUMLP.apply(x, w_up, w_down)
 
 
