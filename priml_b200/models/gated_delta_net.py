@@ -17,6 +17,8 @@ chunk from its entry state ``S0`` with ``gamma_t = prod_{r<=t} alpha_r``:
 
 so each chunk costs one unit-lower-triangular solve and a few matmuls.
 ``gated_delta_recurrent`` is the token-by-token definition used as the oracle.
+On CUDA with 128-wide heads the module runs ``priml_b200.ops.gated_delta``
+(chunk-parallel algebra as batched GEMMs, the chunk scan on tcgen05 kernels).
 """
 
 from __future__ import annotations
@@ -33,6 +35,8 @@ from priml_b200.config import Fig, Makeable
 from priml_b200.models.custom_types import ChannelsIn
 from priml_b200.models.linear import Linear
 from priml_b200.models.norm import CenteredRMSNorm
+from priml_b200.ops import reference_forced
+from priml_b200.ops.gated_delta import gated_delta_rule, kernel_supported
 
 __all__ = ["GatedDeltaNet", "gated_delta_chunked", "gated_delta_recurrent"]
 
@@ -158,6 +162,9 @@ class GatedDeltaNet(nn.Module):
         r = self.heads_v // self.heads_k
         if r > 1:
             q, k = q.repeat_interleave(r, dim=-2), k.repeat_interleave(r, dim=-2)
-        out = gated_delta_chunked(q, k, v, g, beta, chunk=self.chunk)
+        if x.is_cuda and kernel_supported(self.dk, self.dv) and not reference_forced():
+            out = gated_delta_rule(q, k, v, g, beta)  # chunk scan on the tcgen05 kernels
+        else:
+            out = gated_delta_chunked(q, k, v, g, beta, chunk=self.chunk)
         out = self.norm(out.reshape(-1, self.dv)) * F.silu(z.reshape(-1, self.dv).float()).type_as(out)
         return self.out_proj(out.reshape(-1, S, vd)).reshape(*shape[:-1], -1)

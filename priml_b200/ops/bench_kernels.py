@@ -202,7 +202,12 @@ def main() -> None:
     ap.add_argument("--mx", action="store_true", help="MXFP8 GEMMs and quantizers only")
     ap.add_argument("--decode", action="store_true", help="decode attention kernel and graph-replayed decode steps")
     ap.add_argument("--ns", action="store_true", help="Newton-Schulz / Polar-Express chains vs the torch path")
+    ap.add_argument("--gdn", action="store_true", help="gated delta-rule chunk scan vs the torch chunked path")
     args = ap.parse_args()
+    if args.gdn:
+        for r in bench_gated_delta():
+            print(json.dumps(r))
+        return
     if args.ns:
         for r in bench_newton_schulz():
             print(json.dumps(r))
@@ -332,13 +337,50 @@ def bench_decode() -> list[dict]:
     return rows
 
 
+def bench_gated_delta(b: int = 4, s: int = 4096, h: int = 16, d: int = 128) -> list[dict]:
+    """Gated delta rule forward and forward + backward: chunk scan kernels against the torch chunked path."""
+    from priml_b200.models.gated_delta_net import gated_delta_chunked
+    from priml_b200.ops.gated_delta import gated_delta_rule
+
+    torch.manual_seed(0)
+    q = torch.randn(b, s, h, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn_like(q, requires_grad=True)
+    v = torch.randn_like(q, requires_grad=True)
+    g = (-torch.rand(b, s, h, device="cuda") * 2).requires_grad_()
+    beta = torch.rand(b, s, h, device="cuda").requires_grad_()
+    do = torch.randn_like(q)
+    rows = []
+    for name, fn in (("kernel", gated_delta_rule), ("torch_chunked", gated_delta_chunked)):
+        def fwd() -> object:
+            with torch.no_grad():
+                return fn(q, k, v, g, beta)
+
+        def fwd_bwd() -> object:
+            o = fn(q, k, v, g, beta)
+            return torch.autograd.grad(o, (q, k, v, g, beta), do)
+
+        rows.append({"op": "gated_delta", "impl": name, "shape": [b, s, h, d], "fwd_ms": round(time_fn(fwd, iters=5), 3),
+                     "fwd_bwd_ms": round(time_fn(fwd_bwd, iters=5), 3)})  # fmt: skip
+    return rows
+
+
 def profile_case(name: str) -> None:
     """Run one small instance of a kernel a few times (for an external profiler)."""
     from priml_b200.ops import native
     from priml_b200.ops.attention_fn import FlashAttnFn
 
     n = native()
-    if name == "gemm":
+    if name == "gdn":
+        # one forward and one backward chunk scan: 64 batch-heads x 32 chunks of 128 tokens
+        from priml_b200.ops.gated_delta import gated_delta_rule
+
+        q = torch.randn(4, 4096, 16, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        g = -torch.rand(4, 4096, 16, device="cuda")
+        beta = torch.rand(4, 4096, 16, device="cuda")
+        for _ in range(2):
+            o = gated_delta_rule(q, q, q, g, beta)
+            o.backward(torch.ones_like(o))
+    elif name == "gemm":
         a = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
         b = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
         c = torch.empty(8192, 8192, device="cuda", dtype=torch.bfloat16)

@@ -544,6 +544,67 @@ std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, 
   return {o, lse};
 }
 
+// Gated delta-rule chunk scan. Operands are contiguous [bh, n, 128, 128] (bf16, Ut fp32),
+// gc is fp32 [bh, n]. Returns (O bf16, entry states bf16, U bf16), each [bh, n, 128, 128].
+void check_gdn(const Tensor& t, const Tensor& ref, torch::ScalarType dtype, const char* name) {
+  PB_CHECK(t.is_cuda() && t.scalar_type() == dtype && t.is_contiguous(), std::string(name) + " has the wrong dtype or layout");
+  PB_CHECK(t.device() == ref.device(), std::string(name) + " is on another device");
+  PB_CHECK(t.dim() == 4 && t.size(0) == ref.size(0) && t.size(1) == ref.size(1) && t.size(2) == 128 && t.size(3) == 128,
+           std::string(name) + " must be [bh, n, 128, 128]");
+}
+
+std::vector<Tensor> gdn_fwd(const Tensor& w, const Tensor& ut, const Tensor& qg, const Tensor& mqk, const Tensor& kr,
+                            const Tensor& gc) {
+  check_gdn(w, w, torch::kBFloat16, "W");
+  check_gdn(ut, w, torch::kFloat32, "Ut");
+  check_gdn(qg, w, torch::kBFloat16, "Qg");
+  check_gdn(mqk, w, torch::kBFloat16, "Mqk");
+  check_gdn(kr, w, torch::kBFloat16, "Kr");
+  PB_CHECK(gc.is_cuda() && gc.scalar_type() == torch::kFloat32 && gc.is_contiguous() && gc.numel() == w.size(0) * w.size(1),
+           "gc must be contiguous fp32 [bh, n]");
+  const c10::cuda::CUDAGuard guard(w.device());
+  auto o = torch::empty_like(w);
+  auto hs = torch::empty_like(w);
+  auto us = torch::empty_like(w);
+  if (w.numel() == 0) return {o, hs, us};
+  pb::GdnParams p{};
+  p.bh = w.size(0);
+  p.n_chunks = w.size(1);
+  p.ut = ut.data_ptr<float>();
+  p.gc = gc.data_ptr<float>();
+  p.o = static_cast<__nv_bfloat16*>(o.data_ptr());
+  p.hs = static_cast<__nv_bfloat16*>(hs.data_ptr());
+  p.us = static_cast<__nv_bfloat16*>(us.data_ptr());
+  p.status = status_ptr();
+  pb::gdn_chunk_fwd(w.data_ptr(), qg.data_ptr(), mqk.data_ptr(), kr.data_ptr(), p, stream());
+  return {o, hs, us};
+}
+
+// Backward of gdn_fwd's scan: returns (dU fp32, gradient of every chunk's exit state fp32).
+std::vector<Tensor> gdn_bwd(const Tensor& kr, const Tensor& mqk, const Tensor& dout, const Tensor& qg, const Tensor& w,
+                            const Tensor& gc) {
+  check_gdn(kr, kr, torch::kBFloat16, "Kr");
+  check_gdn(mqk, kr, torch::kBFloat16, "Mqk");
+  check_gdn(dout, kr, torch::kBFloat16, "dO");
+  check_gdn(qg, kr, torch::kBFloat16, "Qg");
+  check_gdn(w, kr, torch::kBFloat16, "W");
+  PB_CHECK(gc.is_cuda() && gc.scalar_type() == torch::kFloat32 && gc.is_contiguous() && gc.numel() == kr.size(0) * kr.size(1),
+           "gc must be contiguous fp32 [bh, n]");
+  const c10::cuda::CUDAGuard guard(kr.device());
+  auto du = torch::empty(kr.sizes(), kr.options().dtype(torch::kFloat32));
+  auto dhs = torch::empty(kr.sizes(), kr.options().dtype(torch::kFloat32));
+  if (kr.numel() == 0) return {du, dhs};
+  pb::GdnParams p{};
+  p.bh = kr.size(0);
+  p.n_chunks = kr.size(1);
+  p.gc = gc.data_ptr<float>();
+  p.du = du.data_ptr<float>();
+  p.dhs = dhs.data_ptr<float>();
+  p.status = status_ptr();
+  pb::gdn_chunk_bwd(kr.data_ptr(), mqk.data_ptr(), dout.data_ptr(), qg.data_ptr(), w.data_ptr(), p, stream());
+  return {du, dhs};
+}
+
 // Decode attention: q [B, H, D] over caches [B, Hkv, T, D] (rows contiguous) with
 // int32 lengths [B] on the device; returns [B, H, D].
 Tensor decode_attn(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lengths, double scale,
@@ -1136,6 +1197,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd", &ce_bwd, "d(logits) of ce_fwd, written into out (may alias logits)", py::arg("logits"),
         py::arg("targets"), py::arg("lse"), py::arg("g"), py::arg("out"), py::arg("ignore_index"),
         py::arg("softcap") = 0.0);
+  m.def("gdn_fwd", &gdn_fwd, "gated delta-rule chunk scan, forward (tcgen05)");
+  m.def("gdn_bwd", &gdn_bwd, "gated delta-rule chunk scan, backward (tcgen05)");
   m.def("decode_attn", &decode_attn, "one-token decode attention over a KV cache with device lengths",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("lengths"), py::arg("scale"), py::arg("window") = -1);
   m.def("attn_fwd", &attn_fwd, "flash attention forward (tcgen05); trace: optional int32 [8 * CTAs] progress record",

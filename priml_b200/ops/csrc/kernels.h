@@ -272,4 +272,25 @@ int decode_attn_heads_per_cta(int group);
 int decode_attn_splits(int B, int H, int group, int T, int sm_count);
 void decode_attn(const DecodeAttnParams& p, int B, int D, cudaStream_t stream);
 
+// Gated delta-rule chunk scan (gated_delta.cu): one CTA per (batch, head) walks its
+// `n_chunks` chunks of 128 tokens; dk = dv = 128. Every operand is a row-major
+// [bh * n_chunks * 128, 128] matrix whose rows are ordered (batch-head, chunk, row).
+struct GdnParams {
+  int bh, n_chunks;
+  const float* ut;     // forward: [rows, dv] fp32 (I + A)^-1 (beta V)
+  const float* gc;     // [bh * n_chunks] per-chunk decay gamma_C
+  __nv_bfloat16* o;    // forward out: [rows, dv]
+  __nv_bfloat16* hs;   // forward out: entry state of every chunk, [bh * n_chunks * dk, dv]
+  __nv_bfloat16* us;   // forward out: corrected values U, [rows, dv]
+  float* du;           // backward out: dU, [rows, dv]
+  float* dhs;          // backward out: gradient of every chunk's exit state, [bh * n_chunks * dk, dv]
+  int* status;
+};
+// Forward: operands W, Qg, Mqk, Kr (bf16); writes o, hs, us.
+void gdn_chunk_fwd(const void* w, const void* qg, const void* mqk, const void* kr, const GdnParams& p,
+                   cudaStream_t stream);
+// Backward: operands Kr, Mqk, dO, Qg, W (bf16); writes du, dhs.
+void gdn_chunk_bwd(const void* kr, const void* mqk, const void* dout, const void* qg, const void* w,
+                   const GdnParams& p, cudaStream_t stream);
+
 }  // namespace pb
