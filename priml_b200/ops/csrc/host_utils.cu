@@ -114,6 +114,13 @@ void make_tmap_2d_u8(CUtensorMap* map, const void* base, long long inner, long l
                "2d u8");
 }
 
+// 2-D byte map without swizzle (MXFP8 scale atoms: 512-byte boxes copied as they are).
+void make_tmap_2d_u8_plain(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
+                           int box_inner, int box_outer) {
+  encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, inner, outer, row_stride, box_inner, box_outer,
+            CU_TENSOR_MAP_SWIZZLE_NONE, "2d u8 plain");
+}
+
 void make_tmap_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
                       int box_inner, int box_outer) {
   ensure_context();

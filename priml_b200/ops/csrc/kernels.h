@@ -27,6 +27,8 @@ void make_tmap_2d_f32(CUtensorMap* map, const void* base, long long inner, long 
                       int box_inner, int box_outer);
 void make_tmap_2d_u8(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
                      int box_inner, int box_outer);
+void make_tmap_2d_u8_plain(CUtensorMap* map, const void* base, long long inner, long long outer, long long row_stride,
+                           int box_inner, int box_outer);
 void make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long inner, long long mid, long long outer,
                        long long mid_stride, long long outer_stride, int box_inner, int box_mid, bool swizzle128);
 

@@ -23,8 +23,9 @@
 // then 128-row block; the row-block count is rounded up to an even number so a
 // 256-row GEMM tile always has two atoms. Padding scales are 127 (= 1.0).
 //
-// GEMM structure: 128 x 256 output tiles, 128-deep K steps (128 bytes of fp8 per
-// row = one 128-byte swizzle row), 4 shared-memory stages, one TMA producer
+// GEMM structure (1-CTA kernel, used when the output cannot take bulk tensor stores;
+// the 2-CTA kernel below is the default): 128 x 256 output tiles, 128-deep K steps
+// (128 bytes of fp8 per row = one 128-byte swizzle row), 4 shared-memory stages, one TMA producer
 // warp, one MMA warp, four epilogue warps, one fp32 accumulator of 256 TMEM
 // columns plus 12 columns of scale factors. Per K step the MMA thread copies the
 // A atom and the two B atoms from shared memory into TMEM
@@ -33,6 +34,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -332,6 +334,269 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- 2-CTA tiles
+// A CTA pair (cluster of 2) computes a 256 x 256 output tile with M = 256 block-scaled MMAs
+// (cta_group::2): CTA r holds A rows [128 r, 128 r + 128) and B rows (N) [128 r, 128 r + 128)
+// of every 128-deep K step, so each SM streams 32 KB of fp8 operands per step instead of the
+// 48 KB of a 1-CTA 128 x 256 tile, for the same MMA time. Scale factors: each CTA copies the
+// atom of its own 128 A rows and the two atoms of all 256 B rows into its shared memory;
+// CTA 0's MMA thread moves them into both CTAs' TMEM with tcgen05.cp.cta_group::2 (each CTA's
+// shared memory to its own TMEM) and issues the MMAs. All completion bytes of a stage land
+// on CTA 0's `full` barrier; `empty` and `tfull` commits go to both CTAs.
+//
+// TMEM: one 256-column fp32 accumulator plus 12 scale columns (two accumulators would leave
+// no room for the scales). The eight epilogue warps (two per TMEM lane quarter, 128 columns
+// each) read the whole accumulator into registers first and release it right away, so the
+// next tile's MMAs start while the tile's values are converted and leave through bulk tensor
+// stores (bf16 / fp32) or bulk reduce-adds (fp32 +=).
+constexpr int kMxPairThreads = 320;
+constexpr int kMxPairA = 128 * XBK;  // this CTA's 128 rows of A: 16 KB
+constexpr int kMxPairB = 128 * XBK;  // this CTA's 128 rows (N) of B: 16 KB
+constexpr int kMxPairStage = kMxPairA + kMxPairB + kXSFA + kXSFB;
+
+template <int EPI>
+struct MxPairCfg {
+  static constexpr int kStages = EPI == 0 ? 6 : 5;
+  static constexpr int kChunk = EPI == 0 ? 2048 : 4096;  // per epilogue warp: 32 rows x 32 columns
+  static constexpr int kSmem = kStages * kMxPairStage + 8 * kChunk + 1024 + 256;
+  static_assert(kSmem <= 232448, "MXFP8 pair GEMM shared memory exceeds the per-CTA limit");
+};
+
+__device__ __forceinline__ void tmem_cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void umma_mx_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxPairThreads, 1)
+    mx_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
+                   const __grid_constant__ CUtensorMap tmC, const MxParams p) {
+  using Cfg = MxPairCfg<EPI>;
+  constexpr int S = Cfg::kStages;
+  constexpr int TM = 256, TN = 256;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Operand stages and the swizzled epilogue staging tiles first (1024-byte aligned: the
+  // 128-byte swizzle pattern follows address bits 7-9), the unswizzled scale atoms after them.
+  uint8_t* smA = smem;
+  uint8_t* smB = smA + S * kMxPairA;
+  uint8_t* stg = smB + S * kMxPairB;
+  uint8_t* smSFA = stg + 8 * Cfg::kChunk;
+  uint8_t* smSFB = smSFA + S * kXSFA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smSFB + S * kXSFB);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* drain = tempty + 1;
+  uint64_t* peer_done = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(peer_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  const int num_m = (p.g.M + TM - 1) / TM;
+  const int num_n = (p.g.N + TN - 1) / TN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.g.K + XBK - 1) / XBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 16);  // eight epilogue warps of both CTAs
+    mbar_init(drain, 1);
+    mbar_init(peer_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmSA);
+    prefetch_tmap(&tmSB);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kXTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits of both CTAs visible before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    const uint32_t full0 = cluster_addr(full, 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * TM + 128 * static_cast<int>(rank);
+      const int n0 = nb * TN + 128 * static_cast<int>(rank);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.g.status, kTimeoutProducer, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kMxPairStage);
+        const uint32_t bar = full0 + 8u * stage;
+        tma_load_2d_pair(smA + stage * kMxPairA, &tmA, bar, kb * XBK, m0);
+        tma_load_2d_pair(smB + stage * kMxPairB, &tmB, bar, kb * XBK, n0);
+        // scale atoms (512 bytes = two 256-byte rows of the scale maps): this CTA's A rows, all 256 B rows
+        tma_load_2d_pair(smSFA + stage * kXSFA, &tmSA, bar, 0, 2 * ((2 * mb + static_cast<int>(rank)) * p.nkg + kb));
+        tma_load_2d_pair(smSFB + stage * kXSFB, &tmSB, bar, 0, 2 * ((2 * nb) * p.nkg + kb));
+        tma_load_2d_pair(smSFB + stage * kXSFB + 512, &tmSB, bar, 0, 2 * ((2 * nb + 1) * p.nkg + kb));
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && leader) {
+      for (int i = 0; i < min(issued, S); ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&full[stage], phase, p.g.status, kTimeoutDrain, nullptr);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    if (leader) {
+      // ------------------------------------------------------------ MMA issuer (CTA 0)
+      const uint32_t empty1 = cluster_addr(empty, 1);
+      const uint32_t tfull1 = cluster_addr(tfull, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      uint32_t sf_slot = 0;  // scale columns rotate over 4 slots of 16: a copy never targets the
+                             // columns that the previous K step's MMAs are still reading
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
+        if (!mbar_wait(tempty, (local & 1) ^ 1u, p.g.status, kTimeoutMma, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.g.status, kTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfa_s = smem_u32(smSFA + stage * kXSFA);
+          const uint32_t sfb_s = smem_u32(smSFB + stage * kXSFB);
+          const uint32_t sfa_t = tmem_base + kSfaCol + 16u * (sf_slot++ & 3u), sfb_t = sfa_t + 4;
+          tmem_cp_sf_pair(sfa_t, make_sf_desc(sfa_s));
+          tmem_cp_sf_pair(sfb_t, make_sf_desc(sfb_s));
+          tmem_cp_sf_pair(sfb_t + 4, make_sf_desc(sfb_s + 512));
+          const uint32_t a_base = smem_u32(smA + stage * kMxPairA);
+          const uint32_t b_base = smem_u32(smB + stage * kMxPairB);
+#pragma unroll
+          for (int kk = 0; kk < XBK / 32; ++kk) {
+            const uint32_t sel = static_cast<uint32_t>(kk) << 30;  // scale byte kk of each TMEM word
+            umma_mx_pair(tmem_base, make_sw128_desc(a_base + kk * 32, 16, 1024),
+                         make_sw128_desc(b_base + kk * 32, 16, 1024), make_idesc_mx(TM, TN, static_cast<uint32_t>(kk)),
+                         sfa_t | sel, sfb_t | sel, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage]);
+          umma_commit_pair_to(empty1 + 8u * stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) {
+          umma_commit_pair(tfull);
+          umma_commit_pair_to(tfull1);
+        }
+      }
+      umma_commit_pair(drain);
+      mbar_wait(drain, 0, p.g.status, kTimeoutDrain, nullptr);
+      mbar_arrive_cluster(cluster_addr(peer_done, 1));  // CTA 1 may free its TMEM now
+    } else {
+      mbar_wait(peer_done, 0, p.g.status, kTimeoutDrain, nullptr);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int wq = warp & 3;             // TMEM lane quarter this warp may access
+    const int c_lo = ((warp - 2) >> 2) * 128;  // this warp's 128 accumulator columns
+    const uint32_t tempty0 = cluster_addr(tempty, 0);
+    uint8_t* buf = stg + (warp - 2) * Cfg::kChunk;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int row0 = mb * TM + 128 * static_cast<int>(rank) + wq * 32;
+      if (!mbar_wait_warp(tfull, local & 1, p.g.status, kTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + c_lo;
+      uint32_t v[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_row + 32 * c, v[c]);
+      tmem_wait_ld();
+      // the accumulator is in registers: the next tile's MMAs may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (lane == 0) tma_store_wait_read();  // the previous chunk's store has read the buffer
+        __syncwarp();
+        if constexpr (EPI == 0) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(v[c][2 * j]), __uint_as_float(v[c][2 * j + 1]));
+          stage_row<4>(buf, lane, pk);
+        } else {
+          stage_row<8>(buf, lane, v[c]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (EPI == 2) {
+            tma_reduce_add_2d(&tmC, buf, nb * TN + c_lo + 32 * c, row0);
+          } else {
+            tma_store_2d(&tmC, buf, nb * TN + c_lo + 32 * c, row0);
+          }
+          tma_store_commit();
+        }
+      }
+    }
+    if (lane == 0) tma_store_wait_all();  // staging read and global writes done before exit
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no remote arrive may target a CTA that has exited
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, kXTmemCols);
+  }
+}
+
 void check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -348,6 +613,34 @@ void launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, 
   const int sms = device_sm_count();
   kern<<<tiles < sms ? tiles : sms, kThreads, kXSmem, stream>>>(ta, tb, p);
   check(cudaGetLastError(), "mx gemm launch");
+}
+
+template <int EPI>
+void launch_mx_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa, const CUtensorMap& tsb,
+                    const CUtensorMap& tc, const MxParams& p, cudaStream_t stream) {
+  auto kern = mx_pair_kernel<EPI>;
+  static bool configured = false;
+  if (!configured) {
+    check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MxPairCfg<EPI>::kSmem),
+          "mx pair gemm smem attribute");
+    configured = true;
+  }
+  const int tiles = ((p.g.M + 255) / 256) * ((p.g.N + 255) / 256);
+  const int pairs_max = device_sm_count() / 2;
+  const int pairs = tiles < pairs_max ? tiles : pairs_max;
+  kern<<<2 * pairs, kMxPairThreads, MxPairCfg<EPI>::kSmem, stream>>>(ta, tb, tsa, tsb, tc, p);
+  check(cudaGetLastError(), "mx pair gemm launch");
+}
+
+// The 2-CTA kernel writes through bulk tensor stores, which need a 16-byte aligned output
+// base and row stride; PRIML_B200_MX_PAIR=0 selects the 1-CTA kernel (A/B measurements).
+bool mx_pair_usable(int epi, const void* C, long long ldc) {
+  static const bool on = [] {
+    const char* e = std::getenv("PRIML_B200_MX_PAIR");
+    return e == nullptr || e[0] != '0';
+  }();
+  const long long row_bytes = ldc * (epi == 0 ? 2 : 4);
+  return on && (reinterpret_cast<uintptr_t>(C) & 15) == 0 && row_bytes % 16 == 0;
 }
 
 }  // namespace
@@ -384,14 +677,32 @@ void mx_quantize(const void* x, long long ldx, void* q, void* sf, int R, int K, 
 void mx_gemm(const void* A, const void* sfa, const void* B, const void* sfb, void* C, long long ldc, int M, int N, int K,
              int epi, int* status, cudaStream_t stream) {
   if (K % 32 != 0 || K <= 0) throw std::invalid_argument("mx_gemm: K must be a positive multiple of 32");
-  CUtensorMap ta, tb;
-  make_tmap_2d_u8(&ta, A, K, M, K, XBK, BM);
-  make_tmap_2d_u8(&tb, B, K, N, K, XBK, XBN);
+  if (epi < 0 || epi > 2) throw std::invalid_argument("mx_gemm: epi 0 (bf16), 1 (fp32) or 2 (fp32 +=)");
   MxParams p{};
   p.g = GemmParams{M, N, K, C, ldc, nullptr, status, 0};
   p.sfa = static_cast<const uint8_t*>(sfa);
   p.sfb = static_cast<const uint8_t*>(sfb);
   p.nkg = (K + 127) / 128;
+  CUtensorMap ta, tb;
+  if (mx_pair_usable(epi, C, ldc)) {
+    CUtensorMap tsa, tsb, tc;
+    make_tmap_2d_u8(&ta, A, K, M, K, XBK, 128);
+    make_tmap_2d_u8(&tb, B, K, N, K, XBK, 128);
+    // scale arrays as rows of 256 bytes: one 512-byte atom is a 2-row box
+    make_tmap_2d_u8_plain(&tsa, sfa, 256, mx_scale_bytes(M, K) / 256, 256, 256, 2);
+    make_tmap_2d_u8_plain(&tsb, sfb, 256, mx_scale_bytes(N, K) / 256, 256, 256, 2);
+    if (epi == 0) {
+      make_tmap_2d_bf16_sw64(&tc, C, N, M, ldc, 32, 32);
+      launch_mx_pair<0>(ta, tb, tsa, tsb, tc, p, stream);
+    } else {
+      make_tmap_2d_f32_sw128(&tc, C, N, M, ldc, 32, 32);
+      if (epi == 1) launch_mx_pair<1>(ta, tb, tsa, tsb, tc, p, stream);
+      else launch_mx_pair<2>(ta, tb, tsa, tsb, tc, p, stream);
+    }
+    return;
+  }
+  make_tmap_2d_u8(&ta, A, K, M, K, XBK, BM);
+  make_tmap_2d_u8(&tb, B, K, N, K, XBK, XBN);
   switch (epi) {
     case 0: launch_mx<0>(ta, tb, p, stream); break;
     case 1: launch_mx<1>(ta, tb, p, stream); break;

@@ -112,8 +112,10 @@ def test_mxfp8_loss_curve_tracks_bf16() -> None:
     """The first 40 steps of the same run with MXFP8 linear layers stay on the bf16 curve."""
     from priml_b200.train.precision_curve import run_curve
 
+    # lr 5e-4 keeps both runs out of the loss-spike regime (at 2e-3 a spike near step 10 sends
+    # bf16 and either MXFP8 GEMM onto different chaotic paths), so the gap measures precision
     kw = {"layers": 2, "steps": 40, "seq": 256, "batch": 4, "d_model": 512, "heads": 8, "kv_heads": 4,
-          "head_dim": 64, "ffn": 1536, "vocab": 4096, "lr": 2e-3}  # fmt: skip
+          "head_dim": 64, "ffn": 1536, "vocab": 4096, "lr": 5e-4}  # fmt: skip
     bf16 = run_curve(mxfp8=False, **kw)
     mx = run_curve(mxfp8=True, **kw)
     assert bf16[-1] < bf16[0] - 1.0 and mx[-1] < mx[0] - 1.0  # both learn
