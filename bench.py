@@ -68,6 +68,8 @@ def _parse() -> argparse.Namespace:
     ap.add_argument("--ref-compile", choices=["auto", "on", "off"], default="auto",
                     help="reference arm: auto runs the reference's stock torch.compile path and falls back to its "
                     "eager config (compile=None) only if compilation fails on one GPU")
+    ap.add_argument("--reduce-blocks", type=int, default=None,
+                    help="CTAs per fused reduce-scatter launch (default: the strategy's, one per SM)")
     ap.add_argument("--out", type=str, default="")
     return ap.parse_args()
 
@@ -436,6 +438,7 @@ def main() -> None:
         if getattr(args, k) is None:
             setattr(args, k, v)
     strategy = args.strategy
+    fused_kw: dict[str, Any] = {} if args.reduce_blocks is None else {"reduce_blocks": args.reduce_blocks}
     if strategy == "auto":
         strategy = {"llama3_8b": "tp", "mla_moe": "ep"}.get(args.config, "fused")
         if world == 1:
@@ -480,8 +483,8 @@ def main() -> None:
                       "64 routed experts x 1408 top-6 + 2 shared, vocab 102400)")  # fmt: skip
     vocab = shape.vocab
     parallel = {
-        "fused": lambda: FusedFullySharded.Config(),
-        "fused-shard": lambda: FusedFullySharded.Config(shard_params=True),
+        "fused": lambda: FusedFullySharded.Config(**fused_kw),
+        "fused-shard": lambda: FusedFullySharded.Config(shard_params=True, **fused_kw),
         "fsdp2": lambda: FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True),
         "tp": lambda: FusedSequenceParallel.Config(),
         "ep": lambda: ExpertParallel.Config(),
