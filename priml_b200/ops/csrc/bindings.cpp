@@ -978,6 +978,226 @@ class TpGroup {
   int64_t slot_bytes_ = 0;
 };
 
+// Expert GEMMs fused with the expert-parallel exchange (ep_gemm.cu). Per rank: an IPC-mapped
+// send buffer (rows offered to the expert owners, pulled by their GEMMs), a recv buffer (rows
+// the owners' GEMM epilogues push back) and a signal array; the host keeps the epochs.
+// Every rank must make the same calls in the same order.
+class EpGemmGroup {
+ public:
+  EpGemmGroup(int64_t rank, int64_t world, int64_t send_rows, int64_t recv_rows, int64_t cols, int64_t max_chunks,
+              double timeout_s)
+      : rank_(rank), world_(world), cols_(cols), send_rows_(std::max<int64_t>(send_rows, 1)),
+        recv_rows_(std::max<int64_t>(recv_rows, 1)), timeout_ns_(static_cast<long long>(timeout_s * 1e9)),
+        device_(at::cuda::current_device()) {
+    PB_CHECK(world >= 1 && world <= pb::kMaxRanks, "world size must be 1..8");
+    PB_CHECK(cols % 64 == 0, "channels must be a multiple of 64");
+    local_ = std::make_shared<Local>();
+    local_->send = pb::sym_alloc(send_rows_ * cols * 2);
+    local_->recv = pb::sym_alloc(recv_rows_ * cols * 2);
+    local_->signal = pb::sym_alloc(pb::kSigWords * 8);
+    auto opts = torch::TensorOptions().device(torch::kCUDA, device_);
+    counters_ = torch::zeros({4}, opts.dtype(torch::kInt32));
+    flags_ = torch::zeros({std::max<int64_t>(max_chunks, 1)}, opts.dtype(torch::kInt32));
+  }
+  ~EpGemmGroup() {
+    for (void* p : opened_) pb::ipc_close(p);
+  }
+  py::bytes handles() const {
+    char buf[192];
+    pb::ipc_handle(local_->send, buf);
+    pb::ipc_handle(local_->recv, buf + 64);
+    pb::ipc_handle(local_->signal, buf + 128);
+    return py::bytes(buf, 192);
+  }
+  void open(const std::vector<std::string>& all) {
+    PB_CHECK(static_cast<int64_t>(all.size()) == world_, "need one handle record per rank");
+    const c10::cuda::CUDAGuard guard(device_);
+    for (int64_t r = 0; r < world_; ++r) {
+      void* ptr[3] = {local_->send, local_->recv, local_->signal};
+      if (r != rank_) {
+        for (int i = 0; i < 3; ++i) {
+          ptr[i] = pb::ipc_open(all[r].data() + 64 * i);
+          opened_.push_back(ptr[i]);
+        }
+      }
+      send_[r] = reinterpret_cast<unsigned long long>(ptr[0]);
+      recv_[r] = reinterpret_cast<unsigned long long>(ptr[1]);
+      sig_[r] = reinterpret_cast<unsigned long long>(ptr[2]);
+    }
+    opened_ok_ = true;
+  }
+  // The first `rows` rows of this rank's send buffer, to be filled once wait_send_free() is queued.
+  Tensor send_rows(int64_t rows) const {
+    PB_CHECK(rows <= send_rows_, "more rows than the send buffer holds");
+    auto keep = local_;
+    return torch::from_blob(local_->send, {rows, cols_}, [keep](void*) {},
+                            torch::TensorOptions().device(torch::kCUDA, device_).dtype(torch::kBFloat16));
+  }
+  // Wait (on the stream) until every rank has finished pulling this rank's previous send rows.
+  void wait_send_free() {
+    PB_CHECK(opened_ok_, "open() first");
+    if (send_epoch_ == 0) return;
+    pb::tp_wait(local_->signal, pb::kEpSigSendDone, static_cast<unsigned long long>(send_epoch_) * world_, timeout_ns_,
+                status_ptr(), stream());
+  }
+
+  // C = A @ B_e^T with A's rows pulled from the ranks' send buffers (row_src: int32 [M]) into a_local [M, K].
+  // epi 3: B = up weights [experts * 2H, K], C = h [M, H], aux = gate/up [M, 2H] (written).
+  // epi 4: B = down weights [experts * K, H] (N-major), aux = gate/up (read), C = d(gate/up) [M, 2H].
+  void pull_gemm(const Tensor& row_src, const Tensor& offsets, const Tensor& B, int64_t epi, int64_t b_rows,
+                 int64_t swiglu_h, Tensor& C, Tensor& aux, Tensor& a_local) {
+    PB_CHECK(opened_ok_, "open() first");
+    const int64_t M = a_local.size(0), K = a_local.size(1);
+    PB_CHECK(K == cols_, "a_local must have the group's channel count");
+    PB_CHECK(a_local.is_contiguous() && a_local.scalar_type() == torch::kBFloat16 && M % 128 == 0, "a_local bf16 [M % 128 == 0, K]");
+    PB_CHECK(M / 128 <= flags_.numel(), "more row chunks than the flag buffer holds");
+    PB_CHECK(row_src.scalar_type() == torch::kInt32 && row_src.is_contiguous() && row_src.numel() >= M, "row_src int32 [M]");
+    PB_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.is_contiguous(), "offsets int32");
+    PB_CHECK(B.scalar_type() == torch::kBFloat16 && B.dim() == 2 && B.stride(1) == 1, "B bf16, rows contiguous");
+    PB_CHECK(aux.is_contiguous() && aux.size(0) == M && aux.size(1) == 2 * swiglu_h, "aux = gate/up [M, 2H]");
+    PB_CHECK(C.is_contiguous() && C.size(0) == M, "C rows");
+    pb::EpGemmParams p = base();
+    const int experts = static_cast<int>(offsets.numel()) - 1;
+    if (epi == 3) {
+      PB_CHECK(B.size(1) == K && b_rows == 2 * swiglu_h && C.size(1) == swiglu_h, "epi 3: B [experts * 2H, K], C = h [M, H]");
+      p.N = static_cast<int>(2 * swiglu_h);
+    } else if (epi == 4) {
+      PB_CHECK(B.size(1) == swiglu_h && b_rows == K && C.size(1) == 2 * swiglu_h, "epi 4: B [experts * K, H], C [M, 2H]");
+      p.N = static_cast<int>(swiglu_h);
+    } else {
+      PB_CHECK(false, "epi must be 3 or 4");
+    }
+    PB_CHECK(B.size(0) == static_cast<int64_t>(experts) * b_rows, "B must stack experts * b_rows rows");
+    p.M = static_cast<int>(M);
+    p.K = static_cast<int>(K);
+    p.C = C.data_ptr();
+    p.ldc = C.stride(0);
+    p.aux = aux.data_ptr();
+    p.swiglu_h = static_cast<int>(swiglu_h);
+    p.offsets = offsets.data_ptr<int>();
+    p.experts = experts;
+    p.b_rows = static_cast<int>(b_rows);
+    p.epi = static_cast<int>(epi);
+    p.epoch = ++send_epoch_;
+    p.row_src = row_src.data_ptr<int>();
+    p.a_local = a_local.data_ptr();
+    p.chunk_flags = reinterpret_cast<unsigned int*>(flags_.data_ptr<int32_t>());
+    p.block_counter = reinterpret_cast<unsigned int*>(counters_.data_ptr<int32_t>());
+    const c10::cuda::CUDAGuard guard(device_);
+    pb::ep_pull_gemm(p, B.data_ptr(), row_stride(B), epi == 4, stream());
+  }
+
+  // Rows of A @ B_e^T -> the recv buffers of their sources (row_dst: int32 [M]).
+  // b_mn = false: B [experts * N, K]; true: B [experts * K, N].
+  void push_gemm(const Tensor& A, const Tensor& row_dst, const Tensor& offsets, const Tensor& B, bool b_mn,
+                 int64_t b_rows) {
+    PB_CHECK(opened_ok_, "open() first");
+    check_cuda(A, "A");
+    PB_CHECK(A.scalar_type() == torch::kBFloat16 && A.stride(1) == 1 && A.size(0) % 128 == 0, "A bf16 [M % 128 == 0, K]");
+    PB_CHECK(B.scalar_type() == torch::kBFloat16 && B.dim() == 2 && B.stride(1) == 1, "B bf16, rows contiguous");
+    PB_CHECK(row_dst.scalar_type() == torch::kInt32 && row_dst.is_contiguous() && row_dst.numel() >= A.size(0), "row_dst int32 [M]");
+    PB_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.is_contiguous(), "offsets int32");
+    const int experts = static_cast<int>(offsets.numel()) - 1;
+    const int64_t K = A.size(1);
+    const int64_t N = b_mn ? B.size(1) : b_rows;
+    PB_CHECK(N == cols_, "the output width must be the group's channel count");
+    PB_CHECK(b_mn ? b_rows == K : B.size(1) == K, "B has the wrong K");
+    PB_CHECK(B.size(0) == static_cast<int64_t>(experts) * b_rows, "B must stack experts * b_rows rows");
+    pb::EpGemmParams p = base();
+    p.M = static_cast<int>(A.size(0));
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.offsets = offsets.data_ptr<int>();
+    p.experts = experts;
+    p.b_rows = static_cast<int>(b_rows);
+    p.epoch = ++push_epoch_;
+    p.row_dst = row_dst.data_ptr<int>();
+    p.block_counter = reinterpret_cast<unsigned int*>(counters_.data_ptr<int32_t>()) + 1;
+    const c10::cuda::CUDAGuard guard(device_);
+    pb::ep_push_gemm(p, A.data_ptr(), row_stride(A), B.data_ptr(), row_stride(B), b_mn, stream());
+  }
+
+  // out [tokens, cols] = sum_j weights[t, j] * recv[t * k + j] (plain sum without weights) after every
+  // owner's push of this epoch; keep (optional) receives a copy of the rows. Frees the recv buffer.
+  void combine(int64_t tokens, int64_t k, const c10::optional<Tensor>& weights, Tensor& out,
+               const c10::optional<Tensor>& keep) {
+    PB_CHECK(opened_ok_, "open() first");
+    PB_CHECK(tokens * k <= recv_rows_, "more rows than the recv buffer holds");
+    PB_CHECK(out.is_contiguous() && out.scalar_type() == torch::kBFloat16 && out.numel() == tokens * cols_, "out bf16 [tokens, cols]");
+    if (weights.has_value())
+      PB_CHECK(weights->is_contiguous() && weights->scalar_type() == torch::kFloat32 && weights->numel() == tokens * k, "weights fp32 [tokens, k]");
+    if (keep.has_value())
+      PB_CHECK(keep->is_contiguous() && keep->scalar_type() == torch::kBFloat16 && keep->numel() == tokens * k * cols_, "keep bf16 [tokens * k, cols]");
+    pb::EpCombineParams p{};
+    p.recv = local_->recv;
+    p.weights = weights.has_value() ? weights->data_ptr<float>() : nullptr;
+    p.out = out.data_ptr();
+    p.keep = keep.has_value() ? keep->data_ptr() : nullptr;
+    p.tokens = tokens;
+    p.k = static_cast<int>(k);
+    p.cols = static_cast<int>(cols_);
+    p.rank = static_cast<int>(rank_);
+    p.world = static_cast<int>(world_);
+    p.done_target = static_cast<unsigned long long>(push_epoch_) * world_;
+    for (int r = 0; r < world_; ++r) p.signal[r] = sig_[r];
+    p.block_counter = reinterpret_cast<unsigned int*>(counters_.data_ptr<int32_t>()) + 2;
+    p.timeout_ns = timeout_ns_;
+    p.status = status_ptr();
+    const c10::cuda::CUDAGuard guard(device_);
+    pb::ep_combine(p, stream());
+  }
+
+ private:
+  pb::EpGemmParams base() const {
+    pb::EpGemmParams p{};
+    p.rank = static_cast<int>(rank_);
+    p.world = static_cast<int>(world_);
+    p.timeout_ns = timeout_ns_;
+    p.status = status_ptr();
+    p.dst_rows = recv_rows_;
+    p.src_rows = send_rows_;
+    for (int r = 0; r < world_; ++r) {
+      p.src[r] = send_[r];
+      p.dst[r] = recv_[r];
+      p.signal[r] = sig_[r];
+    }
+    return p;
+  }
+  struct Local {
+    void* send = nullptr;
+    void* recv = nullptr;
+    void* signal = nullptr;
+    ~Local() {
+      pb::sym_free(send);
+      pb::sym_free(recv);
+      pb::sym_free(signal);
+    }
+  };
+  int64_t rank_, world_, cols_, send_rows_, recv_rows_;
+  long long timeout_ns_;
+  int device_;
+  std::shared_ptr<Local> local_;
+  Tensor counters_, flags_;
+  unsigned long long send_[pb::kMaxRanks] = {}, recv_[pb::kMaxRanks] = {}, sig_[pb::kMaxRanks] = {};
+  std::vector<void*> opened_;
+  bool opened_ok_ = false;
+  long long send_epoch_ = 0, push_epoch_ = 0;
+};
+
+// out[t * k + j] = w[t, j] * dy[t] (bf16) and dw[t, j] = <dy[t], y[t * k + j]> (fp32).
+void ep_expand(const Tensor& dy, const Tensor& w, const Tensor& y, Tensor& out, Tensor& dw) {
+  check_cuda(dy, "dy");
+  const int64_t T = dy.size(0), C = dy.size(1), k = w.size(1);
+  PB_CHECK(dy.is_contiguous() && dy.scalar_type() == torch::kBFloat16, "dy bf16 [T, C]");
+  PB_CHECK(w.is_contiguous() && w.scalar_type() == torch::kFloat32 && w.size(0) == T, "w fp32 [T, k]");
+  PB_CHECK(y.is_contiguous() && y.scalar_type() == torch::kBFloat16 && y.numel() == T * k * C, "y bf16 [T * k, C]");
+  PB_CHECK(out.is_contiguous() && out.scalar_type() == torch::kBFloat16 && out.numel() == T * k * C, "out bf16 [T * k, C]");
+  PB_CHECK(dw.is_contiguous() && dw.scalar_type() == torch::kFloat32 && dw.numel() == T * k, "dw fp32 [T, k]");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  pb::ep_expand(dy.data_ptr(), w.data_ptr<float>(), y.data_ptr(), out.data_ptr(), dw.data_ptr<float>(), T * k,
+                static_cast<int>(k), static_cast<int>(C), stream());
+}
+
 // Expert-parallel row exchange (ep.cu): two symmetric row buffers per rank,
 // 0 = rows travelling to the expert owners, 1 = rows travelling back to their sources.
 class EpGroup {
@@ -1234,6 +1454,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("totals"))
       .def("release", &EpGroup::release)
       .def("rows", &EpGroup::rows);
+  py::class_<EpGemmGroup>(m, "EpGemmGroup")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, double>(), py::arg("rank"), py::arg("world"),
+           py::arg("send_rows"), py::arg("recv_rows"), py::arg("cols"), py::arg("max_chunks"), py::arg("timeout_s"))
+      .def("handles", &EpGemmGroup::handles)
+      .def("open", &EpGemmGroup::open)
+      .def("send_rows", &EpGemmGroup::send_rows)
+      .def("wait_send_free", &EpGemmGroup::wait_send_free)
+      .def("pull_gemm", &EpGemmGroup::pull_gemm, py::arg("row_src"), py::arg("offsets"), py::arg("B"), py::arg("epi"),
+           py::arg("b_rows"), py::arg("swiglu_h"), py::arg("C"), py::arg("aux"), py::arg("a_local"))
+      .def("push_gemm", &EpGemmGroup::push_gemm, py::arg("A"), py::arg("row_dst"), py::arg("offsets"), py::arg("B"),
+           py::arg("b_mn"), py::arg("b_rows"))
+      .def("combine", &EpGemmGroup::combine, py::arg("tokens"), py::arg("k"), py::arg("weights"), py::arg("out"),
+           py::arg("keep"));
+  m.def("ep_expand", &ep_expand, "w * dy into the send rows and the routing-weight gradient", py::arg("dy"),
+        py::arg("w"), py::arg("y"), py::arg("out"), py::arg("dw"));
   py::class_<TpGroup>(m, "TpGroup")
       .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, double>(), py::arg("rank"), py::arg("world"),
            py::arg("shard_elems"), py::arg("slot_elems"), py::arg("max_chunks"), py::arg("timeout_s") = 60.0)

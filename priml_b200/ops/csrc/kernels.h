@@ -247,6 +247,59 @@ void ep_collect(const void* buf, const int* meta, void* dst, int* meta_dst, cons
                 int segs, int cols, long long cap, cudaStream_t stream);
 void ep_signal(const EpSignalParams& p, cudaStream_t stream);
 
+// ---------------------------------------------------------------- expert GEMMs fused with the exchange (ep_gemm.cu)
+// Signal words (u64) of an EpGemmGroup's signal array.
+constexpr int kEpSigSendReady = 128;                  // [src rank]: epoch whose rows the source's send buffer holds
+constexpr int kEpSigSendDone = kEpSigSendReady + kMaxRanks;  // ranks finished pulling from this rank's send buffer
+constexpr int kEpSigRecvDone = kEpSigSendDone + 1;    // owners finished pushing into this rank's recv buffer
+constexpr int kEpSigRecvFree = kEpSigSendDone + 2;    // sources finished reading their recv buffers
+
+struct EpGemmParams {
+  int M, N, K;                  // M = row capacity (multiple of 128)
+  void* C;                      // pull epilogue output (local), row stride ldc
+  long long ldc;
+  const void* aux;              // SwiGLU pre-activation [M, 2H] (epilogue 3 writes it, 4 reads it)
+  int swiglu_h;                 // H
+  int* status;
+  const int* offsets;           // [experts + 1] 128-aligned segment starts of this rank's rows
+  int experts, b_rows;          // B stacks experts * b_rows rows
+  int epi;                      // pull: 3 (SwiGLU) or 4 (SwiGLU backward); push: 0
+  int rank, world;
+  long long epoch;              // 1, 2, ... per call of the same kind
+  long long timeout_ns;
+  // pull: row r of A = row (row_src[r] & 0xFFFFFF) of rank (row_src[r] >> 24)'s send buffer; -1 = zero row
+  const int* row_src;
+  unsigned long long src[kMaxRanks];
+  long long src_rows;           // rows of every send buffer (rows at or past it are refused)
+  void* a_local;                // [M, K] gathered A (kept by the caller)
+  unsigned int* chunk_flags;    // [M / 128] pieces in place per chunk (zeroed before the launch)
+  // push: output row r -> row (row_dst[r] & 0xFFFFFF) of rank (row_dst[r] >> 24)'s recv buffer; -1 = dropped
+  const int* row_dst;
+  unsigned long long dst[kMaxRanks];
+  long long dst_rows;           // rows of every recv buffer (rows at or past it are refused)
+  unsigned long long signal[kMaxRanks];
+  unsigned int* block_counter;  // local, zero between launches
+};
+struct EpCombineParams {
+  const void* recv;             // local recv rows [tokens * k, cols] bf16
+  const float* weights;         // [tokens * k] or null (plain sum)
+  void* out;                    // [tokens, cols] bf16
+  void* keep;                   // optional copy of the recv rows
+  long long tokens;
+  int k, cols, rank, world;
+  unsigned long long done_target;
+  unsigned long long signal[kMaxRanks];
+  unsigned int* block_counter;
+  long long timeout_ns;
+  int* status;
+};
+void ep_pull_gemm(const EpGemmParams& p, const void* B, long long ldb, bool b_mn, cudaStream_t stream);
+void ep_push_gemm(const EpGemmParams& p, const void* A, long long lda, const void* B, long long ldb, bool b_mn,
+                  cudaStream_t stream);
+void ep_combine(const EpCombineParams& p, cudaStream_t stream);
+void ep_expand(const void* dy, const float* w, const void* y, void* out, float* dw, long long slots, int k, int cols,
+               cudaStream_t stream);
+
 int tp_gemm_grid(int M, int N);
 void tp_ag_gemm(const TpGemmParams& p, const void* a_shard, const void* B, long long ldb, bool b_mn, int grid,
                 cudaStream_t stream);

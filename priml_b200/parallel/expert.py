@@ -20,6 +20,15 @@ layer:
 Backward runs the same two exchanges in the opposite directions. Without CUDA
 (gloo ranks) an all-gather oracle implements the same exchange API.
 
+With ``comm="gemm"`` (the default on CUDA) the exchange happens inside the
+expert GEMMs (``ops/csrc/ep_gemm.cu``): the up projection's copy warps pull
+every received row from its source's send buffer over NVLink while the tensor
+cores run the chunks already in place, and the down projection's epilogue
+stores each output row straight into its source's receive buffer. Backward
+mirrors it (the down dgrad pulls ``w * dy``, the up dgrad pushes ``dx``). The
+plan then all-gathers the routing indices instead of the counts, so every
+owner knows the source of each row it receives.
+
 Gradients follow the sequence-parallel TP strategy: replicated parameters are
 averaged over all ranks once per step; expert weights (which saw the tokens of
 every rank) are divided by the world size; the clip norm sums the expert
@@ -40,7 +49,17 @@ from priml_b200.config import Fig
 from priml_b200.parallel.runtime import global_device_mesh
 from priml_b200.parallel.strategies import place
 
-__all__ = ["EpComm", "EpOracleComm", "EpPlan", "ExpertParallel", "ep_plan", "shard_experts"]
+__all__ = [
+    "EpComm",
+    "EpGemmComm",
+    "EpOracleComm",
+    "EpPlan",
+    "EpRoutes",
+    "ExpertParallel",
+    "ep_plan",
+    "ep_routes",
+    "shard_experts",
+]
 
 log = logging.getLogger(__name__)
 
@@ -189,6 +208,176 @@ class EpOracleComm:
         return out
 
 
+@dataclass
+class EpRoutes:
+    """Device-side routes of one MoE call on one rank, for the exchange fused into the GEMMs."""
+
+    tokens: int
+    top_k: int
+    row_src: Tensor  # int32 [cap]: (source rank << 24) | source token of each received row, -1 = padding
+    origin: Tensor  # int32 [cap]: (source rank << 24) | source slot of each received row, -1 = padding
+    seg_start: Tensor  # int32 [EL + 1]: this rank's expert segments (multiples of 128)
+    cap: int  # static bound on the received rows (multiple of 128)
+
+
+def ep_routes(indices: Tensor, num_experts: int, rank: int, world: int, group: Any = None) -> EpRoutes:
+    """Routes for ``[T, k]`` global expert indices (one all-gather of the indices; device ops only).
+
+    Every owner lays out expert ``e``'s rows as one 128-aligned segment holding the sources'
+    rows in rank order and, within a source, in slot order: the layout of :func:`ep_plan`,
+    computed here for every source so the owner knows where each of its rows comes from.
+    """
+    t, k = indices.shape
+    s = t * k
+    el = num_experts // world
+    flat = indices.reshape(-1).to(torch.int32).contiguous()
+    all_flat = _all_gather(flat, group, world) if world > 1 else flat.unsqueeze(0)  # [W, S]
+    dev = flat.device
+    g = all_flat.reshape(-1).long()  # global expert of every (source, slot)
+    src = torch.arange(world, device=dev).repeat_interleave(s)
+    slot = torch.arange(s, device=dev).repeat(world)
+    key = src * num_experts + g
+    counts = torch.bincount(key, minlength=world * num_experts)  # [(W, E)]
+    tot = counts.view(world, num_experts).sum(0)
+    padded = ((tot + 127) // 128 * 128).view(world, el)
+    seg = padded.cumsum(1) - padded  # [owner, local expert] segment starts
+    src_off = counts.view(world, num_experts).cumsum(0) - counts.view(world, num_experts)  # rows of lower sources
+    key_start = counts.cumsum(0) - counts
+    order = torch.argsort(key, stable=True)
+    within = torch.empty_like(key)
+    within[order] = torch.arange(world * s, device=dev) - key_start[key[order]]
+    dest_row = seg.reshape(-1)[g] + src_off.reshape(-1)[key] + within
+    cap = (world * s + 127) // 128 * 128 + 128 * el
+    # rows bound for other owners land on a dump row past the end and are cut off
+    at = torch.where(g // el == rank, dest_row, torch.full_like(dest_row, cap))
+    code = (src << 24) | slot
+    origin = torch.full((cap + 1,), -1, device=dev, dtype=torch.int64).scatter_(0, at, code)[:cap]
+    row_src = torch.full((cap + 1,), -1, device=dev, dtype=torch.int64).scatter_(0, at, (src << 24) | (slot // k))[:cap]
+    seg_start = torch.cat([seg[rank], (seg[rank, -1] + padded[rank, -1]).reshape(1)]).to(torch.int32)
+    return EpRoutes(t, k, row_src.to(torch.int32), origin.to(torch.int32), seg_start, cap)
+
+
+class EpGemmComm:
+    """Owner of the native ``EpGemmGroup`` (send / recv rows and signals in IPC-mapped memory).
+
+    Buffers grow on demand, collectively: every rank makes the same calls with the same sizes.
+    """
+
+    fused = True
+    in_gemm = True
+
+    def __init__(self, group: Any, timeout_s: float = 60.0) -> None:
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout_s = timeout_s
+        self._g: Any = None
+        self._cap = (0, 0, 0)
+
+    def ensure(self, slots: int, cap: int, cols: int) -> Any:
+        if self._g is not None and slots <= self._cap[0] and cap <= self._cap[1] and cols == self._cap[2]:
+            return self._g
+        from priml_b200.ops import native
+
+        want = (max(slots, self._cap[0]), max(cap, self._cap[1]), cols)
+        seen: list[Any] = [None] * self.world
+        dist.all_gather_object(seen, want, group=self.group)
+        if any(w != want for w in seen):
+            raise ValueError(f"expert parallelism needs the same tokens per MoE call on every rank; got {seen}")
+        if self._g is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+        g = native().EpGemmGroup(self.rank, self.world, want[0], want[0], cols, want[1] // 128, self.timeout_s)
+        handles: list[Any] = [None] * self.world
+        dist.all_gather_object(handles, g.handles(), group=self.group)
+        g.open(handles)
+        self._g, self._cap = g, want
+        return g
+
+
+class _EpGemmMoE(torch.autograd.Function):
+    """Routed expert SwiGLU with the token exchange inside the expert GEMMs (see ``ep_gemm.cu``)."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, weights: Tensor, up_w: Tensor, down_w: Tensor, routes: EpRoutes, comm: EpGemmComm):  # type: ignore[override]
+        from priml_b200.ops.functional import bf16_shadow
+
+        t, c = x.shape
+        k = routes.top_k
+        el, two_h, _ = up_w.shape
+        h_dim = two_h // 2
+        grp = comm.ensure(t * k, routes.cap, c)
+        up16 = bf16_shadow(up_w).reshape(el * two_h, c)
+        down16 = bf16_shadow(down_w).reshape(el * c, h_dim)
+        grp.wait_send_free()
+        grp.send_rows(t).copy_(x)
+        dev, cap = x.device, routes.cap
+        x_priv = torch.empty(cap, c, device=dev, dtype=torch.bfloat16)
+        h = torch.empty(cap, h_dim, device=dev, dtype=torch.bfloat16)
+        gu = torch.empty(cap, two_h, device=dev, dtype=torch.bfloat16)
+        grp.pull_gemm(routes.row_src, routes.seg_start, up16, 3, two_h, h_dim, h, gu, x_priv)
+        grp.push_gemm(h, routes.origin, routes.seg_start, down16, False, c)
+        w32 = weights.float().contiguous()
+        y = torch.empty(t, c, device=dev, dtype=torch.bfloat16)
+        y_slots = torch.empty(t * k, c, device=dev, dtype=torch.bfloat16)
+        grp.combine(t, k, w32, y, y_slots)
+        ctx.save_for_backward(x_priv, h, gu, y_slots, w32, up16, down16)
+        ctx.routes, ctx.comm, ctx.params, ctx.w_dtype = routes, comm, (up_w, down_w), weights.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        from priml_b200.ops import native
+        from priml_b200.ops.grouped import _grad_into
+
+        n = native()
+        x_priv, h, gu, y_slots, w32, up16, down16 = ctx.saved_tensors
+        routes, comm = ctx.routes, ctx.comm
+        up_w, down_w = ctx.params
+        t, k = w32.shape
+        c = x_priv.shape[1]
+        two_h = gu.shape[1]
+        h_dim = two_h // 2
+        dev, cap = dy.device, routes.cap
+        grp = comm.ensure(t * k, cap, c)
+        dy16 = dy.to(torch.bfloat16).contiguous()
+        grp.wait_send_free()
+        dw = torch.empty(t, k, device=dev, dtype=torch.float32)
+        n.ep_expand(dy16, w32, y_slots, grp.send_rows(t * k), dw)
+        dy_priv = torch.empty(cap, c, device=dev, dtype=torch.bfloat16)
+        dgu = torch.empty(cap, two_h, device=dev, dtype=torch.bfloat16)
+        grp.pull_gemm(routes.origin, routes.seg_start, down16, 4, c, h_dim, dgu, gu, dy_priv)
+        grp.push_gemm(dgu, routes.origin, routes.seg_start, up16, True, two_h)
+        dx = torch.empty(t, c, device=dev, dtype=torch.bfloat16)
+        grp.combine(t, k, None, dx, None)
+        grads = []
+        for param, a, b in ((up_w, dgu, x_priv), (down_w, dy_priv, h)):
+            e_rows = param.shape[0] * param.shape[1]
+            dst, acc, _ = _grad_into(param, e_rows)
+            if dst is not None:
+                n.grouped_gemm(a, b, dst, routes.seg_start, True, 2 if acc else 1, 1, 0)
+                grads.append(None)
+            else:
+                out = torch.empty(e_rows, param.shape[2], device=dev, dtype=torch.float32)
+                n.grouped_gemm(a, b, out, routes.seg_start, True, 1, 1, 0)
+                grads.append(out.view_as(param).to(param.dtype))
+        return dx, dw.to(ctx.w_dtype), grads[0], grads[1], None, None
+
+
+class EpGemmDispatcher:
+    """Installed on ``MoE.expert_parallel`` for ``comm="gemm"``: the exchange runs inside the expert GEMMs."""
+
+    def __init__(self, comm: EpGemmComm) -> None:
+        self.comm = comm
+
+    def __call__(self, moe: nn.Module, xf: Tensor, weights: Tensor, indices: Tensor) -> Tensor:
+        comm = self.comm
+        routes = ep_routes(indices, moe.num_experts, comm.rank, comm.world, comm.group)
+        experts = moe.experts
+        y = _EpGemmMoE.apply(xf.to(torch.bfloat16).contiguous(), weights, experts.up_proj, experts.down_proj, routes, comm)
+        return y.to(xf.dtype)
+
+
 # --------------------------------------------------------------------------- autograd
 class _ToExperts(torch.autograd.Function):
     @staticmethod
@@ -261,7 +450,7 @@ def shard_experts(model: nn.Module, comm: Any) -> list[nn.Parameter]:
         ex.down_proj = nn.Parameter(ex.down_proj.data[r * el : (r + 1) * el].clone())
         ex.num_experts = el
         ex.expert_offset = r * el
-        mod.expert_parallel = EpDispatcher(comm)
+        mod.expert_parallel = EpGemmDispatcher(comm) if getattr(comm, "in_gemm", False) else EpDispatcher(comm)
         sharded += [ex.up_proj, ex.down_proj]
     return sharded
 
@@ -274,7 +463,8 @@ class ExpertParallel:
         mesh_dim: str = "dp"
         timeout_s: float = 60.0
         comm: str = "auto"
-        """``fused`` (NVLink kernels; CUDA), ``oracle`` (all-gather), ``auto`` = fused on CUDA."""
+        """``gemm`` (exchange inside the expert GEMMs; CUDA), ``fused`` (NVLink row-exchange kernels
+        around separate grouped GEMMs; CUDA), ``oracle`` (all-gather), ``auto`` = gemm on CUDA."""
 
     def __init__(self, config: Config | None = None) -> None:
         from priml_b200.parallel.tp_fused import TpGradSync  # noqa: F401  (same gradient rules)
@@ -291,11 +481,15 @@ class ExpertParallel:
         self.group = mesh[config.mesh_dim].get_group()
         use_cuda = mesh.device_type == "cuda"
         self.device = torch.device("cuda", torch.cuda.current_device()) if use_cuda else torch.device(mesh.device_type)
-        if config.comm not in ("auto", "fused", "oracle"):
-            raise ValueError(f"comm must be auto, fused or oracle; got {config.comm!r}")
-        if config.comm == "fused" and not use_cuda:
+        if config.comm not in ("auto", "gemm", "fused", "oracle"):
+            raise ValueError(f"comm must be auto, gemm, fused or oracle; got {config.comm!r}")
+        if config.comm in ("gemm", "fused") and not use_cuda:
             raise RuntimeError("the fused expert exchange needs CUDA ranks")
-        cls = EpComm if (use_cuda and config.comm != "oracle") else EpOracleComm
+        cls: Any = EpOracleComm
+        if use_cuda and config.comm in ("auto", "gemm"):
+            cls = EpGemmComm
+        elif use_cuda and config.comm == "fused":
+            cls = EpComm
         self.comm = cls(self.group, config.timeout_s)
         self.sync: Any = None
 

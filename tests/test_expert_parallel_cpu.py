@@ -96,3 +96,31 @@ def test_ep2_matches_single_process() -> None:
         assert abs(a - b) < 2e-3 * max(1.0, abs(b)), (two[0]["losses"], ref["losses"])
     for a, b in zip(two[0]["norms"], ref["norms"], strict=True):
         assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (two[0]["norms"], ref["norms"])
+
+
+def _routes_body(rank: int, world: int) -> dict:
+    from priml_b200.parallel.expert import ep_plan, ep_routes
+
+    g = torch.Generator().manual_seed(rank)
+    idx = torch.randint(0, 8, (10, 3), generator=g)
+    plan = ep_plan(idx, 8, rank, world)
+    routes = ep_routes(idx, 8, rank, world)
+    return {"dest_rank": plan.dest_rank, "dest_row": plan.dest_row, "seg": plan.seg_start, "cap": plan.cap,
+            "origin": routes.origin, "row_src": routes.row_src, "rseg": routes.seg_start, "rcap": routes.cap}  # fmt: skip
+
+
+def test_routes_name_the_source_of_every_row_the_plan_sends() -> None:
+    """The owner-side routes of the fused exchange agree with the source-side plan."""
+    out = run_ranks(_routes_body, 2, mesh_shape={"dp": 2})
+    for owner in range(2):
+        o = out[owner]
+        assert torch.equal(o["rseg"], o["seg"]) and o["rcap"] == o["cap"]
+        expect = torch.full_like(o["origin"], -1)
+        expect_src = torch.full_like(o["row_src"], -1)
+        for src in range(2):
+            sel = torch.nonzero(out[src]["dest_rank"] == owner).flatten()
+            rows = out[src]["dest_row"][sel]
+            expect[rows] = ((src << 24) | sel).to(torch.int32)
+            expect_src[rows] = ((src << 24) | (sel // 3)).to(torch.int32)
+        assert torch.equal(o["origin"], expect)
+        assert torch.equal(o["row_src"], expect_src)

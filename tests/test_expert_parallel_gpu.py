@@ -1,4 +1,5 @@
-"""Expert parallelism with the NVLink row exchange vs the all-gather oracle (2 GPUs)."""
+"""Expert parallelism vs the all-gather oracle (2 GPUs): the NVLink row-exchange kernels around
+separate grouped GEMMs (``fused``) and the exchange inside the expert GEMMs (``gemm``)."""
 
 from __future__ import annotations
 
@@ -33,7 +34,7 @@ def _rank(rank: int, world: int, port: int, q) -> None:  # noqa: ANN001
         g = torch.Generator().manual_seed(0)
         batches = [torch.randint(0, 512, (4 * world, 129), generator=g) for _ in range(3)]
         res = {}
-        for comm in ("oracle", "fused"):
+        for comm in ("oracle", "fused", "gemm"):
             torch.manual_seed(0)
             step = TrainStep.Config(
                 model=tiny_moe_lm(),
@@ -82,7 +83,9 @@ def test_expert_parallel_fused_exchange_matches_oracle() -> None:
     for rank, out, status in res:
         assert isinstance(out, dict), (rank, out)
         assert status == 0, (rank, status)
-        (lo, no), (lf, nf) = out["oracle"], out["fused"]
-        for a, b in zip(lf, lo, strict=True):
-            assert abs(a - b) < 2e-2 * max(1.0, abs(b)), (lf, lo)
-        assert abs(nf - no) < 5e-2 * max(1.0, no), (nf, no)
+        lo, no = out["oracle"]
+        for comm in ("fused", "gemm"):
+            lf, nf = out[comm]
+            for a, b in zip(lf, lo, strict=True):
+                assert abs(a - b) < 2e-2 * max(1.0, abs(b)), (comm, lf, lo)
+            assert abs(nf - no) < 5e-2 * max(1.0, no), (comm, nf, no)
