@@ -70,6 +70,10 @@ def _parse() -> argparse.Namespace:
                     "eager config (compile=None) only if compilation fails on one GPU")
     ap.add_argument("--reduce-blocks", type=int, default=None,
                     help="CTAs per fused reduce-scatter launch (default: the strategy's, one per SM)")
+    ap.add_argument("--ep-comm", choices=["gemm", "fused", "oracle"], default="gemm",
+                    help="expert parallelism: gemm = exchange inside the expert GEMMs (pull in the up projection, "
+                    "push from the down projection's epilogue); fused = peer-store exchange kernels around "
+                    "separate grouped GEMMs; oracle = NCCL all-gather")
     ap.add_argument("--out", type=str, default="")
     return ap.parse_args()
 
@@ -487,7 +491,7 @@ def main() -> None:
         "fused-shard": lambda: FusedFullySharded.Config(shard_params=True, **fused_kw),
         "fsdp2": lambda: FullySharded.Config(mp_param_dtype="bf16", mp_reduce_dtype="fp32", reshard_after_forward=True),
         "tp": lambda: FusedSequenceParallel.Config(),
-        "ep": lambda: ExpertParallel.Config(),
+        "ep": lambda: ExpertParallel.Config(comm=args.ep_comm),
         "single": lambda: NoParallel.Config(),
     }[strategy]()
     step_kw: dict[str, Any] = {}
@@ -632,8 +636,15 @@ def main() -> None:
                 "fsdp2": "torch FSDP2 fully_shard over NCCL (bf16 params, fp32 reduce)",
                 "tp": "sequence-parallel tensor parallelism: all-gather GEMM and GEMM reduce-scatter fused over "
                 "NVLink peer memory; replicated grads averaged once per step",
-                "ep": "expert parallelism: routed experts sharded over all ranks, token rows exchanged by "
-                "NVLink peer-memory dispatch / combine kernels around the grouped expert GEMM; the rest replicated",
+                "ep": {
+                    "gemm": "expert parallelism: routed experts sharded over all ranks; the token exchange runs "
+                    "inside the expert GEMMs (the up projection pulls routed rows over NVLink while its tiles run, "
+                    "the down projection's epilogue stores rows into the sources); the rest replicated",
+                    "fused": "expert parallelism: routed experts sharded over all ranks, token rows exchanged by "
+                    "NVLink peer-memory dispatch / combine kernels around the grouped expert GEMM; the rest replicated",
+                    "oracle": "expert parallelism: routed experts sharded over all ranks, token rows exchanged by "
+                    "NCCL all-gathers; the rest replicated",
+                }[args.ep_comm],
                 "single": "one GPU, fused AdamW",
             }[strategy],
             "l2": "working set (weights + optimizer state + activations) >> 126 MB L2; no flush",
