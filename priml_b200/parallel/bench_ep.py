@@ -81,8 +81,8 @@ def main() -> None:
 
     comm = EpGemmComm(dist.group.WORLD, timeout_s=30.0)
     routes = ep_routes(idx, E, rank, world, dist.group.WORLD)
-    cap = routes.cap
-    grp = comm.ensure(T * k, cap, C)
+    cap = max(int(routes.seg_start[-1]), 128)  # rows actually received
+    grp = comm.ensure(T * k, routes.cap, C)
     x_priv = torch.empty(cap, C, device="cuda", dtype=torch.bfloat16)
     h = torch.empty(cap, H, device="cuda", dtype=torch.bfloat16)
     gu = torch.empty(cap, 2 * H, device="cuda", dtype=torch.bfloat16)

@@ -218,6 +218,7 @@ class EpRoutes:
     origin: Tensor  # int32 [cap]: (source rank << 24) | source slot of each received row, -1 = padding
     seg_start: Tensor  # int32 [EL + 1]: this rank's expert segments (multiples of 128)
     cap: int  # static bound on the received rows (multiple of 128)
+    rows: int = 0  # rows actually received (seg_start[-1], at least 128), set by the forward
 
 
 def ep_routes(indices: Tensor, num_experts: int, rank: int, world: int, group: Any = None) -> EpRoutes:
@@ -311,7 +312,11 @@ class _EpGemmMoE(torch.autograd.Function):
         down16 = bf16_shadow(down_w).reshape(el * c, h_dim)
         grp.wait_send_free()
         grp.send_rows(t).copy_(x)
-        dev, cap = x.device, routes.cap
+        # The received rows and the tensors kept for the backward are sized by this call's
+        # real row count (one device read per layer) rather than by the static bound, which
+        # is world times larger: at eight ranks the bound would not fit the saved activations.
+        dev, cap = x.device, max(int(routes.seg_start[-1]), 128)
+        routes.rows = cap
         x_priv = torch.empty(cap, c, device=dev, dtype=torch.bfloat16)
         h = torch.empty(cap, h_dim, device=dev, dtype=torch.bfloat16)
         gu = torch.empty(cap, two_h, device=dev, dtype=torch.bfloat16)
@@ -338,8 +343,8 @@ class _EpGemmMoE(torch.autograd.Function):
         c = x_priv.shape[1]
         two_h = gu.shape[1]
         h_dim = two_h // 2
-        dev, cap = dy.device, routes.cap
-        grp = comm.ensure(t * k, cap, c)
+        dev, cap = dy.device, routes.rows
+        grp = comm.ensure(t * k, routes.cap, c)
         dy16 = dy.to(torch.bfloat16).contiguous()
         grp.wait_send_free()
         dw = torch.empty(t, k, device=dev, dtype=torch.float32)
