@@ -215,9 +215,36 @@ FLOOR_SPECIES: Final = ((0, 0, 0), (2, 2, 2), (1, 1, 1), (2, 3, 3), (2, 4, 4), (
 FLOOR_HEALTH: Final = ((3.0, 5.0, 3.0), (4.0, 7.0, 5.0), (6.0, 9.0, 6.0), (8.0, 11.0, 8.0), (0.0, 12.0, 12.0),
                        (0.0, 20.0, 4.0), (0.0, 20.0, 14.0), (0.0, 24.0, 16.0), (0.0, 5.0, 3.0))  # fmt: skip
 """Per floor, fresh creature health (passive, melee, ranged); 0 where the floor has none."""
-SPECIES_DAMAGE: Final = ((2.0, 2.0), (4.0, 4.0), (3.0, 3.0), (5.0, 3.0), (6.0, 5.0), (8.0, 10.0), (8.0, 8.0), (9.0, 9.0))
-"""Per melee / ranged species, (melee hit, projectile) damage: the game's physical, fire and ice
-parts summed (this build models no elemental resistance)."""
+SPECIES_DAMAGE: Final = (
+    ((2.0, 0.0, 0.0), (2.0, 0.0, 0.0)),
+    ((4.0, 0.0, 0.0), (4.0, 0.0, 0.0)),
+    ((3.0, 0.0, 0.0), (0.0, 3.0, 0.0)),
+    ((5.0, 0.0, 0.0), (0.0, 0.0, 3.0)),
+    ((6.0, 0.0, 0.0), (5.0, 0.0, 0.0)),
+    ((6.0, 1.0, 1.0), (4.0, 3.0, 3.0)),
+    ((3.0, 5.0, 0.0), (3.0, 5.0, 0.0)),
+    ((4.0, 0.0, 5.0), (4.0, 0.0, 5.0)),
+)
+"""Per melee / ranged species, (melee hit, projectile) damage as (physical, fire, ice): the orc
+mages throw fire, the kobolds ice, the deep things all three, and the elemental realms' creatures
+add their realm's element."""
+SPECIES_DEFENSE: Final = (
+    (0.0, 0.0, 0.0),
+    (0.0, 0.0, 0.0),
+    (0.0, 0.0, 0.0),
+    (0.0, 0.0, 0.0),
+    (0.5, 0.0, 0.0),
+    (0.2, 0.0, 0.0),
+    (0.9, 1.0, 0.0),
+    (0.9, 0.0, 1.0),
+)
+"""Per melee / ranged species, the fraction of (physical, fire, ice) damage it shrugs off: knights
+and archers wear plate, the fire realm's creatures are immune to fire and the ice realm's to ice
+(and both mostly to blades), so the elemental floors want the opposite element."""
+ARMOUR_DEFENSE: Final = (0.1, 0.2)
+"""Physical share blocked by one iron / diamond armour piece."""
+ENCHANT_DEFENSE: Final = 0.2
+"""Share of its element that one enchanted armour piece blocks."""
 FLOOR_SPAWN: Final = ((0.1, 0.02, 0.05, 0.1),) + ((0.1, 0.06, 0.05, 0.0),) * 3 + ((0.0, 0.06, 0.05, 0.0),) * 5
 """Per floor, spawn probability for (passive, melee, ranged, melee at night)."""
 PASSIVE_ACHIEVEMENT: Final = (Achievement.EAT_COW, Achievement.EAT_BAT, Achievement.EAT_SNAIL)

@@ -156,17 +156,33 @@ def _level_table(s: GameState, table: tuple, column: int) -> Tensor:
 
 
 def _species_damage(s: GameState, cls: int, column: int) -> Tensor:
-    """Damage dealt by the class-``cls`` species of the current floor (0 melee hit, 1 projectile)."""
+    """(physical, fire, ice) damage ``[E, 3]`` dealt by the class-``cls`` species of the current floor
+    (column 0 its melee hit, 1 its projectile)."""
     build = lambda: [C.SPECIES_DAMAGE[row[cls]][column] for row in C.FLOOR_SPECIES]  # noqa: E731
     return _const(("species_damage", cls, column), s.device, build)[s.level]
 
 
+def _species_defense(s: GameState, cls: int) -> Tensor:
+    """(physical, fire, ice) shares ``[E, 3]`` the class-``cls`` species of the current floor resists
+    (passive creatures resist nothing)."""
+    build = lambda: [C.SPECIES_DEFENSE[row[cls]] if cls > 0 else (0.0, 0.0, 0.0) for row in C.FLOOR_SPECIES]  # noqa: E731
+    return _const(("species_defense", cls), s.device, build)[s.level]
+
+
+def _in_element(amount: Tensor, element: Tensor) -> Tensor:
+    """``[E, 3]`` damage vector with ``amount`` in slot ``element`` (0 physical, 1 fire, 2 ice)."""
+    out = torch.zeros(*amount.shape, 3, device=amount.device, dtype=amount.dtype)
+    return out.scatter(-1, element.long().unsqueeze(-1), amount.unsqueeze(-1))
+
+
 def _player_damage(s: GameState) -> Tensor:
-    """Sword damage: the tier's figure, strength adding a quarter per level above 1; an enchanted sword
-    adds half the tier's figure in its element, intelligence adding a twentieth of that per level."""
+    """Sword damage ``[E, 3]`` (physical, fire, ice): the tier's figure as physical damage, strength
+    adding a quarter per level above 1; an enchanted sword adds half the tier's figure in its element,
+    intelligence adding a twentieth of that per level."""
     base = _const("sword", s.device, _SWORD_DAMAGE)[s.sword]
+    physical = base * (1.0 + 0.25 * (s.strength - 1).float())
     element = 0.5 * base * (s.sword_enchant > 0).float() * (1.0 + 0.05 * (s.intelligence - 1).float())
-    return base * (1.0 + 0.25 * (s.strength - 1).float()) + element
+    return _in_element(physical, torch.zeros_like(s.sword)) + _in_element(element, s.sword_enchant.clamp(min=0))
 
 
 def _boss_vulnerable(s: GameState) -> Tensor:
@@ -188,7 +204,8 @@ def _hit_creatures(s: GameState, target: Tensor, doing: Tensor, damage: Tensor) 
     for cls, mobs in enumerate((s.passive, s.melee, s.ranged)):
         at = (mobs.position == target[:, None]).all(-1) & mobs.mask & doing[:, None] & ~absorbed[:, None]
         hit_any = at.any(-1)
-        mobs.health = mobs.health - at.float() * damage[:, None]
+        landed = ((1.0 - _species_defense(s, cls)) * damage).sum(-1)  # what gets through, summed over elements
+        mobs.health = mobs.health - at.float() * landed[:, None]
         killed = at & (mobs.health <= 0)
         mobs.mask = mobs.mask & ~killed
         died = killed.any(-1)
@@ -352,11 +369,15 @@ def _fly_shots(s: GameState) -> None:
     shots.position = shots.position + shots.direction * shots.mask[..., None].long()
     # arrows: 2, dexterity adding a quarter per level, an enchanted bow half again; spells: intelligence
     # adding a tenth per level
-    arrow = 2.0 * (1.0 + 0.25 * (s.dexterity - 1).float()) * (1.0 + 0.5 * (s.bow_enchant > 0).float())
+    # physical, an enchanted bow adding half again in its element
+    arrow_hit = 2.0 * (1.0 + 0.25 * (s.dexterity - 1).float())
+    arrow = _in_element(arrow_hit, torch.zeros_like(s.bow_enchant))
+    arrow = arrow + _in_element(0.5 * arrow_hit * (s.bow_enchant > 0).float(), s.bow_enchant.clamp(min=0))
     spell = C.SPELL_DAMAGE * (1.0 + 0.1 * (s.intelligence - 1).float())
     for slot in range(shots.mask.shape[1]):
         live = shots.mask[:, slot]
-        damage = torch.where(shots.cooldown[:, slot] == 0, arrow, spell)
+        kind = shots.cooldown[:, slot]  # 0 arrow, 1 fireball, 2 iceball: the spell's element is its kind
+        damage = torch.where((kind == 0)[:, None], arrow, _in_element(spell, kind.clamp(0, 2)))
         hit = _hit_creatures(s, shots.position[:, slot], live, damage)
         b = _tile(s.map, shots.position[:, slot])
         passable = torch.stack([b == int(g) for g in (*_GROUND, B.WATER, B.LAVA)]).any(0)
@@ -460,14 +481,17 @@ def _try_move(s: GameState, mobs: Creatures, step: Tensor, allowed: tuple[B, ...
         mobs.position[:, slot] = torch.where(ok[:, None], target, pos)
 
 
-def _armour_factor(s: GameState) -> Tensor:
-    """Fraction of a blow that lands: iron pieces block a tenth, diamond a fifth, an enchanted piece a
-    twentieth more (its element's fifth of the blow's elemental share, summed into one figure here);
-    the graveyard adds half again."""
-    block = 0.1 * (s.armour == 1).sum(-1).float() + 0.2 * (s.armour == 2).sum(-1).float()
-    block = block + 0.05 * ((s.armour_enchant > 0) & (s.armour > 0)).sum(-1).float()
+def _damage_to_player(s: GameState, damage: Tensor) -> Tensor:
+    """What a ``[E, 3]`` (physical, fire, ice) blow takes from the player: each iron piece blocks a
+    tenth and each diamond piece a fifth of the physical part, each piece enchanted in an element a
+    fifth of that element; the graveyard adds half again."""
+    worn = s.armour > 0
+    physical = C.ARMOUR_DEFENSE[0] * (s.armour == 1).sum(-1).float() + C.ARMOUR_DEFENSE[1] * (s.armour == 2).sum(-1).float()
+    fire = C.ENCHANT_DEFENSE * (worn & (s.armour_enchant == 1)).sum(-1).float()
+    ice = C.ENCHANT_DEFENSE * (worn & (s.armour_enchant == 2)).sum(-1).float()
+    resisted = torch.stack([physical, fire, ice], -1).clamp(max=1.0)
     boss = 1.0 + C.BOSS_EXTRA_DAMAGE * (s.level == C.LEVELS - 1).float()
-    return (1.0 - block) * boss
+    return ((1.0 - resisted) * damage).sum(-1) * boss
 
 
 def _creatures(s: GameState, generator: torch.Generator | None) -> None:
@@ -486,8 +510,9 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     dist = (s.position[:, None] - s.melee.position).abs().sum(-1)
     attack = s.melee.mask & (dist <= 1) & (s.melee.cooldown <= 0)
     melee_hit = _species_damage(s, 1, 0)
-    damage = torch.where(s.sleeping, torch.full_like(s.health, 7.0), melee_hit)
-    s.health = s.health - attack.sum(-1).float() * damage * _armour_factor(s)
+    asleep = _in_element(torch.full_like(s.health, 7.0), torch.zeros_like(s.level))  # a sleeper takes a heavy blow
+    damage = torch.where(s.sleeping[:, None], asleep, melee_hit)
+    s.health = s.health - attack.sum(-1).float() * _damage_to_player(s, damage)
     s.melee.cooldown = torch.where(attack, torch.full_like(s.melee.cooldown, 5), (s.melee.cooldown - 1).clamp(min=0))
     # skeletons keep to the caves and shoot along rows / columns when the player is within 4 tiles
     _try_move(s, s.ranged, _random_step(s.ranged, generator), _GROUND[2:], also=(B.GRASS, s.level > 0))
@@ -511,7 +536,7 @@ def _creatures(s: GameState, generator: torch.Generator | None) -> None:
     # arrows fly one tile per step: they hurt the player they reach and stop at solid tiles
     proj.position = proj.position + proj.direction * proj.mask[..., None].long()
     hit = proj.mask & (proj.position == s.position[:, None]).all(-1)
-    s.health = s.health - hit.sum(-1).float() * _species_damage(s, 2, 1) * _armour_factor(s)
+    s.health = s.health - hit.sum(-1).float() * _damage_to_player(s, _species_damage(s, 2, 1))
     blocked = torch.zeros_like(proj.mask)
     for slot in range(proj.mask.shape[1]):
         b = _tile(s.map, proj.position[:, slot])

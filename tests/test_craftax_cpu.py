@@ -279,7 +279,7 @@ def test_nine_floors_entry_achievements_and_gems() -> None:
     assert int(s.sapphire) == 1 and bool(s.achievements[0, A.COLLECT_SAPPHIRE])
     # the troll mines' deep things throw harder than the overworld's skeletons
     s.level[:] = 5
-    assert float(rules._species_damage(s, 2, 1)) > C.SPECIES_DAMAGE[0][1]
+    assert float(rules._species_damage(s, 2, 1).sum()) > sum(C.SPECIES_DAMAGE[0][1])
 
 
 def test_books_spells_enchanting_and_the_necromancer() -> None:
@@ -308,10 +308,11 @@ def test_books_spells_enchanting_and_the_necromancer() -> None:
     # enchanting at a fire table spends a ruby and 9 mana
     _face(s, B.ENCHANTMENT_TABLE_FIRE)
     s.sword[:], s.ruby[:], s.mana[:] = 1, 1, 9
-    before = float(rules._player_damage(s))
+    before = rules._player_damage(s)
     s, _ = _act(s, Act.ENCHANT_SWORD)
     assert int(s.sword_enchant) == 1 and int(s.ruby) == 0 and int(s.mana) <= 1 and bool(s.achievements[0, A.ENCHANT_SWORD])
-    assert float(rules._player_damage(s)) > before
+    after = rules._player_damage(s)
+    assert float(after[0, 1]) > 0 and float(before[0, 1]) == 0 and float(after[0, 0]) == float(before[0, 0])
     s.armour[0] = torch.tensor([1, 0, 0, 0])
     s.sapphire[:], s.mana[:] = 1, 9
     _face(s, B.ENCHANTMENT_TABLE_ICE)
@@ -396,3 +397,23 @@ def test_pixel_renderer_layers_and_shading(tmp_path) -> None:  # noqa: ANN001
     assert cave[0, :8, :8].max() == 0  # the corner tile is 4+ tiles away: unseen
     PixelRenderer.write_png(cave[0], tmp_path / "frame.png")
     assert (tmp_path / "frame.png").stat().st_size > 0
+
+
+def test_elemental_damage_and_resistance() -> None:
+    """Fire-realm creatures shrug off fire and most physical damage; enchanted armour blocks its element."""
+    s = _world(1)
+    s.level[:] = 6  # the fire realm: pigmen and fire elementals
+    hit = rules._species_damage(s, 1, 0)[0].tolist()
+    assert hit[1] > 0 and hit[2] == 0  # a pigman's blow carries fire
+    fire = rules._in_element(torch.tensor([6.0]), torch.tensor([1]))
+    ice = rules._in_element(torch.tensor([6.0]), torch.tensor([2]))
+    defense = rules._species_defense(s, 1)
+    assert float(((1 - defense) * fire).sum()) == 0.0  # immune to a fireball
+    assert float(((1 - defense) * ice).sum()) == 6.0  # an iceball lands in full
+    # a fire-enchanted piece blocks a fifth of a fire blow's fire share, nothing of its physical share
+    s.armour[0] = torch.tensor([1, 0, 0, 0])
+    plain = float(rules._damage_to_player(s, torch.tensor([[0.0, 5.0, 0.0]])))
+    s.armour_enchant[0] = torch.tensor([1, 0, 0, 0])
+    warded = float(rules._damage_to_player(s, torch.tensor([[0.0, 5.0, 0.0]])))
+    assert abs(plain - 5.0) < 1e-6 and abs(warded - 4.0) < 1e-6
+    assert abs(float(rules._damage_to_player(s, torch.tensor([[10.0, 0.0, 0.0]]))) - 9.0) < 1e-6
