@@ -231,6 +231,15 @@ class MultiHeadLatentAttention(nn.Module):
         w_kr, w_uv = self._w_kv_b()
         w_kr, w_uv = w_kr.to(q_nope.dtype), w_uv.to(q_nope.dtype)
         q_abs = torch.einsum("...shd,hdl->...shl", q_nope, w_kr)
+        if s == 1 and self._latent_decode_kernel(q_abs, q_pe, c_kv):
+            # one new token per sequence: latent-space attention on the tcgen05 decode kernel
+            lead = q_abs.shape[:-3]
+            h = q_abs.shape[-2]
+            q_cat = torch.cat([q_abs, q_pe.to(q_abs.dtype)], dim=-1).reshape(-1, h, q_abs.shape[-1] + q_pe.shape[-1])
+            lat = ops.mla_decode(q_cat, c_kv.reshape(-1, t, c_kv.shape[-1]), k_pe.reshape(-1, t, k_pe.shape[-1]),
+                                 scale=self.softmax_scale)  # fmt: skip
+            lat = lat.view(*lead, 1, h, lat.shape[-1])
+            return torch.einsum("...shl,hvl->...shv", lat, w_uv).flatten(-2)
         logits = torch.einsum("...shl,...tl->...hst", q_abs, c_kv) + torch.einsum("...shr,...tr->...hst", q_pe, k_pe)
         logits = logits * self.softmax_scale
         if self.causal and s > 1:
@@ -240,6 +249,19 @@ class MultiHeadLatentAttention(nn.Module):
             attn = F.dropout(attn, p=self.dropout)
         lat = torch.einsum("...hst,...tl->...hsl", attn, c_kv)
         return torch.einsum("...hsl,hvl->...shv", lat, w_uv).flatten(-2)
+
+    def _latent_decode_kernel(self, q_abs: Tensor, q_pe: Tensor, c_kv: Tensor) -> bool:
+        """Whether a one-token step takes the decode kernel: CUDA bf16 inference with 512-wide
+        latents and 64-wide rotary keys (the kernel's shapes)."""
+        return (
+            ops.use_native(q_abs)
+            and not (torch.is_grad_enabled() and (q_abs.requires_grad or c_kv.requires_grad))
+            and q_abs.dtype == torch.bfloat16
+            and c_kv.dtype == torch.bfloat16
+            and q_abs.shape[-1] == 512
+            and q_pe.shape[-1] == 64
+            and not (self.training and self.dropout > 0)
+        )
 
     def _expanded_attention(self, q_nope: Tensor, q_pe: Tensor, c_kv: Tensor, k_pe: Tensor) -> Tensor:
         """Training order: expand K/V per head, then flash attention."""

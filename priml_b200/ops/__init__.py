@@ -26,6 +26,7 @@ __all__ = [
     "decode_attention",
     "grouped_swiglu_experts",
     "grouped_swiglu_mlp",
+    "mla_decode",
     "linear",
     "linear_cross_entropy",
     "linear_swiglu",
@@ -152,6 +153,32 @@ def swiglu(gate_up: Tensor) -> Tensor:
 
         return functional.swiglu(gate_up)
     return reference.swiglu(gate_up)
+
+
+def mla_decode(q: Tensor, c_kv: Tensor, k_pe: Tensor, *, scale: float, lengths: Tensor | None = None) -> Tensor:
+    """Latent-space multi-head latent attention for one query token per sequence.
+
+    ``q`` is ``[B, H, 576]``: the absorbed query ``q_nope @ W_UK`` (512) followed by the
+    rotary query (64); ``c_kv [B, T, 512]`` and ``k_pe [B, T, 64]`` are the cached latent
+    rows and shared rotary keys (any row / sequence strides with contiguous channels).
+    Returns ``softmax(scale * q . [c_kv | k_pe]) @ c_kv`` per head, ``[B, H, 512]``; keys
+    at or past ``lengths[b]`` are hidden. On CUDA (bf16) this is the tcgen05 kernel of
+    ``ops/csrc/mla_decode.cu``.
+    """
+    if (
+        use_native(q)
+        and q.dtype == torch.bfloat16
+        and c_kv.dtype == torch.bfloat16
+        and k_pe.dtype == torch.bfloat16
+        and q.shape[-1] == 576
+        and c_kv.shape[-1] == 512
+        and k_pe.shape[-1] == 64
+        and c_kv.stride(-1) == 1
+        and k_pe.stride(-1) == 1
+        and all(st % 8 == 0 for st in (*c_kv.stride()[:-1], *k_pe.stride()[:-1]))
+    ):
+        return native().mla_decode(q.contiguous(), c_kv, k_pe, lengths, float(scale))
+    return reference.mla_decode(q, c_kv, k_pe, scale=scale, lengths=lengths)
 
 
 def decode_attention(

@@ -203,7 +203,12 @@ def main() -> None:
     ap.add_argument("--decode", action="store_true", help="decode attention kernel and graph-replayed decode steps")
     ap.add_argument("--ns", action="store_true", help="Newton-Schulz / Polar-Express chains vs the torch path")
     ap.add_argument("--gdn", action="store_true", help="gated delta-rule chunk scan vs the torch chunked path")
+    ap.add_argument("--mla-decode", action="store_true", help="latent-space MLA decode kernel vs the einsum order")
     args = ap.parse_args()
+    if args.mla_decode:
+        for r in bench_mla_decode():
+            print(json.dumps(r))
+        return
     if args.gdn:
         for r in bench_gated_delta():
             print(json.dumps(r))
@@ -337,6 +342,28 @@ def bench_decode() -> list[dict]:
     return rows
 
 
+def bench_mla_decode() -> list[dict]:
+    """Latent-space MLA decode (one token per sequence, 512 latent + 64 rotary) against the einsum
+    order on the same bf16 cache; bytes = the cache rows read once (c_kv and k_pe)."""
+    from priml_b200 import ops
+    from priml_b200.ops import reference
+
+    _, hbm = _peaks()
+    rows = []
+    for b, h, t in ((1, 16, 4096), (16, 16, 4096), (64, 16, 4096), (16, 16, 32768), (16, 128, 4096)):
+        q = torch.randn(b, h, 576, device="cuda", dtype=torch.bfloat16)
+        c = torch.randn(b, t, 512, device="cuda", dtype=torch.bfloat16)
+        r = torch.randn(b, t, 64, device="cuda", dtype=torch.bfloat16)
+        scale = 192**-0.5
+        nbytes = (c.numel() + r.numel()) * 2
+        t_ours = time_fn(lambda: ops.mla_decode(q, c, r, scale=scale), iters=20)
+        t_ref = time_fn(lambda: reference.mla_decode(q, c, r, scale=scale), iters=5)
+        rows.append({"case": "mla_decode", "B": b, "H": h, "T": t, "ours_us": round(1e3 * t_ours, 1),
+                     "einsum_us": round(1e3 * t_ref, 1), "ours_gbs": round(nbytes / t_ours / 1e6, 1),
+                     "ours_frac_hbm": round(nbytes / t_ours / 1e6 / hbm, 3)})  # fmt: skip
+    return rows
+
+
 def bench_gated_delta(b: int = 4, s: int = 4096, h: int = 16, d: int = 128) -> list[dict]:
     """Gated delta rule forward and forward + backward: chunk scan kernels against the torch chunked path."""
     from priml_b200.models.gated_delta_net import gated_delta_chunked
@@ -380,6 +407,15 @@ def profile_case(name: str) -> None:
         for _ in range(2):
             o = gated_delta_rule(q, q, q, g, beta)
             o.backward(torch.ones_like(o))
+    elif name == "mla_decode":
+        # latent-space MLA decode: 64 sequences x 4096 cached tokens, 16 heads (302 MB of cache)
+        from priml_b200 import ops
+
+        q = torch.randn(64, 16, 576, device="cuda", dtype=torch.bfloat16)
+        c = torch.randn(64, 4096, 512, device="cuda", dtype=torch.bfloat16)
+        r = torch.randn(64, 4096, 64, device="cuda", dtype=torch.bfloat16)
+        for _ in range(3):
+            ops.mla_decode(q, c, r, scale=192**-0.5)
     elif name == "gemm":
         a = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
         b = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)

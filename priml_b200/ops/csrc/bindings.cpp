@@ -607,6 +607,55 @@ std::vector<Tensor> gdn_bwd(const Tensor& kr, const Tensor& mqk, const Tensor& d
 
 // Decode attention: q [B, H, D] over caches [B, Hkv, T, D] (rows contiguous) with
 // int32 lengths [B] on the device; returns [B, H, D].
+// Multi-head latent attention decode in latent space (mla_decode.cu). q [B, H, 576] = [q_abs | q_pe]
+// (contiguous bf16); c_kv [B, T, 512] and k_pe [B, T, 64] bf16 with contiguous channels and 16-byte
+// aligned row / sequence strides; lengths int32 [B] (keys visible per sequence) or none (all T).
+// Returns the attention-weighted latent rows [B, H, 512] (bf16).
+Tensor mla_decode(const Tensor& q, const Tensor& ckv, const Tensor& kpe, const c10::optional<Tensor>& lengths,
+                  double scale) {
+  check_cuda(q, "q");
+  check_cuda(ckv, "c_kv");
+  check_cuda(kpe, "k_pe");
+  PB_CHECK(q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3 && q.size(2) == 576,
+           "q must be contiguous bf16 [B, H, 576]");
+  const int64_t B = q.size(0), H = q.size(1);
+  PB_CHECK(ckv.scalar_type() == torch::kBFloat16 && ckv.dim() == 3 && ckv.size(0) == B && ckv.size(2) == 512 &&
+               ckv.stride(2) == 1 && ckv.stride(1) % 8 == 0 && ckv.stride(0) % 8 == 0,
+           "c_kv must be bf16 [B, T, 512] with contiguous channels and 16-byte aligned strides");
+  const int64_t T = ckv.size(1);
+  PB_CHECK(kpe.scalar_type() == torch::kBFloat16 && kpe.dim() == 3 && kpe.size(0) == B && kpe.size(1) == T &&
+               kpe.size(2) == 64 && kpe.stride(2) == 1 && kpe.stride(1) % 8 == 0 && kpe.stride(0) % 8 == 0,
+           "k_pe must be bf16 [B, T, 64] with contiguous channels and 16-byte aligned strides");
+  PB_CHECK(T >= 1 && T < (1LL << 31) && B * H < (1LL << 31), "sizes out of range");
+  auto out = torch::empty({B, H, 512}, q.options());
+  pb::MlaDecodeParams p{};
+  p.B = static_cast<int>(B);
+  p.H = static_cast<int>(H);
+  p.T = static_cast<int>(T);
+  const int nh = pb::mla_decode_head_tile(p.H);
+  p.head_groups = (p.H + nh - 1) / nh;
+  pb::mla_decode_plan(p.B, p.H, p.T, pb::device_sm_count(), &p.splits, &p.tiles_per_split);
+  Tensor part_o, part_ml, lens;
+  if (lengths.has_value()) {
+    PB_CHECK(lengths->numel() == B, "lengths must have one entry per sequence");
+    lens = lengths->to(q.device(), torch::kInt32).contiguous();
+    p.lengths = lens.data_ptr<int>();
+  }
+  if (p.splits > 1) {
+    part_o = torch::empty({B, p.splits, H, 512}, q.options().dtype(torch::kFloat32));
+    part_ml = torch::empty({B, p.splits, H, 2}, q.options().dtype(torch::kFloat32));
+    p.part_o = part_o.data_ptr<float>();
+    p.part_ml = part_ml.data_ptr<float>();
+  }
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.status = status_ptr();
+  const c10::cuda::CUDAGuard guard(q.device());
+  pb::mla_decode(p, q.data_ptr(), ckv.data_ptr(), ckv.stride(0), ckv.stride(1), kpe.data_ptr(), kpe.stride(0),
+                 kpe.stride(1), stream());
+  return out;
+}
+
 Tensor decode_attn(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lengths, double scale,
                    int64_t window) {
   PB_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.is_contiguous(),
@@ -1419,6 +1468,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("softcap") = 0.0);
   m.def("gdn_fwd", &gdn_fwd, "gated delta-rule chunk scan, forward (tcgen05)");
   m.def("gdn_bwd", &gdn_bwd, "gated delta-rule chunk scan, backward (tcgen05)");
+  m.def("mla_decode", &mla_decode, "multi-head latent attention decode in latent space (one query per sequence)",
+        py::arg("q"), py::arg("c_kv"), py::arg("k_pe"), py::arg("lengths"), py::arg("scale"));
   m.def("decode_attn", &decode_attn, "one-token decode attention over a KV cache with device lengths",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("lengths"), py::arg("scale"), py::arg("window") = -1);
   m.def("attn_fwd", &attn_fwd, "flash attention forward (tcgen05); trace: optional int32 [8 * CTAs] progress record",

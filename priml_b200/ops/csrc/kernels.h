@@ -300,6 +300,24 @@ void ep_combine(const EpCombineParams& p, cudaStream_t stream);
 void ep_expand(const void* dy, const float* w, const void* y, void* out, float* dw, long long slots, int k, int cols,
                cudaStream_t stream);
 
+// Multi-head latent attention decode in latent space (mla_decode.cu): one query per sequence,
+// q [B, H, 576] = [q_abs (512) | q_pe (64)] rows, caches c_kv [B, T, 512] and k_pe [B, T, 64]
+// (contiguous channels, element strides for rows and sequences); out [B, H, 512] bf16.
+struct MlaDecodeParams {
+  int B, H, T;
+  int splits, tiles_per_split, head_groups;
+  const int* lengths;      // [B] keys visible per sequence, or null (all T)
+  float scale_log2;        // softmax scale * log2(e)
+  __nv_bfloat16* out;
+  float* part_o;           // [B, splits, H, 512] (splits > 1)
+  float* part_ml;          // [B, splits, H, 2]
+  int* status;
+};
+int mla_decode_head_tile(int H);
+void mla_decode_plan(int B, int H, int T, int sm_count, int* splits, int* tiles_per_split);
+void mla_decode(const MlaDecodeParams& p, const void* q, const void* ckv, long long c_sb, long long c_st, const void* kpe,
+                long long r_sb, long long r_st, cudaStream_t stream);
+
 int tp_gemm_grid(int M, int N);
 void tp_ag_gemm(const TpGemmParams& p, const void* a_shard, const void* B, long long ldb, bool b_mn, int grid,
                 cudaStream_t stream);

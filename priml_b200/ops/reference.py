@@ -97,6 +97,23 @@ def decode_attention(
     return torch.einsum("bht,bhtd->bhd", p, vf).to(q.dtype)
 
 
+def mla_decode(
+    q: Tensor, c_kv: Tensor, k_pe: Tensor, *, scale: float, lengths: Tensor | None = None
+) -> Tensor:
+    """fp32 oracle of latent-space MLA decode: ``q [B, H, 576] = [q_abs | q_pe]`` over
+    ``c_kv [B, T, 512]`` and ``k_pe [B, T, 64]``; returns the softmax-weighted latent rows ``[B, H, 512]``."""
+    lat = c_kv.shape[-1]
+    c = c_kv.float()
+    s = (torch.einsum("bhl,btl->bht", q[..., :lat].float(), c)
+         + torch.einsum("bhr,btr->bht", q[..., lat:].float(), k_pe.float())) * scale  # fmt: skip
+    if lengths is not None:
+        pos = torch.arange(c.shape[1], device=q.device)
+        ok = pos[None, :] < lengths.to(device=q.device, dtype=torch.long)[:, None]
+        s = s.masked_fill(~ok[:, None, :], float("-inf"))
+    p = torch.nan_to_num(s.softmax(dim=-1), nan=0.0)
+    return torch.einsum("bht,btl->bhl", p, c).to(q.dtype)
+
+
 def cross_entropy(logits: Tensor, targets: Tensor, *, ignore_index: int = -100, softcap: float | None = None) -> Tensor:
     """Unreduced token cross-entropy computed in fp32."""
     lf = logits.float()
