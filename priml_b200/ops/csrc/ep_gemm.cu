@@ -355,7 +355,6 @@ __global__ void __launch_bounds__(PULL ? 256 : 192, 1)
       for (int q = 0; q < p.world; ++q) st_release_sys(sig(p, q, kEpSigSendReady + p.rank), static_cast<unsigned long long>(p.epoch));
     }
     const int wpr = p.K / 8;  // 16-byte words per row
-    const int words = kEpPieceRows * wpr;
     unsigned int seen = 0;      // sources whose announcement this warp has seen
     bool ok = true;
     const int pieces = num_m * kEpPiecesPerChunk;
@@ -384,24 +383,36 @@ __global__ void __launch_bounds__(PULL ? 256 : 192, 1)
         }
         seen |= need;
       }
+      // Two rows at a time, each with one source pointer for the whole warp (a shuffle per row,
+      // not per word): every lane keeps 16 loads of 16 bytes in flight and spends a handful of
+      // instructions per word, so the copy warps do not steal issue slots from the MMA pipeline.
       uint4* dst = reinterpret_cast<uint4*>(p.a_local) + r0 * wpr;
-      constexpr int U = 16;
-      for (int base = lane; base < words; base += 32 * U) {
-        uint4 buf[U];
+      constexpr int U = 8;
+#pragma unroll 1
+      for (int rr = 0; rr < kEpPieceRows; rr += 2) {
+        const int s0 = __shfl_sync(0xffffffffu, my_src, rr), s1 = __shfl_sync(0xffffffffu, my_src, rr + 1);
+        const uint4* a0 = s0 >= 0 ? reinterpret_cast<const uint4*>(p.src[s0 >> 24]) + static_cast<long long>(s0 & 0xFFFFFF) * wpr : nullptr;
+        const uint4* a1 = s1 >= 0 ? reinterpret_cast<const uint4*>(p.src[s1 >> 24]) + static_cast<long long>(s1 & 0xFFFFFF) * wpr : nullptr;
+        uint4* d0 = dst + rr * wpr;
+        uint4* d1 = d0 + wpr;
+#pragma unroll 1
+        for (int c = lane; c < wpr; c += 32 * U) {
+          uint4 b0[U], b1[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int wi = base + 32 * u;
-          const int rr = min(wi, words - 1) / wpr;
-          const int s = __shfl_sync(0xffffffffu, my_src, rr);
-          buf[u] = make_uint4(0u, 0u, 0u, 0u);
-          if (wi < words && s >= 0) {
-            const uint4* src = reinterpret_cast<const uint4*>(p.src[s >> 24]) + static_cast<long long>(s & 0xFFFFFF) * wpr;
-            buf[u] = __ldcg(src + (wi - rr * wpr));
+          for (int u = 0; u < U; ++u) {
+            const int cc = c + 32 * u;
+            b0[u] = a0 != nullptr && cc < wpr ? __ldcg(a0 + cc) : make_uint4(0u, 0u, 0u, 0u);
+            b1[u] = a1 != nullptr && cc < wpr ? __ldcg(a1 + cc) : make_uint4(0u, 0u, 0u, 0u);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int cc = c + 32 * u;
+            if (cc < wpr) {
+              d0[cc] = b0[u];
+              d1[cc] = b1[u];
+            }
           }
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (base + 32 * u < words) dst[base + 32 * u] = buf[u];
       }
       __threadfence();
       __syncwarp();
