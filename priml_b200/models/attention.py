@@ -482,7 +482,7 @@ class MultiStreamAttention(nn.Module):
         widths = config.channels_in if isinstance(config.channels_in, list) else [config.channels_in] * config.num_streams
         self.heads = config.heads
         self.channels_head = config.channels_head
-        self.proj_qkv = nn.ModuleList(
+        self.proj_qkvs = nn.ModuleList(
             EnsembleLinear.Config(
                 channels_in=w,
                 channels_out=config.channels_head,
@@ -493,7 +493,7 @@ class MultiStreamAttention(nn.Module):
             ).make()
             for w in widths
         )
-        self.proj_out = nn.ModuleList(
+        self.proj_outs = nn.ModuleList(
             Linear.Config(
                 channels_in=config.heads * config.channels_head,
                 channels_out=w,
@@ -503,25 +503,26 @@ class MultiStreamAttention(nn.Module):
             ).make()
             for w in widths
         )
-        self.norm_q = nn.ModuleList(config.norm_qk.make() for _ in widths) if config.norm_qk else None
-        self.norm_k = nn.ModuleList(config.norm_qk.make() for _ in widths) if config.norm_qk else None
+        # one q / k norm shared by every stream (the reference's state-dict layout)
+        self.norm_q = config.norm_qk.make() if config.norm_qk else None
+        self.norm_k = config.norm_qk.make() if config.norm_qk else None
         self.attn_kernel = config.attn_kernel.make()
 
     def reset_parameters(self) -> None:
-        for m in (*self.proj_qkv, *self.proj_out):
+        for m in (*self.proj_qkvs, *self.proj_outs):
             m.reset_parameters()
 
     def forward(self, streams: list[Tensor], *args: Any, **kwargs: Any) -> list[Tensor]:
         del args, kwargs
         qs, ks, vs, lens = [], [], [], []
         for i, x in enumerate(streams):
-            q, k, v = self.proj_qkv[i](x).split([self.heads] * 3, dim=-2)
+            q, k, v = self.proj_qkvs[i](x).split([self.heads] * 3, dim=-2)
             if self.norm_q is not None and self.norm_k is not None:
-                q, k = self.norm_q[i](q), self.norm_k[i](k)
+                q, k = self.norm_q(q), self.norm_k(k)
             qs.append(q)
             ks.append(k)
             vs.append(v)
             lens.append(x.shape[-2])
         out = self.attn_kernel(torch.cat(qs, -3), torch.cat(ks, -3), torch.cat(vs, -3))
         outs = out.flatten(-2).split(lens, dim=-2)
-        return [self.proj_out[i](o) for i, o in enumerate(outs)]
+        return [self.proj_outs[i](o) for i, o in enumerate(outs)]

@@ -104,7 +104,8 @@ class AdaLNZero(nn.Module):
 
 class MMDiTBlock(nn.Module):
     """N token streams with joint attention; each stream its own norms / FFN and
-    optional AdaLN-zero conditioning (``priml/model/mmdit.py:111-293``)."""
+    optional AdaLN-zero conditioning (``priml/model/mmdit.py:111-293``). Submodule names
+    (``norms1``, ``norms2``, ``ffns``, ``adalns``) give the reference's state-dict keys."""
 
     class Config(Fig["MMDiTBlock"], kw_only=False):
         channels_in: int = 768
@@ -126,10 +127,10 @@ class MMDiTBlock(nn.Module):
         super().__init__()
         c, n = config.channels_in, config.num_streams
         self.attn = config.attn.make()
-        self.norm1 = nn.ModuleList(LayerNorm.Config(c).make() for _ in range(n))
-        self.norm2 = nn.ModuleList(LayerNorm.Config(c).make() for _ in range(n))
-        self.ffn = nn.ModuleList(config.ffn.make() for _ in range(n))
-        self.mod = (
+        self.norms1 = nn.ModuleList(LayerNorm.Config(c).make() for _ in range(n))
+        self.norms2 = nn.ModuleList(LayerNorm.Config(c).make() for _ in range(n))
+        self.ffns = nn.ModuleList(config.ffn.make() for _ in range(n))
+        self.adalns = (
             nn.ModuleList(AdaLNZero.Config(c, cond_dim=config.cond_dim).make() for _ in range(n))
             if config.cond_dim > 0
             else None
@@ -139,10 +140,10 @@ class MMDiTBlock(nn.Module):
         del kwargs
         n = len(xs)
         conds = [c] * n if isinstance(c, Tensor) or c is None else list(c)
-        mods = [self.mod[i](conds[i]) if self.mod is not None and conds[i] is not None else None for i in range(n)]
+        mods = [self.adalns[i](conds[i]) if self.adalns is not None and conds[i] is not None else None for i in range(n)]
         normed = []
         for i, x in enumerate(xs):
-            h = self.norm1[i](x)
+            h = self.norms1[i](x)
             if mods[i] is not None:
                 h = h * (1 + mods[i].attn_scale) + mods[i].attn_shift
             normed.append(h)
@@ -151,10 +152,10 @@ class MMDiTBlock(nn.Module):
         for i, x in enumerate(xs):
             a = attn[i] * mods[i].attn_gate if mods[i] is not None else attn[i]
             x = x + a
-            h = self.norm2[i](x)
+            h = self.norms2[i](x)
             if mods[i] is not None:
                 h = h * (1 + mods[i].ffn_scale) + mods[i].ffn_shift
-            f = self.ffn[i](h)
+            f = self.ffns[i](h)
             out.append(x + (f * mods[i].ffn_gate if mods[i] is not None else f))
         return out
 
