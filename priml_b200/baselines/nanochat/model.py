@@ -80,6 +80,19 @@ class NanoChatLM(nn.Module):
         mix: ResidualMix.Config = field(default_factory=ResidualMix.Config)
 
         @property
+        def template(self) -> Any:
+            """The block config every layer copies when ``block`` is a single transformer block.
+
+            A per-layer list (or a block that is not a transformer) has no single template, so
+            asking for one is an error rather than a silent pick of the first layer.
+            """
+            from priml_b200.models.transformer import TransformerBlock
+
+            if not isinstance(self.block, TransformerBlock.Config):
+                raise TypeError(f"block is {type(self.block).__name__}, not one TransformerBlock.Config: no single template")
+            return self.block
+
+        @property
         def value_embedding_layers(self) -> list[int]:
             if self.value_embedding_stride <= 0:
                 return []

@@ -183,6 +183,9 @@ class SudokuNet(nn.Module):
         self.slow_init = nn.Buffer(_latent_init(c), persistent=True)
         self.fast_init = nn.Buffer(_latent_init(c), persistent=True)
         self.recurrence = config.recurrence.make() if config.recurrence is not None else None
+        # an empty persistent buffer that the reference's checkpoints carry (``_dummy``): kept so that
+        # its state dicts load strictly
+        self._dummy = nn.Buffer(torch.empty(0), persistent=True)
         logger.info("sudoku model parameters: %.2fM", sum(p.numel() for p in self.parameters()) / 1e6)
 
     @property

@@ -152,4 +152,6 @@ class SwiGLUReluSquared(SwiGLU):
         gate: bool = False
         act: TensorFn = _relu_squared
         expansion: float = 4.0
+        round_to: int = 1
+        """No rounding: the hidden width is exactly ``expansion * channels_in``."""
         init_weight_out: InitFn | None = zeros
