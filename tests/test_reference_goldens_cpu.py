@@ -2,7 +2,8 @@
 
 The reference ships bit-for-bit goldens (``*/goldens/*_min_cpu.pt``: a module's
 state dict, an input and the output of its CPU forward) for five model blocks and
-for the nanochat, CIFAR-10 and sudoku models. Each case builds the module here
+for the nanochat (including the model its experiment ladder builds), CIFAR-10 and
+sudoku models. Each case builds the module here
 with the golden test's configuration, loads the reference state dict strictly (so
 parameter names and shapes are the reference's) and checks:
 
@@ -148,6 +149,15 @@ def _sudoku(ref: bool, recurrent: bool = False) -> nn.Module:
     return cfg.make()
 
 
+def _nanochat_smoke(ref: bool) -> nn.Module:
+    """The model the experiment ladder's smallest rung builds (exp_smoke, run under bf16 autocast)."""
+    if ref:
+        from priml.baselines.nanochat import experiments
+    else:
+        from priml_b200.baselines.nanochat import experiments
+    return experiments.exp_smoke().step.model.make()
+
+
 # cases evaluated in another order than the reference's module (see the module docstring)
 REORDERED = {"moe", "gated_delta_net", "mmdit_block"}
 
@@ -161,6 +171,8 @@ CASES: dict[str, tuple[str, Callable[..., nn.Module], float]] = {
     "nanochat": ("baselines/nanochat/goldens/plain_min_cpu.pt", _nanochat, 1e-5),
     "nanochat_value_embedding": ("baselines/nanochat/goldens/value_embedding_min_cpu.pt",
                                  lambda ref: _nanochat(ref, value_embedding_stride=1), 1e-5),  # fmt: skip
+    # bf16 autocast: the mint host's bf16 matmuls round differently from this host's
+    "nanochat_exp_smoke": ("baselines/nanochat/goldens/exp_smoke_forward_min_cpu.pt", _nanochat_smoke, 3e-2),
     "cifar10_resnet": ("baselines/cifar10/goldens/resnet_min_cpu.pt", _resnet, 1e-5),
     "cifar10_speednet": ("baselines/cifar10/goldens/speednet_min_cpu.pt", _speednet, 1e-5),
     # the post-norm recurrence compounds the reduction-order difference over its cycles
@@ -177,7 +189,8 @@ def test_module_matches_reference_golden_and_module(name: str) -> None:
     ours, theirs = build(False), build(True)
     ours.load_state_dict(golden["state_dict"], strict=True)
     theirs.load_state_dict(golden["state_dict"], strict=True)
-    with torch.no_grad():
+    autocast = torch.amp.autocast(device_type="cpu", dtype=torch.bfloat16, enabled=name == "nanochat_exp_smoke")
+    with torch.no_grad(), autocast:
         out = _out(ours(golden["input"]))
         ref_out = _out(theirs(golden["input"]))
     stored = golden["output"]
