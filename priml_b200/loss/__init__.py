@@ -11,7 +11,7 @@ import functools
 import math
 from collections.abc import Callable
 from dataclasses import field
-from typing import Any
+from typing import Any, Protocol
 
 import torch
 import torch.nn.functional as F
@@ -28,6 +28,7 @@ __all__ = [
     "LPIPSLoss",
     "LossOutput",
     "SimpleLoss",
+    "SimpleLossFn",
     "TokenCrossEntropy",
     "WeightedSum",
     "categorical_entropy",
@@ -36,6 +37,12 @@ __all__ = [
 
 LossOutput = dict[str, Tensor]
 
+
+
+class SimpleLossFn(Protocol):
+    """A PyTorch-style loss function: ``fn(input, target, reduction=...)``."""
+
+    def __call__(self, input: Tensor, target: Tensor, *, reduction: str = "mean") -> Tensor: ...  # noqa: A002
 
 class SimpleLoss:
     """Wraps a functional loss: ``{"loss": loss_fn(prediction, batch[target_key], **kwargs)}``."""

@@ -68,17 +68,12 @@ from priml_b200.models.vision import (
     Unpatchify,
 )
 
+from priml_b200.models.init import InitFn
+from priml_b200.models.kimi_k2 import KimiK2
+from priml_b200.models.norm import NormConfigProtocol, NormProtocol
+from priml_b200.models.qwen3 import Qwen3
+
 __all__ = [
-    "ValueGatedAttention",
-    "Unpatchify",
-    "PCAWhiteningConv2d",
-    "Patchify",
-    "MMDiTBlock",
-    "MLPMixerBlock",
-    "GatedDeltaNet",
-    "Conv3d",
-    "Conv2d",
-    "Conv1d",
     "AdaLNZero",
     "BatchNorm",
     "BatchNorm2d",
@@ -88,21 +83,34 @@ __all__ = [
     "ChannelsIn",
     "ChannelsInOut",
     "ChannelsOut",
+    "Conv1d",
+    "Conv2d",
+    "Conv3d",
     "Embedding",
     "EnsembleLinear",
+    "GatedDeltaNet",
     "GroupNorm",
     "GroupNorm2d",
     "HasDepth",
     "HeadGeometry",
     "Identity",
+    "InitFn",
     "KVCache",
+    "KimiK2",
     "LayerNorm",
     "Linear",
+    "MLPMixerBlock",
+    "MMDiTBlock",
     "MoE",
     "MultiHeadLatentAttention",
     "MultiStreamAttention",
     "NarrowEmbedding",
+    "NormConfigProtocol",
+    "NormProtocol",
     "OutputGate",
+    "PCAWhiteningConv2d",
+    "Patchify",
+    "Qwen3",
     "RMSNorm",
     "ResidualMix",
     "RoPE",
@@ -119,6 +127,8 @@ __all__ = [
     "SwiGLU",
     "SwiGLUReluSquared",
     "TransformerBlock",
+    "Unpatchify",
+    "ValueGatedAttention",
     "YarnScaling",
     "call_init",
     "dirac",

@@ -7,7 +7,7 @@ fp32 statistics, optional weight) and ATen's ``rms_norm`` on CPU.
 from __future__ import annotations
 
 from dataclasses import KW_ONLY
-from typing import Any
+from typing import Any, Protocol
 
 import torch
 from torch import Tensor, nn
@@ -26,6 +26,22 @@ __all__ = [
     "RMSNorm",
 ]
 
+
+
+class NormProtocol(Protocol):
+    """A normalization layer: called on a tensor, returns one of the same shape."""
+
+    def __call__(self, input: Tensor, *args: Any, **kwargs: Any) -> Tensor: ...  # noqa: A002
+
+
+class NormConfigProtocol(Protocol):
+    """The fields every norm config shares, so a container can push its width (and whether the
+    norm has a learned scale) into a nested norm config of any type."""
+
+    channels_in: int
+    elementwise_affine: bool
+
+    def make(self) -> Any: ...
 
 class RMSNorm(nn.RMSNorm):
     """Root-mean-square norm; ``eps=None`` takes the input dtype's epsilon."""

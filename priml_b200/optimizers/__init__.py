@@ -8,7 +8,7 @@ from typing import Any, Protocol
 
 import torch
 
-from priml_b200.optimizers.composite import CompositeOptimizer, complement, everything, excluding, matching
+from priml_b200.optimizers.composite import Selector, CompositeOptimizer, complement, everything, excluding, matching
 from priml_b200.optimizers.fused_adamw import FusedAdamW
 from priml_b200.optimizers.misc import AdamATan2, Newton, SignSGD
 from priml_b200.optimizers.muon import (
@@ -23,9 +23,11 @@ __all__ = [
     "AdamATan2",
     "CompositeOptimizer",
     "FusedAdamW",
+    "HasParamGroups",
     "Muon",
     "Newton",
     "NorMuon",
+    "Selector",
     "SignSGD",
     "adjust_lr_conv_heuristic",
     "adjust_lr_match_rms_adamw",

@@ -11,7 +11,7 @@ from __future__ import annotations
 from collections.abc import Callable, Iterator, MutableMapping, Sequence
 from dataclasses import field
 from functools import partial
-from typing import Any
+from typing import Any, Protocol
 
 from torch import nn
 from torch.nn import Parameter
@@ -31,6 +31,12 @@ def _name(sel: Any) -> str:
     q = getattr(sel, "__qualname__", None)
     return q if isinstance(q, str) else repr(sel)
 
+
+
+class Selector(Protocol):
+    """Whether one named parameter belongs to a member optimizer of a composite."""
+
+    def __call__(self, name: str, parameter: Any) -> bool: ...
 
 class excluding:  # noqa: N801
     __slots__ = ("fragments", "select")

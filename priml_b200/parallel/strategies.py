@@ -17,6 +17,8 @@ all-gather-GEMM / reduce-scatter-optimizer path lives in
 
 from __future__ import annotations
 
+from collections.abc import Sequence
+
 from dataclasses import field
 from typing import Any
 
@@ -33,6 +35,7 @@ __all__ = [
     "HybridSharded",
     "NoParallel",
     "RecursiveFullySharded",
+    "RecursiveSharded",
     "materialize_meta",
     "place",
 ]
@@ -233,3 +236,23 @@ class RecursiveFullySharded(FullySharded):
         else:
             model.to(dev)
         return model
+
+
+class RecursiveSharded(RecursiveFullySharded):
+    """The reference's name and configuration for recursive FSDP (``priml/train/parallelism.py:275-330``):
+    modules are selected by class (``module_types``) instead of by class name; sharding, mixed
+    precision and materialization are :class:`RecursiveFullySharded`'s."""
+
+    class Config(Fig["RecursiveSharded"]):
+        device: torch.device | str | None = "auto"
+        mesh_dim: str = "dp"
+        module_types: Sequence[type[nn.Module]] = ()
+        reshard_after_forward: bool = True
+        mp_param_dtype: Any = None
+        mp_reduce_dtype: Any = None
+        mp_output_dtype: Any = None
+        per_block: bool = False
+
+        @property
+        def block_types(self) -> list[str]:
+            return [t.__name__ for t in self.module_types]

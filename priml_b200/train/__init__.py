@@ -28,33 +28,37 @@ from priml_b200.train.results import format_summary, read_metrics, summarize
 from priml_b200.train.train_step import TrainStep, TrainStepOutput
 from priml_b200.train.train_step_gan import GANTrainStep
 
+from priml_b200.optimizers.misc import Newton
+from priml_b200.parallel.strategies import RecursiveSharded
+from priml_b200.train.custom_types import ModelQuantizationProtocol, ParallelStrategyProtocol
+
 __all__ = [
-    "Float8ModelQuantization",
-    "NoModelQuantization",
-    "GANTrainStep",
-    "format_summary",
-    "read_metrics",
-    "summarize",
-    "write_progress",
-    "EMA",
     "AsyncLocalStateDictStorer",
     "AsyncTracker",
     "Checkpointer",
     "DataParallel",
     "DefaultActivationStorage",
+    "EMA",
     "EvalTimeLimitError",
     "FileTracker",
     "Float8ActivationStorage",
+    "Float8ModelQuantization",
     "FullySharded",
+    "GANTrainStep",
     "HybridSharded",
     "LayerActivationCheckpointing",
-    "QuantizedActivationStorage",
-    "QuantizedModuleActivationStorage",
+    "ModelQuantizationProtocol",
+    "Newton",
     "NoEMA",
+    "NoModelQuantization",
     "NoParallel",
     "NoTracker",
+    "ParallelStrategyProtocol",
     "PhaseTimer",
+    "QuantizedActivationStorage",
+    "QuantizedModuleActivationStorage",
     "RecursiveFullySharded",
+    "RecursiveSharded",
     "SelectiveActivationCheckpointing",
     "SyncLocalStateDictStorer",
     "TensorBoardTracker",
@@ -66,6 +70,10 @@ __all__ = [
     "TrainStepOutput",
     "WandbTracker",
     "apply_tensor_parallel",
+    "format_summary",
     "karras_decay",
     "materialize_meta",
+    "read_metrics",
+    "summarize",
+    "write_progress",
 ]

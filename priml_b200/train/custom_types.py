@@ -127,3 +127,18 @@ class PhaseTimerProtocol(Protocol):
     def cuda_events_enabled(self) -> bool: ...
 
     def phase(self, name: str) -> AbstractContextManager[None]: ...
+
+
+@runtime_checkable
+class ParallelStrategyProtocol(Protocol):
+    """A parallel strategy: ``__call__`` places, shards and materializes a model on ``device``."""
+
+    device: torch.device
+
+    def __call__(self, model: nn.Module) -> nn.Module: ...
+
+
+class ModelQuantizationProtocol(Protocol):
+    """A model quantization: ``__call__`` returns the model with its layers converted."""
+
+    def __call__(self, model: nn.Module) -> nn.Module: ...

@@ -195,6 +195,12 @@ def _strategy_losses(rank: int, world: int, steps: int, kind: str) -> list[float
     torch.manual_seed(0)
     if kind == "hsdp":
         parallel = HybridSharded.Config(device="cpu", replicate_dim="dp", shard_dim="tp")
+    elif kind == "recursive_types":  # the reference's configuration surface: classes, not names
+        from priml_b200.models.swiglu import SwiGLU
+        from priml_b200.models.transformer import TransformerBlock
+        from priml_b200.parallel.strategies import RecursiveSharded
+
+        parallel = RecursiveSharded.Config(device="cpu", module_types=(TransformerBlock, SwiGLU))
     else:
         parallel = RecursiveFullySharded.Config(device="cpu", block_types=["TransformerBlock", "SwiGLU"])
     step = _tiny_step_cfg(parallel).make()
@@ -208,7 +214,9 @@ def _strategy_losses(rank: int, world: int, steps: int, kind: str) -> list[float
     return losses
 
 
-@pytest.mark.parametrize("kind,world,mesh", [("hsdp", 4, {"dp": 2, "tp": 2}), ("recursive", 2, {"dp": 2})])
+@pytest.mark.parametrize(
+    "kind,world,mesh", [("hsdp", 4, {"dp": 2, "tp": 2}), ("recursive", 2, {"dp": 2}), ("recursive_types", 2, {"dp": 2})]
+)
 def test_hybrid_and_recursive_sharding_match_single_process(kind: str, world: int, mesh: dict) -> None:
     """HSDP (replicate over dp, shard over tp) and per-module FSDP track the one-process run."""
     steps = 4
